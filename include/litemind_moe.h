@@ -1,0 +1,209 @@
+/*
+ * litemind_moe.h -- C ABI of the B200 MoE feed-forward path.
+ *
+ * Drop-in boundary for LiteMind's mixture-of-experts block (ragavanperarasu/LiteMind).
+ * The reference runs that block on the CPU, one token at a time, inside
+ * DeepSeekRunner::Impl::forward (src/DeepSeekRunner.cpp:264-290) over three
+ * interfaces: MoeRouter (include/MoeRouter.hpp:27-55), the gemm:: kernels
+ * (include/Gemm.hpp:23-72) and ExpertCache (include/ExpertCache.hpp:29-89).
+ * This header exposes the same path for T tokens at once on one B200:
+ *
+ *   lm_moe_create / lm_moe_upload_layer   load: weights resident in HBM
+ *                                         (replaces DeepSeekRunner::Impl::resolve_layer
+ *                                          src/DeepSeekRunner.cpp:179-224 and the
+ *                                          ExpertCache's SSD paging)
+ *   lm_moe_route, lm_moe_select           MoeRouter::select (src/MoeRouter.cpp:54-107)
+ *                                         after gemm::matvec_f32 (src/Gemm.cpp:132-137)
+ *   lm_moe_forward                        the whole MoE block of src/DeepSeekRunner.cpp:268-288
+ *   lm_gemm_*                             the gemm:: kernels of include/Gemm.hpp, on device
+ *
+ * Conventions
+ *  - Plain C: pointers and sizes only.  bf16 tensors are passed as uint16_t bit
+ *    patterns; a stream is a cudaStream_t passed as void* (NULL = legacy stream).
+ *  - Every entry point returns an lm_status (0 = LM_OK).  No exception crosses the
+ *    ABI.  The context keeps a message for the last failure (lm_moe_last_error).
+ *  - "device" pointers are CUDA device memory on the context's device; "host"
+ *    pointers are ordinary CPU memory.  Calls that take device pointers are
+ *    asynchronous on the given stream; lm_moe_sync waits and reports device-side
+ *    errors (a kernel that gave up waiting sets a status word instead of hanging).
+ *  - One context per device per host thread; calls on one context are not
+ *    thread-safe, as MoeRouter is not (include/MoeRouter.hpp:53-54).
+ *  - There is no CPU fallback: a missing GPU is an error (LM_ERR_CUDA).
+ */
+#ifndef LITEMIND_MOE_H
+#define LITEMIND_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t lm_status;
+
+#define LM_OK 0
+#define LM_ERR_INVALID_ARGUMENT 1 /* bad size, null pointer, unsupported shape */
+#define LM_ERR_CUDA 2             /* a CUDA runtime call failed (message has details) */
+#define LM_ERR_NOT_LOADED 3       /* layer weights were never uploaded */
+#define LM_ERR_TOO_MANY_TOKENS 4  /* T exceeds the context's max_tokens */
+#define LM_ERR_DEVICE_TIMEOUT 5   /* a kernel's bounded wait expired; results are invalid */
+#define LM_ERR_COMM 6             /* NCCL failure in expert-parallel mode */
+#define LM_ERR_UNSUPPORTED 7
+
+#define LM_TOPK_GREEDY 0               /* Config::topk_method "greedy" */
+#define LM_TOPK_GROUP_LIMITED_GREEDY 1 /* Config::topk_method "group_limited_greedy" */
+
+/* The Config fields that drive the MoE path (include/Config.hpp:59-71), plus the
+ * sizing of what the context keeps resident. */
+typedef struct lm_moe_config {
+    int32_t hidden_size;           /* 2048 on DeepSeek-V2-Lite */
+    int32_t moe_intermediate_size; /* 1408 */
+    int32_t n_routed_experts;      /* 64 */
+    int32_t n_shared_experts;      /* 2: one shared FFN of width inter * n_shared */
+    int32_t num_experts_per_tok;   /* 6 */
+    int32_t norm_topk_prob;        /* 0: weights are raw softmax probabilities */
+    float routed_scaling_factor;   /* 1.0; applied only when not normalising */
+    int32_t topk_method;           /* LM_TOPK_* */
+    int32_t n_group;               /* group-limited routing: groups of experts */
+    int32_t topk_group;            /* group-limited routing: groups kept */
+    float rms_norm_eps;            /* 1e-6, used by lm_moe_block_forward */
+    int32_t num_layers;            /* MoE layers held resident */
+    int32_t max_tokens;            /* largest T of one call (sizes the workspace) */
+} lm_moe_config;
+
+typedef struct lm_moe_ctx lm_moe_ctx;
+
+/* DeepSeek-V2-Lite defaults (include/Config.hpp:43-71), one layer, 16384 tokens. */
+void lm_moe_config_default(lm_moe_config* config);
+
+/* Validates the configuration, selects the device and allocates the workspace.
+ * Replaces DeepSeekRunner::load's router/expert-cache set-up (src/DeepSeekRunner.cpp:358-362). */
+lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** out);
+lm_status lm_moe_destroy(lm_moe_ctx* ctx);
+
+/* Message for the last failing call on this context ("" when none). */
+const char* lm_moe_last_error(const lm_moe_ctx* ctx);
+const char* lm_status_string(lm_status status);
+
+/*
+ * Uploads one MoE layer from host memory, in the reference's safetensors layouts
+ * (src/DeepSeekRunner.cpp:157-222):
+ *   router      [E, hidden] f32   (mlp.gate.weight, widened as read_float32 does)
+ *   gate, up    [E, inter, hidden] bf16     down [E, hidden, inter] bf16
+ *   shared_gate, shared_up [S, hidden] bf16 shared_down [hidden, S] bf16,  S = inter * n_shared
+ *   norm_weight [hidden] f32 or NULL (post_attention_layernorm, for lm_moe_block_forward)
+ * The host arrays are read once; the context owns the device copies.
+ */
+lm_status lm_moe_upload_layer(lm_moe_ctx* ctx, int32_t layer, const float* router,
+                              const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                              const uint16_t* shared_gate, const uint16_t* shared_up,
+                              const uint16_t* shared_down, const float* norm_weight);
+
+/* Uploads one routed expert (the unit ExpertCache::touch streams,
+ * src/ExpertCache.cpp:9-47): gate, up [inter, hidden], down [hidden, inter]. */
+lm_status lm_moe_upload_expert(lm_moe_ctx* ctx, int32_t layer, int32_t expert,
+                               const uint16_t* gate, const uint16_t* up, const uint16_t* down);
+
+/*
+ * Router only: logits = router . x (+ bias) and MoeRouter::select per token.
+ *   x           device bf16 [T, hidden]
+ *   logit_bias  device f32 [E] or NULL (added to every token's logits before the softmax)
+ *   topk_idx    device int32 [T, k]   topk_w device f32 [T, k]  (descending weight)
+ *   logits      device f32 [T, E] or NULL (after the bias)
+ */
+lm_status lm_moe_route(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int32_t tokens,
+                       const float* logit_bias, int32_t* topk_idx, float* topk_w, float* logits,
+                       void* stream);
+
+/* MoeRouter::select on caller-provided logits (device f32 [T, E]). */
+lm_status lm_moe_select(lm_moe_ctx* ctx, const float* logits, int32_t tokens, int32_t* topk_idx,
+                        float* topk_w, void* stream);
+
+/*
+ * The MoE block for T tokens: route, dispatch, grouped SwiGLU experts, weighted
+ * combine with the shared experts (weight 1.0).
+ *   x       device bf16 [T, hidden]
+ *   y       device f32 [T, hidden]; overwritten, or added to when accumulate != 0
+ *           (the reference accumulates into a zeroed buffer, src/DeepSeekRunner.cpp:268)
+ */
+lm_status lm_moe_forward(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int32_t tokens,
+                         const float* logit_bias, float* y, int32_t accumulate, void* stream);
+
+/* lm_moe_forward from host memory: copies x (and the bias) in, runs, copies y out,
+ * and waits.  The end-to-end form of the call the reference makes per token. */
+lm_status lm_moe_forward_host(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x_host,
+                              int32_t tokens, const float* logit_bias_host, float* y_host);
+
+/*
+ * One decoder feed-forward sub-layer, as src/DeepSeekRunner.cpp:264-290 runs it:
+ * normalised = rms_norm(hidden, post_attention_layernorm); hidden += moe(normalised).
+ *   hidden  device f32 [T, hidden], updated in place.
+ * The router sees the f32 normalised activations; the experts see them rounded to bf16.
+ */
+lm_status lm_moe_block_forward(lm_moe_ctx* ctx, int32_t layer, float* hidden, int32_t tokens,
+                               void* stream);
+
+/* Waits for the stream and reports a device-side timeout recorded since the last
+ * call (then clears it). */
+lm_status lm_moe_sync(lm_moe_ctx* ctx, void* stream);
+
+/* Tokens routed to each expert by the last route/forward (host int32 [E]); the
+ * per-expert token histogram.  Waits for the device. */
+lm_status lm_moe_expert_counts(lm_moe_ctx* ctx, int32_t* counts);
+
+/* Bytes of weights resident on the device, and bytes uploaded so far. */
+lm_status lm_moe_memory(const lm_moe_ctx* ctx, uint64_t* resident_bytes, uint64_t* uploaded_bytes);
+
+/*
+ * Profiling hook.  While enabled, each forward records a CUDA event after every
+ * launch of its sequence, waits for the last one and adds each launch's device
+ * time to a per-slot total: slot 0 zeroing y, 1 router logits, 2 router top-k,
+ * 3 dispatch scan, 4 permute, 5 gate/up GEMM, 6 down GEMM, 7 expert-parallel
+ * exchange.  lm_moe_profile_read copies LM_PROFILE_SLOTS totals (ms) and launch
+ * counts to host memory and, when reset != 0, clears them.  No counterpart in the
+ * reference, which has no device launches to time.
+ */
+#define LM_PROFILE_SLOTS 8
+lm_status lm_moe_profile_enable(lm_moe_ctx* ctx, int32_t enable);
+lm_status lm_moe_profile_read(lm_moe_ctx* ctx, double* total_ms, int64_t* launches, int32_t reset);
+
+/*
+ * Expert parallelism over NCCL.  Every rank creates its context with the same
+ * config, then calls this with the same 128-byte ncclUniqueId.  Rank r then keeps
+ * routed experts [r*E/N, (r+1)*E/N) (upload_layer still takes the full arrays and
+ * uploads the rank's shard plus the shared experts), and lm_moe_forward routes
+ * each rank's own T tokens, sends them to the experts' ranks (all-to-all), runs
+ * the local experts and returns the weighted outputs (reverse all-to-all).
+ */
+lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t rank,
+                         int32_t nranks);
+
+/* ── gemm:: kernels on device memory (include/Gemm.hpp:23-72) ──────────────── */
+
+/* gemm::matvec_bf16 (src/Gemm.cpp:139-154): out = W x, W [rows, cols] bf16. */
+lm_status lm_gemm_matvec_bf16(const uint16_t* weights, const float* input, float* out,
+                              int64_t rows, int64_t cols, void* stream);
+/* gemm::matvec_bf16_accumulate (src/Gemm.cpp:156-175): out += scale * W x. */
+lm_status lm_gemm_matvec_bf16_accumulate(const uint16_t* weights, const float* input, float* out,
+                                         int64_t rows, int64_t cols, float scale, void* stream);
+/* gemm::matvec_f32 (src/Gemm.cpp:132-137). */
+lm_status lm_gemm_matvec_f32(const float* weights, const float* input, float* out, int64_t rows,
+                             int64_t cols, void* stream);
+/* gemm::softmax (src/Gemm.cpp:209-223), in place, over `count` values of each of `rows` rows. */
+lm_status lm_gemm_softmax(float* values, int64_t rows, int64_t count, void* stream);
+/* gemm::silu_multiply (src/Gemm.cpp:225-231). */
+lm_status lm_gemm_silu_multiply(const float* gate, const float* up, float* destination,
+                                int64_t count, void* stream);
+/* gemm::rms_norm (src/Gemm.cpp:197-207), in place over each of `rows` rows. */
+lm_status lm_gemm_rms_norm(float* values, const float* weight, int64_t rows, int64_t count,
+                           float epsilon, void* stream);
+/* gemm::axpy (src/Gemm.cpp:191-195): destination += scale * source. */
+lm_status lm_gemm_axpy(float scale, const float* source, float* destination, int64_t count,
+                       void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LITEMIND_MOE_H */

@@ -1,0 +1,378 @@
+// grouped_gemm.cu -- the expert products of the MoE path on tcgen05 tensor cores.
+//
+// The reference computes each selected expert per token as three BF16 matvecs
+// (Impl::feed_forward, src/DeepSeekRunner.cpp:228-240: gemm::matvec_bf16 for gate
+// and up, gemm::silu_multiply, gemm::matvec_bf16_accumulate for down with the
+// routing weight).  Here all tokens of all experts run as two grouped GEMMs over
+// ragged expert segments, weights on the MMA's M side ("swap-AB"), tokens on N:
+//
+//   gate/up:  D[128 weight rows, BN tokens] = W13_e[rows] . X_e^T     (K = hidden)
+//             W13 interleaves gate and up rows in pairs, so the epilogue pairs
+//             lanes 2i/2i+1 and writes h = silu(gate) * up (bf16) for 64 columns
+//             of the intermediate axis.
+//   down:     D[128 hidden rows, BN tokens] = W2_e[rows] . H_e^T       (K = inter)
+//             The epilogue multiplies by each token's routing weight (1.0 for the
+//             shared experts) and adds into y[token] -- the weighted combine and
+//             the un-permute in one step.  Lanes of a warp hold 32 consecutive
+//             hidden rows, so every atomic add is a coalesced 128-byte run.
+//
+// One persistent CTA per SM walks the tile list in the device-built Schedule.
+// Warp 0 issues TMA loads (128-byte swizzle, no multicast) into a ring of smem
+// stages, warp 1 allocates TMEM and issues tcgen05.mma from one thread, warps 2-5
+// drain the double-buffered TMEM accumulators.  Every mbarrier wait is bounded
+// (ptx.cuh): a stalled pipeline records a status code and the kernel returns.
+#include "moe_internal.h"
+#include "ptx.cuh"
+
+#include <cuda_bf16.h>
+
+namespace lm {
+namespace {
+
+constexpr int kBlockM = 128;
+constexpr int kBlockK = 64;
+constexpr int kThreads = 192;
+constexpr int kATileBytes = kBlockM * kBlockK * 2;
+constexpr int kSmemBudget = 225 * 1024;
+
+enum class Kind { GateUp, Down };
+
+template <int BN, Kind KIND>
+struct Cfg {
+    static constexpr int kBTileBytes = BN * kBlockK * 2;
+    static constexpr int kStageBytes = kATileBytes + kBTileBytes;
+    static constexpr int kStagingBytes = (KIND == Kind::GateUp) ? BN * 64 * 2 : 0;
+    static constexpr int kBarrierBytes = 1024;
+    static constexpr int kStagesFit = (kSmemBudget - kStagingBytes - kBarrierBytes - 1024) / kStageBytes;
+    static constexpr int kStages = kStagesFit > 12 ? 12 : kStagesFit;
+    static constexpr int kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
+    static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kStagingBytes + kBarrierBytes;
+    static_assert(kStages >= 2, "pipeline needs at least two stages");
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+};
+
+__device__ __forceinline__ int find_segment(const int* tiles, int n_seg, int tile) {
+    int lo = 0, hi = n_seg;  // tiles[lo] <= tile < tiles[hi]
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (tiles[mid] <= tile) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ float silu_times(float g, float u) {
+    // src/Gemm.cpp:225-231: value / (1 + exp(-value)) * up
+    return g / (1.0f + expf(-g)) * u;
+}
+
+template <int BN, Kind KIND>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                    const __grid_constant__ CUtensorMap map_x, const GemmArgs args) {
+    using C = Cfg<BN, KIND>;
+    constexpr int S = C::kStages;
+    constexpr uint32_t kIdesc = umma_idesc_bf16(kBlockM, BN);
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ int s_tiles[kMaxSegments + 1];
+    __shared__ int s_off[kMaxSegments];
+    __shared__ int s_cnt[kMaxSegments];
+    __shared__ int s_n_seg;
+    __shared__ int s_epi_go[2];
+
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem_a = smem;
+    uint8_t* smem_b = smem + S * kATileBytes;
+    uint8_t* staging = smem_b + S * C::kBTileBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + C::kStagingBytes);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + S;
+    uint64_t* tmem_full = bars + 2 * S;
+    uint64_t* tmem_empty = bars + 2 * S + 2;
+    uint64_t* drain_bar = bars + 2 * S + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tmem_full[i], 1);
+            mbar_init(&tmem_empty[i], 4);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&map_a);
+        tma_prefetch_desc(&map_b);
+        if (KIND == Kind::GateUp) tma_prefetch_desc(&map_x);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::kTmemCols);
+        tmem_relinquish();
+    }
+    // Everything above overlaps the previous kernel; the schedule is its output.
+    pdl_wait();
+    const Schedule* sched = args.sched;
+    if (threadIdx.x == 0) s_n_seg = sched->n_seg;
+    for (int i = threadIdx.x; i <= kMaxSegments; i += kThreads) {
+        if (i < kMaxSegments) {
+            s_off[i] = sched->seg_off[i];
+            s_cnt[i] = sched->seg_cnt[i];
+        }
+        s_tiles[i] = (KIND == Kind::GateUp) ? sched->tiles1[i] : sched->tiles2[i];
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    pdl_launch_dependents();
+
+    const int n_seg = s_n_seg;
+    const int total_tiles = s_tiles[n_seg];
+    const uint32_t tmem_base = *tmem_slot;
+    const int K = (KIND == Kind::GateUp) ? args.hidden : args.inter;
+    const int num_kb = K / kBlockK;
+    const int rows_a = (KIND == Kind::GateUp) ? 2 * args.inter : args.hidden;
+    const int mb_per = rows_a / kBlockM;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ── TMA producer ──
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0;
+            uint32_t issued_phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+                const int s = find_segment(s_tiles, n_seg, tile);
+                const int local = tile - s_tiles[s];
+                const int nb = local / mb_per;
+                const int mb = local - nb * mb_per;
+                const int a_row = s * rows_a + mb * kBlockM;
+                const bool from_x = (KIND == Kind::GateUp) && s >= args.n_routed_local;
+                const int b_row = from_x ? nb * BN : s_off[s] + nb * BN;
+                const CUtensorMap* bmap = from_x ? &map_x : &map_b;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status, kDevTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[stage], kATileBytes + C::kBTileBytes);
+                    tma_load_2d(smem_a + stage * kATileBytes, &map_a, &full[stage], kb * kBlockK, a_row);
+                    tma_load_2d(smem_b + stage * C::kBTileBytes, bmap, &full[stage], kb * kBlockK, b_row);
+                    issued_mask |= 1u << stage;
+                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // Let every issued copy land before the CTA's shared memory goes away.
+                for (int st = 0; st < S; ++st)
+                    if (issued_mask & (1u << st)) mbar_wait_drain(&full[st], (issued_phase >> st) & 1u, 100000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ── MMA issuer ──
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            bool issued_any = false;
+            for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+                if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, args.status, kDevTimeoutMma)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, args.status, kDevTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t a_desc = umma_desc_sw128(smem_u32(smem_a + stage * kATileBytes));
+                    const uint64_t b_desc = umma_desc_sw128(smem_u32(smem_b + stage * C::kBTileBytes));
+#pragma unroll
+                    for (int kk = 0; kk < kBlockK / 16; ++kk) {
+                        // +32 bytes per 16-element K step inside the swizzle atom (>> 4 in the descriptor).
+                        umma_bf16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, kIdesc, (kb | kk) != 0);
+                    }
+                    issued_any = true;
+                    umma_commit(&empty[stage]);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&tmem_full[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            if (!ok && issued_any) {
+                // Wait for the MMAs already issued before TMEM is released.
+                umma_commit(drain_bar);
+                mbar_wait_drain(drain_bar, 0, 100000000ull);
+            }
+        }
+    } else {
+        // ── Epilogue: warps 2..5 own TMEM lane quadrants (warp % 4) ──
+        const int quad = warp & 3;
+        const int epi_tid = threadIdx.x - 64;  // 0..127
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        int iter = 0;
+        for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++iter) {
+            const int s = find_segment(s_tiles, n_seg, tile);
+            const int local = tile - s_tiles[s];
+            const int nb = local / mb_per;
+            const int mb = local - nb * mb_per;
+            const int valid = min(BN, s_cnt[s] - nb * BN);
+            // One thread waits; the named barrier hands its verdict to all four
+            // warps, so they leave together and never strand each other at a barrier.
+            // The verdict slot alternates per tile so a slow warp never reads the next one.
+            if (epi_tid == 0)
+                s_epi_go[iter & 1] =
+                    mbar_wait(&tmem_full[acc], acc_phase, abort_flag, args.status, kDevTimeoutEpilogue) ? 1 : 0;
+            named_bar_sync(2, 128);
+            if (!s_epi_go[iter & 1]) break;
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+            const int row0 = s_off[s] + nb * BN;  // first h row / routed row of this tile
+            if constexpr (KIND == Kind::GateUp) {
+                __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(staging);
+                const int i_local = (quad * 32 + lane) >> 1;  // h column within the tile's 64
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    if (c0 >= valid) break;  // warp-uniform
+                    uint32_t r[16];
+                    tmem_ld16(t_row + c0, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float mine = __uint_as_float(r[j]);
+                        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+                        if ((lane & 1) == 0) st[(c0 + j) * 64 + i_local] = __float2bfloat16_rn(silu_times(mine, other));
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+                named_bar_sync(1, 128);
+                // Staging [valid tokens][64] -> h rows, 128 contiguous bytes per row.
+                const uint4* src = reinterpret_cast<const uint4*>(staging);
+                for (int q = epi_tid; q < valid * 8; q += 128) {
+                    const int c = q >> 3;
+                    const int part = q & 7;
+                    uint4* dst = reinterpret_cast<uint4*>(args.h + static_cast<size_t>(row0 + c) * args.inter +
+                                                          mb * 64) + part;
+                    *dst = src[c * 8 + part];
+                }
+                named_bar_sync(1, 128);
+            } else {
+                const int d = mb * kBlockM + quad * 32 + lane;  // hidden row
+                const bool routed = s < args.n_routed_local;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    if (c0 >= valid) break;
+                    uint32_t r[16];
+                    tmem_ld16(t_row + c0, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int c = c0 + j;
+                        if (c < valid) {
+                            int tok;
+                            float w;
+                            if (routed) {
+                                tok = args.row_token[row0 + c];
+                                w = args.row_weight[row0 + c];
+                            } else {
+                                tok = nb * BN + c;
+                                w = 1.0f;
+                            }
+                            atomicAdd(args.y + static_cast<size_t>(tok) * args.hidden + d, w * __uint_as_float(r[j]));
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+            }
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+template <int BN, Kind KIND>
+cudaError_t launch_one(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& x, const GemmArgs& args,
+                       int sms, cudaStream_t stream, bool pdl) {
+    using C = Cfg<BN, KIND>;
+    auto kernel = moe_gemm_kernel<BN, KIND>;
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, a, b, x, args);
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_gate_up(int bn, const CUtensorMap& w13, const CUtensorMap& xperm, const CUtensorMap& x,
+                                const GemmArgs& args, int sms, cudaStream_t stream, bool pdl) {
+    switch (bn) {
+        case 16: return launch_one<16, Kind::GateUp>(w13, xperm, x, args, sms, stream, pdl);
+        case 32: return launch_one<32, Kind::GateUp>(w13, xperm, x, args, sms, stream, pdl);
+        case 64: return launch_one<64, Kind::GateUp>(w13, xperm, x, args, sms, stream, pdl);
+        case 128: return launch_one<128, Kind::GateUp>(w13, xperm, x, args, sms, stream, pdl);
+        case 256: return launch_one<256, Kind::GateUp>(w13, xperm, x, args, sms, stream, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_gemm_down(int bn, const CUtensorMap& w2, const CUtensorMap& hmap, const GemmArgs& args, int sms,
+                             cudaStream_t stream, bool pdl) {
+    switch (bn) {
+        case 16: return launch_one<16, Kind::Down>(w2, hmap, hmap, args, sms, stream, pdl);
+        case 32: return launch_one<32, Kind::Down>(w2, hmap, hmap, args, sms, stream, pdl);
+        case 64: return launch_one<64, Kind::Down>(w2, hmap, hmap, args, sms, stream, pdl);
+        case 128: return launch_one<128, Kind::Down>(w2, hmap, hmap, args, sms, stream, pdl);
+        case 256: return launch_one<256, Kind::Down>(w2, hmap, hmap, args, sms, stream, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace lm

@@ -1,0 +1,661 @@
+// moe_api.cu -- the C ABI of include/litemind_moe.h: context, weight residency,
+// and the per-call launch sequence of the MoE path.
+//
+// Residency replaces the reference's ExpertCache paging (src/ExpertCache.cpp:9-47):
+// every expert of every resident layer lives in HBM in the layout the grouped GEMMs
+// read, so a forward call never moves weights.  Per layer:
+//   w13   [segments, 2*inter, hidden] bf16  gate and up rows interleaved in pairs
+//   w2    [segments, hidden, inter]   bf16  down (the shared FFN split by columns)
+//   router [E, hidden] f32 and its transpose [hidden, E]
+// where segments = the routed experts held on this device + n_shared_experts
+// shared splits of width inter (sum over the splits == the reference's one
+// shared FFN of width inter * n_shared, src/DeepSeekRunner.cpp:217-222).
+#include "moe_internal.h"
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace lm {
+
+struct LayerWeights {
+    uint16_t* w13 = nullptr;
+    uint16_t* w2 = nullptr;
+    float* router = nullptr;
+    float* router_t = nullptr;
+    float* norm = nullptr;
+    CUtensorMap map_w13{};
+    CUtensorMap map_w2{};
+    std::vector<uint8_t> expert_loaded;  // per local routed expert
+    bool shared_loaded = false;
+    bool router_loaded = false;
+    bool complete() const {
+        return router_loaded && shared_loaded &&
+               std::all_of(expert_loaded.begin(), expert_loaded.end(), [](uint8_t v) { return v != 0; });
+    }
+};
+
+constexpr int kBnChoices[5] = {16, 32, 64, 128, 256};
+
+}  // namespace lm
+
+struct lm_moe_ctx {
+    lm_moe_config cfg{};
+    int device = 0;
+    int sms = 148;
+    int rank = 0;
+    int nranks = 1;
+    int first_expert = 0;
+    int local_experts = 0;
+    int n_seg = 0;
+    int routed_cap = 0;  // rows reserved for routed tokens in x_perm / h
+    std::vector<lm::LayerWeights> layers;
+
+    float* logits = nullptr;
+    int32_t* topk_idx = nullptr;
+    float* topk_w = nullptr;
+    int32_t* tile_counts = nullptr;
+    int32_t* tile_base = nullptr;
+    int32_t* expert_totals = nullptr;
+    lm::Schedule* sched = nullptr;
+    int32_t* row_token = nullptr;
+    float* row_weight = nullptr;
+    int32_t* slot_row = nullptr;
+    uint16_t* x_perm = nullptr;
+    uint16_t* h = nullptr;
+    int32_t* status = nullptr;
+    CUtensorMap map_xperm[5]{};
+    CUtensorMap map_h[5]{};
+
+    // Host-API staging and the decoder sub-layer's normalised activations.
+    uint16_t* x_stage = nullptr;
+    float* y_stage = nullptr;
+    float* bias_stage = nullptr;
+    float* norm_f32 = nullptr;
+    uint16_t* norm_bf16 = nullptr;
+    cudaStream_t own_stream = nullptr;
+
+    bool profiling = false;
+    cudaEvent_t prof_events[LM_PROFILE_SLOTS + 1]{};
+    double prof_ms[LM_PROFILE_SLOTS]{};
+    int64_t prof_count[LM_PROFILE_SLOTS]{};
+    int prof_last = -1;  // slot of the last recorded event in the current call
+
+    uint64_t resident_bytes = 0;
+    uint64_t uploaded_bytes = 0;
+    std::string last_error;
+    std::vector<void*> allocations;
+};
+
+namespace lm {
+namespace {
+
+lm_status fail(lm_moe_ctx* ctx, lm_status code, const std::string& message) {
+    if (ctx != nullptr) ctx->last_error = message;
+    return code;
+}
+
+lm_status cuda_fail(lm_moe_ctx* ctx, cudaError_t e, const char* what) {
+    return fail(ctx, LM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define LM_CUDA(ctx, expr)                                         \
+    do {                                                           \
+        const cudaError_t lm_e_ = (expr);                          \
+        if (lm_e_ != cudaSuccess) return cuda_fail(ctx, lm_e_, #expr); \
+    } while (0)
+
+template <typename T>
+lm_status alloc(lm_moe_ctx* ctx, T** ptr, size_t count) {
+    void* p = nullptr;
+    const size_t bytes = std::max<size_t>(count * sizeof(T), 256);
+    const cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMalloc");
+    ctx->allocations.push_back(p);
+    *ptr = static_cast<T*>(p);
+    return LM_OK;
+}
+
+int bn_index(int bn) {
+    for (int i = 0; i < 5; ++i)
+        if (kBnChoices[i] == bn) return i;
+    return -1;
+}
+
+// Token-tile width of the grouped GEMMs from the average rows per expert segment.
+int choose_bn(int tokens, int top_k, int experts) {
+    const long avg = (static_cast<long>(tokens) * top_k + experts - 1) / experts;
+    if (avg <= 16) return 16;
+    if (avg <= 32) return 32;
+    if (avg <= 64) return 64;
+    if (avg <= 128) return 128;
+    return 256;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+lm_status check_layer(lm_moe_ctx* ctx, int32_t layer) {
+    if (layer < 0 || layer >= static_cast<int32_t>(ctx->layers.size()))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "layer index out of range");
+    if (!ctx->layers[layer].complete())
+        return fail(ctx, LM_ERR_NOT_LOADED, "layer " + std::to_string(layer) + " is not fully uploaded");
+    return LM_OK;
+}
+
+RouterParams router_params(const lm_moe_config& c) {
+    RouterParams rp{};
+    rp.experts = c.n_routed_experts;
+    rp.top_k = c.num_experts_per_tok;
+    int n_group = std::max(c.n_group, 1);
+    rp.topk_group = std::max(c.topk_group, 1);
+    rp.group_limited = c.topk_method == LM_TOPK_GROUP_LIMITED_GREEDY;
+    if (c.n_routed_experts % n_group != 0) {  // src/MoeRouter.cpp:46-51
+        rp.group_limited = 0;
+        n_group = 1;
+    }
+    rp.n_group = n_group;
+    rp.normalize = c.norm_topk_prob != 0;
+    rp.scale = c.routed_scaling_factor;
+    return rp;
+}
+
+lm_status ensure_layer_buffers(lm_moe_ctx* ctx, int32_t layer) {
+    LayerWeights& L = ctx->layers[layer];
+    if (L.w13 != nullptr) return LM_OK;
+    const lm_moe_config& c = ctx->cfg;
+    const size_t H = c.hidden_size, I = c.moe_intermediate_size, E = c.n_routed_experts;
+    const size_t segs = ctx->n_seg;
+    lm_status st;
+    if ((st = alloc(ctx, &L.w13, segs * 2 * I * H)) != LM_OK) return st;
+    if ((st = alloc(ctx, &L.w2, segs * H * I)) != LM_OK) return st;
+    if ((st = alloc(ctx, &L.router, E * H)) != LM_OK) return st;
+    if ((st = alloc(ctx, &L.router_t, E * H)) != LM_OK) return st;
+    if ((st = alloc(ctx, &L.norm, H)) != LM_OK) return st;
+    ctx->resident_bytes += segs * 3 * I * H * 2 + 2 * E * H * 4 + H * 4;
+    std::string err;
+    if (!encode_tensor_map_bf16(&L.map_w13, L.w13, segs * 2 * I, H, 128, 64, err) ||
+        !encode_tensor_map_bf16(&L.map_w2, L.w2, segs * H, I, 128, 64, err))
+        return fail(ctx, LM_ERR_CUDA, err);
+    L.expert_loaded.assign(ctx->local_experts, 0);
+    return LM_OK;
+}
+
+// One SwiGLU block into segment `seg`: gate rows to the even rows of w13, up rows
+// to the odd rows, down [hidden, inter] with source row pitch `down_pitch` elements.
+lm_status upload_segment(lm_moe_ctx* ctx, LayerWeights& L, int seg, const uint16_t* gate, const uint16_t* up,
+                         const uint16_t* down, size_t down_pitch) {
+    const size_t H = ctx->cfg.hidden_size, I = ctx->cfg.moe_intermediate_size;
+    uint16_t* w13 = L.w13 + static_cast<size_t>(seg) * 2 * I * H;
+    LM_CUDA(ctx, cudaMemcpy2D(w13, 2 * H * 2, gate, H * 2, H * 2, I, cudaMemcpyHostToDevice));
+    LM_CUDA(ctx, cudaMemcpy2D(w13 + H, 2 * H * 2, up, H * 2, H * 2, I, cudaMemcpyHostToDevice));
+    LM_CUDA(ctx, cudaMemcpy2D(L.w2 + static_cast<size_t>(seg) * H * I, I * 2, down, down_pitch * 2, I * 2, H,
+                              cudaMemcpyHostToDevice));
+    ctx->uploaded_bytes += 3 * I * H * 2;
+    return LM_OK;
+}
+
+lm_status set_device(lm_moe_ctx* ctx) {
+    LM_CUDA(ctx, cudaSetDevice(ctx->device));
+    return LM_OK;
+}
+
+// Profiling: event 0 marks the start of a forward, event slot+1 the end of that
+// slot's launch.  Times are attributed from the previous recorded event.
+void prof_begin(lm_moe_ctx* ctx, cudaStream_t s) {
+    if (!ctx->profiling) return;
+    cudaEventRecord(ctx->prof_events[0], s);
+    ctx->prof_last = -1;
+}
+void prof_mark(lm_moe_ctx* ctx, int slot, cudaStream_t s) {
+    if (!ctx->profiling) return;
+    cudaEventRecord(ctx->prof_events[slot + 1], s);
+}
+lm_status prof_end(lm_moe_ctx* ctx, const int* slots, int n) {
+    if (!ctx->profiling) return LM_OK;
+    LM_CUDA(ctx, cudaEventSynchronize(ctx->prof_events[slots[n - 1] + 1]));
+    int prev = 0;
+    for (int i = 0; i < n; ++i) {
+        float ms = 0.0f;
+        LM_CUDA(ctx, cudaEventElapsedTime(&ms, ctx->prof_events[prev], ctx->prof_events[slots[i] + 1]));
+        ctx->prof_ms[slots[i]] += ms;
+        ctx->prof_count[slots[i]] += 1;
+        prev = slots[i] + 1;
+    }
+    return LM_OK;
+}
+
+}  // namespace
+}  // namespace lm
+
+using namespace lm;
+
+extern "C" {
+
+void lm_moe_config_default(lm_moe_config* c) {
+    if (c == nullptr) return;
+    std::memset(c, 0, sizeof(*c));
+    c->hidden_size = 2048;
+    c->moe_intermediate_size = 1408;
+    c->n_routed_experts = 64;
+    c->n_shared_experts = 2;
+    c->num_experts_per_tok = 6;
+    c->norm_topk_prob = 0;
+    c->routed_scaling_factor = 1.0f;
+    c->topk_method = LM_TOPK_GREEDY;
+    c->n_group = 1;
+    c->topk_group = 1;
+    c->rms_norm_eps = 1e-6f;
+    c->num_layers = 1;
+    c->max_tokens = 16384;
+}
+
+const char* lm_status_string(lm_status s) {
+    switch (s) {
+        case LM_OK: return "ok";
+        case LM_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case LM_ERR_CUDA: return "CUDA error";
+        case LM_ERR_NOT_LOADED: return "weights not loaded";
+        case LM_ERR_TOO_MANY_TOKENS: return "too many tokens";
+        case LM_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+        case LM_ERR_COMM: return "communication error";
+        case LM_ERR_UNSUPPORTED: return "unsupported";
+        default: return "unknown status";
+    }
+}
+
+const char* lm_moe_last_error(const lm_moe_ctx* ctx) {
+    return ctx != nullptr ? ctx->last_error.c_str() : context_free_error().c_str();
+}
+
+lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** out) {
+    if (config == nullptr || out == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    const lm_moe_config& c = *config;
+    // Config::validate (src/Config.cpp:156-191) plus what the kernels need.
+    if (c.hidden_size <= 0 || c.moe_intermediate_size <= 0 || c.n_routed_experts <= 0 ||
+        c.num_experts_per_tok <= 0 || c.num_experts_per_tok > c.n_routed_experts || c.n_shared_experts < 0 ||
+        c.num_layers <= 0 || c.max_tokens <= 0)
+        return LM_ERR_INVALID_ARGUMENT;
+    if (c.hidden_size % 128 != 0 || c.moe_intermediate_size % 64 != 0 || c.n_routed_experts > kMaxExperts ||
+        c.num_experts_per_tok > kMaxTopK || c.n_shared_experts > kMaxShared ||
+        (c.topk_method == LM_TOPK_GROUP_LIMITED_GREEDY && c.n_group > 32))
+        return LM_ERR_UNSUPPORTED;
+    if (c.topk_method != LM_TOPK_GREEDY && c.topk_method != LM_TOPK_GROUP_LIMITED_GREEDY)
+        return LM_ERR_INVALID_ARGUMENT;
+
+    auto ctx = std::make_unique<lm_moe_ctx>();
+    ctx->cfg = c;
+    ctx->device = device;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+        context_free_error();
+        return LM_ERR_CUDA;  // no GPU: there is no CPU fallback
+    }
+    if (device < 0 || device >= count) return LM_ERR_INVALID_ARGUMENT;
+    if (cudaSetDevice(device) != cudaSuccess) return LM_ERR_CUDA;
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return LM_ERR_CUDA;
+    if (prop.major != 10) return LM_ERR_UNSUPPORTED;  // built for sm_100a only
+    ctx->sms = prop.multiProcessorCount;
+    ctx->local_experts = c.n_routed_experts;
+    ctx->n_seg = ctx->local_experts + c.n_shared_experts;
+    ctx->routed_cap = c.max_tokens * c.num_experts_per_tok;
+    ctx->layers.resize(c.num_layers);
+
+    lm_moe_ctx* p = ctx.get();
+    const size_t T = c.max_tokens, K = c.num_experts_per_tok, E = c.n_routed_experts, H = c.hidden_size,
+                 I = c.moe_intermediate_size;
+    const size_t tiles = (T + kRouteTile - 1) / kRouteTile;
+    const size_t h_rows = static_cast<size_t>(p->routed_cap) + c.n_shared_experts * T;
+    lm_status st;
+    if ((st = alloc(p, &p->logits, T * E)) || (st = alloc(p, &p->topk_idx, T * K)) ||
+        (st = alloc(p, &p->topk_w, T * K)) || (st = alloc(p, &p->tile_counts, tiles * E)) ||
+        (st = alloc(p, &p->tile_base, tiles * E)) || (st = alloc(p, &p->expert_totals, E)) ||
+        (st = alloc(p, &p->sched, 1)) || (st = alloc(p, &p->row_token, static_cast<size_t>(p->routed_cap))) ||
+        (st = alloc(p, &p->row_weight, static_cast<size_t>(p->routed_cap))) || (st = alloc(p, &p->slot_row, T * K)) ||
+        (st = alloc(p, &p->x_perm, static_cast<size_t>(p->routed_cap) * H)) || (st = alloc(p, &p->h, h_rows * I)) ||
+        (st = alloc(p, &p->status, 1))) {
+        lm_moe_destroy(ctx.release());
+        return st;
+    }
+    if (cudaMemset(p->status, 0, sizeof(int32_t)) != cudaSuccess ||
+        cudaMemset(p->expert_totals, 0, E * sizeof(int32_t)) != cudaSuccess ||
+        cudaMemset(p->sched, 0, sizeof(Schedule)) != cudaSuccess) {
+        lm_moe_destroy(ctx.release());
+        return LM_ERR_CUDA;
+    }
+    std::string err;
+    for (int i = 0; i < 5; ++i) {
+        if (!encode_tensor_map_bf16(&p->map_xperm[i], p->x_perm, p->routed_cap, H, kBnChoices[i], 64, err) ||
+            !encode_tensor_map_bf16(&p->map_h[i], p->h, h_rows, I, kBnChoices[i], 64, err)) {
+            lm_moe_destroy(ctx.release());
+            return LM_ERR_CUDA;
+        }
+    }
+    *out = ctx.release();
+    return LM_OK;
+}
+
+lm_status lm_moe_destroy(lm_moe_ctx* ctx) {
+    if (ctx == nullptr) return LM_OK;
+    cudaSetDevice(ctx->device);
+    for (void* ptr : ctx->allocations) cudaFree(ptr);
+    if (ctx->x_stage) cudaFree(ctx->x_stage);
+    if (ctx->y_stage) cudaFree(ctx->y_stage);
+    if (ctx->bias_stage) cudaFree(ctx->bias_stage);
+    if (ctx->norm_f32) cudaFree(ctx->norm_f32);
+    if (ctx->norm_bf16) cudaFree(ctx->norm_bf16);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    for (auto& e : ctx->prof_events)
+        if (e) cudaEventDestroy(e);
+    delete ctx;
+    return LM_OK;
+}
+
+lm_status lm_moe_upload_layer(lm_moe_ctx* ctx, int32_t layer, const float* router, const uint16_t* gate,
+                              const uint16_t* up, const uint16_t* down, const uint16_t* shared_gate,
+                              const uint16_t* shared_up, const uint16_t* shared_down, const float* norm_weight) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= static_cast<int32_t>(ctx->layers.size()))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "layer index out of range");
+    const lm_moe_config& c = ctx->cfg;
+    if (router == nullptr || gate == nullptr || up == nullptr || down == nullptr ||
+        (c.n_shared_experts > 0 && (shared_gate == nullptr || shared_up == nullptr || shared_down == nullptr)))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "null weight pointer");
+    lm_status st;
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    if ((st = ensure_layer_buffers(ctx, layer)) != LM_OK) return st;
+    LayerWeights& L = ctx->layers[layer];
+    const size_t H = c.hidden_size, I = c.moe_intermediate_size, E = c.n_routed_experts;
+    for (int s = 0; s < ctx->local_experts; ++s) {
+        const size_t e = static_cast<size_t>(ctx->first_expert + s);
+        if ((st = upload_segment(ctx, L, s, gate + e * I * H, up + e * I * H, down + e * H * I, I)) != LM_OK)
+            return st;
+        L.expert_loaded[s] = 1;
+    }
+    const size_t S = I * c.n_shared_experts;
+    for (int t = 0; t < c.n_shared_experts; ++t) {
+        if ((st = upload_segment(ctx, L, ctx->local_experts + t, shared_gate + t * I * H, shared_up + t * I * H,
+                                 shared_down + t * I, S)) != LM_OK)
+            return st;
+    }
+    L.shared_loaded = true;
+    std::vector<float> transposed(E * H);
+    for (size_t e = 0; e < E; ++e)
+        for (size_t k = 0; k < H; ++k) transposed[k * E + e] = router[e * H + k];
+    LM_CUDA(ctx, cudaMemcpy(L.router, router, E * H * sizeof(float), cudaMemcpyHostToDevice));
+    LM_CUDA(ctx, cudaMemcpy(L.router_t, transposed.data(), E * H * sizeof(float), cudaMemcpyHostToDevice));
+    if (norm_weight != nullptr)
+        LM_CUDA(ctx, cudaMemcpy(L.norm, norm_weight, H * sizeof(float), cudaMemcpyHostToDevice));
+    else {
+        std::vector<float> ones(H, 1.0f);
+        LM_CUDA(ctx, cudaMemcpy(L.norm, ones.data(), H * sizeof(float), cudaMemcpyHostToDevice));
+    }
+    ctx->uploaded_bytes += 2 * E * H * 4;
+    L.router_loaded = true;
+    return LM_OK;
+}
+
+lm_status lm_moe_upload_expert(lm_moe_ctx* ctx, int32_t layer, int32_t expert, const uint16_t* gate,
+                               const uint16_t* up, const uint16_t* down) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= static_cast<int32_t>(ctx->layers.size()))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "layer index out of range");
+    if (expert < ctx->first_expert || expert >= ctx->first_expert + ctx->local_experts)
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "expert is not held by this device");
+    if (gate == nullptr || up == nullptr || down == nullptr) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "null weight");
+    lm_status st;
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    if ((st = ensure_layer_buffers(ctx, layer)) != LM_OK) return st;
+    LayerWeights& L = ctx->layers[layer];
+    const int s = expert - ctx->first_expert;
+    if ((st = upload_segment(ctx, L, s, gate, up, down, ctx->cfg.moe_intermediate_size)) != LM_OK) return st;
+    L.expert_loaded[s] = 1;
+    return LM_OK;
+}
+
+static lm_status route_common(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, const float* x_f32, int32_t T,
+                              const float* bias, float* logits, cudaStream_t stream) {
+    const lm_moe_config& c = ctx->cfg;
+    const LayerWeights& L = ctx->layers[layer];
+    LM_CUDA(ctx, launch_router_logits(x, x_f32, L.router, L.router_t, bias, logits, T, c.hidden_size,
+                                      c.n_routed_experts, stream, false));
+    LM_CUDA(ctx, launch_router_topk(logits, T, router_params(c), ctx->topk_idx, ctx->topk_w, ctx->tile_counts,
+                                    stream, true));
+    return LM_OK;
+}
+
+lm_status lm_moe_route(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int32_t tokens, const float* logit_bias,
+                       int32_t* topk_idx, float* topk_w, float* logits, void* stream) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    lm_status st;
+    if ((st = check_layer(ctx, layer)) != LM_OK) return st;
+    if (tokens < 0) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "negative token count");
+    if (tokens > ctx->cfg.max_tokens) return fail(ctx, LM_ERR_TOO_MANY_TOKENS, "tokens exceed max_tokens");
+    if (tokens == 0) return LM_OK;
+    if (x == nullptr || topk_idx == nullptr || topk_w == nullptr || !aligned16(x))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "x must be a 16-byte aligned device pointer; outputs non-null");
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* lg = logits != nullptr ? logits : ctx->logits;
+    if ((st = route_common(ctx, layer, x, nullptr, tokens, logit_bias, lg, s)) != LM_OK) return st;
+    const lm_moe_config& c = ctx->cfg;
+    LM_CUDA(ctx, launch_dispatch_scan(ctx->tile_counts, ctx->tile_base, ctx->expert_totals, ctx->sched, tokens,
+                                      c.num_experts_per_tok, c.n_routed_experts, c.n_shared_experts, ctx->first_expert,
+                                      ctx->local_experts, ctx->routed_cap, 16, 1, 1, s, true));
+    const size_t n = static_cast<size_t>(tokens) * c.num_experts_per_tok;
+    LM_CUDA(ctx, cudaMemcpyAsync(topk_idx, ctx->topk_idx, n * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+    LM_CUDA(ctx, cudaMemcpyAsync(topk_w, ctx->topk_w, n * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    return LM_OK;
+}
+
+lm_status lm_moe_select(lm_moe_ctx* ctx, const float* logits, int32_t tokens, int32_t* topk_idx, float* topk_w,
+                        void* stream) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    if (tokens < 0) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "negative token count");
+    if (tokens == 0) return LM_OK;
+    if (logits == nullptr || topk_idx == nullptr || topk_w == nullptr)
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "null pointer");
+    lm_status st;
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    LM_CUDA(ctx, launch_router_topk(logits, tokens, router_params(ctx->cfg), topk_idx, topk_w, nullptr,
+                                    static_cast<cudaStream_t>(stream), false));
+    return LM_OK;
+}
+
+static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, const float* x_f32, int32_t T,
+                              const float* bias, float* y, int32_t accumulate, cudaStream_t s) {
+    const lm_moe_config& c = ctx->cfg;
+    const LayerWeights& L = ctx->layers[layer];
+    const int K = c.num_experts_per_tok, E = c.n_routed_experts, H = c.hidden_size, I = c.moe_intermediate_size;
+    const int bn = choose_bn(T, K, E);
+    const int bi = bn_index(bn);
+    prof_begin(ctx, s);
+    int slots[8];
+    int n_slots = 0;
+    if (!accumulate) {
+        LM_CUDA(ctx, cudaMemsetAsync(y, 0, static_cast<size_t>(T) * H * sizeof(float), s));
+        prof_mark(ctx, 0, s);
+        slots[n_slots++] = 0;
+    }
+    LM_CUDA(ctx, launch_router_logits(x, x_f32, L.router, L.router_t, bias, ctx->logits, T, c.hidden_size,
+                                      c.n_routed_experts, s, false));
+    prof_mark(ctx, 1, s);
+    slots[n_slots++] = 1;
+    LM_CUDA(ctx, launch_router_topk(ctx->logits, T, router_params(c), ctx->topk_idx, ctx->topk_w, ctx->tile_counts,
+                                    s, true));
+    prof_mark(ctx, 2, s);
+    slots[n_slots++] = 2;
+    LM_CUDA(ctx, launch_dispatch_scan(ctx->tile_counts, ctx->tile_base, ctx->expert_totals, ctx->sched, T, K, E,
+                                      c.n_shared_experts, ctx->first_expert, ctx->local_experts, ctx->routed_cap, bn,
+                                      2 * I / 128, H / 128, s, true));
+    prof_mark(ctx, 3, s);
+    slots[n_slots++] = 3;
+    LM_CUDA(ctx, launch_permute(x, ctx->topk_idx, ctx->topk_w, ctx->tile_base, T, H, K, E, ctx->first_expert,
+                                ctx->local_experts, ctx->row_token, ctx->row_weight, ctx->slot_row, ctx->x_perm, s,
+                                true));
+    prof_mark(ctx, 4, s);
+    slots[n_slots++] = 4;
+    CUtensorMap map_x{};
+    std::string err;
+    if (!encode_tensor_map_bf16(&map_x, x, T, H, bn, 64, err)) return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+    GemmArgs args{};
+    args.sched = ctx->sched;
+    args.h = ctx->h;
+    args.y = y;
+    args.row_token = ctx->row_token;
+    args.row_weight = ctx->row_weight;
+    args.status = ctx->status;
+    args.tokens = T;
+    args.hidden = H;
+    args.inter = I;
+    args.routed_rows = ctx->routed_cap;
+    args.n_routed_local = ctx->local_experts;
+    LM_CUDA(ctx, launch_gemm_gate_up(bn, L.map_w13, ctx->map_xperm[bi], map_x, args, ctx->sms, s, true));
+    prof_mark(ctx, 5, s);
+    slots[n_slots++] = 5;
+    LM_CUDA(ctx, launch_gemm_down(bn, L.map_w2, ctx->map_h[bi], args, ctx->sms, s, true));
+    prof_mark(ctx, 6, s);
+    slots[n_slots++] = 6;
+    return prof_end(ctx, slots, n_slots);
+}
+
+lm_status lm_moe_forward(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int32_t tokens, const float* logit_bias,
+                         float* y, int32_t accumulate, void* stream) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    lm_status st;
+    if ((st = check_layer(ctx, layer)) != LM_OK) return st;
+    if (tokens < 0) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "negative token count");
+    if (tokens > ctx->cfg.max_tokens) return fail(ctx, LM_ERR_TOO_MANY_TOKENS, "tokens exceed max_tokens");
+    if (tokens == 0) return LM_OK;
+    if (x == nullptr || y == nullptr || !aligned16(x) || !aligned16(y))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "x and y must be 16-byte aligned device pointers");
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    return forward_impl(ctx, layer, x, nullptr, tokens, logit_bias, y, accumulate, static_cast<cudaStream_t>(stream));
+}
+
+lm_status lm_moe_forward_host(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x_host, int32_t tokens,
+                              const float* logit_bias_host, float* y_host) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    lm_status st;
+    if ((st = check_layer(ctx, layer)) != LM_OK) return st;
+    if (tokens < 0) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "negative token count");
+    if (tokens > ctx->cfg.max_tokens) return fail(ctx, LM_ERR_TOO_MANY_TOKENS, "tokens exceed max_tokens");
+    if (tokens == 0) return LM_OK;
+    if (x_host == nullptr || y_host == nullptr) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "null host buffer");
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    const lm_moe_config& c = ctx->cfg;
+    const size_t T = c.max_tokens, H = c.hidden_size;
+    if (ctx->x_stage == nullptr) {
+        LM_CUDA(ctx, cudaMalloc(&ctx->x_stage, T * H * sizeof(uint16_t)));
+        LM_CUDA(ctx, cudaMalloc(&ctx->y_stage, T * H * sizeof(float)));
+        LM_CUDA(ctx, cudaMalloc(&ctx->bias_stage, static_cast<size_t>(c.n_routed_experts) * sizeof(float)));
+        LM_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking));
+    }
+    cudaStream_t s = ctx->own_stream;
+    const size_t n = static_cast<size_t>(tokens) * H;
+    LM_CUDA(ctx, cudaMemcpyAsync(ctx->x_stage, x_host, n * sizeof(uint16_t), cudaMemcpyHostToDevice, s));
+    const float* bias = nullptr;
+    if (logit_bias_host != nullptr) {
+        LM_CUDA(ctx, cudaMemcpyAsync(ctx->bias_stage, logit_bias_host, c.n_routed_experts * sizeof(float),
+                                     cudaMemcpyHostToDevice, s));
+        bias = ctx->bias_stage;
+    }
+    if ((st = forward_impl(ctx, layer, ctx->x_stage, nullptr, tokens, bias, ctx->y_stage, 0, s)) != LM_OK) return st;
+    LM_CUDA(ctx, cudaMemcpyAsync(y_host, ctx->y_stage, n * sizeof(float), cudaMemcpyDeviceToHost, s));
+    return lm_moe_sync(ctx, s);
+}
+
+lm_status lm_moe_block_forward(lm_moe_ctx* ctx, int32_t layer, float* hidden, int32_t tokens, void* stream) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    lm_status st;
+    if ((st = check_layer(ctx, layer)) != LM_OK) return st;
+    if (tokens < 0) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "negative token count");
+    if (tokens > ctx->cfg.max_tokens) return fail(ctx, LM_ERR_TOO_MANY_TOKENS, "tokens exceed max_tokens");
+    if (tokens == 0) return LM_OK;
+    if (hidden == nullptr || !aligned16(hidden)) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "hidden must be aligned");
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    const lm_moe_config& c = ctx->cfg;
+    const size_t T = c.max_tokens, H = c.hidden_size;
+    if (ctx->norm_f32 == nullptr) {
+        LM_CUDA(ctx, cudaMalloc(&ctx->norm_f32, T * H * sizeof(float)));
+        LM_CUDA(ctx, cudaMalloc(&ctx->norm_bf16, T * H * sizeof(uint16_t)));
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // src/DeepSeekRunner.cpp:265-267: rms_norm(post_attention_layernorm); the router
+    // sees the f32 result (:273), the experts its bf16 rounding.
+    LM_CUDA(ctx, launch_rms_norm_rows(hidden, ctx->norm_f32, ctx->norm_bf16, ctx->layers[layer].norm, tokens,
+                                      c.hidden_size, c.rms_norm_eps, s));
+    // The residual add (:290) is folded into the down-projection epilogue: it
+    // accumulates straight into `hidden`.
+    return forward_impl(ctx, layer, ctx->norm_bf16, ctx->norm_f32, tokens, nullptr, hidden, 1, s);
+}
+
+lm_status lm_moe_sync(lm_moe_ctx* ctx, void* stream) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    lm_status st;
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    LM_CUDA(ctx, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    int32_t status = 0;
+    LM_CUDA(ctx, cudaMemcpy(&status, ctx->status, sizeof(status), cudaMemcpyDeviceToHost));
+    if (status != 0) {
+        LM_CUDA(ctx, cudaMemset(ctx->status, 0, sizeof(int32_t)));
+        return fail(ctx, LM_ERR_DEVICE_TIMEOUT,
+                    "a kernel's bounded wait expired (code " + std::to_string(status) + "); results are invalid");
+    }
+    return LM_OK;
+}
+
+lm_status lm_moe_expert_counts(lm_moe_ctx* ctx, int32_t* counts) {
+    if (ctx == nullptr || counts == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    lm_status st;
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    LM_CUDA(ctx, cudaDeviceSynchronize());
+    LM_CUDA(ctx, cudaMemcpy(counts, ctx->expert_totals, ctx->cfg.n_routed_experts * sizeof(int32_t),
+                            cudaMemcpyDeviceToHost));
+    return LM_OK;
+}
+
+lm_status lm_moe_memory(const lm_moe_ctx* ctx, uint64_t* resident_bytes, uint64_t* uploaded_bytes) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    if (resident_bytes) *resident_bytes = ctx->resident_bytes;
+    if (uploaded_bytes) *uploaded_bytes = ctx->uploaded_bytes;
+    return LM_OK;
+}
+
+lm_status lm_moe_profile_enable(lm_moe_ctx* ctx, int32_t enable) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    lm_status st;
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    if (enable && ctx->prof_events[0] == nullptr) {
+        for (auto& e : ctx->prof_events) LM_CUDA(ctx, cudaEventCreate(&e));
+    }
+    ctx->profiling = enable != 0;
+    return LM_OK;
+}
+
+lm_status lm_moe_profile_read(lm_moe_ctx* ctx, double* total_ms, int64_t* launches, int32_t reset) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < LM_PROFILE_SLOTS; ++i) {
+        if (total_ms) total_ms[i] = ctx->prof_ms[i];
+        if (launches) launches[i] = ctx->prof_count[i];
+        if (reset) {
+            ctx->prof_ms[i] = 0.0;
+            ctx->prof_count[i] = 0;
+        }
+    }
+    return LM_OK;
+}
+
+lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t rank, int32_t nranks) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    (void)nccl_unique_id;
+    (void)rank;
+    (void)nranks;
+    return fail(ctx, LM_ERR_UNSUPPORTED, "expert parallelism is not built yet");
+}
+
+}  // extern "C"

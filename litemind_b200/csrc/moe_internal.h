@@ -1,0 +1,87 @@
+// moe_internal.h -- shared declarations of the MoE path's kernels and context.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "litemind_moe.h"
+
+namespace lm {
+
+constexpr int kMaxExperts = 256;          // routed experts supported by the router kernels
+constexpr int kMaxShared = 8;             // shared-expert splits (n_shared_experts)
+constexpr int kMaxSegments = kMaxExperts + kMaxShared;
+constexpr int kMaxTopK = 16;
+constexpr int kRouteTile = 64;            // tokens per routing tile (histogram granularity)
+
+// Per-call schedule written on the device by the scan kernel and read by the
+// grouped GEMMs.  Segment s < E is routed expert s; s >= E is shared split s-E.
+struct Schedule {
+    int32_t seg_off[kMaxSegments];     // first row of the segment in x_perm / h
+    int32_t seg_cnt[kMaxSegments];     // rows in the segment
+    int32_t tiles1[kMaxSegments + 1];  // exclusive prefix of gate/up tiles
+    int32_t tiles2[kMaxSegments + 1];  // exclusive prefix of down tiles
+    int32_t n_seg;                     // segments with weights on this device
+    int32_t first_expert;              // expert-parallel shard start (0 on one GPU)
+};
+
+struct RouterParams {
+    int32_t experts;
+    int32_t top_k;
+    int32_t n_group;
+    int32_t topk_group;
+    int32_t group_limited;
+    int32_t normalize;
+    float scale;
+};
+
+// Kernel launchers (router.cu).  All return cudaGetLastError() after launching.
+cudaError_t launch_router_logits(const uint16_t* x, const float* x_f32, const float* w, const float* w_t,
+                                 const float* bias, float* logits, int tokens, int hidden, int experts,
+                                 cudaStream_t stream, bool pdl);
+cudaError_t launch_router_topk(const float* logits, int tokens, RouterParams rp, int32_t* topk_idx,
+                               float* topk_w, int32_t* tile_counts, cudaStream_t stream, bool pdl);
+cudaError_t launch_dispatch_scan(const int32_t* tile_counts, int32_t* tile_base, int32_t* expert_totals,
+                                 Schedule* sched, int tokens, int top_k, int experts, int n_shared,
+                                 int first_expert, int local_experts, int shared_base, int bn, int mb1,
+                                 int mb2, cudaStream_t stream, bool pdl);
+cudaError_t launch_permute(const uint16_t* x, const int32_t* topk_idx, const float* topk_w,
+                           const int32_t* tile_base, int tokens, int hidden, int top_k, int experts,
+                           int first_expert, int local_experts, int32_t* row_token, float* row_weight,
+                           int32_t* slot_row, uint16_t* x_perm, cudaStream_t stream, bool pdl);
+
+// Grouped SwiGLU GEMMs (grouped_gemm.cu).
+struct GemmArgs {
+    const Schedule* sched;
+    uint16_t* h;               // [rows, inter] bf16 (gate/up output, down input)
+    float* y;                  // [T, hidden] f32 (down output, accumulated)
+    const int32_t* row_token;  // routed row -> token
+    const float* row_weight;   // routed row -> routing weight
+    int32_t* status;           // device status word
+    int32_t tokens;
+    int32_t hidden;
+    int32_t inter;
+    int32_t routed_rows;       // rows of routed segments (shared segments use tokens directly)
+    int32_t n_routed_local;    // segments [0, n_routed_local) are routed experts
+};
+cudaError_t launch_gemm_gate_up(int bn, const CUtensorMap& w13, const CUtensorMap& xperm,
+                                const CUtensorMap& x, const GemmArgs& args, int sms, cudaStream_t stream,
+                                bool pdl);
+cudaError_t launch_gemm_down(int bn, const CUtensorMap& w2, const CUtensorMap& hmap, const GemmArgs& args,
+                             int sms, cudaStream_t stream, bool pdl);
+
+// gemm:: mirror kernels and row kernels (gemm_ops.cu).
+cudaError_t launch_rms_norm_rows(const float* in, float* out_f32, uint16_t* out_bf16, const float* weight,
+                                 int rows, int count, float eps, cudaStream_t stream);
+cudaError_t launch_add_rows(float* dst, const float* src, int64_t count, cudaStream_t stream);
+const std::string& context_free_error();
+
+// Host-side TMA descriptor encoding (tensor_map.cpp).
+bool encode_tensor_map_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                            uint32_t box_rows, uint32_t box_cols, std::string& error);
+
+}  // namespace lm

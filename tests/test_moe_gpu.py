@@ -1,0 +1,144 @@
+"""The MoE block on the GPU against the oracle (oracle/moe_oracle.c).
+
+Small shapes cover the ragged cases (empty experts, one expert taking every token,
+every token-tile width); DeepSeek-V2-Lite shapes cover the benchmark
+configurations.  Where T is too large for the CPU oracle to finish in seconds, a
+sample of tokens is checked: tokens are independent, so the oracle run on the
+sample must reproduce those rows of the GPU output.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+from litemind_b200 import synthetic as syn  # noqa: E402
+from litemind_b200._lib import LM_ERR_INVALID_ARGUMENT, LM_ERR_NOT_LOADED, LM_ERR_TOO_MANY_TOKENS, LiteMindError  # noqa: E402
+from litemind_b200.moe import MoeConfig, MoeLayer, bf16_tensor  # noqa: E402
+from oracle.oracle import RouterConfig  # noqa: E402
+from tests.parity import assert_layer_parity  # noqa: E402
+
+SMALL = syn.MoeShape(hidden=256, inter=128, n_routed_experts=8, n_shared_experts=1, top_k=2)
+
+
+def run_gpu(layer: MoeLayer, x_bits, bias=None):
+    x = bf16_tensor(x_bits)
+    b = None if bias is None else torch.from_numpy(bias).cuda()
+    y = layer.forward(0, x, bias=b)
+    idx, w, logits = layer.route(0, x, bias=b)
+    layer.sync()
+    return y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), logits.cpu().numpy()
+
+
+def run_oracle(oracle_lib, shape, W, x_bits, bias=None):
+    x = syn.bf16_to_f32(x_bits).reshape(x_bits.shape)
+    cfg = RouterConfig(shape.n_routed_experts, shape.top_k)
+    return oracle_lib.moe_layer(x, W, cfg, shape.n_shared_experts, bias=bias, threads=0)
+
+
+@pytest.fixture(scope="module")
+def small_layer():
+    W = syn.layer_weights(SMALL, seed=11, std=0.1)
+    layer = MoeLayer(MoeConfig.from_shape(SMALL, max_tokens=4096))
+    layer.upload_layer(0, W)
+    yield layer, W
+    layer.close()
+
+
+@pytest.mark.parametrize("T", [1, 2, 5, 37, 64, 65, 300, 1000, 4096])
+def test_small_shape_parity(oracle_lib, small_layer, T):
+    layer, W = small_layer
+    x = syn.tokens(SMALL, T, seed=T)
+    y, idx, w, _ = run_gpu(layer, x)
+    ry, ridx, rw, rlog = run_oracle(oracle_lib, SMALL, W, x)
+    assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what=f"small T={T}")
+
+
+def test_all_tokens_on_one_expert(oracle_lib, small_layer):
+    layer, W = small_layer
+    bias = np.full(SMALL.n_routed_experts, -30.0, np.float32)
+    bias[5] = 30.0
+    bias[2] = 20.0  # second choice for everyone; six experts get nothing
+    x = syn.tokens(SMALL, 333, seed=5)
+    y, idx, w, _ = run_gpu(layer, x, bias)
+    assert (idx[:, 0] == 5).all() and (idx[:, 1] == 2).all()
+    counts = layer.expert_counts()
+    assert counts[5] == 333 and counts[2] == 333 and counts.sum() == 666
+    ry, ridx, rw, rlog = run_oracle(oracle_lib, SMALL, W, x, bias)
+    assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what="one expert")
+
+
+def test_zero_tokens_and_errors(small_layer):
+    layer, _ = small_layer
+    x = bf16_tensor(syn.tokens(SMALL, 1, seed=1))
+    y = torch.full((1, SMALL.hidden), 7.0, device="cuda")
+    layer.forward(0, x[:0], y=y[:0])  # T = 0 is a no-op
+    layer.sync()
+    assert float(y[0, 0]) == 7.0
+    with pytest.raises(LiteMindError) as e:
+        layer.forward(1, x)
+    assert e.value.status == LM_ERR_INVALID_ARGUMENT
+    big = torch.zeros((4097, SMALL.hidden), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(LiteMindError) as e:
+        layer.forward(0, big)
+    assert e.value.status == LM_ERR_TOO_MANY_TOKENS
+    fresh = MoeLayer(MoeConfig.from_shape(SMALL, max_tokens=16))
+    with pytest.raises(LiteMindError) as e:
+        fresh.forward(0, x)
+    assert e.value.status == LM_ERR_NOT_LOADED
+    fresh.close()
+
+
+def test_accumulate_adds_to_output(small_layer):
+    layer, _ = small_layer
+    x = bf16_tensor(syn.tokens(SMALL, 50, seed=9))
+    y0 = layer.forward(0, x)
+    y1 = torch.ones_like(y0)
+    layer.forward(0, x, y=y1, accumulate=True)
+    layer.sync()
+    torch.testing.assert_close(y1 - 1.0, y0, rtol=1e-5, atol=1e-5)
+
+
+def test_forward_host_matches_device(small_layer):
+    layer, _ = small_layer
+    xb = syn.tokens(SMALL, 77, seed=3)
+    y_dev = layer.forward(0, bf16_tensor(xb))
+    layer.sync()
+    y_host = layer.forward_host(0, xb)
+    np.testing.assert_allclose(y_host, y_dev.cpu().numpy(), rtol=1e-5, atol=1e-6)
+
+
+# ── DeepSeek-V2-Lite shapes ────────────────────────────────────────────────
+
+@pytest.fixture(scope="module")
+def v2_layer(v2lite_weights):
+    layer = MoeLayer(MoeConfig(max_tokens=16384))
+    layer.upload_layer(0, v2lite_weights)
+    yield layer
+    layer.close()
+
+
+@pytest.mark.parametrize("T,seed", [(1, 1), (8, 1), (32, 1), (128, 0), (256, 1)])
+def test_v2lite_decode_parity(oracle_lib, v2lite_weights, v2_layer, T, seed):
+    """BASELINE configs 0 (T=128, seed 0) and 1 (T in 1/8/32/256, seed 1)."""
+    x = syn.tokens(syn.V2_LITE, T, seed=seed)
+    y, idx, w, _ = run_gpu(v2_layer, x)
+    ry, ridx, rw, rlog = run_oracle(oracle_lib, syn.V2_LITE, v2lite_weights, x)
+    stats = assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what=f"V2-Lite T={T}")
+    print(f"T={T}: {stats}")
+
+
+@pytest.mark.parametrize("T,zipf", [(2048, False), (16384, True)])
+def test_v2lite_prefill_sampled_parity(oracle_lib, v2lite_weights, v2_layer, T, zipf):
+    """BASELINE config 2 (T=16384, Zipf(1.2) expert load) and a 2048-token prefill."""
+    x = syn.tokens(syn.V2_LITE, T, seed=2)
+    bias = syn.zipf_bias(syn.V2_LITE, seed=2) if zipf else None
+    y, idx, w, _ = run_gpu(v2_layer, x, bias)
+    counts = v2_layer.expert_counts()
+    assert counts.sum() == T * 6
+    np.testing.assert_array_equal(np.bincount(idx.reshape(-1), minlength=64), counts)
+    sample = np.random.default_rng(T).choice(T, 48, replace=False)
+    sample.sort()
+    ry, ridx, rw, rlog = run_oracle(oracle_lib, syn.V2_LITE, v2lite_weights, x[sample], bias)
+    assert_layer_parity(y[sample], idx[sample], w[sample], ry, ridx, rw, rlog, what=f"V2-Lite T={T}")
