@@ -1,0 +1,369 @@
+#!/usr/bin/env python
+"""MoE-layer benchmark on B200 (DeepSeek-V2-Lite shape), one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
+
+Workload: one DeepSeek-V2-Lite MoE layer -- 64 routed experts
+(gate/up [1408, 2048], down [2048, 1408] bf16), 2 shared experts, router [64, 2048]
+f32, softmax top-6, no renormalisation -- with weights N(0, 0.02) seed 0 and
+activations N(0, 1) bf16 seed 1.  A step is one forward of the layer over T tokens
+(default 32, the decode batch the north star's HBM target names); the sweep
+T in {1, 8, 32, 256} is reported under "sweep".  Weights and activations are
+synthetic (no checkpoint exists on the box).  L2 is flushed (a 256 MiB write)
+before every timed step, outside its events, so each step streams its experts
+from HBM.
+
+--impl ours (default): the CUDA path through liblitemind_b200.so.
+  value      tokens/s over all ranks, device time from CUDA events per step
+  e2e        tokens/s through lm_moe_forward_host from pinned host buffers
+             (host->device copy of x, device->host copy of y, inside the timing)
+  roofline   the dominant kernel (the gate/up grouped GEMM): algorithmic bytes
+             per launch / its mean CUDA-event duration, against MEASURED_PEAKS.json
+  cpu_baseline  the reference's own CPU code (oracle/_ref, built from the
+             reference's sources) on the host's cores, rank 0, N=1 only
+--impl reference: the reference CPU path alone, same metric and config.
+
+With N > 1 (torchrun, one rank per GPU) each rank runs the same per-rank workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "MoE-layer tokens/s (V2-Lite shape) + % HBM/TC roofline at 1/2/4/8 B200"
+SEED_WEIGHTS = 0
+SEED_TOKENS = 1
+SWEEP = (1, 8, 32, 256)
+FLUSH_BYTES = 256 << 20
+KERNELS_PER_FORWARD = 6  # router_logits, router_topk, dispatch_scan, permute, gemm_gate_up, gemm_down
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--tokens", type=int, default=32, help="tokens per rank per step")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    return ap.parse_args(argv)
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def committed_traffic(workload: str):
+    """DRAM bytes per launch of the dominant kernel from a committed ncu capture."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f).get(workload)
+
+
+# ── clocks ────────────────────────────────────────────────────────────────
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+            os.close(fd)
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.device), "-lms", "200"], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.close()
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sms.append(float(parts[1]))
+                    maxes.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxes) if maxes else None,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+# ── algorithmic work ──────────────────────────────────────────────────────
+
+def layer_bytes(shape, touched_experts: int, T: int) -> int:
+    """Algorithmic HBM bytes of one layer forward: touched experts, shared experts,
+    router, x in (bf16), y out (f32)."""
+    return (shape.expert_bytes * touched_experts + shape.shared_bytes + shape.router_bytes
+            + T * shape.hidden * (2 + 4))
+
+
+def gate_up_bytes(shape, touched_experts: int, T: int) -> int:
+    """Algorithmic bytes of one gate/up GEMM launch: gate and up of every touched
+    expert and of the shared experts, plus the token activations."""
+    return (2 * shape.inter * shape.hidden * 2) * (touched_experts + shape.n_shared_experts) + T * shape.hidden * 2
+
+
+# ── reference CPU path ────────────────────────────────────────────────────
+
+def cpu_reference_rate(weights, x_f32, seconds: float, min_reps: int = 1, max_reps: int = 1000):
+    """tokens/s of the reference's own MoE block (oracle/_ref) on all host threads."""
+    from oracle.oracle import Reference, RouterConfig
+
+    ref = Reference()
+    threads = ref.hardware_threads()
+    cfg = RouterConfig()
+    T = x_f32.shape[0]
+    ref.moe_layer(x_f32[:1], weights, cfg, 2, threads=threads)  # warm the pool and page in the weights
+    reps, t0 = 0, time.perf_counter()
+    while reps < min_reps or (time.perf_counter() - t0 < seconds and reps < max_reps):
+        ref.moe_layer(x_f32, weights, cfg, 2, threads=threads)
+        reps += 1
+    dt = time.perf_counter() - t0
+    return {"value": T * reps / dt, "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": f"{reps} x {T}-token batches of the same workload, {dt:.1f} s, reference "
+                      f"gemm::/MoeRouter built from its sources ({ref.kernel_description()})"}
+
+
+def run_reference_arm(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    from litemind_b200 import synthetic as syn
+
+    W = syn.layer_weights(syn.V2_LITE, seed=SEED_WEIGHTS)
+    x = syn.bf16_to_f32(syn.tokens(syn.V2_LITE, args.tokens, seed=SEED_TOKENS)).reshape(args.tokens, -1)
+    from oracle.oracle import Reference, RouterConfig
+
+    ref = Reference()
+    threads = ref.hardware_threads()
+    for _ in range(max(args.warmup, 0)):
+        ref.moe_layer(x[:1], W, RouterConfig(), 2, threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        ref.moe_layer(x, W, RouterConfig(), 2, threads=threads)
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    value = args.tokens / (ms / 1e3)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(args, world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "sample": f"{args.steps} steps of one {args.tokens}-token batch on rank 0's host "
+                                   f"({ref.kernel_description()})"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args, world: int) -> dict:
+    return {"workload": "config1-decode: V2-Lite MoE layer, tokens per rank per step", "tokens_per_rank": args.tokens,
+            "global_tokens": args.tokens * world, "seed_weights": SEED_WEIGHTS, "seed_tokens": SEED_TOKENS,
+            "experts": "64 routed top-6 + 2 shared, hidden 2048, inter 1408",
+            "l2": "flushed before every timed step (256 MiB write), outside the step's events",
+            "parallelism": "single GPU" if world == 1 else f"{world} independent replicas"}
+
+
+# ── our arm ───────────────────────────────────────────────────────────────
+
+def time_forward(layer, x, y, flush, steps: int, torch):
+    """Per-step CUDA-event time (ms) of layer.forward, L2 flushed before each step."""
+    total = 0.0
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    for _ in range(steps):
+        flush.zero_()
+        start.record()
+        layer.forward(0, x, y=y)
+        end.record()
+        end.synchronize()
+        total += start.elapsed_time(end)
+    return total / steps
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return 0
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from litemind_b200 import synthetic as syn
+    from litemind_b200.moe import MoeConfig, MoeLayer, bf16_tensor
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    shape = syn.V2_LITE
+    T = args.tokens
+    W = syn.layer_weights(shape, seed=SEED_WEIGHTS)
+    max_tokens = max([T] + ([] if args.no_sweep else list(SWEEP)))
+    layer = MoeLayer(MoeConfig(max_tokens=max_tokens), device=local_rank)
+    layer.upload_layer(0, W)
+    x_bits = syn.tokens(shape, T, seed=SEED_TOKENS, stream=rank)
+    x = bf16_tensor(x_bits)
+    y = torch.empty((T, shape.hidden), dtype=torch.float32, device="cuda")
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+
+    for _ in range(max(args.warmup, 3)):
+        layer.forward(0, x, y=y)
+    layer.sync()
+    touched = int((layer.expert_counts() > 0).sum())
+
+    # ── timed region: K steps, barrier + synchronize on both sides ──
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    ms = time_forward(layer, x, y, flush, args.steps, torch)
+    torch.cuda.synchronize()
+    barrier()
+    wall = time.perf_counter() - wall0
+    clock_info = clocks.stop()
+    layer.sync()
+    ms = max_over_ranks(ms)
+    value = T * world / (ms / 1e3)
+
+    # ── per-launch device times for the roofline (same workload, instrumented) ──
+    layer.profile(True)
+    layer.profile_read(reset=True)
+    for _ in range(args.steps):
+        flush.zero_()
+        layer.forward(0, x, y=y)
+    prof = layer.profile_read(reset=True)
+    layer.profile(False)
+    peaks = measured_peaks()
+    gu_ms, gu_n = prof.get("gemm_gate_up", (0.0, 0))
+    gu_avg = gu_ms / max(gu_n, 1)
+    gu_bytes = gate_up_bytes(shape, touched, T)
+    achieved = gu_bytes / (gu_avg / 1e3) / 1e9 if gu_avg > 0 else 0.0
+    total_prof = sum(v[0] for v in prof.values())
+    roofline = {"bound": "hbm", "kernel": "gemm_gate_up (tcgen05 grouped GEMM, gate/up + SiLU epilogue)",
+                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} (hbm_gbs)",
+                "bytes_per_launch": gu_bytes, "mean_launch_ms": gu_avg,
+                "traffic": committed_traffic(f"gemm_gate_up_T{T}"),
+                "share_of_step": {k: round(v[0] / total_prof, 4) for k, v in prof.items()} if total_prof else {}}
+    lb = layer_bytes(shape, touched, T)
+    layer_roofline = {"bytes": lb, "achieved": lb / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                      "frac": lb / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "touched_experts": touched}
+
+    # ── end to end through the C ABI with host buffers ──
+    x_host = torch.from_numpy(x_bits.view(np.int16)).pin_memory()
+    y_host = torch.empty((T, shape.hidden), dtype=torch.float32).pin_memory()
+    layer.forward_host_ptr(0, x_host.data_ptr(), T, y_host.data_ptr())
+    e2e_total = 0.0
+    barrier()
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        layer.forward_host_ptr(0, x_host.data_ptr(), T, y_host.data_ptr())
+        e2e_total += time.perf_counter() - t0
+    e2e_ms = max_over_ranks(1e3 * e2e_total / args.steps)
+    e2e = {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+           "h2d_bytes_per_step": T * shape.hidden * 2, "d2h_bytes_per_step": T * shape.hidden * 4,
+           "how": "lm_moe_forward_host from pinned host memory, wall clock per call (copies + sync inside)"}
+
+    # ── decode sweep (config 1) ──
+    sweep = []
+    if not args.no_sweep:
+        for t in SWEEP:
+            xs = bf16_tensor(syn.tokens(shape, t, seed=SEED_TOKENS, stream=rank))
+            ys = torch.empty((t, shape.hidden), dtype=torch.float32, device="cuda")
+            for _ in range(3):
+                layer.forward(0, xs, y=ys)
+            layer.sync()
+            tt = int((layer.expert_counts() > 0).sum())
+            m = max_over_ranks(time_forward(layer, xs, ys, flush, max(5, args.steps // 2), torch))
+            b = layer_bytes(shape, tt, t)
+            sweep.append({"tokens": t, "tokens_per_s": t * world / (m / 1e3), "ms": m, "touched_experts": tt,
+                          "layer_gbs": b / (m / 1e3) / 1e9, "frac_hbm": b / (m / 1e3) / 1e9 / peaks["hbm_gbs"]})
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        xf = syn.bf16_to_f32(x_bits).reshape(T, -1)
+        cpu = cpu_reference_rate(W, xf, args.cpu_seconds)
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(args, world),
+        "roofline": roofline, "layer_roofline": layer_roofline, "cpu_baseline": cpu, "e2e": e2e,
+        "clocks": clock_info, "gpu_launches": KERNELS_PER_FORWARD * args.steps, "sweep": sweep,
+        "wall_s_timed_region": wall,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    layer.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

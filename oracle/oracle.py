@@ -223,6 +223,7 @@ class Reference(_Base):
                                     C.c_void_p, _u16p, _u16p, _u16p, _u16p, _u16p, _u16p, _f32p,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
         L.ref_moe_layer.restype = C.c_int
+        L.ref_kerneltest_inputs.argtypes = [_f32p, _u16p, _f32p]
         L.ref_cache_new.restype = C.c_void_p
         L.ref_cache_free.argtypes = [C.c_void_p]
         L.ref_cache_configure.argtypes = [C.c_void_p, C.c_uint64]
@@ -235,6 +236,14 @@ class Reference(_Base):
         self._matvec_bf16 = lambda w, x, out, r, c: L.ref_matvec_bf16(w, x, out, r, c, self.threads)
         self._matvec_bf16_acc = lambda w, x, out, r, c, s: L.ref_matvec_bf16_accumulate(
             w, x, out, r, c, s, self.threads)
+
+    def kerneltest_inputs(self):
+        """tests/KernelTest.cpp's seeded 67x253 inputs: (w_f32, w_bf16, x)."""
+        w32 = np.zeros(67 * 253, np.float32)
+        w16 = np.zeros(67 * 253, np.uint16)
+        x = np.zeros(253, np.float32)
+        self.lib.ref_kerneltest_inputs(w32, w16, x)
+        return w32.reshape(67, 253), w16.reshape(67, 253), x
 
     def hardware_threads(self) -> int:
         return int(self.lib.ref_hardware_threads())

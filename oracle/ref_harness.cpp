@@ -19,7 +19,9 @@
 #include "Threading.hpp"
 
 #include <algorithm>
+#include <bit>
 #include <cstdint>
+#include <random>
 #include <cstring>
 #include <memory>
 #include <span>
@@ -60,6 +62,21 @@ ThreadPool& pool_with(int threads) {
 }  // namespace
 
 extern "C" {
+
+// The inputs tests/KernelTest.cpp:28-51 draws: a 67x253 bf16 matrix (round to
+// nearest even of U(-1,1) from std::mt19937(12345)), its widened copy, and the
+// U(-1,1) input vector, in the same draw order.
+void ref_kerneltest_inputs(float* weights_f32, uint16_t* weights_bf16, float* input) {
+    constexpr std::size_t out_dim = 67U, in_dim = 253U;
+    std::mt19937 generator(12345U);
+    std::uniform_real_distribution<float> distribution(-1.0F, 1.0F);
+    for (std::size_t i = 0; i < out_dim * in_dim; ++i) {
+        const std::uint32_t bits = std::bit_cast<std::uint32_t>(distribution(generator));
+        weights_bf16[i] = static_cast<uint16_t>((bits + 0x7fffU + ((bits >> 16U) & 1U)) >> 16U);
+        weights_f32[i] = std::bit_cast<float>(static_cast<std::uint32_t>(weights_bf16[i]) << 16U);
+    }
+    for (std::size_t i = 0; i < in_dim; ++i) input[i] = distribution(generator);
+}
 
 int64_t ref_hardware_threads() { return static_cast<int64_t>(ThreadPool::hardware_threads()); }
 
