@@ -125,7 +125,7 @@ def moe_small(ref: orc.Reference) -> None:
         cases[f"{name}_logits"] = logits
         cases[f"{name}_shape"] = np.array([shape.hidden, shape.inter, shape.n_routed_experts,
                                            shape.n_shared_experts, shape.top_k], np.int64)
-        cases[f"{name}_router"] = np.array([cfg.n_group, cfg.topk_group, int(cfg.group_limited),
+        cases[f"{name}_routing"] = np.array([cfg.n_group, cfg.topk_group, int(cfg.group_limited),
                                             int(cfg.norm_topk_prob)], np.int64)
         cases[f"{name}_scale"] = np.float32(cfg.routed_scaling_factor)
     np.savez_compressed(os.path.join(HERE, "moe_small.npz"), **cases)

@@ -98,7 +98,7 @@ def test_router_golden(oracle_lib):
 def test_moe_small_golden(oracle_lib, name):
     g = load("moe_small.npz")
     H, I, E, S, K = (int(v) for v in g[f"{name}_shape"])
-    ng, tg, gl, norm = (int(v) for v in g[f"{name}_router"])
+    ng, tg, gl, norm = (int(v) for v in g[f"{name}_routing"])
     cfg = RouterConfig(E, K, ng, tg, bool(gl), bool(norm), float(g[f"{name}_scale"]))
     W = {k: g[f"{name}_{k}"] for k in ("router", "gate", "up", "down", "shared_gate", "shared_up", "shared_down")}
     bias = g[f"{name}_bias"] if f"{name}_bias" in g.files else None
