@@ -179,6 +179,29 @@ lm_status lm_moe_profile_read(lm_moe_ctx* ctx, double* total_ms, int64_t* launch
 lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t rank,
                          int32_t nranks);
 
+/*
+ * Routing that allocates nothing, for callers that cannot allocate device memory:
+ * code inside a CUDA graph capture (cudaMalloc cannot be captured), plugins whose
+ * host application owns all device memory through its own pool, and paths that
+ * must never trigger an allocation's implicit synchronisation.  It has no
+ * counterpart in the reference, which routes on the CPU.
+ *
+ * Same results as lm_moe_route with greedy top-k (normalise or scale as given),
+ * but without a context: the caller passes the router weights (device f32 [E, H],
+ * the layout of lm_moe_upload_layer's `router`), x (device bf16 [T, H]), the
+ * optional bias (device f32 [E]) and the outputs (device int32 / f32 [T, k]).
+ * Its only scratch is a fixed 1 MiB device array inside the library (held by every
+ * GPU that loads it until the process exits), so: T <= 2047 and T * E <= 262144,
+ * else LM_ERR_TOO_MANY_TOKENS.  The first call on a device looks up that array's
+ * address (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the array: calls whose kernels overlap on the GPU (different
+ * streams without ordering) race on it and give wrong results.  Errors are
+ * status codes only; lm_moe_last_error does not describe them.
+ */
+lm_status lm_moe_route_static(const float* router, const uint16_t* x, int32_t tokens, int32_t hidden,
+                              int32_t experts, int32_t top_k, int32_t norm_topk_prob, float routed_scaling_factor,
+                              const float* logit_bias, int32_t* topk_idx, float* topk_w, void* stream);
+
 /* ── gemm:: kernels on device memory (include/Gemm.hpp:23-72) ──────────────── */
 
 /* gemm::matvec_bf16 (src/Gemm.cpp:139-154): out = W x, W [rows, cols] bf16. */

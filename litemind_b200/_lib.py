@@ -68,6 +68,7 @@ SIGNATURES = {
     "lm_moe_ep_init": (_i32, [_vp, _vp, _i32, _i32]),
     "lm_moe_profile_enable": (_i32, [_vp, _i32]),
     "lm_moe_profile_read": (_i32, [_vp, _vp, _vp, _i32]),
+    "lm_moe_route_static": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp]),
     "lm_gemm_matvec_bf16": (_i32, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "lm_gemm_matvec_bf16_accumulate": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp]),
     "lm_gemm_matvec_f32": (_i32, [_vp, _vp, _vp, _i64, _i64, _vp]),

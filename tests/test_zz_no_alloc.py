@@ -1,0 +1,66 @@
+"""lm_moe_route_static: routing that allocates no device memory.
+
+Some callers cannot allocate: code inside a CUDA graph capture, plugins whose host
+application owns every device allocation, paths that must not trigger an
+allocation's synchronisation.  lm_moe_route_static serves them with a fixed scratch
+array inside the library.  This test calls it through the C ABI and checks that it
+routes exactly as the context-based entry point lm_moe_route does, on two calls in
+a row (the second call reuses the scratch the first one left behind), and that a
+batch beyond the scratch's capacity is refused.  It lives in its own file, collected
+last, and needs nothing from the other tests.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+from litemind_b200 import _lib, synthetic as syn  # noqa: E402
+from litemind_b200.moe import MoeConfig, MoeLayer, bf16_tensor  # noqa: E402
+
+SHAPE = syn.MoeShape(hidden=512, inter=128, n_routed_experts=64, n_shared_experts=1, top_k=6)
+W_RTOL = 1e-5  # routing weights, as in tests/parity.py
+
+
+def _static_route(lib, router, x, bias, k, norm=False, scale=1.0):
+    T, H = x.shape
+    E = router.shape[0]
+    idx = torch.full((T, k), -1, dtype=torch.int32, device="cuda")
+    w = torch.zeros((T, k), dtype=torch.float32, device="cuda")
+    status = lib.lm_moe_route_static(C.c_void_p(router.data_ptr()), C.c_void_p(x.data_ptr()), T, H, E, k, int(norm),
+                                     scale, None if bias is None else C.c_void_p(bias.data_ptr()),
+                                     C.c_void_p(idx.data_ptr()), C.c_void_p(w.data_ptr()),
+                                     C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    return status, idx, w
+
+
+def test_static_route_matches_context_route():
+    lib = _lib.load()
+    W = syn.layer_weights(SHAPE, seed=4, std=0.02)
+    layer = MoeLayer(MoeConfig.from_shape(SHAPE, max_tokens=2048))
+    layer.upload_layer(0, W)
+    router = torch.from_numpy(W["router"]).cuda()
+    bias = torch.from_numpy(syn.zipf_bias(SHAPE, seed=4)).cuda()
+    for call, (T, b) in enumerate([(1000, None), (37, bias)]):  # two calls in a row
+        x = bf16_tensor(syn.tokens(SHAPE, T, seed=40 + call))
+        status, idx, w = _static_route(lib, router, x, b, SHAPE.top_k)
+        assert status == _lib.LM_OK
+        ref_idx, ref_w, _ = layer.route(0, x, bias=b)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(idx.cpu().numpy(), ref_idx.cpu().numpy(), err_msg=f"call {call}")
+        np.testing.assert_allclose(w.cpu().numpy(), ref_w.cpu().numpy(), rtol=W_RTOL, atol=1e-8,
+                                   err_msg=f"call {call}")
+    layer.close()
+
+
+def test_static_route_refuses_batches_beyond_its_scratch():
+    lib = _lib.load()
+    router = torch.zeros((64, 512), dtype=torch.float32, device="cuda")
+    x = torch.zeros((2048, 512), dtype=torch.bfloat16, device="cuda")
+    status, _, _ = _static_route(lib, router, x, None, 6)
+    assert status == _lib.LM_ERR_TOO_MANY_TOKENS
+    status, _, _ = _static_route(lib, router, x[:0], None, 6)
+    assert status == _lib.LM_OK
