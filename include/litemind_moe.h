@@ -158,8 +158,9 @@ lm_status lm_moe_memory(const lm_moe_ctx* ctx, uint64_t* resident_bytes, uint64_
 /*
  * Profiling hook.  While enabled, each forward records a CUDA event after every
  * launch of its sequence, waits for the last one and adds each launch's device
- * time to a per-slot total: slot 0 zeroing y, 1 router logits, 2 router top-k,
- * 3 dispatch scan, 4 permute, 5 gate/up GEMM, 6 down GEMM, 7 expert-parallel
+ * time to a per-slot total: slot 1 routing (the fused kernel for T <= 32, else the
+ * router logits), 2 router top-k, 3 dispatch scan, 4 placement, 0 the copy of
+ * token rows into expert order, 5 gate/up GEMM, 6 down GEMM, 7 expert-parallel
  * exchange.  lm_moe_profile_read copies LM_PROFILE_SLOTS totals (ms) and launch
  * counts to host memory and, when reset != 0, clears them.  No counterpart in the
  * reference, which has no device launches to time.

@@ -21,8 +21,8 @@ LM_ERR_COMM = 6
 LM_ERR_UNSUPPORTED = 7
 
 LM_PROFILE_SLOTS = 8
-PROFILE_SLOT_NAMES = ["zero_y", "router_logits", "router_topk", "dispatch_scan", "permute", "gemm_gate_up",
-                      "gemm_down", "ep_exchange"]
+PROFILE_SLOT_NAMES = ["gather_rows", "route", "router_topk", "dispatch_scan", "place", "gemm_gate_up", "gemm_down",
+                      "ep_exchange"]
 
 LM_TOPK_GREEDY = 0
 LM_TOPK_GROUP_LIMITED_GREEDY = 1

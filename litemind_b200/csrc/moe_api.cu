@@ -51,7 +51,7 @@ struct lm_moe_ctx {
     int first_expert = 0;
     int local_experts = 0;
     int n_seg = 0;
-    int routed_cap = 0;  // rows reserved for routed tokens in x_perm / h
+    int routed_cap = 0;  // rows reserved for routed tokens in h (expert-sorted order)
     std::vector<lm::LayerWeights> layers;
 
     float* logits = nullptr;
@@ -64,9 +64,10 @@ struct lm_moe_ctx {
     int32_t* row_token = nullptr;
     float* row_weight = nullptr;
     int32_t* slot_row = nullptr;
-    uint16_t* x_perm = nullptr;
+    uint16_t* x_perm = nullptr;      // routed token rows in expert-sorted order
     uint16_t* h = nullptr;
     int32_t* status = nullptr;
+    unsigned int* ticket = nullptr;  // last-CTA ticket of the fused small-T route kernel
     CUtensorMap map_xperm[5]{};
     CUtensorMap map_h[5]{};
 
@@ -317,11 +318,12 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
         (st = alloc(p, &p->sched, 1)) || (st = alloc(p, &p->row_token, static_cast<size_t>(p->routed_cap))) ||
         (st = alloc(p, &p->row_weight, static_cast<size_t>(p->routed_cap))) || (st = alloc(p, &p->slot_row, T * K)) ||
         (st = alloc(p, &p->x_perm, static_cast<size_t>(p->routed_cap) * H)) || (st = alloc(p, &p->h, h_rows * I)) ||
-        (st = alloc(p, &p->status, 1))) {
+        (st = alloc(p, &p->status, 1)) || (st = alloc(p, &p->ticket, 1))) {
         lm_moe_destroy(ctx.release());
         return st;
     }
     if (cudaMemset(p->status, 0, sizeof(int32_t)) != cudaSuccess ||
+        cudaMemset(p->ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
         cudaMemset(p->expert_totals, 0, E * sizeof(int32_t)) != cudaSuccess ||
         cudaMemset(p->sched, 0, sizeof(Schedule)) != cudaSuccess) {
         lm_moe_destroy(ctx.release());
@@ -476,34 +478,43 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
     prof_begin(ctx, s);
     int slots[8];
     int n_slots = 0;
-    if (!accumulate) {
-        LM_CUDA(ctx, cudaMemsetAsync(y, 0, static_cast<size_t>(T) * H * sizeof(float), s));
-        prof_mark(ctx, 0, s);
-        slots[n_slots++] = 0;
+    const RouterParams rp = router_params(c);
+    float* y_zero = accumulate ? nullptr : y;  // the down GEMM adds into y
+    if (T <= kRouteTile) {
+        // Decode: logits, top-k, counts, schedule and placement in one launch.
+        LM_CUDA(ctx, launch_route_small(x, x_f32, L.router, bias, ctx->logits, T, H, rp, ctx->topk_idx, ctx->topk_w,
+                                        ctx->expert_totals, ctx->sched, ctx->row_token, ctx->row_weight,
+                                        ctx->slot_row, y_zero, ctx->ticket, c.n_shared_experts, ctx->first_expert,
+                                        ctx->local_experts, ctx->routed_cap, bn, 2 * I / 128, H / 128, s, false));
+        prof_mark(ctx, 1, s);
+        slots[n_slots++] = 1;
+    } else {
+        LM_CUDA(ctx, launch_router_logits(x, x_f32, L.router, L.router_t, bias, ctx->logits, T, c.hidden_size,
+                                          c.n_routed_experts, s, false));
+        prof_mark(ctx, 1, s);
+        slots[n_slots++] = 1;
+        LM_CUDA(ctx, launch_router_topk(ctx->logits, T, rp, ctx->topk_idx, ctx->topk_w, ctx->tile_counts, s, true));
+        prof_mark(ctx, 2, s);
+        slots[n_slots++] = 2;
+        LM_CUDA(ctx, launch_dispatch_scan(ctx->tile_counts, ctx->tile_base, ctx->expert_totals, ctx->sched, T, K, E,
+                                          c.n_shared_experts, ctx->first_expert, ctx->local_experts, ctx->routed_cap,
+                                          bn, 2 * I / 128, H / 128, s, true));
+        prof_mark(ctx, 3, s);
+        slots[n_slots++] = 3;
+        LM_CUDA(ctx, launch_place(ctx->topk_idx, ctx->topk_w, ctx->tile_base, T, H, K, E, ctx->first_expert,
+                                  ctx->local_experts, ctx->row_token, ctx->row_weight, ctx->slot_row, y_zero, s, true));
+        prof_mark(ctx, 4, s);
+        slots[n_slots++] = 4;
     }
-    LM_CUDA(ctx, launch_router_logits(x, x_f32, L.router, L.router_t, bias, ctx->logits, T, c.hidden_size,
-                                      c.n_routed_experts, s, false));
-    prof_mark(ctx, 1, s);
-    slots[n_slots++] = 1;
-    LM_CUDA(ctx, launch_router_topk(ctx->logits, T, router_params(c), ctx->topk_idx, ctx->topk_w, ctx->tile_counts,
-                                    s, true));
-    prof_mark(ctx, 2, s);
-    slots[n_slots++] = 2;
-    LM_CUDA(ctx, launch_dispatch_scan(ctx->tile_counts, ctx->tile_base, ctx->expert_totals, ctx->sched, T, K, E,
-                                      c.n_shared_experts, ctx->first_expert, ctx->local_experts, ctx->routed_cap, bn,
-                                      2 * I / 128, H / 128, s, true));
-    prof_mark(ctx, 3, s);
-    slots[n_slots++] = 3;
-    LM_CUDA(ctx, launch_permute(x, ctx->topk_idx, ctx->topk_w, ctx->tile_base, T, H, K, E, ctx->first_expert,
-                                ctx->local_experts, ctx->row_token, ctx->row_weight, ctx->slot_row, ctx->x_perm, s,
-                                true));
-    prof_mark(ctx, 4, s);
-    slots[n_slots++] = 4;
+    LM_CUDA(ctx, launch_gather_rows(x, ctx->row_token, T * K, H, ctx->x_perm, s, true));
+    prof_mark(ctx, 0, s);
+    slots[n_slots++] = 0;
     CUtensorMap map_x{};
     std::string err;
     if (!encode_tensor_map_bf16(&map_x, x, T, H, bn, 64, err)) return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
     GemmArgs args{};
     args.sched = ctx->sched;
+    args.x = x;
     args.h = ctx->h;
     args.y = y;
     args.row_token = ctx->row_token;

@@ -16,12 +16,12 @@ constexpr int kMaxExperts = 256;          // routed experts supported by the rou
 constexpr int kMaxShared = 8;             // shared-expert splits (n_shared_experts)
 constexpr int kMaxSegments = kMaxExperts + kMaxShared;
 constexpr int kMaxTopK = 16;
-constexpr int kRouteTile = 64;            // tokens per routing tile (histogram granularity)
+constexpr int kRouteTile = 32;            // tokens per routing tile (one warp per token)
 
 // Per-call schedule written on the device by the scan kernel and read by the
 // grouped GEMMs.  Segment s < E is routed expert s; s >= E is shared split s-E.
 struct Schedule {
-    int32_t seg_off[kMaxSegments];     // first row of the segment in x_perm / h
+    int32_t seg_off[kMaxSegments];     // first row of the segment in h (expert-sorted rows)
     int32_t seg_cnt[kMaxSegments];     // rows in the segment
     int32_t tiles1[kMaxSegments + 1];  // exclusive prefix of gate/up tiles
     int32_t tiles2[kMaxSegments + 1];  // exclusive prefix of down tiles
@@ -49,14 +49,22 @@ cudaError_t launch_dispatch_scan(const int32_t* tile_counts, int32_t* tile_base,
                                  Schedule* sched, int tokens, int top_k, int experts, int n_shared,
                                  int first_expert, int local_experts, int shared_base, int bn, int mb1,
                                  int mb2, cudaStream_t stream, bool pdl);
-cudaError_t launch_permute(const uint16_t* x, const int32_t* topk_idx, const float* topk_w,
-                           const int32_t* tile_base, int tokens, int hidden, int top_k, int experts,
-                           int first_expert, int local_experts, int32_t* row_token, float* row_weight,
-                           int32_t* slot_row, uint16_t* x_perm, cudaStream_t stream, bool pdl);
+cudaError_t launch_place(const int32_t* topk_idx, const float* topk_w, const int32_t* tile_base, int tokens,
+                         int hidden, int top_k, int experts, int first_expert, int local_experts, int32_t* row_token,
+                         float* row_weight, int32_t* slot_row, float* y_zero, cudaStream_t stream, bool pdl);
+cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* row_token, int rows, int hidden, uint16_t* x_perm,
+                               cudaStream_t stream, bool pdl);
+cudaError_t launch_route_small(const uint16_t* x, const float* x_f32, const float* w, const float* bias,
+                               float* logits, int tokens, int hidden, RouterParams rp, int32_t* topk_idx,
+                               float* topk_w, int32_t* expert_totals, Schedule* sched, int32_t* row_token,
+                               float* row_weight, int32_t* slot_row, float* y_zero, unsigned int* ticket,
+                               int n_shared, int first_expert, int local_experts, int shared_base, int bn, int mb1,
+                               int mb2, cudaStream_t stream, bool pdl);
 
 // Grouped SwiGLU GEMMs (grouped_gemm.cu).
 struct GemmArgs {
     const Schedule* sched;
+    const uint16_t* x;         // [T, hidden] bf16 tokens (the shared experts' operand)
     uint16_t* h;               // [rows, inter] bf16 (gate/up output, down input)
     float* y;                  // [T, hidden] f32 (down output, accumulated)
     const int32_t* row_token;  // routed row -> token
@@ -68,9 +76,8 @@ struct GemmArgs {
     int32_t routed_rows;       // rows of routed segments (shared segments use tokens directly)
     int32_t n_routed_local;    // segments [0, n_routed_local) are routed experts
 };
-cudaError_t launch_gemm_gate_up(int bn, const CUtensorMap& w13, const CUtensorMap& xperm,
-                                const CUtensorMap& x, const GemmArgs& args, int sms, cudaStream_t stream,
-                                bool pdl);
+cudaError_t launch_gemm_gate_up(int bn, const CUtensorMap& w13, const CUtensorMap& xperm, const CUtensorMap& x,
+                                const GemmArgs& args, int sms, cudaStream_t stream, bool pdl);
 cudaError_t launch_gemm_down(int bn, const CUtensorMap& w2, const CUtensorMap& hmap, const GemmArgs& args,
                              int sms, cudaStream_t stream, bool pdl);
 

@@ -4,18 +4,21 @@
 // logits (src/Gemm.cpp:132-137), then MoeRouter::select (src/MoeRouter.cpp:54-107):
 // softmax over every expert, optional group-limited masking, greedy top-k by
 // (allowed, probability descending, index ascending), then normalise or scale.
-// Here that is four kernels over all T tokens:
+// Here, for T tokens at once:
+//   route_small       T <= 32 (decode): the whole stage below in one launch
 //   router_logits_*   logits[T, E] in f32 (+ optional per-expert bias)
 //   router_topk       warp per token: softmax, group mask, top-k, weights, and the
 //                     per-routing-tile expert histogram
 //   dispatch_scan     one CTA: per-expert totals, segment offsets, each tile's
 //                     first row per expert, and the grouped GEMMs' tile tables
-//   permute           token rows copied into expert-sorted order (x_perm) with the
-//                     row -> (token, weight) maps; stable in token order, so the
-//                     permutation is deterministic.
+//   place             the row -> (token, weight) maps of the expert-sorted order,
+//                     stable in token order, so the permutation is deterministic.
+//   gather_rows       x_perm[r] = x[row_token[r]]: token rows in expert-sorted order,
+//                     so each expert's token tile is one contiguous TMA load.
 #include "moe_internal.h"
 #include "ptx.cuh"
 
+#include <algorithm>
 #include <cfloat>
 
 namespace lm {
@@ -154,23 +157,163 @@ __global__ void __launch_bounds__(256) router_logits_tiled_kernel(const XT* __re
     }
 }
 
-// (allowed, probability, index) ordering of top_k_indices (src/MoeRouter.cpp:21-32).
-__device__ __forceinline__ bool ranks_ahead(bool a_ok, float a_p, int a_i, bool b_ok, float b_p, int b_i) {
-    if (b_i < 0) return a_i >= 0;
-    if (a_i < 0) return false;
-    if (a_ok != b_ok) return a_ok;
-    if (a_p != b_p) return a_p > b_p;
-    return a_i < b_i;
+constexpr uint32_t kFull = 0xffffffffu;
+
+// One token's routing by one warp: MoeRouter::select (src/MoeRouter.cpp:54-107).
+// Softmax over every expert before the cut (:61-64, src/Gemm.cpp:209-223), optional
+// group-limited masking (:66-84), greedy top-k ordered by (allowed, probability
+// descending, index ascending) as top_k_indices orders them (:21-32), then
+// normalise or scale, never both (:96-106).  Each round of the top-k packs
+// (allowed, probability) into one 32-bit key -- probabilities are non-negative, so
+// their bit patterns order like their values -- and takes the warp's maximum key,
+// then the lowest expert index holding it, with two redux.sync reductions.
+// Lane s < K returns selection s.  `lg` holds the token's E logits; `probs` is E
+// floats of per-warp shared scratch (group-limited routing only).
+struct Selection {
+    int idx;
+    float w;
+};
+
+__device__ __forceinline__ Selection route_one_token(const float* lg, const RouterParams& rp, float* probs,
+                                                     int lane) {
+    const int E = rp.experts;
+    const int K = rp.top_k;
+    float p[kMaxExperts / 32];
+    float m = -FLT_MAX;
+#pragma unroll
+    for (int j = 0; j < kMaxExperts / 32; ++j) {
+        const int e = lane + 32 * j;
+        p[j] = (e < E) ? __ldcg(lg + e) : -FLT_MAX;
+        m = fmaxf(m, p[j]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxExperts / 32; ++j) {
+        const int e = lane + 32 * j;
+        p[j] = (e < E) ? expf(p[j] - m) : 0.0f;
+        sum += p[j];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(kFull, sum, off);
+    const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxExperts / 32; ++j) p[j] *= inv;
+
+    uint32_t group_mask = 0xffffffffu;
+    int per_group = E;
+    if (rp.group_limited && rp.n_group > 1) {
+        per_group = E / rp.n_group;
+#pragma unroll
+        for (int j = 0; j < kMaxExperts / 32; ++j) {
+            const int e = lane + 32 * j;
+            if (e < E) probs[e] = p[j];
+        }
+        __syncwarp();
+        uint32_t gkey = 0;
+        bool g_avail = lane < rp.n_group;
+        if (g_avail) {
+            float best = probs[lane * per_group];
+            for (int o = 1; o < per_group; ++o) best = fmaxf(best, probs[lane * per_group + o]);
+            gkey = __float_as_uint(best);
+        }
+        __syncwarp();
+        group_mask = 0u;
+        const int keep = min(rp.topk_group, rp.n_group);
+        for (int r = 0; r < keep; ++r) {
+            const uint32_t gmax = __reduce_max_sync(kFull, g_avail ? gkey : 0u);
+            const uint32_t gc = (g_avail && gkey == gmax) ? static_cast<uint32_t>(lane) : 0xffffffffu;
+            const uint32_t g = __reduce_min_sync(kFull, gc);
+            if (g < 32u) {
+                group_mask |= 1u << g;
+                if (g == static_cast<uint32_t>(lane)) g_avail = false;
+            }
+        }
+    }
+
+    uint32_t key[kMaxExperts / 32];
+    uint32_t avail = 0;
+#pragma unroll
+    for (int j = 0; j < kMaxExperts / 32; ++j) {
+        const int e = lane + 32 * j;
+        key[j] = 0;
+        if (e < E) {
+            const uint32_t allowed = (group_mask >> (e / per_group)) & 1u;
+            key[j] = (allowed << 31) | __float_as_uint(p[j]);
+            avail |= 1u << j;
+        }
+    }
+    Selection mine{-1, 0.0f};
+    for (int s = 0; s < K; ++s) {
+        uint32_t best = 0;
+        int bj = -1;
+#pragma unroll
+        for (int j = 0; j < kMaxExperts / 32; ++j) {
+            if (((avail >> j) & 1u) && (bj < 0 || key[j] > best)) {
+                best = key[j];
+                bj = j;
+            }
+        }
+        const uint32_t wmax = __reduce_max_sync(kFull, bj >= 0 ? best : 0u);
+        const uint32_t cand = (bj >= 0 && best == wmax) ? static_cast<uint32_t>(lane + 32 * bj) : 0xffffffffu;
+        const uint32_t win = __reduce_min_sync(kFull, cand);
+        if ((win & 31u) == static_cast<uint32_t>(lane)) avail &= ~(1u << (win >> 5));
+        if (lane == s) {
+            mine.idx = static_cast<int>(win);
+            mine.w = __uint_as_float(wmax & 0x7fffffffu);
+        }
+    }
+    if (K > 1 && rp.normalize) {
+        float selected = 0.0f;  // in selection order, as the reference sums it
+        for (int s = 0; s < K; ++s) selected += __shfl_sync(kFull, mine.w, s);
+        mine.w = mine.w / (selected + 1e-20f);
+    } else if (rp.scale != 1.0f) {
+        mine.w = mine.w * rp.scale;
+    }
+    return mine;
 }
 
-constexpr int kTopkWarps = 8;
+// Thread 0: segment offsets, counts and both GEMMs' tile prefixes from per-expert
+// totals (`totals` in shared memory, global expert index).  Everything is computed
+// in registers and only written to global memory, never read back.
+__device__ void build_schedule(Schedule* sched, const int* totals, int T, int n_shared, int first_expert,
+                               int local_E, int shared_base, int bn, int mb1, int mb2, int* seg_off_out) {
+    const int n_seg = local_E + n_shared;
+    int off = 0, p1 = 0, p2 = 0;
+    for (int s = 0; s < n_seg; ++s) {
+        int seg_off, cnt;
+        if (s < local_E) {
+            cnt = totals[first_expert + s];
+            seg_off = off;
+            if (seg_off_out != nullptr) seg_off_out[first_expert + s] = off;
+            off += cnt;
+        } else {
+            cnt = T;
+            seg_off = shared_base + (s - local_E) * T;
+        }
+        sched->seg_off[s] = seg_off;
+        sched->seg_cnt[s] = cnt;
+        sched->tiles1[s] = p1;
+        sched->tiles2[s] = p2;
+        const int nb = (cnt + bn - 1) / bn;
+        p1 += nb * mb1;
+        p2 += nb * mb2;
+    }
+    sched->tiles1[n_seg] = p1;
+    sched->tiles2[n_seg] = p2;
+    sched->n_seg = n_seg;
+    sched->first_expert = first_expert;
+}
 
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, int T, RouterParams rp,
-                                                          int32_t* __restrict__ topk_idx,
-                                                          float* __restrict__ topk_w,
-                                                          int32_t* __restrict__ tile_counts) {
+constexpr int kTopkThreads = 32 * kRouteTile;  // one warp per token of a routing tile
+
+__global__ void __launch_bounds__(kTopkThreads) router_topk_kernel(const float* __restrict__ logits, int T,
+                                                                   RouterParams rp, int32_t* __restrict__ topk_idx,
+                                                                   float* __restrict__ topk_w,
+                                                                   int32_t* __restrict__ tile_counts) {
     __shared__ int counts[kMaxExperts];
-    __shared__ float probs[kTopkWarps][kMaxExperts];
+    __shared__ float probs[kRouteTile][kMaxExperts];
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
@@ -180,127 +323,13 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     __syncthreads();
     pdl_wait();
     pdl_launch_dependents();
-
-    const int t_begin = blockIdx.x * kRouteTile;
-    const int t_end = min(T, t_begin + kRouteTile);
-    for (int t = t_begin + warp; t < t_end; t += kTopkWarps) {
-        float p[kMaxExperts / 32];
-        uint32_t taken = 0u;  // bit j: expert lane + 32 j already selected
-        float m = -FLT_MAX;
-#pragma unroll
-        for (int j = 0; j < kMaxExperts / 32; ++j) {
-            const int e = lane + 32 * j;
-            p[j] = (e < E) ? logits[static_cast<size_t>(t) * E + e] : -FLT_MAX;
-            m = fmaxf(m, p[j]);
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-        // Softmax over every expert before the cut (src/MoeRouter.cpp:61-64, src/Gemm.cpp:209-223).
-        float sum = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kMaxExperts / 32; ++j) {
-            const int e = lane + 32 * j;
-            p[j] = (e < E) ? expf(p[j] - m) : 0.0f;
-            sum += p[j];
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-        const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
-#pragma unroll
-        for (int j = 0; j < kMaxExperts / 32; ++j) p[j] *= inv;
-
-        // Group-limited masking (src/MoeRouter.cpp:66-84): keep the topk_group groups
-        // whose best probability ranks highest.
-        uint32_t group_mask = 0xffffffffu;
-        int per_group = E;
-        if (rp.group_limited && rp.n_group > 1) {
-            per_group = E / rp.n_group;
-#pragma unroll
-            for (int j = 0; j < kMaxExperts / 32; ++j) {
-                const int e = lane + 32 * j;
-                if (e < E) probs[warp][e] = p[j];
-            }
-            __syncwarp();
-            float gbest = -FLT_MAX;
-            int gi = -1;
-            if (lane < rp.n_group) {
-                gi = lane;
-                gbest = probs[warp][lane * per_group];
-                for (int o = 1; o < per_group; ++o) gbest = fmaxf(gbest, probs[warp][lane * per_group + o]);
-            }
-            __syncwarp();
-            group_mask = 0u;
-            const int keep = min(rp.topk_group, rp.n_group);
-            bool g_taken = false;
-            for (int r = 0; r < keep; ++r) {
-                float bp = (!g_taken && gi >= 0) ? gbest : -FLT_MAX;
-                int bi = (!g_taken && gi >= 0) ? gi : -1;
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) {
-                    const float op = __shfl_xor_sync(0xffffffffu, bp, off);
-                    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-                    if (ranks_ahead(true, op, oi, true, bp, bi)) {
-                        bp = op;
-                        bi = oi;
-                    }
-                }
-                if (bi >= 0) {
-                    group_mask |= 1u << bi;
-                    if (bi == gi) g_taken = true;
-                }
-            }
-        }
-
-        // Greedy top-k, lower index first on equal probability.
-        int my_idx = -1;
-        float my_p = 0.0f;
-        for (int s = 0; s < K; ++s) {
-            bool b_ok = false;
-            float b_p = -FLT_MAX;
-            int b_i = -1;
-#pragma unroll
-            for (int j = 0; j < kMaxExperts / 32; ++j) {
-                const int e = lane + 32 * j;
-                if (e < E && !((taken >> j) & 1u)) {
-                    const bool ok = (group_mask >> (e / per_group)) & 1u;
-                    if (ranks_ahead(ok, p[j], e, b_ok, b_p, b_i)) {
-                        b_ok = ok;
-                        b_p = p[j];
-                        b_i = e;
-                    }
-                }
-            }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) {
-                const bool o_ok = __shfl_xor_sync(0xffffffffu, static_cast<int>(b_ok), off) != 0;
-                const float o_p = __shfl_xor_sync(0xffffffffu, b_p, off);
-                const int o_i = __shfl_xor_sync(0xffffffffu, b_i, off);
-                if (ranks_ahead(o_ok, o_p, o_i, b_ok, b_p, b_i)) {
-                    b_ok = o_ok;
-                    b_p = o_p;
-                    b_i = o_i;
-                }
-            }
-            if (b_i >= 0 && (b_i & 31) == lane) taken |= 1u << (b_i >> 5);
-            if (lane == s) {
-                my_idx = b_i;
-                my_p = b_p;
-            }
-        }
-        // Normalise or scale, never both (src/MoeRouter.cpp:96-106).  The sum runs
-        // in selection order, as the reference's does.
-        float w = my_p;
-        if (K > 1 && rp.normalize) {
-            float selected = 0.0f;
-            for (int s = 0; s < K; ++s) selected += __shfl_sync(0xffffffffu, my_p, s);
-            w = my_p / (selected + 1e-20f);
-        } else if (rp.scale != 1.0f) {
-            w = my_p * rp.scale;
-        }
+    const int t = blockIdx.x * kRouteTile + warp;
+    if (t < T) {
+        const Selection sel = route_one_token(logits + static_cast<size_t>(t) * E, rp, probs[warp], lane);
         if (lane < K) {
-            topk_idx[static_cast<size_t>(t) * K + lane] = my_idx;
-            topk_w[static_cast<size_t>(t) * K + lane] = w;
-            if (tile_counts != nullptr && my_idx >= 0) atomicAdd(&counts[my_idx], 1);
+            topk_idx[static_cast<size_t>(t) * K + lane] = sel.idx;
+            topk_w[static_cast<size_t>(t) * K + lane] = sel.w;
+            if (tile_counts != nullptr) atomicAdd(&counts[sel.idx], 1);
         }
     }
     if (tile_counts != nullptr) {
@@ -319,6 +348,7 @@ __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(const int32
                                                                      int local_E, int shared_base, int bn,
                                                                      int mb1, int mb2) {
     __shared__ int part_sum[kScanThreads];
+    __shared__ int totals[kMaxExperts];
     __shared__ int seg_off_s[kMaxExperts];
     pdl_wait();
     pdl_launch_dependents();
@@ -346,36 +376,11 @@ __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(const int32
             run += v;
         }
         expert_totals[tid] = run;
-        seg_off_s[tid] = run;  // total for now
+        totals[tid] = run;
+        seg_off_s[tid] = 0;
     }
     __syncthreads();
-    if (tid == 0) {
-        int off = 0;
-        for (int s = 0; s < local_E; ++s) {
-            const int total = seg_off_s[first_expert + s];
-            sched->seg_off[s] = off;
-            sched->seg_cnt[s] = total;
-            off += total;
-        }
-        for (int s = 0; s < n_shared; ++s) {
-            sched->seg_off[local_E + s] = shared_base + s * T;
-            sched->seg_cnt[local_E + s] = T;
-        }
-        const int n_seg = local_E + n_shared;
-        int p1 = 0, p2 = 0;
-        for (int s = 0; s < n_seg; ++s) {
-            const int nb = (sched->seg_cnt[s] + bn - 1) / bn;
-            sched->tiles1[s] = p1;
-            sched->tiles2[s] = p2;
-            p1 += nb * mb1;
-            p2 += nb * mb2;
-        }
-        sched->tiles1[n_seg] = p1;
-        sched->tiles2[n_seg] = p2;
-        sched->n_seg = n_seg;
-        sched->first_expert = first_expert;
-        for (int s = 0; s < local_E; ++s) seg_off_s[first_expert + s] = sched->seg_off[s];
-    }
+    if (tid == 0) build_schedule(sched, totals, T, n_shared, first_expert, local_E, shared_base, bn, mb1, mb2, seg_off_s);
     __syncthreads();
     if (active) {
         const bool local = e >= first_expert && e < first_expert + local_E;
@@ -389,15 +394,15 @@ __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(const int32
     }
 }
 
-__global__ void __launch_bounds__(256) permute_kernel(const uint16_t* __restrict__ x,
-                                                      const int32_t* __restrict__ topk_idx,
-                                                      const float* __restrict__ topk_w,
-                                                      const int32_t* __restrict__ tile_base, int T, int H, int K,
-                                                      int E, int first_expert, int local_E,
-                                                      int32_t* __restrict__ row_token,
-                                                      float* __restrict__ row_weight,
-                                                      int32_t* __restrict__ slot_row,
-                                                      uint16_t* __restrict__ x_perm) {
+// Permutation maps for one routing tile: each local expert walks the tile in
+// (token, slot) order, so rows are stable in token order and the placement is
+// deterministic.  Also zeroes the tile's rows of y when asked (the combine adds).
+__global__ void __launch_bounds__(256) place_kernel(const int32_t* __restrict__ topk_idx,
+                                                    const float* __restrict__ topk_w,
+                                                    const int32_t* __restrict__ tile_base, int T, int H, int K, int E,
+                                                    int first_expert, int local_E, int32_t* __restrict__ row_token,
+                                                    float* __restrict__ row_weight, int32_t* __restrict__ slot_row,
+                                                    float* __restrict__ y_zero) {
     __shared__ int s_idx[kRouteTile * kMaxTopK];
     __shared__ int s_row[kRouteTile * kMaxTopK];
     pdl_wait();
@@ -407,12 +412,16 @@ __global__ void __launch_bounds__(256) permute_kernel(const uint16_t* __restrict
     const int t0 = tile * kRouteTile;
     const int n_tok = min(kRouteTile, T - t0);
     const int n_pairs = n_tok * K;
+    if (y_zero != nullptr) {
+        float4* yz = reinterpret_cast<float4*>(y_zero + static_cast<size_t>(t0) * H);
+        const int n4 = n_tok * H / 4;
+        for (int i = tid; i < n4; i += blockDim.x) yz[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     for (int q = tid; q < n_pairs; q += blockDim.x) {
         s_idx[q] = topk_idx[static_cast<size_t>(t0) * K + q];
         s_row[q] = -1;
     }
     __syncthreads();
-    // Each local expert walks the tile in (token, slot) order: stable placement.
     for (int e = first_expert + tid; e < first_expert + local_E; e += blockDim.x) {
         int run = tile_base[static_cast<size_t>(tile) * E + e];
         for (int q = 0; q < n_pairs; ++q) {
@@ -420,44 +429,165 @@ __global__ void __launch_bounds__(256) permute_kernel(const uint16_t* __restrict
         }
     }
     __syncthreads();
-    if (blockIdx.y == 0) {
-        for (int q = tid; q < n_pairs; q += blockDim.x) {
-            const int row = s_row[q];
-            const size_t slot = static_cast<size_t>(t0) * K + q;
-            if (slot_row != nullptr) slot_row[slot] = row;
-            if (row >= 0) {
-                row_token[row] = t0 + q / K;
-                row_weight[row] = topk_w[slot];
-            }
+    for (int q = tid; q < n_pairs; q += blockDim.x) {
+        const int row = s_row[q];
+        const size_t slot = static_cast<size_t>(t0) * K + q;
+        if (slot_row != nullptr) slot_row[slot] = row;
+        if (row >= 0) {
+            row_token[row] = t0 + q / K;
+            row_weight[row] = topk_w[slot];
         }
     }
-    // Copy token rows to their expert-sorted positions, 16 bytes per thread,
-    // four loads in flight before the stores.
-    const int vec_per_row = H / 8;
-    const int64_t total = static_cast<int64_t>(n_pairs) * vec_per_row;
-    const int64_t stride = static_cast<int64_t>(blockDim.x) * gridDim.y;
+}
+
+// x_perm[r] = x[row_token[r]] for the routed rows, 16 bytes per thread with four
+// loads in flight.
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __restrict__ x,
+                                                          const int32_t* __restrict__ row_token, int rows, int H,
+                                                          uint16_t* __restrict__ x_perm) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int vec = H / 8;
+    const int64_t total = static_cast<int64_t>(rows) * vec;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     const uint4* src = reinterpret_cast<const uint4*>(x);
     uint4* dst = reinterpret_cast<uint4*>(x_perm);
-    for (int64_t i = static_cast<int64_t>(blockIdx.y) * blockDim.x + tid; i < total; i += 4 * stride) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += 4 * stride) {
         uint4 v[4];
-        int64_t d[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int64_t j = i + u * stride;
-            d[u] = -1;
             if (j < total) {
-                const int q = static_cast<int>(j / vec_per_row);
-                const int c = static_cast<int>(j - static_cast<int64_t>(q) * vec_per_row);
-                const int row = s_row[q];
-                if (row >= 0) {
-                    v[u] = src[static_cast<size_t>(t0 + q / K) * vec_per_row + c];
-                    d[u] = static_cast<int64_t>(row) * vec_per_row + c;
+                const int r = static_cast<int>(j / vec);
+                v[u] = src[static_cast<int64_t>(row_token[r]) * vec + (j - static_cast<int64_t>(r) * vec)];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t j = i + u * stride;
+            if (j < total) dst[j] = v[u];
+        }
+    }
+}
+
+// Small T (<= kRouteTile): the whole routing stage in one launch.  CTA b computes
+// the logits of experts [b*kSmallExperts, ...) for every token and zeroes a slice
+// of y; the last CTA to finish (an atomic ticket) routes every token, counts the
+// experts, builds the schedule and the permutation maps, and re-arms the ticket.
+constexpr int kSmallExperts = 4;
+constexpr int kSmallThreads = 512;
+
+template <typename XT>
+__global__ void __launch_bounds__(kSmallThreads) route_small_kernel(
+    const XT* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias, float* __restrict__ logits,
+    int T, int H, RouterParams rp, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+    int32_t* __restrict__ expert_totals, Schedule* __restrict__ sched, int32_t* __restrict__ row_token,
+    float* __restrict__ row_weight, int32_t* __restrict__ slot_row, float* __restrict__ y_zero,
+    unsigned int* __restrict__ ticket, int n_shared, int first_expert, int local_E, int shared_base, int bn, int mb1,
+    int mb2) {
+    __shared__ float probs[kSmallThreads / 32][kMaxExperts];
+    __shared__ int s_idx[kRouteTile * kMaxTopK];
+    __shared__ float s_w[kRouteTile * kMaxTopK];
+    __shared__ int totals[kMaxExperts];
+    __shared__ int seg_off_s[kMaxExperts];
+    __shared__ int s_last;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    constexpr int kWarps = kSmallThreads / 32;
+    const int E = rp.experts;
+    const int K = rp.top_k;
+    pdl_wait();
+    pdl_launch_dependents();
+
+    if (y_zero != nullptr) {  // y is accumulated into by the down GEMM
+        const int n4 = T * H / 4;
+        const int per = (n4 + gridDim.x - 1) / gridDim.x;
+        float4* yz = reinterpret_cast<float4*>(y_zero);
+        for (int i = blockIdx.x * per + tid; i < min(n4, (blockIdx.x + 1) * per); i += blockDim.x)
+            yz[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+
+    // Logits of this CTA's experts: warp -> tokens warp, warp + 16; lanes split H.
+    const int e0 = blockIdx.x * kSmallExperts;
+    for (int t = warp; t < T; t += kWarps) {
+        float acc[kSmallExperts];
+#pragma unroll
+        for (int j = 0; j < kSmallExperts; ++j) acc[j] = 0.0f;
+        const XT* xt = x + static_cast<size_t>(t) * H;
+        for (int h = lane * 8; h < H; h += 256) {
+            float xv[8];
+            load8(xt + h, xv);
+#pragma unroll
+            for (int j = 0; j < kSmallExperts; ++j) {
+                if (e0 + j < E) {
+                    float wv[8];
+                    load8(w + static_cast<size_t>(e0 + j) * H + h, wv);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[j] = fmaf(xv[i], wv[i], acc[j]);
                 }
             }
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-            if (d[u] >= 0) dst[d[u]] = v[u];
+        for (int j = 0; j < kSmallExperts; ++j) {
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) acc[j] += __shfl_xor_sync(kFull, acc[j], off);
+        }
+        if (lane < kSmallExperts && e0 + lane < E) {
+            float v = acc[0];
+#pragma unroll
+            for (int j = 1; j < kSmallExperts; ++j) v = (lane == j) ? acc[j] : v;
+            logits[static_cast<size_t>(t) * E + e0 + lane] = bias != nullptr ? v + bias[e0 + lane] : v;
+        }
+    }
+
+    // Last CTA in: route, count, schedule, place.
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(ticket, 1u) == gridDim.x - 1) ? 1 : 0;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int t = warp; t < T; t += kWarps) {
+        const Selection sel = route_one_token(logits + static_cast<size_t>(t) * E, rp, probs[warp], lane);
+        if (lane < K) {
+            topk_idx[static_cast<size_t>(t) * K + lane] = sel.idx;
+            topk_w[static_cast<size_t>(t) * K + lane] = sel.w;
+            s_idx[t * K + lane] = sel.idx;
+            s_w[t * K + lane] = sel.w;
+        }
+    }
+    __syncthreads();
+    const int n_pairs = T * K;
+    for (int e = tid; e < E; e += blockDim.x) {
+        int c = 0;
+        for (int q = 0; q < n_pairs; ++q) c += (s_idx[q] == e);
+        totals[e] = c;
+        expert_totals[e] = c;
+        seg_off_s[e] = 0;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        build_schedule(sched, totals, T, n_shared, first_expert, local_E, shared_base, bn, mb1, mb2, seg_off_s);
+        *ticket = 0u;  // every CTA has taken its ticket: re-arm for the next launch
+    }
+    __syncthreads();
+    for (int e = first_expert + tid; e < first_expert + local_E; e += blockDim.x) {
+        int run = seg_off_s[e];
+        for (int q = 0; q < n_pairs; ++q) {
+            if (s_idx[q] == e) {
+                row_token[run] = q / K;
+                row_weight[run] = s_w[q];
+                if (slot_row != nullptr) slot_row[q] = run;
+                ++run;
+            }
+        }
+    }
+    if (slot_row != nullptr && local_E < E) {
+        for (int q = tid; q < n_pairs; q += blockDim.x) {
+            const int e = s_idx[q];
+            if (e < first_expert || e >= first_expert + local_E) slot_row[q] = -1;
+        }
     }
 }
 
@@ -504,8 +634,8 @@ cudaError_t launch_router_topk(const float* logits, int tokens, RouterParams rp,
                                float* topk_w, int32_t* tile_counts, cudaStream_t stream, bool pdl) {
     if (tokens <= 0) return cudaSuccess;
     const dim3 grid((tokens + kRouteTile - 1) / kRouteTile);
-    return launch_k(router_topk_kernel, grid, dim3(kTopkWarps * 32), stream, pdl, logits, tokens, rp, topk_idx,
-                    topk_w, tile_counts);
+    return launch_k(router_topk_kernel, grid, dim3(kTopkThreads), stream, pdl, logits, tokens, rp, topk_idx, topk_w,
+                    tile_counts);
 }
 
 cudaError_t launch_dispatch_scan(const int32_t* tile_counts, int32_t* tile_base, int32_t* expert_totals,
@@ -517,17 +647,39 @@ cudaError_t launch_dispatch_scan(const int32_t* tile_counts, int32_t* tile_base,
                     shared_base, bn, mb1, mb2);
 }
 
-cudaError_t launch_permute(const uint16_t* x, const int32_t* topk_idx, const float* topk_w,
-                           const int32_t* tile_base, int tokens, int hidden, int top_k, int experts,
-                           int first_expert, int local_experts, int32_t* row_token, float* row_weight,
-                           int32_t* slot_row, uint16_t* x_perm, cudaStream_t stream, bool pdl) {
+cudaError_t launch_place(const int32_t* topk_idx, const float* topk_w, const int32_t* tile_base, int tokens,
+                         int hidden, int top_k, int experts, int first_expert, int local_experts, int32_t* row_token,
+                         float* row_weight, int32_t* slot_row, float* y_zero, cudaStream_t stream, bool pdl) {
     if (tokens <= 0) return cudaSuccess;
     const int tiles = (tokens + kRouteTile - 1) / kRouteTile;
-    // Enough CTAs to keep the row copies bandwidth-bound at small T.
-    const int split = tiles >= 128 ? 1 : min(16, (256 + tiles - 1) / tiles);
-    return launch_k(permute_kernel, dim3(tiles, split), dim3(256), stream, pdl, x, topk_idx, topk_w, tile_base,
-                    tokens, hidden, top_k, experts, first_expert, local_experts, row_token, row_weight,
-                    slot_row, x_perm);
+    return launch_k(place_kernel, dim3(tiles), dim3(256), stream, pdl, topk_idx, topk_w, tile_base, tokens, hidden,
+                    top_k, experts, first_expert, local_experts, row_token, row_weight, slot_row, y_zero);
+}
+
+cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* row_token, int rows, int hidden, uint16_t* x_perm,
+                               cudaStream_t stream, bool pdl) {
+    if (rows <= 0) return cudaSuccess;
+    const int64_t vecs = static_cast<int64_t>(rows) * (hidden / 8);
+    const int blocks = static_cast<int>(std::min<int64_t>(2048, (vecs + 1023) / 1024));
+    return launch_k(gather_rows_kernel, dim3(blocks), dim3(256), stream, pdl, x, row_token, rows, hidden, x_perm);
+}
+
+cudaError_t launch_route_small(const uint16_t* x, const float* x_f32, const float* w, const float* bias,
+                               float* logits, int tokens, int hidden, RouterParams rp, int32_t* topk_idx,
+                               float* topk_w, int32_t* expert_totals, Schedule* sched, int32_t* row_token,
+                               float* row_weight, int32_t* slot_row, float* y_zero, unsigned int* ticket,
+                               int n_shared, int first_expert, int local_experts, int shared_base, int bn, int mb1,
+                               int mb2, cudaStream_t stream, bool pdl) {
+    if (tokens <= 0) return cudaSuccess;
+    if (tokens > kRouteTile) return cudaErrorInvalidValue;
+    const dim3 grid((rp.experts + kSmallExperts - 1) / kSmallExperts);
+    if (x_f32 != nullptr)
+        return launch_k(route_small_kernel<float>, grid, dim3(kSmallThreads), stream, pdl, x_f32, w, bias, logits,
+                        tokens, hidden, rp, topk_idx, topk_w, expert_totals, sched, row_token, row_weight, slot_row,
+                        y_zero, ticket, n_shared, first_expert, local_experts, shared_base, bn, mb1, mb2);
+    return launch_k(route_small_kernel<uint16_t>, grid, dim3(kSmallThreads), stream, pdl, x, w, bias, logits, tokens,
+                    hidden, rp, topk_idx, topk_w, expert_totals, sched, row_token, row_weight, slot_row, y_zero,
+                    ticket, n_shared, first_expert, local_experts, shared_base, bn, mb1, mb2);
 }
 
 }  // namespace lm
