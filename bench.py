@@ -23,7 +23,11 @@ from HBM.
              reference's sources) on the host's cores, rank 0, N=1 only
 --impl reference: the reference CPU path alone, same metric and config.
 
-With N > 1 (torchrun, one rank per GPU) each rank runs the same per-rank workload.
+With N > 1 (torchrun, one rank per GPU) each rank runs the same per-rank workload
+(T tokens of its own) under expert parallelism: rank r holds routed experts
+[r*64/N, (r+1)*64/N) and the shared experts, and every forward exchanges token rows
+and expert outputs with NCCL all-to-all over NVLink (BASELINE config 3's scheme;
+config 3's own size is --tokens 8192).  Scaling is weak: tokens per GPU fixed.
 """
 from __future__ import annotations
 
@@ -45,7 +49,14 @@ SEED_WEIGHTS = 0
 SEED_TOKENS = 1
 SWEEP = (1, 8, 32, 256)
 FLUSH_BYTES = 256 << 20
-KERNELS_PER_FORWARD = 6  # router_logits, router_topk, dispatch_scan, permute, gemm_gate_up, gemm_down
+
+
+def kernels_per_forward(tokens: int, world: int) -> int:
+    """Our kernel launches in one forward: the fused route (T <= 32) or logits, top-k,
+    scan and place; the row gather; the two grouped GEMMs; and, with expert
+    parallelism, the combine (NCCL's own kernels are not counted)."""
+    route = 1 if tokens <= 32 else 4
+    return route + 1 + 2 + (1 if world > 1 else 0)
 
 
 def parse_args(argv=None):
@@ -58,6 +69,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    ap.add_argument("--clock-window", type=float, default=1.5,
+                    help="seconds of the forward loop run under the clock sampler before the timed steps")
     return ap.parse_args(argv)
 
 
@@ -128,7 +141,8 @@ class ClockSampler:
                         reasons.add(name)
         os.unlink(self.path)
         return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxes) if maxes else None,
-                "reasons": sorted(reasons), "samples": len(sms)}
+                "reasons": sorted(reasons), "samples": len(sms),
+                "window": "nvidia-smi every 200 ms over the load window that ends with the timed steps"}
 
 
 # ── algorithmic work ──────────────────────────────────────────────────────
@@ -204,7 +218,8 @@ def workload_config(args, world: int) -> dict:
             "global_tokens": args.tokens * world, "seed_weights": SEED_WEIGHTS, "seed_tokens": SEED_TOKENS,
             "experts": "64 routed top-6 + 2 shared, hidden 2048, inter 1408",
             "l2": "flushed before every timed step (256 MiB write), outside the step's events",
-            "parallelism": "single GPU" if world == 1 else f"{world} independent replicas"}
+            "parallelism": "single GPU" if world == 1 else
+            f"expert parallel: {64 // world} routed experts per GPU, NCCL all-to-all dispatch/combine"}
 
 
 # ── our arm ───────────────────────────────────────────────────────────────
@@ -262,6 +277,10 @@ def main(argv=None) -> int:
     W = syn.layer_weights(shape, seed=SEED_WEIGHTS)
     max_tokens = max([T] + ([] if args.no_sweep else list(SWEEP)))
     layer = MoeLayer(MoeConfig(max_tokens=max_tokens), device=local_rank)
+    if world > 1:
+        uid = [MoeLayer.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        layer.ep_init(uid[0], rank, world)
     layer.upload_layer(0, W)
     x_bits = syn.tokens(shape, T, seed=SEED_TOKENS, stream=rank)
     x = bf16_tensor(x_bits)
@@ -271,11 +290,23 @@ def main(argv=None) -> int:
     for _ in range(max(args.warmup, 3)):
         layer.forward(0, x, y=y)
     layer.sync()
-    touched = int((layer.expert_counts() > 0).sum())
+    # Experts whose weights this GPU streams: the touched ones on one GPU; with
+    # expert parallelism every local expert (all are hit at >= 32 tokens per rank).
+    touched = int((layer.expert_counts() > 0).sum()) if world == 1 else shape.n_routed_experts // world
 
-    # ── timed region: K steps, barrier + synchronize on both sides ──
+    # nvidia-smi samples every 200 ms and the timed steps take milliseconds, so the
+    # sampler runs through a load window of the same forward loop that ends with
+    # the timed region.
     clocks = ClockSampler(local_rank)
     clocks.start()
+    t_load = time.perf_counter()
+    while time.perf_counter() - t_load < args.clock_window:
+        for _ in range(20):
+            flush.zero_()
+            layer.forward(0, x, y=y)
+        torch.cuda.synchronize()
+
+    # ── timed region: K steps, barrier + synchronize on both sides ──
     barrier()
     torch.cuda.synchronize()
     wall0 = time.perf_counter()
@@ -331,7 +362,7 @@ def main(argv=None) -> int:
 
     # ── decode sweep (config 1) ──
     sweep = []
-    if not args.no_sweep:
+    if not args.no_sweep and world == 1:
         for t in SWEEP:
             xs = bf16_tensor(syn.tokens(shape, t, seed=SEED_TOKENS, stream=rank))
             ys = torch.empty((t, shape.hidden), dtype=torch.float32, device="cuda")
@@ -354,7 +385,7 @@ def main(argv=None) -> int:
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(args, world),
         "roofline": roofline, "layer_roofline": layer_roofline, "cpu_baseline": cpu, "e2e": e2e,
-        "clocks": clock_info, "gpu_launches": KERNELS_PER_FORWARD * args.steps, "sweep": sweep,
+        "clocks": clock_info, "gpu_launches": kernels_per_forward(T, world) * args.steps, "sweep": sweep,
         "wall_s_timed_region": wall,
     }
     if rank == 0:

@@ -170,15 +170,45 @@ lm_status lm_moe_profile_enable(lm_moe_ctx* ctx, int32_t enable);
 lm_status lm_moe_profile_read(lm_moe_ctx* ctx, double* total_ms, int64_t* launches, int32_t reset);
 
 /*
- * Expert parallelism over NCCL.  Every rank creates its context with the same
- * config, then calls this with the same 128-byte ncclUniqueId.  Rank r then keeps
- * routed experts [r*E/N, (r+1)*E/N) (upload_layer still takes the full arrays and
- * uploads the rank's shard plus the shared experts), and lm_moe_forward routes
- * each rank's own T tokens, sends them to the experts' ranks (all-to-all), runs
- * the local experts and returns the weighted outputs (reverse all-to-all).
+ * Expert parallelism over NCCL (NVLink within a node).  Every rank creates its
+ * context with the same config, then calls this with the same 128-byte
+ * ncclUniqueId, before uploading any weights.  Rank r then keeps routed experts
+ * [r*E/N, (r+1)*E/N) (upload_layer still takes the full arrays and uploads the
+ * rank's shard plus the shared experts), and lm_moe_forward -- called by every rank
+ * with its own T tokens, T <= max_tokens, possibly 0 -- routes them over all
+ * experts, exchanges per-expert row counts, sends the rows to the experts' ranks,
+ * runs the local experts, returns their outputs and combines them with the
+ * routing weights and the shared experts.  It waits once on the host for the
+ * counts.  NCCL is loaded at run time (libnccl.so.2).
  */
 lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t rank,
                          int32_t nranks);
+
+/*
+ * The exchange plan of one expert-parallel forward, computed on the host from
+ * row counts: this rank sends send_count[d] rows to rank d starting at row
+ * send_offset[d] of its expert-sorted send buffer, and receives recv_count[s] rows
+ * from rank s at row recv_offset[s] of its receive buffer.
+ *   send_expert_counts  [E]: this rank's rows per expert (all experts)
+ *   recv_expert_counts  [nranks, E/nranks]: rows each rank sends to this rank's experts
+ * lm_moe_forward uses exactly this plan; it is exported so callers can size
+ * buffers and so the plan can be checked across ranks without a GPU.
+ */
+#define LM_EP_MAX_RANKS 64
+typedef struct lm_ep_plan {
+    int32_t send_count[LM_EP_MAX_RANKS];
+    int32_t send_offset[LM_EP_MAX_RANKS];
+    int32_t recv_count[LM_EP_MAX_RANKS];
+    int32_t recv_offset[LM_EP_MAX_RANKS];
+    int32_t n_send;
+    int32_t n_recv;
+} lm_ep_plan;
+lm_status lm_moe_ep_plan(int32_t nranks, int32_t experts, const int32_t* send_expert_counts,
+                         const int32_t* recv_expert_counts, lm_ep_plan* plan);
+
+/* A fresh 128-byte ncclUniqueId for lm_moe_ep_init (rank 0 makes it; the caller
+ * shares it with the other ranks by any host channel). */
+lm_status lm_moe_ep_unique_id(void* nccl_unique_id_out);
 
 /*
  * Routing that allocates nothing, for callers that cannot allocate device memory:

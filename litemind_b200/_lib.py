@@ -49,6 +49,11 @@ class LmMoeConfig(C.Structure):
     ]
 
 
+class LmEpPlan(C.Structure):
+    _fields_ = [("send_count", C.c_int32 * 64), ("send_offset", C.c_int32 * 64), ("recv_count", C.c_int32 * 64),
+                ("recv_offset", C.c_int32 * 64), ("n_send", C.c_int32), ("n_recv", C.c_int32)]
+
+
 SIGNATURES = {
     "lm_moe_config_default": (None, [C.POINTER(LmMoeConfig)]),
     "lm_moe_create": (_i32, [C.POINTER(LmMoeConfig), C.c_int, C.POINTER(_vp)]),
@@ -66,6 +71,8 @@ SIGNATURES = {
     "lm_moe_expert_counts": (_i32, [_vp, _vp]),
     "lm_moe_memory": (_i32, [_vp, _u64p, _u64p]),
     "lm_moe_ep_init": (_i32, [_vp, _vp, _i32, _i32]),
+    "lm_moe_ep_unique_id": (_i32, [_vp]),
+    "lm_moe_ep_plan": (_i32, [_i32, _i32, _vp, _vp, C.POINTER(LmEpPlan)]),
     "lm_moe_profile_enable": (_i32, [_vp, _i32]),
     "lm_moe_profile_read": (_i32, [_vp, _vp, _vp, _i32]),
     "lm_moe_route_static": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp]),

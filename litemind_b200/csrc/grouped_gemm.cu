@@ -82,6 +82,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ int s_tiles[kMaxSegments + 1];
     __shared__ int s_off[kMaxSegments];
     __shared__ int s_cnt[kMaxSegments];
+    __shared__ int s_wslot[kMaxSegments];
     __shared__ int s_n_seg;
     __shared__ int s_epi_go[2];
 
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (i < kMaxSegments) {
             s_off[i] = sched->seg_off[i];
             s_cnt[i] = sched->seg_cnt[i];
+            s_wslot[i] = sched->seg_weight[i];
         }
         s_tiles[i] = (KIND == Kind::GateUp) ? sched->tiles1[i] : sched->tiles2[i];
     }
@@ -158,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int local = tile - s_tiles[s];
                 const int nb = local / mb_per;
                 const int mb = local - nb * mb_per;
-                const int a_row = s * rows_a + mb * kBlockM;
+                const int a_row = s_wslot[s] * rows_a + mb * kBlockM;
                 // Routed experts read their expert-sorted rows of x_perm (gate/up) or h
                 // (down); the shared experts read x itself, token by token.
                 const bool from_x = (KIND == Kind::GateUp) && s >= args.n_routed_local;
@@ -288,6 +290,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
                 const int d = mb * kBlockM + quad * 32 + lane;  // hidden row
                 const bool routed = s < args.n_routed_local;
+                if (routed && args.y_rows != nullptr) {
+                    // Expert parallelism: each routed row's output goes back to its
+                    // token's rank, which applies the weight; one writer per element.
+#pragma unroll 1
+                    for (int c0 = 0; c0 < BN; c0 += 16) {
+                        if (c0 >= valid) break;
+                        uint32_t r[16];
+                        tmem_ld16(t_row + c0, r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (c0 + j < valid)
+                                args.y_rows[static_cast<size_t>(row0 + c0 + j) * args.hidden + d] = __uint_as_float(r[j]);
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+                    if (++acc == 2) {
+                        acc = 0;
+                        acc_phase ^= 1u;
+                    }
+                    continue;
+                }
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     if (c0 >= valid) break;

@@ -11,6 +11,7 @@
 // shared splits of width inter (sum over the splits == the reference's one
 // shared FFN of width inter * n_shared, src/DeepSeekRunner.cpp:217-222).
 #include "moe_internal.h"
+#include "nccl_dl.h"
 
 #include <algorithm>
 #include <cstdio>
@@ -78,6 +79,19 @@ struct lm_moe_ctx {
     float* norm_f32 = nullptr;
     uint16_t* norm_bf16 = nullptr;
     cudaStream_t own_stream = nullptr;
+
+    // Expert parallelism (lm_moe_ep_init).
+    ncclComm_t comm = nullptr;
+    const lm::NcclApi* nccl = nullptr;
+    uint16_t* x_recv = nullptr;    // received token rows, (source rank, local expert) segments
+    float* y_ret = nullptr;        // expert outputs of the received rows, returned to their ranks
+    float* y_back = nullptr;       // this rank's rows' expert outputs, in send order
+    int32_t* recv_counts = nullptr;  // [nranks, local experts] rows received per source and expert
+    lm::Schedule* sched_ep = nullptr;
+    lm::Schedule* host_sched = nullptr;  // pinned
+    int32_t* host_totals = nullptr;      // pinned [E]
+    int32_t* host_recv = nullptr;        // pinned [nranks * local experts]
+    CUtensorMap map_xrecv[5]{};
 
     bool profiling = false;
     cudaEvent_t prof_events[LM_PROFILE_SLOTS + 1]{};
@@ -351,6 +365,10 @@ lm_status lm_moe_destroy(lm_moe_ctx* ctx) {
     if (ctx->norm_f32) cudaFree(ctx->norm_f32);
     if (ctx->norm_bf16) cudaFree(ctx->norm_bf16);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    if (ctx->comm != nullptr && ctx->nccl != nullptr) ctx->nccl->CommDestroy(ctx->comm);
+    if (ctx->host_sched) cudaFreeHost(ctx->host_sched);
+    if (ctx->host_totals) cudaFreeHost(ctx->host_totals);
+    if (ctx->host_recv) cudaFreeHost(ctx->host_recv);
     for (auto& e : ctx->prof_events)
         if (e) cudaEventDestroy(e);
     delete ctx;
@@ -523,7 +541,6 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
     args.tokens = T;
     args.hidden = H;
     args.inter = I;
-    args.routed_rows = ctx->routed_cap;
     args.n_routed_local = ctx->local_experts;
     LM_CUDA(ctx, launch_gemm_gate_up(bn, L.map_w13, ctx->map_xperm[bi], map_x, args, ctx->sms, s, true));
     prof_mark(ctx, 5, s);
@@ -534,6 +551,150 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
     return prof_end(ctx, slots, n_slots);
 }
 
+#define LM_NCCL(ctx, expr)                                                                       \
+    do {                                                                                         \
+        const ncclResult_t lm_r_ = (expr);                                                       \
+        if (lm_r_ != ncclSuccess)                                                                \
+            return fail(ctx, LM_ERR_COMM, std::string(#expr) + ": " + ctx->nccl->GetErrorString(lm_r_)); \
+    } while (0)
+
+// Expert-parallel forward.  Every rank runs this same sequence of collectives.
+static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, const float* x_f32, int32_t T,
+                            const float* bias, float* y, int32_t accumulate, cudaStream_t s) {
+    const lm_moe_config& c = ctx->cfg;
+    const LayerWeights& L = ctx->layers[layer];
+    const int K = c.num_experts_per_tok, E = c.n_routed_experts, H = c.hidden_size, I = c.moe_intermediate_size;
+    const int N = ctx->nranks, El = ctx->local_experts;
+    const NcclApi& nc = *ctx->nccl;
+    const RouterParams rp = router_params(c);
+    float* y_zero = accumulate ? nullptr : y;
+    prof_begin(ctx, s);
+    int slots[8];
+    int n_slots = 0;
+    // 1. Route this rank's tokens over all experts; rows sorted by expert are
+    //    sorted by destination rank, so x_perm is the send buffer.
+    if (T > 0 && T <= kRouteTile) {
+        LM_CUDA(ctx, launch_route_small(x, x_f32, L.router, bias, ctx->logits, T, H, rp, ctx->topk_idx, ctx->topk_w,
+                                        ctx->expert_totals, ctx->sched, ctx->row_token, ctx->row_weight,
+                                        ctx->slot_row, y_zero, ctx->ticket, 0, 0, E, 0, 16, 1, 1, s, false));
+    } else if (T > 0) {
+        LM_CUDA(ctx, launch_router_logits(x, x_f32, L.router, L.router_t, bias, ctx->logits, T, H, E, s, false));
+        LM_CUDA(ctx, launch_router_topk(ctx->logits, T, rp, ctx->topk_idx, ctx->topk_w, ctx->tile_counts, s, true));
+        LM_CUDA(ctx, launch_dispatch_scan(ctx->tile_counts, ctx->tile_base, ctx->expert_totals, ctx->sched, T, K, E,
+                                          0, 0, E, 0, 16, 1, 1, s, true));
+        LM_CUDA(ctx, launch_place(ctx->topk_idx, ctx->topk_w, ctx->tile_base, T, H, K, E, 0, E, ctx->row_token,
+                                  ctx->row_weight, ctx->slot_row, y_zero, s, true));
+    } else {
+        LM_CUDA(ctx, cudaMemsetAsync(ctx->expert_totals, 0, E * sizeof(int32_t), s));
+    }
+    LM_CUDA(ctx, launch_gather_rows(x, ctx->row_token, T * K, H, ctx->x_perm, s, true));
+    prof_mark(ctx, 1, s);
+    slots[n_slots++] = 1;
+    // 2. Rows per (destination, expert) to every rank; one host sync to plan.
+    LM_NCCL(ctx, nc.GroupStart());
+    for (int d = 0; d < N; ++d) {
+        LM_NCCL(ctx, nc.Send(ctx->expert_totals + d * El, El, ncclInt32, d, ctx->comm, s));
+        LM_NCCL(ctx, nc.Recv(ctx->recv_counts + d * El, El, ncclInt32, d, ctx->comm, s));
+    }
+    LM_NCCL(ctx, nc.GroupEnd());
+    LM_CUDA(ctx, cudaMemcpyAsync(ctx->host_totals, ctx->expert_totals, E * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    LM_CUDA(ctx, cudaMemcpyAsync(ctx->host_recv, ctx->recv_counts, N * El * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    LM_CUDA(ctx, cudaStreamSynchronize(s));
+    lm_ep_plan plan;
+    if (lm_moe_ep_plan(N, E, ctx->host_totals, ctx->host_recv, &plan) != LM_OK)
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "invalid expert-parallel plan");
+    const int32_t* send_cnt = plan.send_count;
+    const int32_t* send_off = plan.send_offset;
+    const int32_t* recv_cnt = plan.recv_count;
+    const int32_t* recv_off = plan.recv_offset;
+    const int n_recv = plan.n_recv;
+    // Receiver schedule: segment (source r, local expert e), then the shared splits.
+    const int n_routed = N * El;
+    const int bn = choose_bn(n_recv, 1, n_routed);  // from the mean rows per received segment
+    const int bi = bn_index(bn);
+    Schedule& hs = *ctx->host_sched;
+    int p1 = 0, p2 = 0, seg = 0;
+    const int mb1 = 2 * I / 128, mb2 = H / 128;
+    auto add_segment = [&](int off, int cnt, int wslot) {
+        hs.seg_off[seg] = off;
+        hs.seg_cnt[seg] = cnt;
+        hs.seg_weight[seg] = wslot;
+        hs.tiles1[seg] = p1;
+        hs.tiles2[seg] = p2;
+        const int nb = (cnt + bn - 1) / bn;
+        p1 += nb * mb1;
+        p2 += nb * mb2;
+        ++seg;
+    };
+    for (int r = 0; r < N; ++r) {
+        int off = recv_off[r];
+        for (int e = 0; e < El; ++e) {
+            add_segment(off, ctx->host_recv[r * El + e], e);
+            off += ctx->host_recv[r * El + e];
+        }
+    }
+    for (int j = 0; j < c.n_shared_experts; ++j) add_segment(ctx->routed_cap + j * T, T, El + j);
+    hs.tiles1[seg] = p1;
+    hs.tiles2[seg] = p2;
+    hs.n_seg = seg;
+    hs.first_expert = ctx->first_expert;
+    LM_CUDA(ctx, cudaMemcpyAsync(ctx->sched_ep, &hs, sizeof(Schedule), cudaMemcpyHostToDevice, s));
+    // 3. Dispatch token rows.
+    LM_NCCL(ctx, nc.GroupStart());
+    for (int d = 0; d < N; ++d) {
+        if (send_cnt[d] > 0)
+            LM_NCCL(ctx, nc.Send(ctx->x_perm + static_cast<size_t>(send_off[d]) * H, static_cast<size_t>(send_cnt[d]) * H,
+                                 ncclBfloat16, d, ctx->comm, s));
+        if (recv_cnt[d] > 0)
+            LM_NCCL(ctx, nc.Recv(ctx->x_recv + static_cast<size_t>(recv_off[d]) * H, static_cast<size_t>(recv_cnt[d]) * H,
+                                 ncclBfloat16, d, ctx->comm, s));
+    }
+    LM_NCCL(ctx, nc.GroupEnd());
+    prof_mark(ctx, 7, s);
+    slots[n_slots++] = 7;
+    // 4. Local experts on the received rows, shared experts on this rank's tokens.
+    CUtensorMap map_x{};
+    std::string err;
+    // A rank without tokens still serves its experts; its (unread) token map points
+    // at a workspace buffer.
+    if (!encode_tensor_map_bf16(&map_x, T > 0 ? x : ctx->x_perm, std::max(T, 1), H, bn, 64, err))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+    GemmArgs args{};
+    args.sched = ctx->sched_ep;
+    args.x = x;
+    args.h = ctx->h;
+    args.y = y;
+    args.y_rows = ctx->y_ret;
+    args.row_token = ctx->row_token;
+    args.row_weight = ctx->row_weight;
+    args.status = ctx->status;
+    args.tokens = T;
+    args.hidden = H;
+    args.inter = I;
+    args.n_routed_local = n_routed;
+    LM_CUDA(ctx, launch_gemm_gate_up(bn, L.map_w13, ctx->map_xrecv[bi], map_x, args, ctx->sms, s, false));
+    prof_mark(ctx, 5, s);
+    slots[n_slots++] = 5;
+    LM_CUDA(ctx, launch_gemm_down(bn, L.map_w2, ctx->map_h[bi], args, ctx->sms, s, true));
+    prof_mark(ctx, 6, s);
+    slots[n_slots++] = 6;
+    // 5. Outputs back to the tokens' ranks, then the weighted combine.
+    LM_NCCL(ctx, nc.GroupStart());
+    for (int d = 0; d < N; ++d) {
+        if (recv_cnt[d] > 0)
+            LM_NCCL(ctx, nc.Send(ctx->y_ret + static_cast<size_t>(recv_off[d]) * H, static_cast<size_t>(recv_cnt[d]) * H,
+                                 ncclFloat32, d, ctx->comm, s));
+        if (send_cnt[d] > 0)
+            LM_NCCL(ctx, nc.Recv(ctx->y_back + static_cast<size_t>(send_off[d]) * H, static_cast<size_t>(send_cnt[d]) * H,
+                                 ncclFloat32, d, ctx->comm, s));
+    }
+    LM_NCCL(ctx, nc.GroupEnd());
+    LM_CUDA(ctx, launch_ep_combine(y, ctx->y_back, ctx->slot_row, ctx->topk_w, T, K, H, s, false));
+    prof_mark(ctx, 4, s);
+    slots[n_slots++] = 4;
+    return prof_end(ctx, slots, n_slots);
+}
+
 lm_status lm_moe_forward(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int32_t tokens, const float* logit_bias,
                          float* y, int32_t accumulate, void* stream) {
     if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
@@ -541,10 +702,12 @@ lm_status lm_moe_forward(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int3
     if ((st = check_layer(ctx, layer)) != LM_OK) return st;
     if (tokens < 0) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "negative token count");
     if (tokens > ctx->cfg.max_tokens) return fail(ctx, LM_ERR_TOO_MANY_TOKENS, "tokens exceed max_tokens");
-    if (tokens == 0) return LM_OK;
-    if (x == nullptr || y == nullptr || !aligned16(x) || !aligned16(y))
+    if (tokens == 0 && ctx->nranks == 1) return LM_OK;  // with experts on several ranks, this one still serves
+    if (tokens > 0 && (x == nullptr || y == nullptr || !aligned16(x) || !aligned16(y)))
         return fail(ctx, LM_ERR_INVALID_ARGUMENT, "x and y must be 16-byte aligned device pointers");
     if ((st = set_device(ctx)) != LM_OK) return st;
+    if (ctx->nranks > 1)
+        return forward_ep(ctx, layer, x, nullptr, tokens, logit_bias, y, accumulate, static_cast<cudaStream_t>(stream));
     return forward_impl(ctx, layer, x, nullptr, tokens, logit_bias, y, accumulate, static_cast<cudaStream_t>(stream));
 }
 
@@ -575,7 +738,9 @@ lm_status lm_moe_forward_host(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x_
                                      cudaMemcpyHostToDevice, s));
         bias = ctx->bias_stage;
     }
-    if ((st = forward_impl(ctx, layer, ctx->x_stage, nullptr, tokens, bias, ctx->y_stage, 0, s)) != LM_OK) return st;
+    st = ctx->nranks > 1 ? forward_ep(ctx, layer, ctx->x_stage, nullptr, tokens, bias, ctx->y_stage, 0, s)
+                         : forward_impl(ctx, layer, ctx->x_stage, nullptr, tokens, bias, ctx->y_stage, 0, s);
+    if (st != LM_OK) return st;
     LM_CUDA(ctx, cudaMemcpyAsync(y_host, ctx->y_stage, n * sizeof(float), cudaMemcpyDeviceToHost, s));
     return lm_moe_sync(ctx, s);
 }
@@ -602,6 +767,7 @@ lm_status lm_moe_block_forward(lm_moe_ctx* ctx, int32_t layer, float* hidden, in
                                       c.hidden_size, c.rms_norm_eps, s));
     // The residual add (:290) is folded into the down-projection epilogue: it
     // accumulates straight into `hidden`.
+    if (ctx->nranks > 1) return forward_ep(ctx, layer, ctx->norm_bf16, ctx->norm_f32, tokens, nullptr, hidden, 1, s);
     return forward_impl(ctx, layer, ctx->norm_bf16, ctx->norm_f32, tokens, nullptr, hidden, 1, s);
 }
 
@@ -661,12 +827,93 @@ lm_status lm_moe_profile_read(lm_moe_ctx* ctx, double* total_ms, int64_t* launch
     return LM_OK;
 }
 
+lm_status lm_moe_ep_plan(int32_t nranks, int32_t experts, const int32_t* send_expert_counts,
+                         const int32_t* recv_expert_counts, lm_ep_plan* plan) {
+    if (plan == nullptr || send_expert_counts == nullptr || recv_expert_counts == nullptr || nranks < 1 ||
+        nranks > LM_EP_MAX_RANKS || experts < 1 || experts % nranks != 0)
+        return LM_ERR_INVALID_ARGUMENT;
+    std::memset(plan, 0, sizeof(*plan));
+    const int El = experts / nranks;
+    for (int d = 0; d < nranks; ++d) {
+        plan->send_offset[d] = plan->n_send;
+        plan->recv_offset[d] = plan->n_recv;
+        for (int e = 0; e < El; ++e) {
+            const int32_t sc = send_expert_counts[d * El + e];
+            const int32_t rc = recv_expert_counts[d * El + e];
+            if (sc < 0 || rc < 0) return LM_ERR_INVALID_ARGUMENT;
+            plan->send_count[d] += sc;
+            plan->recv_count[d] += rc;
+        }
+        plan->n_send += plan->send_count[d];
+        plan->n_recv += plan->recv_count[d];
+    }
+    return LM_OK;
+}
+
+lm_status lm_moe_ep_unique_id(void* out) {
+    if (out == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    std::string err;
+    const NcclApi* nc = nccl_api(err);
+    if (nc == nullptr) return LM_ERR_COMM;
+    ncclUniqueId id;
+    if (nc->GetUniqueId(&id) != ncclSuccess) return LM_ERR_COMM;
+    std::memcpy(out, &id, sizeof(id));
+    return LM_OK;
+}
+
 lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t rank, int32_t nranks) {
-    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
-    (void)nccl_unique_id;
-    (void)rank;
-    (void)nranks;
-    return fail(ctx, LM_ERR_UNSUPPORTED, "expert parallelism is not built yet");
+    if (ctx == nullptr || nccl_unique_id == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    const lm_moe_config& c = ctx->cfg;
+    if (nranks < 1 || rank < 0 || rank >= nranks || c.n_routed_experts % nranks != 0)
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "need 0 <= rank < nranks and nranks dividing n_routed_experts");
+    if (ctx->comm != nullptr) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "expert parallelism is already initialised");
+    for (const LayerWeights& L : ctx->layers)
+        if (L.w13 != nullptr) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "call lm_moe_ep_init before uploading weights");
+    lm_status st;
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    std::string err;
+    ctx->nccl = nccl_api(err);
+    if (ctx->nccl == nullptr) return fail(ctx, LM_ERR_COMM, err);
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_unique_id, sizeof(id));
+    const ncclResult_t r = ctx->nccl->CommInitRank(&ctx->comm, nranks, id, rank);
+    if (r != ncclSuccess) {
+        ctx->comm = nullptr;
+        return fail(ctx, LM_ERR_COMM, std::string("ncclCommInitRank: ") + ctx->nccl->GetErrorString(r));
+    }
+    const int El = c.n_routed_experts / nranks;
+    ctx->rank = rank;
+    ctx->nranks = nranks;
+    ctx->first_expert = rank * El;
+    ctx->local_experts = El;
+    ctx->n_seg = El + c.n_shared_experts;
+    // Receive capacity for the worst case (every rank's every slot on this rank),
+    // so no rank can overflow mid-exchange and leave its peers waiting.
+    const size_t T = c.max_tokens, K = c.num_experts_per_tok, H = c.hidden_size, I = c.moe_intermediate_size;
+    const size_t cap = static_cast<size_t>(nranks) * T * K;
+    ctx->routed_cap = static_cast<int>(cap);
+    const size_t h_rows = cap + c.n_shared_experts * T;
+    // Replace the single-GPU h with one sized for the received rows.
+    for (auto it = ctx->allocations.begin(); it != ctx->allocations.end(); ++it)
+        if (*it == ctx->h) {
+            cudaFree(*it);
+            ctx->allocations.erase(it);
+            break;
+        }
+    if ((st = alloc(ctx, &ctx->h, h_rows * I)) || (st = alloc(ctx, &ctx->x_recv, cap * H)) ||
+        (st = alloc(ctx, &ctx->y_ret, cap * H)) || (st = alloc(ctx, &ctx->y_back, T * K * H)) ||
+        (st = alloc(ctx, &ctx->recv_counts, static_cast<size_t>(nranks) * El)) || (st = alloc(ctx, &ctx->sched_ep, 1)))
+        return st;
+    LM_CUDA(ctx, cudaMallocHost(&ctx->host_sched, sizeof(Schedule)));
+    LM_CUDA(ctx, cudaMallocHost(&ctx->host_totals, c.n_routed_experts * sizeof(int32_t)));
+    LM_CUDA(ctx, cudaMallocHost(&ctx->host_recv, static_cast<size_t>(nranks) * El * sizeof(int32_t)));
+    std::memset(ctx->host_sched, 0, sizeof(Schedule));
+    for (int i = 0; i < 5; ++i) {
+        if (!encode_tensor_map_bf16(&ctx->map_xrecv[i], ctx->x_recv, cap, H, kBnChoices[i], 64, err) ||
+            !encode_tensor_map_bf16(&ctx->map_h[i], ctx->h, h_rows, I, kBnChoices[i], 64, err))
+            return fail(ctx, LM_ERR_CUDA, err);
+    }
+    return LM_OK;
 }
 
 }  // extern "C"

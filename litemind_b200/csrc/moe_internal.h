@@ -18,14 +18,17 @@ constexpr int kMaxSegments = kMaxExperts + kMaxShared;
 constexpr int kMaxTopK = 16;
 constexpr int kRouteTile = 32;            // tokens per routing tile (one warp per token)
 
-// Per-call schedule written on the device by the scan kernel and read by the
-// grouped GEMMs.  Segment s < E is routed expert s; s >= E is shared split s-E.
+// Per-call schedule read by the grouped GEMMs: written on the device by the
+// routing kernels (one GPU: segment s is local expert s, then the shared splits),
+// or on the host from the exchanged counts (expert parallelism: one segment per
+// (source rank, local expert), then the shared splits).
 struct Schedule {
     int32_t seg_off[kMaxSegments];     // first row of the segment in h (expert-sorted rows)
     int32_t seg_cnt[kMaxSegments];     // rows in the segment
     int32_t tiles1[kMaxSegments + 1];  // exclusive prefix of gate/up tiles
     int32_t tiles2[kMaxSegments + 1];  // exclusive prefix of down tiles
-    int32_t n_seg;                     // segments with weights on this device
+    int32_t seg_weight[kMaxSegments];  // weight slot (local expert, then shared split) of each segment
+    int32_t n_seg;                     // segments in this schedule
     int32_t first_expert;              // expert-parallel shard start (0 on one GPU)
 };
 
@@ -52,6 +55,8 @@ cudaError_t launch_dispatch_scan(const int32_t* tile_counts, int32_t* tile_base,
 cudaError_t launch_place(const int32_t* topk_idx, const float* topk_w, const int32_t* tile_base, int tokens,
                          int hidden, int top_k, int experts, int first_expert, int local_experts, int32_t* row_token,
                          float* row_weight, int32_t* slot_row, float* y_zero, cudaStream_t stream, bool pdl);
+cudaError_t launch_ep_combine(float* y, const float* back, const int32_t* slot_row, const float* topk_w, int tokens,
+                              int top_k, int hidden, cudaStream_t stream, bool pdl);
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* row_token, int rows, int hidden, uint16_t* x_perm,
                                cudaStream_t stream, bool pdl);
 cudaError_t launch_route_small(const uint16_t* x, const float* x_f32, const float* w, const float* bias,
@@ -73,7 +78,7 @@ struct GemmArgs {
     int32_t tokens;
     int32_t hidden;
     int32_t inter;
-    int32_t routed_rows;       // rows of routed segments (shared segments use tokens directly)
+    float* y_rows;             // when set, routed rows' down outputs are stored here by row, unweighted
     int32_t n_routed_local;    // segments [0, n_routed_local) are routed experts
 };
 cudaError_t launch_gemm_gate_up(int bn, const CUtensorMap& w13, const CUtensorMap& xperm, const CUtensorMap& x,

@@ -1,0 +1,48 @@
+// nccl_dl.cpp -- dlopen/dlsym of the NCCL entry points used by expert parallelism.
+#include "nccl_dl.h"
+
+#include <dlfcn.h>
+
+#include <mutex>
+
+namespace lm {
+
+const NcclApi* nccl_api(std::string& error) {
+    static NcclApi api;
+    static std::string load_error;
+    static bool ok = false;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        // Prefer a copy already in the process, then the usual soname.
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+        if (h == nullptr) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (h == nullptr) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (h == nullptr) {
+            load_error = std::string("cannot load libnccl.so.2: ") + dlerror();
+            return;
+        }
+        auto sym = [&](const char* name) -> void* {
+            void* p = dlsym(h, name);
+            if (p == nullptr && load_error.empty()) load_error = std::string("libnccl lacks ") + name;
+            return p;
+        };
+        api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(sym("ncclGetUniqueId"));
+        api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(sym("ncclCommInitRank"));
+        api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(sym("ncclCommDestroy"));
+        api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(sym("ncclCommAbort"));
+        api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(sym("ncclGroupStart"));
+        api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(sym("ncclGroupEnd"));
+        api.Send = reinterpret_cast<decltype(api.Send)>(sym("ncclSend"));
+        api.Recv = reinterpret_cast<decltype(api.Recv)>(sym("ncclRecv"));
+        api.CommGetAsyncError = reinterpret_cast<decltype(api.CommGetAsyncError)>(sym("ncclCommGetAsyncError"));
+        api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(sym("ncclGetErrorString"));
+        ok = load_error.empty();
+    });
+    if (!ok) {
+        error = load_error;
+        return nullptr;
+    }
+    return &api;
+}
+
+}  // namespace lm

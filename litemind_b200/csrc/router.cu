@@ -294,6 +294,7 @@ __device__ void build_schedule(Schedule* sched, const int* totals, int T, int n_
         }
         sched->seg_off[s] = seg_off;
         sched->seg_cnt[s] = cnt;
+        sched->seg_weight[s] = s;
         sched->tiles1[s] = p1;
         sched->tiles2[s] = p2;
         const int nb = (cnt + bn - 1) / bn;
@@ -468,6 +469,33 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
             if (j < total) dst[j] = v[u];
         }
     }
+}
+
+// Expert-parallel combine: y[t] += sum over slots s (in selection order) of
+// w[t, s] * back[slot_row[t, s]], where `back` holds the expert outputs returned
+// by the experts' ranks in this rank's send order.  y already holds the shared
+// experts' output.  One thread per 4 consecutive hidden elements of a token.
+__global__ void __launch_bounds__(256) ep_combine_kernel(float* __restrict__ y, const float* __restrict__ back,
+                                                         const int32_t* __restrict__ slot_row,
+                                                         const float* __restrict__ topk_w, int T, int K, int H) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int per_token = H / 4;
+    if (i >= static_cast<int64_t>(T) * per_token) return;
+    const int t = static_cast<int>(i / per_token);
+    const int c = static_cast<int>(i - static_cast<int64_t>(t) * per_token);
+    float4 acc = reinterpret_cast<float4*>(y + static_cast<size_t>(t) * H)[c];
+    for (int s = 0; s < K; ++s) {
+        const int row = slot_row[t * K + s];
+        const float w = topk_w[t * K + s];
+        const float4 v = reinterpret_cast<const float4*>(back + static_cast<size_t>(row) * H)[c];
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+    }
+    reinterpret_cast<float4*>(y + static_cast<size_t>(t) * H)[c] = acc;
 }
 
 // Small T (<= kRouteTile): the whole routing stage in one launch.  CTA b computes
@@ -662,6 +690,14 @@ cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* row_token, int 
     const int64_t vecs = static_cast<int64_t>(rows) * (hidden / 8);
     const int blocks = static_cast<int>(std::min<int64_t>(2048, (vecs + 1023) / 1024));
     return launch_k(gather_rows_kernel, dim3(blocks), dim3(256), stream, pdl, x, row_token, rows, hidden, x_perm);
+}
+
+cudaError_t launch_ep_combine(float* y, const float* back, const int32_t* slot_row, const float* topk_w, int tokens,
+                              int top_k, int hidden, cudaStream_t stream, bool pdl) {
+    if (tokens <= 0) return cudaSuccess;
+    const int64_t threads = static_cast<int64_t>(tokens) * (hidden / 4);
+    return launch_k(ep_combine_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), stream, pdl, y,
+                    back, slot_row, topk_w, tokens, top_k, hidden);
 }
 
 cudaError_t launch_route_small(const uint16_t* x, const float* x_f32, const float* w, const float* bias,

@@ -70,6 +70,17 @@ class ExpertSelection:
     weight: float
 
 
+def ep_plan(nranks: int, send_expert_counts, recv_expert_counts) -> dict:
+    """lm_moe_ep_plan: send/recv row counts and offsets of one expert-parallel forward."""
+    s = np.ascontiguousarray(send_expert_counts, np.int32)
+    r = np.ascontiguousarray(recv_expert_counts, np.int32)
+    plan = _lib.LmEpPlan()
+    check(load().lm_moe_ep_plan(nranks, s.size, C.c_void_p(s.ctypes.data), C.c_void_p(r.ctypes.data), C.byref(plan)))
+    return {"send_count": list(plan.send_count[:nranks]), "send_offset": list(plan.send_offset[:nranks]),
+            "recv_count": list(plan.recv_count[:nranks]), "recv_offset": list(plan.recv_offset[:nranks]),
+            "n_send": plan.n_send, "n_recv": plan.n_recv}
+
+
 def _ptr(t) -> C.c_void_p | None:
     if t is None:
         return None
@@ -130,6 +141,18 @@ class MoeLayer:
         g, u, d = (np.ascontiguousarray(a) for a in (gate, up, down))
         self._check(self.lib.lm_moe_upload_expert(self.ctx, layer, expert, _ptr(g), _ptr(u), _ptr(d)))
 
+    # --- expert parallelism --------------------------------------------------
+    @staticmethod
+    def ep_unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        check(load().lm_moe_ep_unique_id(buf))
+        return buf.raw
+
+    def ep_init(self, unique_id: bytes, rank: int, nranks: int) -> None:
+        """Joins the expert-parallel group; call before uploading weights."""
+        buf = C.create_string_buffer(bytes(unique_id), 128)
+        self._check(self.lib.lm_moe_ep_init(self.ctx, buf, rank, nranks))
+
     def memory(self) -> tuple[int, int]:
         r, u = C.c_uint64(), C.c_uint64()
         self._check(self.lib.lm_moe_memory(self.ctx, C.byref(r), C.byref(u)))
@@ -141,7 +164,9 @@ class MoeLayer:
         T = x.shape[0]
         if y is None:
             y = torch.empty((T, self.config.hidden_size), dtype=torch.float32, device=x.device)
-        self._check(self.lib.lm_moe_forward(self.ctx, layer, _ptr(x), T, _ptr(bias), _ptr(y), int(accumulate),
+        xp = _ptr(x) if T > 0 else None
+        yp = _ptr(y) if T > 0 else None
+        self._check(self.lib.lm_moe_forward(self.ctx, layer, xp, T, _ptr(bias), yp, int(accumulate),
                                             _stream_ptr(stream)))
         return y
 

@@ -1,0 +1,73 @@
+"""Expert parallelism on two B200s: each rank holds half of the routed experts,
+runs lm_moe_forward on its own tokens over NCCL, and its outputs must match the
+oracle's single-process MoE block for those tokens.  Needs 2 GPUs (gpurun --gpus 2);
+gloo carries only the NCCL unique id.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+import torch.distributed as dist  # noqa: E402
+import torch.multiprocessing as mp  # noqa: E402
+
+from litemind_b200 import synthetic as syn  # noqa: E402
+
+SMALL = syn.MoeShape(hidden=256, inter=128, n_routed_experts=8, n_shared_experts=1, top_k=2)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, shape_name, token_counts):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        from litemind_b200.moe import MoeConfig, MoeLayer, bf16_tensor
+        from oracle.oracle import Oracle, RouterConfig
+        from tests.parity import assert_layer_parity
+
+        torch.cuda.set_device(rank)
+        shape = SMALL if shape_name == "small" else syn.V2_LITE
+        W = syn.layer_weights(shape, seed=5, std=0.1 if shape_name == "small" else 0.02)
+        uid = [MoeLayer.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        layer = MoeLayer(MoeConfig.from_shape(shape, max_tokens=max(token_counts)), device=rank)
+        layer.ep_init(uid[0], rank, world)
+        layer.upload_layer(0, W)
+        T = token_counts[rank]
+        xb = syn.tokens(shape, max(T, 1), seed=100 + rank)[:T]
+        x = bf16_tensor(xb) if T > 0 else torch.zeros((0, shape.hidden), dtype=torch.bfloat16, device="cuda")
+        for _ in range(2):  # two calls in a row reuse every exchange buffer
+            y = layer.forward(0, x)
+            layer.sync()
+        if T > 0:
+            idx, w, _ = layer.route(0, x)
+            layer.sync()
+            ref = Oracle().moe_layer(syn.bf16_to_f32(xb).reshape(T, -1), W,
+                                     RouterConfig(shape.n_routed_experts, shape.top_k), shape.n_shared_experts)
+            stats = assert_layer_parity(y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), *ref,
+                                        what=f"EP rank {rank} T={T}")
+            print(f"rank {rank}: {stats}")
+        dist.barrier()
+        layer.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("shape_name,token_counts", [("small", (37, 11)), ("small", (0, 20)),
+                                                     ("small", (300, 300)), ("v2lite", (32, 64))])
+def test_expert_parallel_two_gpus(shape_name, token_counts):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.spawn(_worker, args=(2, _free_port(), shape_name, token_counts), nprocs=2, join=True)
