@@ -160,7 +160,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int local = tile - s_tiles[s];
                 const int nb = local / mb_per;
                 const int mb = local - nb * mb_per;
-                const int a_row = s_wslot[s] * rows_a + mb * kBlockM;
+                // Weights are tile-major: tile (segment slot, row block, k block) is 128
+                // consecutive rows of a [*, 64] matrix.
+                const int a_tile0 = (s_wslot[s] * mb_per + mb) * num_kb;
                 // Routed experts read their expert-sorted rows of x_perm (gate/up) or h
                 // (down); the shared experts read x itself, token by token.
                 const bool from_x = (KIND == Kind::GateUp) && s >= args.n_routed_local;
@@ -172,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&full[stage], kATileBytes + C::kBTileBytes);
-                    tma_load_2d(smem_a + stage * kATileBytes, &map_a, &full[stage], kb * kBlockK, a_row);
+                    tma_load_2d(smem_a + stage * kATileBytes, &map_a, &full[stage], 0, (a_tile0 + kb) * kBlockM);
                     tma_load_2d(smem_b + stage * C::kBTileBytes, bmap, &full[stage], kb * kBlockK, b_row);
                     issued_mask |= 1u << stage;
                     issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);

@@ -4,9 +4,13 @@
 // Residency replaces the reference's ExpertCache paging (src/ExpertCache.cpp:9-47):
 // every expert of every resident layer lives in HBM in the layout the grouped GEMMs
 // read, so a forward call never moves weights.  Per layer:
-//   w13   [segments, 2*inter, hidden] bf16  gate and up rows interleaved in pairs
-//   w2    [segments, hidden, inter]   bf16  down (the shared FFN split by columns)
+//   w13   gate and up rows interleaved in pairs: logically [segments, 2*inter, hidden]
+//   w2    down (the shared FFN split by columns): logically [segments, hidden, inter]
 //   router [E, hidden] f32 and its transpose [hidden, E]
+// Both weight matrices are stored tile-major: every 128-row x 64-column tile the
+// GEMM loads is one contiguous 16 KiB block, tiles ordered (segment, row block,
+// column block), so each TMA load reads whole DRAM pages instead of 128-byte pieces
+// of 128 rows.
 // where segments = the routed experts held on this device + n_shared_experts
 // shared splits of width inter (sum over the splits == the reference's one
 // shared FFN of width inter * n_shared, src/DeepSeekRunner.cpp:217-222).
@@ -191,23 +195,42 @@ lm_status ensure_layer_buffers(lm_moe_ctx* ctx, int32_t layer) {
     if ((st = alloc(ctx, &L.norm, H)) != LM_OK) return st;
     ctx->resident_bytes += segs * 3 * I * H * 2 + 2 * E * H * 4 + H * 4;
     std::string err;
-    if (!encode_tensor_map_bf16(&L.map_w13, L.w13, segs * 2 * I, H, 128, 64, err) ||
-        !encode_tensor_map_bf16(&L.map_w2, L.w2, segs * H, I, 128, 64, err))
+    // Tile-major storage: a [rows, 64] matrix of 128-row tiles.
+    if (!encode_tensor_map_bf16(&L.map_w13, L.w13, segs * 2 * I * H / 64, 64, 128, 64, err) ||
+        !encode_tensor_map_bf16(&L.map_w2, L.w2, segs * H * I / 64, 64, 128, 64, err))
         return fail(ctx, LM_ERR_CUDA, err);
     L.expert_loaded.assign(ctx->local_experts, 0);
     return LM_OK;
 }
 
+// Copies a logical row-major [rows, cols] matrix into tile-major order: 128 x 64
+// tiles, tile (rb, cb) at ((rb * (cols / 64)) + cb) * 8192 elements.  `row(r)`
+// returns the source row r.
+template <typename RowFn>
+void tile_major(uint16_t* dst, size_t rows, size_t cols, RowFn row) {
+    const size_t cb_n = cols / 64;
+    for (size_t r = 0; r < rows; ++r) {
+        const uint16_t* src = row(r);
+        const size_t rb = r / 128, rr = r % 128;
+        for (size_t cb = 0; cb < cb_n; ++cb)
+            std::memcpy(dst + ((rb * cb_n + cb) * 128 + rr) * 64, src + cb * 64, 64 * sizeof(uint16_t));
+    }
+}
+
 // One SwiGLU block into segment `seg`: gate rows to the even rows of w13, up rows
-// to the odd rows, down [hidden, inter] with source row pitch `down_pitch` elements.
+// to the odd rows, down [hidden, inter] with source row pitch `down_pitch` elements;
+// both stored tile-major.
 lm_status upload_segment(lm_moe_ctx* ctx, LayerWeights& L, int seg, const uint16_t* gate, const uint16_t* up,
                          const uint16_t* down, size_t down_pitch) {
     const size_t H = ctx->cfg.hidden_size, I = ctx->cfg.moe_intermediate_size;
-    uint16_t* w13 = L.w13 + static_cast<size_t>(seg) * 2 * I * H;
-    LM_CUDA(ctx, cudaMemcpy2D(w13, 2 * H * 2, gate, H * 2, H * 2, I, cudaMemcpyHostToDevice));
-    LM_CUDA(ctx, cudaMemcpy2D(w13 + H, 2 * H * 2, up, H * 2, H * 2, I, cudaMemcpyHostToDevice));
-    LM_CUDA(ctx, cudaMemcpy2D(L.w2 + static_cast<size_t>(seg) * H * I, I * 2, down, down_pitch * 2, I * 2, H,
-                              cudaMemcpyHostToDevice));
+    static thread_local std::vector<uint16_t> staging;
+    staging.resize(2 * I * H);
+    tile_major(staging.data(), 2 * I, H, [&](size_t r) { return ((r & 1) ? up : gate) + (r >> 1) * H; });
+    LM_CUDA(ctx, cudaMemcpy(L.w13 + static_cast<size_t>(seg) * 2 * I * H, staging.data(), 2 * I * H * 2,
+                            cudaMemcpyHostToDevice));
+    tile_major(staging.data(), H, I, [&](size_t r) { return down + r * down_pitch; });
+    LM_CUDA(ctx, cudaMemcpy(L.w2 + static_cast<size_t>(seg) * H * I, staging.data(), H * I * 2,
+                            cudaMemcpyHostToDevice));
     ctx->uploaded_bytes += 3 * I * H * 2;
     return LM_OK;
 }

@@ -174,14 +174,15 @@ struct Selection {
     float w;
 };
 
+template <int EPL>  // experts per lane: ceil(E / 32) rounded up to 1, 2, 4 or 8
 __device__ __forceinline__ Selection route_one_token(const float* lg, const RouterParams& rp, float* probs,
                                                      int lane) {
     const int E = rp.experts;
     const int K = rp.top_k;
-    float p[kMaxExperts / 32];
+    float p[EPL];
     float m = -FLT_MAX;
 #pragma unroll
-    for (int j = 0; j < kMaxExperts / 32; ++j) {
+    for (int j = 0; j < EPL; ++j) {
         const int e = lane + 32 * j;
         p[j] = (e < E) ? __ldcg(lg + e) : -FLT_MAX;
         m = fmaxf(m, p[j]);
@@ -190,7 +191,7 @@ __device__ __forceinline__ Selection route_one_token(const float* lg, const Rout
     for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
     float sum = 0.0f;
 #pragma unroll
-    for (int j = 0; j < kMaxExperts / 32; ++j) {
+    for (int j = 0; j < EPL; ++j) {
         const int e = lane + 32 * j;
         p[j] = (e < E) ? expf(p[j] - m) : 0.0f;
         sum += p[j];
@@ -199,14 +200,14 @@ __device__ __forceinline__ Selection route_one_token(const float* lg, const Rout
     for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(kFull, sum, off);
     const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
 #pragma unroll
-    for (int j = 0; j < kMaxExperts / 32; ++j) p[j] *= inv;
+    for (int j = 0; j < EPL; ++j) p[j] *= inv;
 
     uint32_t group_mask = 0xffffffffu;
     int per_group = E;
     if (rp.group_limited && rp.n_group > 1) {
         per_group = E / rp.n_group;
 #pragma unroll
-        for (int j = 0; j < kMaxExperts / 32; ++j) {
+        for (int j = 0; j < EPL; ++j) {
             const int e = lane + 32 * j;
             if (e < E) probs[e] = p[j];
         }
@@ -232,10 +233,10 @@ __device__ __forceinline__ Selection route_one_token(const float* lg, const Rout
         }
     }
 
-    uint32_t key[kMaxExperts / 32];
+    uint32_t key[EPL];
     uint32_t avail = 0;
 #pragma unroll
-    for (int j = 0; j < kMaxExperts / 32; ++j) {
+    for (int j = 0; j < EPL; ++j) {
         const int e = lane + 32 * j;
         key[j] = 0;
         if (e < E) {
@@ -249,7 +250,7 @@ __device__ __forceinline__ Selection route_one_token(const float* lg, const Rout
         uint32_t best = 0;
         int bj = -1;
 #pragma unroll
-        for (int j = 0; j < kMaxExperts / 32; ++j) {
+        for (int j = 0; j < EPL; ++j) {
             if (((avail >> j) & 1u) && (bj < 0 || key[j] > best)) {
                 best = key[j];
                 bj = j;
@@ -309,6 +310,7 @@ __device__ void build_schedule(Schedule* sched, const int* totals, int T, int n_
 
 constexpr int kTopkThreads = 32 * kRouteTile;  // one warp per token of a routing tile
 
+template <int EPL>
 __global__ void __launch_bounds__(kTopkThreads) router_topk_kernel(const float* __restrict__ logits, int T,
                                                                    RouterParams rp, int32_t* __restrict__ topk_idx,
                                                                    float* __restrict__ topk_w,
@@ -326,7 +328,7 @@ __global__ void __launch_bounds__(kTopkThreads) router_topk_kernel(const float* 
     pdl_launch_dependents();
     const int t = blockIdx.x * kRouteTile + warp;
     if (t < T) {
-        const Selection sel = route_one_token(logits + static_cast<size_t>(t) * E, rp, probs[warp], lane);
+        const Selection sel = route_one_token<EPL>(logits + static_cast<size_t>(t) * E, rp, probs[warp], lane);
         if (lane < K) {
             topk_idx[static_cast<size_t>(t) * K + lane] = sel.idx;
             topk_w[static_cast<size_t>(t) * K + lane] = sel.w;
@@ -499,13 +501,14 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(float* __restrict__ y, 
 }
 
 // Small T (<= kRouteTile): the whole routing stage in one launch.  CTA b computes
-// the logits of experts [b*kSmallExperts, ...) for every token and zeroes a slice
-// of y; the last CTA to finish (an atomic ticket) routes every token, counts the
-// experts, builds the schedule and the permutation maps, and re-arms the ticket.
-constexpr int kSmallExperts = 4;
-constexpr int kSmallThreads = 512;
+// expert b's logit for every token (one warp per token) and zeroes a slice of y;
+// the last CTA to finish (an atomic ticket) routes every token (again one warp per
+// token), counts the experts, builds the schedule and the permutation maps, and
+// re-arms the ticket.
+constexpr int kSmallExperts = 1;  // experts per CTA in the logits phase
+constexpr int kSmallThreads = 1024;  // one warp per token of the tile in the routing step
 
-template <typename XT>
+template <typename XT, int EPL>
 __global__ void __launch_bounds__(kSmallThreads) route_small_kernel(
     const XT* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias, float* __restrict__ logits,
     int T, int H, RouterParams rp, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
@@ -536,13 +539,16 @@ __global__ void __launch_bounds__(kSmallThreads) route_small_kernel(
             yz[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
 
-    // Logits of this CTA's experts: warp -> tokens warp, warp + 16; lanes split H.
+    // Logits of this CTA's expert(s): warp t computes token t's dot products; the
+    // loop is unrolled so each lane's loads of x and of the router row are all in
+    // flight together (one memory round trip instead of H / 256).
     const int e0 = blockIdx.x * kSmallExperts;
     for (int t = warp; t < T; t += kWarps) {
         float acc[kSmallExperts];
 #pragma unroll
         for (int j = 0; j < kSmallExperts; ++j) acc[j] = 0.0f;
         const XT* xt = x + static_cast<size_t>(t) * H;
+#pragma unroll 8
         for (int h = lane * 8; h < H; h += 256) {
             float xv[8];
             load8(xt + h, xv);
@@ -576,25 +582,24 @@ __global__ void __launch_bounds__(kSmallThreads) route_small_kernel(
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    for (int e = tid; e < E; e += blockDim.x) {
+        totals[e] = 0;
+        seg_off_s[e] = 0;
+    }
+    __syncthreads();
     for (int t = warp; t < T; t += kWarps) {
-        const Selection sel = route_one_token(logits + static_cast<size_t>(t) * E, rp, probs[warp], lane);
+        const Selection sel = route_one_token<EPL>(logits + static_cast<size_t>(t) * E, rp, probs[warp], lane);
         if (lane < K) {
             topk_idx[static_cast<size_t>(t) * K + lane] = sel.idx;
             topk_w[static_cast<size_t>(t) * K + lane] = sel.w;
             s_idx[t * K + lane] = sel.idx;
             s_w[t * K + lane] = sel.w;
+            atomicAdd(&totals[sel.idx], 1);
         }
     }
     __syncthreads();
     const int n_pairs = T * K;
-    for (int e = tid; e < E; e += blockDim.x) {
-        int c = 0;
-        for (int q = 0; q < n_pairs; ++q) c += (s_idx[q] == e);
-        totals[e] = c;
-        expert_totals[e] = c;
-        seg_off_s[e] = 0;
-    }
-    __syncthreads();
+    for (int e = tid; e < E; e += blockDim.x) expert_totals[e] = totals[e];
     if (tid == 0) {
         build_schedule(sched, totals, T, n_shared, first_expert, local_E, shared_base, bn, mb1, mb2, seg_off_s);
         *ticket = 0u;  // every CTA has taken its ticket: re-arm for the next launch
@@ -658,12 +663,22 @@ cudaError_t launch_router_logits(const uint16_t* x, const float* x_f32, const fl
                     hidden, experts);
 }
 
+int experts_per_lane(int experts) {
+    const int need = (experts + 31) / 32;
+    return need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : 8;
+}
+
 cudaError_t launch_router_topk(const float* logits, int tokens, RouterParams rp, int32_t* topk_idx,
                                float* topk_w, int32_t* tile_counts, cudaStream_t stream, bool pdl) {
     if (tokens <= 0) return cudaSuccess;
     const dim3 grid((tokens + kRouteTile - 1) / kRouteTile);
-    return launch_k(router_topk_kernel, grid, dim3(kTopkThreads), stream, pdl, logits, tokens, rp, topk_idx, topk_w,
-                    tile_counts);
+    const dim3 block(kTopkThreads);
+    switch (experts_per_lane(rp.experts)) {
+        case 1: return launch_k(router_topk_kernel<1>, grid, block, stream, pdl, logits, tokens, rp, topk_idx, topk_w, tile_counts);
+        case 2: return launch_k(router_topk_kernel<2>, grid, block, stream, pdl, logits, tokens, rp, topk_idx, topk_w, tile_counts);
+        case 4: return launch_k(router_topk_kernel<4>, grid, block, stream, pdl, logits, tokens, rp, topk_idx, topk_w, tile_counts);
+        default: return launch_k(router_topk_kernel<8>, grid, block, stream, pdl, logits, tokens, rp, topk_idx, topk_w, tile_counts);
+    }
 }
 
 cudaError_t launch_dispatch_scan(const int32_t* tile_counts, int32_t* tile_base, int32_t* expert_totals,
@@ -700,6 +715,39 @@ cudaError_t launch_ep_combine(float* y, const float* back, const int32_t* slot_r
                     back, slot_row, topk_w, tokens, top_k, hidden);
 }
 
+template <typename XT, int EPL>
+cudaError_t launch_route_small_t(const XT* x, const float* w, const float* bias, float* logits, int tokens, int hidden,
+                                 RouterParams rp, int32_t* topk_idx, float* topk_w, int32_t* expert_totals,
+                                 Schedule* sched, int32_t* row_token, float* row_weight, int32_t* slot_row,
+                                 float* y_zero, unsigned int* ticket, int n_shared, int first_expert,
+                                 int local_experts, int shared_base, int bn, int mb1, int mb2, cudaStream_t stream,
+                                 bool pdl) {
+    const dim3 grid((rp.experts + kSmallExperts - 1) / kSmallExperts);
+    return launch_k(route_small_kernel<XT, EPL>, grid, dim3(kSmallThreads), stream, pdl, x, w, bias, logits, tokens,
+                    hidden, rp, topk_idx, topk_w, expert_totals, sched, row_token, row_weight, slot_row, y_zero,
+                    ticket, n_shared, first_expert, local_experts, shared_base, bn, mb1, mb2);
+}
+
+template <typename XT>
+cudaError_t route_small_dispatch(const XT* x, const float* w, const float* bias, float* logits, int tokens,
+                                 int hidden, RouterParams rp, int32_t* topk_idx, float* topk_w,
+                                 int32_t* expert_totals, Schedule* sched, int32_t* row_token, float* row_weight,
+                                 int32_t* slot_row, float* y_zero, unsigned int* ticket, int n_shared,
+                                 int first_expert, int local_experts, int shared_base, int bn, int mb1, int mb2,
+                                 cudaStream_t stream, bool pdl) {
+#define LM_ROUTE_SMALL(EPL)                                                                                      \
+    launch_route_small_t<XT, EPL>(x, w, bias, logits, tokens, hidden, rp, topk_idx, topk_w, expert_totals, sched, \
+                                  row_token, row_weight, slot_row, y_zero, ticket, n_shared, first_expert,        \
+                                  local_experts, shared_base, bn, mb1, mb2, stream, pdl)
+    switch (experts_per_lane(rp.experts)) {
+        case 1: return LM_ROUTE_SMALL(1);
+        case 2: return LM_ROUTE_SMALL(2);
+        case 4: return LM_ROUTE_SMALL(4);
+        default: return LM_ROUTE_SMALL(8);
+    }
+#undef LM_ROUTE_SMALL
+}
+
 cudaError_t launch_route_small(const uint16_t* x, const float* x_f32, const float* w, const float* bias,
                                float* logits, int tokens, int hidden, RouterParams rp, int32_t* topk_idx,
                                float* topk_w, int32_t* expert_totals, Schedule* sched, int32_t* row_token,
@@ -708,14 +756,14 @@ cudaError_t launch_route_small(const uint16_t* x, const float* x_f32, const floa
                                int mb2, cudaStream_t stream, bool pdl) {
     if (tokens <= 0) return cudaSuccess;
     if (tokens > kRouteTile) return cudaErrorInvalidValue;
-    const dim3 grid((rp.experts + kSmallExperts - 1) / kSmallExperts);
     if (x_f32 != nullptr)
-        return launch_k(route_small_kernel<float>, grid, dim3(kSmallThreads), stream, pdl, x_f32, w, bias, logits,
-                        tokens, hidden, rp, topk_idx, topk_w, expert_totals, sched, row_token, row_weight, slot_row,
-                        y_zero, ticket, n_shared, first_expert, local_experts, shared_base, bn, mb1, mb2);
-    return launch_k(route_small_kernel<uint16_t>, grid, dim3(kSmallThreads), stream, pdl, x, w, bias, logits, tokens,
-                    hidden, rp, topk_idx, topk_w, expert_totals, sched, row_token, row_weight, slot_row, y_zero,
-                    ticket, n_shared, first_expert, local_experts, shared_base, bn, mb1, mb2);
+        return route_small_dispatch<float>(x_f32, w, bias, logits, tokens, hidden, rp, topk_idx, topk_w,
+                                           expert_totals, sched, row_token, row_weight, slot_row, y_zero, ticket,
+                                           n_shared, first_expert, local_experts, shared_base, bn, mb1, mb2, stream,
+                                           pdl);
+    return route_small_dispatch<uint16_t>(x, w, bias, logits, tokens, hidden, rp, topk_idx, topk_w, expert_totals,
+                                          sched, row_token, row_weight, slot_row, y_zero, ticket, n_shared,
+                                          first_expert, local_experts, shared_base, bn, mb1, mb2, stream, pdl);
 }
 
 }  // namespace lm
