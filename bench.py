@@ -64,7 +64,12 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--tokens", type=int, default=32, help="tokens per rank per step")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="tokens per rank per step (default 32 for decode, 4096 for stack)")
+    ap.add_argument("--workload", choices=["decode", "stack"], default="decode",
+                    help="decode: one MoE layer (BASELINE config 1, headline); stack: 26 x (RMSNorm, MoE, "
+                         "residual) (BASELINE config 4)")
+    ap.add_argument("--layers", type=int, default=26, help="blocks in the stack workload")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -239,14 +244,98 @@ def time_forward(layer, x, y, flush, steps: int, torch):
     return total / steps
 
 
+def run_stack(args, rank: int, world: int, local_rank: int) -> int:
+    """`layers` x (RMSNorm -> MoE -> residual) over T tokens per rank."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from litemind_b200 import synthetic as syn
+    from litemind_b200.moe import MoeConfig, MoeLayer
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local_rank))
+    shape, T, L = syn.V2_LITE, args.tokens, args.layers
+    layer = MoeLayer(MoeConfig(num_layers=L, max_tokens=T), device=local_rank)
+    if world > 1:
+        uid = [MoeLayer.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        layer.ep_init(uid[0], rank, world)
+    ones = np.ones(shape.hidden, np.float32)  # RMSNorm weights: ones, as tools/make_test_model.py writes them
+    t_up = time.perf_counter()
+    for l in range(L):
+        layer.upload_layer(l, syn.layer_weights(shape, seed=4, layer=l), norm_weight=ones)
+    upload_s = time.perf_counter() - t_up
+    x0 = torch.from_numpy(syn.bf16_to_f32(syn.tokens(shape, T, seed=4, stream=rank)).reshape(T, -1)).cuda()
+    hidden = x0.clone()
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+
+    def step():
+        hidden.copy_(x0)
+        for l in range(L):
+            layer.block_forward(l, hidden)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    layer.sync()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    total = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        start.record()
+        step()
+        end.record()
+        end.synchronize()
+        total += start.elapsed_time(end)
+    ms = total / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    peaks = measured_peaks()
+    flops = 138_674_176 * T * L * world
+    hbm = (shape.expert_bytes * shape.n_routed_experts + shape.shared_bytes + shape.router_bytes) * L
+    line = {
+        "metric": METRIC, "value": T * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"config4-stack: {L} x (RMSNorm, V2-Lite MoE layer, residual)", "tokens_per_rank": T,
+                   "layers": L, "seed": 4, "norm_weights": "ones", "resident_weight_gb": hbm / 1e9 / world,
+                   "upload_s": upload_s,
+                   "parallelism": "single GPU" if world == 1 else f"expert parallel, {64 // world} experts per GPU"},
+        "roofline": {"bound": "tensor", "achieved": flops / (ms / 1e3) / 1e12 / world,
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": flops / (ms / 1e3) / 1e12 / world / peaks["bf16_tflops"],
+                     "peak_source": f"{peaks['source']} (bf16_tflops)",
+                     "hbm_frac": hbm / world / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "traffic": None},
+        "gpu_launches": None,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    layer.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
+    if args.tokens is None:
+        args.tokens = 32 if args.workload == "decode" else 4096
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
         return 0
+    if args.workload == "stack":
+        return run_stack(args, rank, world, local_rank)
 
     import numpy as np
     import torch
