@@ -39,7 +39,7 @@ constexpr int kThreads = 192;
 constexpr int kATileBytes = kBlockM * kBlockK * 2;
 constexpr int kSmemBudget = 225 * 1024;
 
-enum class Kind { GateUp, Down };
+enum class Kind { GateUp, Down, Router };
 
 template <int BN, Kind KIND>
 struct Cfg {
@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_mbar_init();
         tma_prefetch_desc(&map_a);
         tma_prefetch_desc(&map_b);
-        if (KIND == Kind::GateUp) tma_prefetch_desc(&map_x);
+        if (KIND != Kind::Down) tma_prefetch_desc(&map_x);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::kTmemCols);
@@ -124,15 +124,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // Everything above overlaps the previous kernel; the schedule is its output.
     pdl_wait();
-    const Schedule* sched = args.sched;
-    if (threadIdx.x == 0) s_n_seg = sched->n_seg;
-    for (int i = threadIdx.x; i <= kMaxSegments; i += kThreads) {
-        if (i < kMaxSegments) {
-            s_off[i] = sched->seg_off[i];
-            s_cnt[i] = sched->seg_cnt[i];
-            s_wslot[i] = sched->seg_weight[i];
+    if constexpr (KIND == Kind::Router) {
+        // One segment: every token, one 128-row block of router weights.
+        if (threadIdx.x == 0) {
+            s_n_seg = 1;
+            s_off[0] = 0;
+            s_cnt[0] = args.tokens;
+            s_wslot[0] = 0;
+            s_tiles[0] = 0;
+            s_tiles[1] = (args.tokens + BN - 1) / BN;
         }
-        s_tiles[i] = (KIND == Kind::GateUp) ? sched->tiles1[i] : sched->tiles2[i];
+    } else {
+        const Schedule* sched = args.sched;
+        if (threadIdx.x == 0) s_n_seg = sched->n_seg;
+        for (int i = threadIdx.x; i <= kMaxSegments; i += kThreads) {
+            if (i < kMaxSegments) {
+                s_off[i] = sched->seg_off[i];
+                s_cnt[i] = sched->seg_cnt[i];
+                s_wslot[i] = sched->seg_weight[i];
+            }
+            s_tiles[i] = (KIND == Kind::GateUp) ? sched->tiles1[i] : sched->tiles2[i];
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -142,9 +154,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_seg = s_n_seg;
     const int total_tiles = s_tiles[n_seg];
     const uint32_t tmem_base = *tmem_slot;
-    const int K = (KIND == Kind::GateUp) ? args.hidden : args.inter;
+    // Router: K runs over [x | x | x] against the router split into three bf16
+    // parts; A is one 128-row block (experts, zero-padded).
+    const int K = (KIND == Kind::GateUp) ? args.hidden : (KIND == Kind::Down) ? args.inter : 3 * args.hidden;
     const int num_kb = K / kBlockK;
-    const int rows_a = (KIND == Kind::GateUp) ? 2 * args.inter : args.hidden;
+    const int x_kb = args.hidden / kBlockK;
+    const int rows_a = (KIND == Kind::GateUp) ? 2 * args.inter : (KIND == Kind::Down) ? args.hidden : kBlockM;
     const int mb_per = rows_a / kBlockM;
 
     if (warp == 0) {
@@ -165,7 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int a_tile0 = (s_wslot[s] * mb_per + mb) * num_kb;
                 // Routed experts read their expert-sorted rows of x_perm (gate/up) or h
                 // (down); the shared experts read x itself, token by token.
-                const bool from_x = (KIND == Kind::GateUp) && s >= args.n_routed_local;
+                const bool from_x =
+                    (KIND == Kind::Router) || ((KIND == Kind::GateUp) && s >= args.n_routed_local);
                 const int b_row = from_x ? nb * BN : s_off[s] + nb * BN;
                 const CUtensorMap* bmap = from_x ? &map_x : &map_b;
                 for (int kb = 0; kb < num_kb; ++kb) {
@@ -174,8 +190,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&full[stage], kATileBytes + C::kBTileBytes);
-                    tma_load_2d(smem_a + stage * kATileBytes, &map_a, &full[stage], 0, (a_tile0 + kb) * kBlockM);
-                    tma_load_2d(smem_b + stage * C::kBTileBytes, bmap, &full[stage], kb * kBlockK, b_row);
+                    if constexpr (KIND == Kind::Router) {
+                        tma_load_2d(smem_a + stage * kATileBytes, &map_a, &full[stage], kb * kBlockK, 0);
+                        tma_load_2d(smem_b + stage * C::kBTileBytes, bmap, &full[stage], (kb % x_kb) * kBlockK, b_row);
+                    } else {
+                        tma_load_2d(smem_a + stage * kATileBytes, &map_a, &full[stage], 0, (a_tile0 + kb) * kBlockM);
+                        tma_load_2d(smem_b + stage * C::kBTileBytes, bmap, &full[stage], kb * kBlockK, b_row);
+                    }
                     issued_mask |= 1u << stage;
                     issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == S) {
@@ -259,7 +280,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
             const int row0 = s_off[s] + nb * BN;  // first h row / routed row of this tile
-            if constexpr (KIND == Kind::GateUp) {
+            if constexpr (KIND == Kind::Router) {
+                // Lane = expert, column = token: logits[token][expert] (+ bias), 32
+                // consecutive experts per warp per token.
+                const int e = quad * 32 + lane;
+                const bool live = e < args.experts;
+                const float b = (live && args.bias != nullptr) ? args.bias[e] : 0.0f;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    if (c0 >= valid) break;
+                    uint32_t r[16];
+                    tmem_ld16(t_row + c0, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (live && c0 + j < valid)
+                            args.logits[static_cast<size_t>(nb * BN + c0 + j) * args.experts + e] =
+                                args.bias != nullptr ? __uint_as_float(r[j]) + b : __uint_as_float(r[j]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+            } else if constexpr (KIND == Kind::GateUp) {
                 __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(staging);
                 const int i_local = (quad * 32 + lane) >> 1;  // h column within the tile's 64
 #pragma unroll 1
@@ -391,6 +433,19 @@ cudaError_t launch_gemm_gate_up(int bn, const CUtensorMap& w13, const CUtensorMa
         case 64: return launch_one<64, Kind::GateUp>(w13, xperm, x, args, sms, stream, pdl);
         case 128: return launch_one<128, Kind::GateUp>(w13, xperm, x, args, sms, stream, pdl);
         case 256: return launch_one<256, Kind::GateUp>(w13, xperm, x, args, sms, stream, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_gemm_router(int bn, const CUtensorMap& wcat, const CUtensorMap& x, const GemmArgs& args, int sms,
+                               cudaStream_t stream, bool pdl) {
+    const int tiles = (args.tokens + bn - 1) / bn;
+    const int grid = tiles < sms ? tiles : sms;
+    switch (bn) {
+        case 16: return launch_one<16, Kind::Router>(wcat, x, x, args, grid, stream, pdl);
+        case 32: return launch_one<32, Kind::Router>(wcat, x, x, args, grid, stream, pdl);
+        case 64: return launch_one<64, Kind::Router>(wcat, x, x, args, grid, stream, pdl);
+        case 128: return launch_one<128, Kind::Router>(wcat, x, x, args, grid, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -32,8 +32,10 @@ struct LayerWeights {
     float* router = nullptr;
     float* router_t = nullptr;
     float* norm = nullptr;
+    uint16_t* router_cat = nullptr;  // [128, 3*hidden] bf16: router = hi + mid + lo, for the tensor-core router
     CUtensorMap map_w13{};
     CUtensorMap map_w2{};
+    CUtensorMap map_router{};
     std::vector<uint8_t> expert_loaded;  // per local routed expert
     bool shared_loaded = false;
     bool router_loaded = false;
@@ -193,11 +195,13 @@ lm_status ensure_layer_buffers(lm_moe_ctx* ctx, int32_t layer) {
     if ((st = alloc(ctx, &L.router, E * H)) != LM_OK) return st;
     if ((st = alloc(ctx, &L.router_t, E * H)) != LM_OK) return st;
     if ((st = alloc(ctx, &L.norm, H)) != LM_OK) return st;
+    if ((st = alloc(ctx, &L.router_cat, 128 * 3 * H)) != LM_OK) return st;
     ctx->resident_bytes += segs * 3 * I * H * 2 + 2 * E * H * 4 + H * 4;
     std::string err;
     // Tile-major storage: a [rows, 64] matrix of 128-row tiles.
     if (!encode_tensor_map_bf16(&L.map_w13, L.w13, segs * 2 * I * H / 64, 64, 128, 64, err) ||
-        !encode_tensor_map_bf16(&L.map_w2, L.w2, segs * H * I / 64, 64, 128, 64, err))
+        !encode_tensor_map_bf16(&L.map_w2, L.w2, segs * H * I / 64, 64, 128, 64, err) ||
+        !encode_tensor_map_bf16(&L.map_router, L.router_cat, 128, 3 * H, 128, 64, err))
         return fail(ctx, LM_ERR_CUDA, err);
     L.expert_loaded.assign(ctx->local_experts, 0);
     return LM_OK;
@@ -430,6 +434,35 @@ lm_status lm_moe_upload_layer(lm_moe_ctx* ctx, int32_t layer, const float* route
     for (size_t e = 0; e < E; ++e)
         for (size_t k = 0; k < H; ++k) transposed[k * E + e] = router[e * H + k];
     LM_CUDA(ctx, cudaMemcpy(L.router, router, E * H * sizeof(float), cudaMemcpyHostToDevice));
+    // The f32 router as three bf16 parts (each the rounding of what the previous
+    // ones leave), so hi + mid + lo == router exactly and every product with a bf16
+    // token is exact in f32 on the tensor cores.
+    if (E <= 128) {
+        std::vector<uint16_t> cat(128 * 3 * H, 0);
+        auto rne = [](float v) -> uint16_t {
+            uint32_t b;
+            std::memcpy(&b, &v, 4);
+            return static_cast<uint16_t>((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
+        };
+        auto widen = [](uint16_t h) -> float {
+            const uint32_t b = static_cast<uint32_t>(h) << 16;
+            float v;
+            std::memcpy(&v, &b, 4);
+            return v;
+        };
+        for (size_t e = 0; e < E; ++e)
+            for (size_t k = 0; k < H; ++k) {
+                const float w = router[e * H + k];
+                const uint16_t hi = rne(w);
+                const float r1 = w - widen(hi);
+                const uint16_t mid = rne(r1);
+                const float r2 = r1 - widen(mid);
+                cat[e * 3 * H + k] = hi;
+                cat[e * 3 * H + H + k] = mid;
+                cat[e * 3 * H + 2 * H + k] = rne(r2);
+            }
+        LM_CUDA(ctx, cudaMemcpy(L.router_cat, cat.data(), cat.size() * sizeof(uint16_t), cudaMemcpyHostToDevice));
+    }
     LM_CUDA(ctx, cudaMemcpy(L.router_t, transposed.data(), E * H * sizeof(float), cudaMemcpyHostToDevice));
     if (norm_weight != nullptr)
         LM_CUDA(ctx, cudaMemcpy(L.norm, norm_weight, H * sizeof(float), cudaMemcpyHostToDevice));
@@ -460,14 +493,50 @@ lm_status lm_moe_upload_expert(lm_moe_ctx* ctx, int32_t layer, int32_t expert, c
     return LM_OK;
 }
 
+// Router logits: on the tensor cores for large batches of bf16 tokens, else the
+// f32 CUDA-core kernels (which also serve the f32 activations of block_forward).
+static lm_status router_logits(lm_moe_ctx* ctx, const LayerWeights& L, const uint16_t* x, const float* x_f32, int32_t T,
+                               const float* bias, float* logits, cudaStream_t s, bool pdl, RouterFix* fix) {
+    const lm_moe_config& c = ctx->cfg;
+    *fix = RouterFix{};
+    // Group-limited routing also ranks groups; it keeps the plain f32 logits.
+    if (x_f32 == nullptr && T >= 512 && c.n_routed_experts <= 128 && !router_params(c).group_limited) {
+        int bn = 16;
+        while (bn < 128 && (T + bn - 1) / bn > ctx->sms) bn *= 2;
+        CUtensorMap map_x{};
+        std::string err;
+        if (!encode_tensor_map_bf16(&map_x, x, T, c.hidden_size, bn, 64, err))
+            return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+        GemmArgs args{};
+        args.status = ctx->status;
+        args.tokens = T;
+        args.hidden = c.hidden_size;
+        args.inter = c.moe_intermediate_size;
+        args.logits = logits;
+        args.bias = bias;
+        args.experts = c.n_routed_experts;
+        LM_CUDA(ctx, launch_gemm_router(bn, L.map_router, map_x, args, ctx->sms, s, pdl));
+        fix->x = x;
+        fix->w = L.router;
+        fix->bias = bias;
+        fix->hidden = c.hidden_size;
+        fix->margin = 2e-5f;  // ten times the largest probability error seen from tensor-core logits
+        return LM_OK;
+    }
+    LM_CUDA(ctx, launch_router_logits(x, x_f32, L.router, L.router_t, bias, logits, T, c.hidden_size,
+                                      c.n_routed_experts, s, pdl));
+    return LM_OK;
+}
+
 static lm_status route_common(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, const float* x_f32, int32_t T,
                               const float* bias, float* logits, cudaStream_t stream) {
     const lm_moe_config& c = ctx->cfg;
     const LayerWeights& L = ctx->layers[layer];
-    LM_CUDA(ctx, launch_router_logits(x, x_f32, L.router, L.router_t, bias, logits, T, c.hidden_size,
-                                      c.n_routed_experts, stream, false));
+    lm_status st;
+    RouterFix fix;
+    if ((st = router_logits(ctx, L, x, x_f32, T, bias, logits, stream, false, &fix)) != LM_OK) return st;
     LM_CUDA(ctx, launch_router_topk(logits, T, router_params(c), ctx->topk_idx, ctx->topk_w, ctx->tile_counts,
-                                    stream, true));
+                                    stream, true, fix));
     return LM_OK;
 }
 
@@ -504,7 +573,7 @@ lm_status lm_moe_select(lm_moe_ctx* ctx, const float* logits, int32_t tokens, in
         return fail(ctx, LM_ERR_INVALID_ARGUMENT, "null pointer");
     lm_status st;
     if ((st = set_device(ctx)) != LM_OK) return st;
-    LM_CUDA(ctx, launch_router_topk(logits, tokens, router_params(ctx->cfg), topk_idx, topk_w, nullptr,
+    LM_CUDA(ctx, launch_router_topk(const_cast<float*>(logits), tokens, router_params(ctx->cfg), topk_idx, topk_w, nullptr,
                                     static_cast<cudaStream_t>(stream), false));
     return LM_OK;
 }
@@ -530,11 +599,12 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
         prof_mark(ctx, 1, s);
         slots[n_slots++] = 1;
     } else {
-        LM_CUDA(ctx, launch_router_logits(x, x_f32, L.router, L.router_t, bias, ctx->logits, T, c.hidden_size,
-                                          c.n_routed_experts, s, false));
+        lm_status rst;
+        RouterFix fix;
+        if ((rst = router_logits(ctx, L, x, x_f32, T, bias, ctx->logits, s, false, &fix)) != LM_OK) return rst;
         prof_mark(ctx, 1, s);
         slots[n_slots++] = 1;
-        LM_CUDA(ctx, launch_router_topk(ctx->logits, T, rp, ctx->topk_idx, ctx->topk_w, ctx->tile_counts, s, true));
+        LM_CUDA(ctx, launch_router_topk(ctx->logits, T, rp, ctx->topk_idx, ctx->topk_w, ctx->tile_counts, s, true, fix));
         prof_mark(ctx, 2, s);
         slots[n_slots++] = 2;
         LM_CUDA(ctx, launch_dispatch_scan(ctx->tile_counts, ctx->tile_base, ctx->expert_totals, ctx->sched, T, K, E,
@@ -601,8 +671,10 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
                                         ctx->expert_totals, ctx->sched, ctx->row_token, ctx->row_weight,
                                         ctx->slot_row, y_zero, ctx->ticket, 0, 0, E, 0, 16, 1, 1, s, false));
     } else if (T > 0) {
-        LM_CUDA(ctx, launch_router_logits(x, x_f32, L.router, L.router_t, bias, ctx->logits, T, H, E, s, false));
-        LM_CUDA(ctx, launch_router_topk(ctx->logits, T, rp, ctx->topk_idx, ctx->topk_w, ctx->tile_counts, s, true));
+        lm_status rst;
+        RouterFix fix;
+        if ((rst = router_logits(ctx, L, x, x_f32, T, bias, ctx->logits, s, false, &fix)) != LM_OK) return rst;
+        LM_CUDA(ctx, launch_router_topk(ctx->logits, T, rp, ctx->topk_idx, ctx->topk_w, ctx->tile_counts, s, true, fix));
         LM_CUDA(ctx, launch_dispatch_scan(ctx->tile_counts, ctx->tile_base, ctx->expert_totals, ctx->sched, T, K, E,
                                           0, 0, E, 0, 16, 1, 1, s, true));
         LM_CUDA(ctx, launch_place(ctx->topk_idx, ctx->topk_w, ctx->tile_base, T, H, K, E, 0, E, ctx->row_token,

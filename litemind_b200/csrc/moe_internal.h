@@ -42,12 +42,23 @@ struct RouterParams {
     float scale;
 };
 
+// When router logits come from the tensor cores, the top-k kernel recomputes a
+// token's logits in plain f32 wherever two of its first k+1 ranked probabilities
+// are closer than `margin` (x null: logits are already plain f32).
+struct RouterFix {
+    const uint16_t* x = nullptr;   // [T, hidden] bf16 tokens
+    const float* w = nullptr;      // [E, hidden] f32 router
+    const float* bias = nullptr;   // [E] or null
+    int32_t hidden = 0;
+    float margin = 0.0f;
+};
+
 // Kernel launchers (router.cu).  All return cudaGetLastError() after launching.
 cudaError_t launch_router_logits(const uint16_t* x, const float* x_f32, const float* w, const float* w_t,
                                  const float* bias, float* logits, int tokens, int hidden, int experts,
                                  cudaStream_t stream, bool pdl);
-cudaError_t launch_router_topk(const float* logits, int tokens, RouterParams rp, int32_t* topk_idx,
-                               float* topk_w, int32_t* tile_counts, cudaStream_t stream, bool pdl);
+cudaError_t launch_router_topk(float* logits, int tokens, RouterParams rp, int32_t* topk_idx, float* topk_w,
+                               int32_t* tile_counts, cudaStream_t stream, bool pdl, RouterFix fix = RouterFix{});
 cudaError_t launch_dispatch_scan(const int32_t* tile_counts, int32_t* tile_base, int32_t* expert_totals,
                                  Schedule* sched, int tokens, int top_k, int experts, int n_shared,
                                  int first_expert, int local_experts, int shared_base, int bn, int mb1,
@@ -79,10 +90,17 @@ struct GemmArgs {
     int32_t hidden;
     int32_t inter;
     float* y_rows;             // when set, routed rows' down outputs are stored here by row, unweighted
+    float* logits;             // router kind: [T, experts] f32 output
+    const float* bias;         // router kind: per-expert logit bias or null
+    int32_t experts;           // router kind: experts (<= 128)
     int32_t n_routed_local;    // segments [0, n_routed_local) are routed experts
 };
 cudaError_t launch_gemm_gate_up(int bn, const CUtensorMap& w13, const CUtensorMap& xperm, const CUtensorMap& x,
                                 const GemmArgs& args, int sms, cudaStream_t stream, bool pdl);
+// Router logits on tensor cores: wcat is [128, 3*hidden] bf16 (the f32 router
+// split exactly into three bf16 parts, concatenated along K; rows >= experts zero).
+cudaError_t launch_gemm_router(int bn, const CUtensorMap& wcat, const CUtensorMap& x, const GemmArgs& args, int sms,
+                               cudaStream_t stream, bool pdl);
 cudaError_t launch_gemm_down(int bn, const CUtensorMap& w2, const CUtensorMap& hmap, const GemmArgs& args,
                              int sms, cudaStream_t stream, bool pdl);
 

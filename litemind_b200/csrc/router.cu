@@ -172,11 +172,12 @@ constexpr uint32_t kFull = 0xffffffffu;
 struct Selection {
     int idx;
     float w;
+    bool ambiguous;  // two of the first k+1 ranked probabilities are closer than the margin
 };
 
 template <int EPL>  // experts per lane: ceil(E / 32) rounded up to 1, 2, 4 or 8
-__device__ __forceinline__ Selection route_one_token(const float* lg, const RouterParams& rp, float* probs,
-                                                     int lane) {
+__device__ __forceinline__ Selection route_one_token(const float* lg, const RouterParams& rp, float* probs, int lane,
+                                                     float margin = 0.0f) {
     const int E = rp.experts;
     const int K = rp.top_k;
     float p[EPL];
@@ -245,8 +246,13 @@ __device__ __forceinline__ Selection route_one_token(const float* lg, const Rout
             avail |= 1u << j;
         }
     }
-    Selection mine{-1, 0.0f};
-    for (int s = 0; s < K; ++s) {
+    Selection mine{-1, 0.0f, false};
+    // One round past K when a margin is asked for: the (k+1)-th probability decides
+    // whether an approximate logit could have moved the cut.
+    const int rounds = (margin > 0.0f && K < E) ? K + 1 : K;
+    float prev = 0.0f;
+    float min_gap = 1.0f;
+    for (int s = 0; s < rounds; ++s) {
         uint32_t best = 0;
         int bj = -1;
 #pragma unroll
@@ -260,11 +266,15 @@ __device__ __forceinline__ Selection route_one_token(const float* lg, const Rout
         const uint32_t cand = (bj >= 0 && best == wmax) ? static_cast<uint32_t>(lane + 32 * bj) : 0xffffffffu;
         const uint32_t win = __reduce_min_sync(kFull, cand);
         if ((win & 31u) == static_cast<uint32_t>(lane)) avail &= ~(1u << (win >> 5));
-        if (lane == s) {
+        const float pw = __uint_as_float(wmax & 0x7fffffffu);
+        if (s > 0) min_gap = fminf(min_gap, prev - pw);
+        prev = pw;
+        if (lane == s && s < K) {
             mine.idx = static_cast<int>(win);
-            mine.w = __uint_as_float(wmax & 0x7fffffffu);
+            mine.w = pw;
         }
     }
+    mine.ambiguous = margin > 0.0f && min_gap < margin;
     if (K > 1 && rp.normalize) {
         float selected = 0.0f;  // in selection order, as the reference sums it
         for (int s = 0; s < K; ++s) selected += __shfl_sync(kFull, mine.w, s);
@@ -311,10 +321,11 @@ __device__ void build_schedule(Schedule* sched, const int* totals, int T, int n_
 constexpr int kTopkThreads = 32 * kRouteTile;  // one warp per token of a routing tile
 
 template <int EPL>
-__global__ void __launch_bounds__(kTopkThreads) router_topk_kernel(const float* __restrict__ logits, int T,
-                                                                   RouterParams rp, int32_t* __restrict__ topk_idx,
+__global__ void __launch_bounds__(kTopkThreads) router_topk_kernel(float* __restrict__ logits, int T, RouterParams rp,
+                                                                   int32_t* __restrict__ topk_idx,
                                                                    float* __restrict__ topk_w,
-                                                                   int32_t* __restrict__ tile_counts) {
+                                                                   int32_t* __restrict__ tile_counts,
+                                                                   RouterFix fix) {
     __shared__ int counts[kMaxExperts];
     __shared__ float probs[kRouteTile][kMaxExperts];
     const int tid = threadIdx.x;
@@ -328,7 +339,38 @@ __global__ void __launch_bounds__(kTopkThreads) router_topk_kernel(const float* 
     pdl_launch_dependents();
     const int t = blockIdx.x * kRouteTile + warp;
     if (t < T) {
-        const Selection sel = route_one_token<EPL>(logits + static_cast<size_t>(t) * E, rp, probs[warp], lane);
+        float* lg = logits + static_cast<size_t>(t) * E;
+        Selection sel = route_one_token<EPL>(lg, rp, probs[warp], lane, fix.x != nullptr ? fix.margin : 0.0f);
+        if (sel.ambiguous) {
+            // The logits came from the tensor cores, whose f32 accumulation is
+            // coarser than a CUDA-core f32 sum.  Probability order is logit order, so
+            // only the experts around the cut can change the choice: recompute the
+            // logits of the k+4 best-ranked experts as plain f32 dot products (lanes
+            // split the hidden axis) and route again.
+            RouterParams rank_rp = rp;
+            rank_rp.top_k = min(E, K + 4);
+            rank_rp.normalize = 0;
+            rank_rp.scale = 1.0f;
+            const Selection ranked = route_one_token<EPL>(lg, rank_rp, probs[warp], lane, 0.0f);
+            const uint16_t* xt = fix.x + static_cast<size_t>(t) * fix.hidden;
+            for (int r = 0; r < rank_rp.top_k; ++r) {
+                const int e = __shfl_sync(kFull, ranked.idx, r);
+                const float* wr = fix.w + static_cast<size_t>(e) * fix.hidden;
+                float acc = 0.0f;
+                for (int h = lane * 8; h < fix.hidden; h += 256) {
+                    float xv[8], wv[8];
+                    load8(xt + h, xv);
+                    load8(wr + h, wv);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[i], acc);
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(kFull, acc, off);
+                if (lane == 0) lg[e] = fix.bias != nullptr ? acc + fix.bias[e] : acc;
+            }
+            __syncwarp();
+            sel = route_one_token<EPL>(lg, rp, probs[warp], lane, 0.0f);
+        }
         if (lane < K) {
             topk_idx[static_cast<size_t>(t) * K + lane] = sel.idx;
             topk_w[static_cast<size_t>(t) * K + lane] = sel.w;
@@ -668,16 +710,16 @@ int experts_per_lane(int experts) {
     return need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : 8;
 }
 
-cudaError_t launch_router_topk(const float* logits, int tokens, RouterParams rp, int32_t* topk_idx,
-                               float* topk_w, int32_t* tile_counts, cudaStream_t stream, bool pdl) {
+cudaError_t launch_router_topk(float* logits, int tokens, RouterParams rp, int32_t* topk_idx, float* topk_w,
+                               int32_t* tile_counts, cudaStream_t stream, bool pdl, RouterFix fix) {
     if (tokens <= 0) return cudaSuccess;
     const dim3 grid((tokens + kRouteTile - 1) / kRouteTile);
     const dim3 block(kTopkThreads);
     switch (experts_per_lane(rp.experts)) {
-        case 1: return launch_k(router_topk_kernel<1>, grid, block, stream, pdl, logits, tokens, rp, topk_idx, topk_w, tile_counts);
-        case 2: return launch_k(router_topk_kernel<2>, grid, block, stream, pdl, logits, tokens, rp, topk_idx, topk_w, tile_counts);
-        case 4: return launch_k(router_topk_kernel<4>, grid, block, stream, pdl, logits, tokens, rp, topk_idx, topk_w, tile_counts);
-        default: return launch_k(router_topk_kernel<8>, grid, block, stream, pdl, logits, tokens, rp, topk_idx, topk_w, tile_counts);
+        case 1: return launch_k(router_topk_kernel<1>, grid, block, stream, pdl, logits, tokens, rp, topk_idx, topk_w, tile_counts, fix);
+        case 2: return launch_k(router_topk_kernel<2>, grid, block, stream, pdl, logits, tokens, rp, topk_idx, topk_w, tile_counts, fix);
+        case 4: return launch_k(router_topk_kernel<4>, grid, block, stream, pdl, logits, tokens, rp, topk_idx, topk_w, tile_counts, fix);
+        default: return launch_k(router_topk_kernel<8>, grid, block, stream, pdl, logits, tokens, rp, topk_idx, topk_w, tile_counts, fix);
     }
 }
 

@@ -14,7 +14,10 @@ import numpy as np
 ROUTE_TIE = 1e-6
 MAX_REL = 1e-2
 MIN_COS = 0.9999
-WEIGHT_RTOL = 1e-5  # routing weights: softmax probabilities from f32 logits
+# Routing weights: softmax probabilities of f32 logits.  Large bf16 batches get their
+# logits from the tensor cores (the f32 router split exactly into three bf16 parts),
+# whose f32 accumulation is coarser than a CUDA-core sum: up to ~2e-5 relative.
+WEIGHT_RTOL = 1e-4
 
 
 def softmax64(logits: np.ndarray) -> np.ndarray:

@@ -20,9 +20,10 @@ torch = pytest.importorskip("torch")
 
 from litemind_b200 import _lib, synthetic as syn  # noqa: E402
 from litemind_b200.moe import MoeConfig, MoeLayer, bf16_tensor  # noqa: E402
+from tests.parity import routing_mismatches  # noqa: E402
 
 SHAPE = syn.MoeShape(hidden=512, inter=128, n_routed_experts=64, n_shared_experts=1, top_k=6)
-W_RTOL = 1e-5  # routing weights, as in tests/parity.py
+W_RTOL = 1e-4  # routing weights, as in tests/parity.py
 
 
 def _static_route(lib, router, x, bias, k, norm=False, scale=1.0):
@@ -48,11 +49,17 @@ def test_static_route_matches_context_route():
         x = bf16_tensor(syn.tokens(SHAPE, T, seed=40 + call))
         status, idx, w = _static_route(lib, router, x, b, SHAPE.top_k)
         assert status == _lib.LM_OK
-        ref_idx, ref_w, _ = layer.route(0, x, bias=b)
+        ref_idx, ref_w, ref_logits = layer.route(0, x, bias=b)
         torch.cuda.synchronize()
-        np.testing.assert_array_equal(idx.cpu().numpy(), ref_idx.cpu().numpy(), err_msg=f"call {call}")
-        np.testing.assert_allclose(w.cpu().numpy(), ref_w.cpu().numpy(), rtol=W_RTOL, atol=1e-8,
-                                   err_msg=f"call {call}")
+        # The two entry points may sum the logits in different orders (CUDA cores
+        # here, tensor cores for large batches there): indices must agree except
+        # where two experts' probabilities are within 1e-6, as everywhere else.
+        idx, ref_idx, w, ref_w = idx.cpu().numpy(), ref_idx.cpu().numpy(), w.cpu().numpy(), ref_w.cpu().numpy()
+        exempt, bad = routing_mismatches(idx, ref_idx, ref_logits.cpu().numpy())
+        assert not bad, f"call {call}: routing differs beyond near-ties for tokens {bad[:10]}"
+        keep = np.ones(T, bool)
+        keep[exempt] = False
+        np.testing.assert_allclose(w[keep], ref_w[keep], rtol=W_RTOL, atol=1e-8, err_msg=f"call {call}")
     layer.close()
 
 
