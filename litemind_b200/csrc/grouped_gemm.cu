@@ -17,8 +17,8 @@
 //             hidden rows, so every atomic add is a coalesced 128-byte run.
 //
 // One persistent CTA per SM walks the tile list in the device-built Schedule.
-// Warp 0 fills a ring of smem stages by TMA tile loads (128-byte swizzle, no
-// multicast): weight tiles, and token tiles from the expert-sorted copy x_perm
+// Warp 0 fills a ring of smem stages by TMA tile loads (128-byte swizzle, each
+// CTA loading its own tiles): weight tiles, and token tiles from the expert-sorted copy x_perm
 // (routed experts) or from x itself (shared experts).  Contiguous rows keep every
 // token tile one TMA request; gathering rows individually (TMA gather4 or cp.async)
 // measured 1.3x (decode) to 2.6x (prefill) slower on B200.  Warp 1 allocates TMEM
@@ -35,7 +35,8 @@ namespace {
 
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpiThreads = 256;  // 8 epilogue warps: two per TMEM lane quadrant
+constexpr int kThreads = 64 + kEpiThreads;  // + TMA producer warp, MMA warp
 constexpr int kATileBytes = kBlockM * kBlockK * 2;
 constexpr int kSmemBudget = 225 * 1024;
 
@@ -66,8 +67,9 @@ __device__ __forceinline__ int find_segment(const int* tiles, int n_seg, int til
 }
 
 __device__ __forceinline__ float silu_times(float g, float u) {
-    // src/Gemm.cpp:225-231: value / (1 + exp(-value)) * up
-    return g / (1.0f + expf(-g)) * u;
+    // src/Gemm.cpp:225-231: value / (1 + exp(-value)) * up, with fast exp and
+    // divide: the result is rounded to bf16 (8 significant bits) right after.
+    return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 
 template <int BN, Kind KIND>
@@ -85,6 +87,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ int s_wslot[kMaxSegments];
     __shared__ int s_n_seg;
     __shared__ int s_epi_go[2];
+    constexpr int kMapCols = (KIND == Kind::Down) ? BN : 1;
+    __shared__ int s_ep_tok[2][kMapCols];  // down epilogue: this tile's token and routing weight per column
+    __shared__ float s_ep_w[2][kMapCols];
 
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smem_a = smem;
@@ -109,7 +114,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tmem_full[i], 1);
-            mbar_init(&tmem_empty[i], 4);
+            mbar_init(&tmem_empty[i], kEpiThreads / 32);
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -257,9 +262,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ── Epilogue: warps 2..5 own TMEM lane quadrants (warp % 4) ──
+        // ── Epilogue: warps 2..9; warp % 4 is the TMEM lane quadrant, two warps per
+        // quadrant split the accumulator's 16-column chunks between them ──
         const int quad = warp & 3;
-        const int epi_tid = threadIdx.x - 64;  // 0..127
+        const int half = (warp - 2) >> 2;  // which 16-column chunks: c0 = 16 * half + 32 k
+        const int epi_tid = threadIdx.x - 64;  // 0..255
         int acc = 0;
         uint32_t acc_phase = 0;
         int iter = 0;
@@ -269,17 +276,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int nb = local / mb_per;
             const int mb = local - nb * mb_per;
             const int valid = min(BN, s_cnt[s] - nb * BN);
-            // One thread waits; the named barrier hands its verdict to all four
+            const int row0 = s_off[s] + nb * BN;  // first h row / routed row of this tile
+            if constexpr (KIND == Kind::Down) {
+                // This tile's token and routing weight per column, read once into
+                // shared memory (published by the named barrier below).
+                if (args.y_rows == nullptr || s >= args.n_routed_local) {
+                    const bool routed = s < args.n_routed_local;
+                    for (int c = epi_tid; c < valid; c += kEpiThreads) {
+                        s_ep_tok[iter & 1][c] = routed ? args.row_token[row0 + c] : nb * BN + c;
+                        s_ep_w[iter & 1][c] = routed ? args.row_weight[row0 + c] : 1.0f;
+                    }
+                }
+            }
+            // One thread waits; the named barrier hands its verdict to all eight
             // warps, so they leave together and never strand each other at a barrier.
             // The verdict slot alternates per tile so a slow warp never reads the next one.
             if (epi_tid == 0)
                 s_epi_go[iter & 1] =
                     mbar_wait(&tmem_full[acc], acc_phase, abort_flag, args.status, kDevTimeoutEpilogue) ? 1 : 0;
-            named_bar_sync(2, 128);
+            named_bar_sync(2, kEpiThreads);
             if (!s_epi_go[iter & 1]) break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            const int row0 = s_off[s] + nb * BN;  // first h row / routed row of this tile
             if constexpr (KIND == Kind::Router) {
                 // Lane = expert, column = token: logits[token][expert] (+ bias), 32
                 // consecutive experts per warp per token.
@@ -287,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool live = e < args.experts;
                 const float b = (live && args.bias != nullptr) ? args.bias[e] : 0.0f;
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
+                for (int c0 = 16 * half; c0 < BN; c0 += 32) {
                     if (c0 >= valid) break;
                     uint32_t r[16];
                     tmem_ld16(t_row + c0, r);
@@ -305,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(staging);
                 const int i_local = (quad * 32 + lane) >> 1;  // h column within the tile's 64
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
+                for (int c0 = 16 * half; c0 < BN; c0 += 32) {
                     if (c0 >= valid) break;  // warp-uniform
                     uint32_t r[16];
                     tmem_ld16(t_row + c0, r);
@@ -320,17 +338,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tmem_empty[acc]);
-                named_bar_sync(1, 128);
+                named_bar_sync(1, kEpiThreads);
                 // Staging [valid tokens][64] -> h rows, 128 contiguous bytes per row.
                 const uint4* src = reinterpret_cast<const uint4*>(staging);
-                for (int q = epi_tid; q < valid * 8; q += 128) {
+                for (int q = epi_tid; q < valid * 8; q += kEpiThreads) {
                     const int c = q >> 3;
                     const int part = q & 7;
                     uint4* dst = reinterpret_cast<uint4*>(args.h + static_cast<size_t>(row0 + c) * args.inter +
                                                           mb * 64) + part;
                     *dst = src[c * 8 + part];
                 }
-                named_bar_sync(1, 128);
+                named_bar_sync(1, kEpiThreads);
             } else {
                 const int d = mb * kBlockM + quad * 32 + lane;  // hidden row
                 const bool routed = s < args.n_routed_local;
@@ -338,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // Expert parallelism: each routed row's output goes back to its
                     // token's rank, which applies the weight; one writer per element.
 #pragma unroll 1
-                    for (int c0 = 0; c0 < BN; c0 += 16) {
+                    for (int c0 = 16 * half; c0 < BN; c0 += 32) {
                         if (c0 >= valid) break;
                         uint32_t r[16];
                         tmem_ld16(t_row + c0, r);
@@ -358,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     continue;
                 }
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
+                for (int c0 = 16 * half; c0 < BN; c0 += 32) {
                     if (c0 >= valid) break;
                     uint32_t r[16];
                     tmem_ld16(t_row + c0, r);
@@ -366,18 +384,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int c = c0 + j;
-                        if (c < valid) {
-                            int tok;
-                            float w;
-                            if (routed) {
-                                tok = args.row_token[row0 + c];
-                                w = args.row_weight[row0 + c];
-                            } else {
-                                tok = nb * BN + c;
-                                w = 1.0f;
-                            }
-                            atomicAdd(args.y + static_cast<size_t>(tok) * args.hidden + d, w * __uint_as_float(r[j]));
-                        }
+                        if (c < valid)
+                            atomicAdd(args.y + static_cast<size_t>(s_ep_tok[iter & 1][c]) * args.hidden + d,
+                                      s_ep_w[iter & 1][c] * __uint_as_float(r[j]));
                     }
                 }
                 tc_fence_before();

@@ -620,9 +620,13 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
     LM_CUDA(ctx, launch_gather_rows(x, ctx->row_token, T * K, H, ctx->x_perm, s, true));
     prof_mark(ctx, 0, s);
     slots[n_slots++] = 0;
+    // Prefill-sized token tiles run on CTA pairs (256-row weight tiles); each CTA
+    // loads half of a token tile, so the token maps' boxes are bn/2 rows.
+    const bool pair = bn == 256;
     CUtensorMap map_x{};
     std::string err;
-    if (!encode_tensor_map_bf16(&map_x, x, T, H, bn, 64, err)) return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+    if (!encode_tensor_map_bf16(&map_x, x, T, H, pair ? bn / 2 : bn, 64, err))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
     GemmArgs args{};
     args.sched = ctx->sched;
     args.x = x;
@@ -635,10 +639,18 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
     args.hidden = H;
     args.inter = I;
     args.n_routed_local = ctx->local_experts;
-    LM_CUDA(ctx, launch_gemm_gate_up(bn, L.map_w13, ctx->map_xperm[bi], map_x, args, ctx->sms, s, true));
-    prof_mark(ctx, 5, s);
-    slots[n_slots++] = 5;
-    LM_CUDA(ctx, launch_gemm_down(bn, L.map_w2, ctx->map_h[bi], args, ctx->sms, s, true));
+    if (pair) {
+        const int hi = bn_index(bn / 2);
+        LM_CUDA(ctx, launch_gemm_gate_up_pair(bn, L.map_w13, ctx->map_xperm[hi], map_x, args, ctx->sms, s, true));
+        prof_mark(ctx, 5, s);
+        slots[n_slots++] = 5;
+        LM_CUDA(ctx, launch_gemm_down_pair(bn, L.map_w2, ctx->map_h[hi], args, ctx->sms, s, true));
+    } else {
+        LM_CUDA(ctx, launch_gemm_gate_up(bn, L.map_w13, ctx->map_xperm[bi], map_x, args, ctx->sms, s, true));
+        prof_mark(ctx, 5, s);
+        slots[n_slots++] = 5;
+        LM_CUDA(ctx, launch_gemm_down(bn, L.map_w2, ctx->map_h[bi], args, ctx->sms, s, true));
+    }
     prof_mark(ctx, 6, s);
     slots[n_slots++] = 6;
     return prof_end(ctx, slots, n_slots);
@@ -750,9 +762,10 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     // 4. Local experts on the received rows, shared experts on this rank's tokens.
     CUtensorMap map_x{};
     std::string err;
+    const bool pair = bn == 256;
     // A rank without tokens still serves its experts; its (unread) token map points
     // at a workspace buffer.
-    if (!encode_tensor_map_bf16(&map_x, T > 0 ? x : ctx->x_perm, std::max(T, 1), H, bn, 64, err))
+    if (!encode_tensor_map_bf16(&map_x, T > 0 ? x : ctx->x_perm, std::max(T, 1), H, pair ? bn / 2 : bn, 64, err))
         return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
     GemmArgs args{};
     args.sched = ctx->sched_ep;
@@ -767,10 +780,18 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     args.hidden = H;
     args.inter = I;
     args.n_routed_local = n_routed;
-    LM_CUDA(ctx, launch_gemm_gate_up(bn, L.map_w13, ctx->map_xrecv[bi], map_x, args, ctx->sms, s, false));
-    prof_mark(ctx, 5, s);
-    slots[n_slots++] = 5;
-    LM_CUDA(ctx, launch_gemm_down(bn, L.map_w2, ctx->map_h[bi], args, ctx->sms, s, true));
+    if (pair) {
+        const int hi = bn_index(bn / 2);
+        LM_CUDA(ctx, launch_gemm_gate_up_pair(bn, L.map_w13, ctx->map_xrecv[hi], map_x, args, ctx->sms, s, false));
+        prof_mark(ctx, 5, s);
+        slots[n_slots++] = 5;
+        LM_CUDA(ctx, launch_gemm_down_pair(bn, L.map_w2, ctx->map_h[hi], args, ctx->sms, s, true));
+    } else {
+        LM_CUDA(ctx, launch_gemm_gate_up(bn, L.map_w13, ctx->map_xrecv[bi], map_x, args, ctx->sms, s, false));
+        prof_mark(ctx, 5, s);
+        slots[n_slots++] = 5;
+        LM_CUDA(ctx, launch_gemm_down(bn, L.map_w2, ctx->map_h[bi], args, ctx->sms, s, true));
+    }
     prof_mark(ctx, 6, s);
     slots[n_slots++] = 6;
     // 5. Outputs back to the tokens' ranks, then the weighted combine.

@@ -104,6 +104,14 @@ cudaError_t launch_gemm_router(int bn, const CUtensorMap& wcat, const CUtensorMa
 cudaError_t launch_gemm_down(int bn, const CUtensorMap& w2, const CUtensorMap& hmap, const GemmArgs& args,
                              int sms, cudaStream_t stream, bool pdl);
 
+// The same two GEMMs on CTA pairs (tcgen05 cta_group::2, 256-row weight tiles) for
+// prefill-sized token tiles (grouped_gemm_pair.cu).  Token maps have boxes of bn/2 rows.
+cudaError_t launch_gemm_gate_up_pair(int bn, const CUtensorMap& w13, const CUtensorMap& xperm_half,
+                                     const CUtensorMap& x_half, const GemmArgs& args, int sms, cudaStream_t stream,
+                                     bool pdl);
+cudaError_t launch_gemm_down_pair(int bn, const CUtensorMap& w2, const CUtensorMap& h_half, const GemmArgs& args,
+                                  int sms, cudaStream_t stream, bool pdl);
+
 // gemm:: mirror kernels and row kernels (gemm_ops.cu).
 cudaError_t launch_rms_norm_rows(const float* in, float* out_f32, uint16_t* out_bf16, const float* weight,
                                  int rows, int count, float eps, cudaStream_t stream);
