@@ -66,6 +66,41 @@ __device__ __forceinline__ int find_segment(const int* tiles, int n_seg, int til
     return lo;
 }
 
+// Every role of a CTA walks the same list of work units (tile, k-blocks [kb0, kb1)).
+// Unsplit: whole tiles, blockIdx.x + i * gridDim.x.  Split ("stream-K"): the
+// tiles' k-block iterations laid end to end and cut into gridDim.x equal
+// contiguous ranges, so a launch of few tiles keeps every SM streaming weights
+// instead of leaving a part-empty last wave.
+struct UnitWalk {
+    int64_t it, end;  // split: this CTA's iteration range
+    int tile;         // unsplit: next tile
+    int total, num_kb;
+    bool split;
+    __device__ UnitWalk(bool split_, int total_tiles, int num_kb_)
+        : tile(blockIdx.x), total(total_tiles), num_kb(num_kb_), split(split_) {
+        const int64_t iters = static_cast<int64_t>(total_tiles) * num_kb_;
+        it = iters * blockIdx.x / gridDim.x;
+        end = iters * (blockIdx.x + 1) / gridDim.x;
+    }
+    __device__ bool next(int& t, int& kb0, int& kb1) {
+        if (!split) {
+            if (tile >= total) return false;
+            t = tile;
+            kb0 = 0;
+            kb1 = num_kb;
+            tile += gridDim.x;
+            return true;
+        }
+        if (it >= end) return false;
+        t = static_cast<int>(it / num_kb);
+        kb0 = static_cast<int>(it - static_cast<int64_t>(t) * num_kb);
+        const int64_t left = end - it;
+        kb1 = left < num_kb - kb0 ? kb0 + static_cast<int>(left) : num_kb;
+        it += kb1 - kb0;
+        return true;
+    }
+};
+
 __device__ __forceinline__ float silu_times(float g, float u) {
     // src/Gemm.cpp:225-231: value / (1 + exp(-value)) * up, with fast exp and
     // divide: the result is rounded to bf16 (8 significant bits) right after.
@@ -87,6 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ int s_wslot[kMaxSegments];
     __shared__ int s_n_seg;
     __shared__ int s_epi_go[2];
+    __shared__ int s_split_last;
     constexpr int kMapCols = (KIND == Kind::Down) ? BN : 1;
     __shared__ int s_ep_tok[2][kMapCols];  // down epilogue: this tile's token and routing weight per column
     __shared__ float s_ep_w[2][kMapCols];
@@ -166,6 +202,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int x_kb = args.hidden / kBlockK;
     const int rows_a = (KIND == Kind::GateUp) ? 2 * args.inter : (KIND == Kind::Down) ? args.hidden : kBlockM;
     const int mb_per = rows_a / kBlockM;
+    // Down partial sums add into y like whole tiles (the combine is linear), unless
+    // rows are stored unweighted for expert parallelism; gate/up partial sums need
+    // the workspace.
+    const bool split = total_tiles > 0 && total_tiles < args.split_max_waves * static_cast<int>(gridDim.x) &&
+                       ((KIND == Kind::Down && args.y_rows == nullptr) ||
+                        (KIND == Kind::GateUp && args.split_ws != nullptr && total_tiles <= kSplitTickets &&
+                         static_cast<int64_t>(2 * gridDim.x) * kBlockM * BN <= args.split_ws_floats));
 
     if (warp == 0) {
         if (lane == 0) {
@@ -175,7 +218,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t issued_mask = 0;
             uint32_t issued_phase = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+            UnitWalk walk(split, total_tiles, num_kb);
+            int tile, kb0, kb1;
+            while (ok && walk.next(tile, kb0, kb1)) {
                 const int s = find_segment(s_tiles, n_seg, tile);
                 const int local = tile - s_tiles[s];
                 const int nb = local / mb_per;
@@ -189,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     (KIND == Kind::Router) || ((KIND == Kind::GateUp) && s >= args.n_routed_local);
                 const int b_row = from_x ? nb * BN : s_off[s] + nb * BN;
                 const CUtensorMap* bmap = from_x ? &map_x : &map_b;
-                for (int kb = 0; kb < num_kb; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status, kDevTimeoutProducer)) {
                         ok = false;
                         break;
@@ -224,11 +269,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t acc_phase = 0;
             bool ok = true;
             bool issued_any = false;
-            for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+            UnitWalk walk(split, total_tiles, num_kb);
+            int tile, kb0, kb1;
+            while (ok && walk.next(tile, kb0, kb1)) {
                 if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, args.status, kDevTimeoutMma)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = 0; kb < num_kb; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag, args.status, kDevTimeoutMma)) {
                         ok = false;
                         break;
@@ -239,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < kBlockK / 16; ++kk) {
                         // +32 bytes per 16-element K step inside the swizzle atom (>> 4 in the descriptor).
-                        umma_bf16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, kIdesc, (kb | kk) != 0);
+                        umma_bf16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, kIdesc, (kb != kb0) || (kk != 0));
                     }
                     issued_any = true;
                     umma_commit(&empty[stage]);
@@ -270,7 +317,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         int iter = 0;
-        for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++iter) {
+        UnitWalk walk(split, total_tiles, num_kb);
+        int tile, kb0, kb1;
+        for (; walk.next(tile, kb0, kb1); ++iter) {
             const int s = find_segment(s_tiles, n_seg, tile);
             const int local = tile - s_tiles[s];
             const int nb = local / mb_per;
@@ -320,6 +369,66 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tmem_empty[acc]);
             } else if constexpr (KIND == Kind::GateUp) {
+                if (kb0 != 0 || kb1 != num_kb) {
+                    // Part of the tile's k-blocks.  Each CTA owns two workspace slots
+                    // (its range's first and last unit -- the only ones that can be
+                    // partial); it stores the partial gate/up sums there and counts
+                    // the k-blocks.  The CTA that completes the tile sums the parts in
+                    // CTA order -- the same order whichever CTA finishes last, so the
+                    // result is deterministic -- and applies SiLU.
+                    const int slot = 2 * static_cast<int>(blockIdx.x) + (iter == 0 ? 0 : 1);
+                    float* wt = args.split_ws + static_cast<size_t>(slot) * (kBlockM * BN);
+                    const int row = quad * 32 + lane;
+#pragma unroll 1
+                    for (int c0 = 16 * half; c0 < BN; c0 += 32) {
+                        if (c0 >= valid) break;
+                        uint32_t r[16];
+                        tmem_ld16(t_row + c0, r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (c0 + j < valid) __stcg(wt + (c0 + j) * kBlockM + row, __uint_as_float(r[j]));
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+                    __threadfence();
+                    named_bar_sync(1, kEpiThreads);
+                    if (epi_tid == 0)
+                        s_split_last = atomicAdd(args.split_ticket + tile, kb1 - kb0) + (kb1 - kb0) == num_kb;
+                    named_bar_sync(1, kEpiThreads);
+                    if (s_split_last) {
+                        __threadfence();
+                        const int64_t iters = static_cast<int64_t>(total_tiles) * num_kb;
+                        const int G = gridDim.x;
+                        const int64_t j0 = static_cast<int64_t>(tile) * num_kb;
+                        // CTA owning iteration j: the largest c with iters * c / G <= j.
+                        const int c_lo = static_cast<int>(((j0 + 1) * G + iters - 1) / iters) - 1;
+                        const int c_hi = static_cast<int>(((j0 + num_kb) * G + iters - 1) / iters) - 1;
+                        for (int q = epi_tid; q < valid * 64; q += kEpiThreads) {
+                            const int c = q >> 6;
+                            const int i = q & 63;
+                            float g = 0.0f, u = 0.0f;
+                            for (int cta = c_lo; cta <= c_hi; ++cta) {
+                                const int64_t b = iters * cta / G;
+                                if (iters * (cta + 1) / G == b) continue;  // empty range
+                                const int sl = 2 * cta + (b >= j0 ? 0 : 1);
+                                const float2 v = __ldcg(reinterpret_cast<const float2*>(
+                                    args.split_ws + static_cast<size_t>(sl) * (kBlockM * BN) + c * kBlockM + 2 * i));
+                                g += v.x;
+                                u += v.y;
+                            }
+                            reinterpret_cast<__nv_bfloat16*>(args.h)[static_cast<size_t>(row0 + c) * args.inter +
+                                                                     mb * 64 + i] = __float2bfloat16_rn(silu_times(g, u));
+                        }
+                        if (epi_tid == 0) args.split_ticket[tile] = 0;
+                    }
+                    if (++acc == 2) {
+                        acc = 0;
+                        acc_phase ^= 1u;
+                    }
+                    continue;
+                }
                 __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(staging);
                 const int i_local = (quad * 32 + lane) >> 1;  // h column within the tile's 64
 #pragma unroll 1

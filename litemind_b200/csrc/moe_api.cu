@@ -18,6 +18,7 @@
 #include "nccl_dl.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <memory>
@@ -74,6 +75,9 @@ struct lm_moe_ctx {
     uint16_t* x_perm = nullptr;      // routed token rows in expert-sorted order
     uint16_t* h = nullptr;
     int32_t* status = nullptr;
+    int split_max_waves = 4;          // split-K below this many waves of tiles (LITEMIND_B200_SPLIT_WAVES)
+    float* split_ws = nullptr;        // gate/up split-K partial tiles
+    int32_t* split_ticket = nullptr;  // k-blocks done per split tile, zero between uses
     unsigned int* ticket = nullptr;  // last-CTA ticket of the fused small-T route kernel
     CUtensorMap map_xperm[5]{};
     CUtensorMap map_h[5]{};
@@ -342,6 +346,7 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
     if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return LM_ERR_CUDA;
     if (prop.major != 10) return LM_ERR_UNSUPPORTED;  // built for sm_100a only
     ctx->sms = prop.multiProcessorCount;
+    if (const char* w = std::getenv("LITEMIND_B200_SPLIT_WAVES")) ctx->split_max_waves = std::max(0, std::atoi(w));
     ctx->local_experts = c.n_routed_experts;
     ctx->n_seg = ctx->local_experts + c.n_shared_experts;
     ctx->routed_cap = c.max_tokens * c.num_experts_per_tok;
@@ -359,14 +364,18 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
         (st = alloc(p, &p->sched, 1)) || (st = alloc(p, &p->row_token, static_cast<size_t>(p->routed_cap))) ||
         (st = alloc(p, &p->row_weight, static_cast<size_t>(p->routed_cap))) || (st = alloc(p, &p->slot_row, T * K)) ||
         (st = alloc(p, &p->x_perm, static_cast<size_t>(p->routed_cap) * H)) || (st = alloc(p, &p->h, h_rows * I)) ||
-        (st = alloc(p, &p->status, 1)) || (st = alloc(p, &p->ticket, 1))) {
+        (st = alloc(p, &p->status, 1)) || (st = alloc(p, &p->ticket, 1)) ||
+        (st = alloc(p, &p->split_ws, kSplitWsBytes / sizeof(float))) ||
+        (st = alloc(p, &p->split_ticket, static_cast<size_t>(kSplitTickets)))) {
         lm_moe_destroy(ctx.release());
         return st;
     }
     if (cudaMemset(p->status, 0, sizeof(int32_t)) != cudaSuccess ||
         cudaMemset(p->ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
         cudaMemset(p->expert_totals, 0, E * sizeof(int32_t)) != cudaSuccess ||
-        cudaMemset(p->sched, 0, sizeof(Schedule)) != cudaSuccess) {
+        cudaMemset(p->sched, 0, sizeof(Schedule)) != cudaSuccess ||
+        cudaMemset(p->split_ws, 0, kSplitWsBytes) != cudaSuccess ||
+        cudaMemset(p->split_ticket, 0, kSplitTickets * sizeof(int32_t)) != cudaSuccess) {
         lm_moe_destroy(ctx.release());
         return LM_ERR_CUDA;
     }
@@ -639,6 +648,10 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
     args.hidden = H;
     args.inter = I;
     args.n_routed_local = ctx->local_experts;
+    args.split_ws = ctx->split_ws;
+    args.split_ticket = ctx->split_ticket;
+    args.split_ws_floats = static_cast<int32_t>(kSplitWsBytes / sizeof(float));
+    args.split_max_waves = ctx->split_max_waves;
     if (pair) {
         const int hi = bn_index(bn / 2);
         LM_CUDA(ctx, launch_gemm_gate_up_pair(bn, L.map_w13, ctx->map_xperm[hi], map_x, args, ctx->sms, s, true));
@@ -780,6 +793,10 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     args.hidden = H;
     args.inter = I;
     args.n_routed_local = n_routed;
+    args.split_ws = ctx->split_ws;
+    args.split_ticket = ctx->split_ticket;
+    args.split_ws_floats = static_cast<int32_t>(kSplitWsBytes / sizeof(float));
+    args.split_max_waves = ctx->split_max_waves;
     if (pair) {
         const int hi = bn_index(bn / 2);
         LM_CUDA(ctx, launch_gemm_gate_up_pair(bn, L.map_w13, ctx->map_xrecv[hi], map_x, args, ctx->sms, s, false));

@@ -94,7 +94,20 @@ struct GemmArgs {
     const float* bias;         // router kind: per-expert logit bias or null
     int32_t experts;           // router kind: experts (<= 128)
     int32_t n_routed_local;    // segments [0, n_routed_local) are routed experts
+    // Split-K ("stream-K") for launches of few tiles: a CTA whose k-block range
+    // cuts a gate/up tile stores its partial sums in split_ws slot 2 * cta (its
+    // first unit) or 2 * cta + 1 (its last), [BN][128] f32 each, and counts
+    // k-blocks in split_ticket[tile] (zero between uses); the CTA that completes
+    // the tile sums the slots in CTA order and applies SiLU.  Null split_ws: no
+    // split for gate/up.
+    float* split_ws;
+    int32_t* split_ticket;
+    int32_t split_ws_floats;   // capacity of split_ws in floats
+    int32_t split_max_waves;   // split when the tiles fill fewer waves of the grid than this (0: never)
 };
+// Split-K workspace for gate/up partial tiles (bytes) and its ticket count.
+constexpr size_t kSplitWsBytes = size_t(32) << 20;
+constexpr int kSplitTickets = 4096;
 cudaError_t launch_gemm_gate_up(int bn, const CUtensorMap& w13, const CUtensorMap& xperm, const CUtensorMap& x,
                                 const GemmArgs& args, int sms, cudaStream_t stream, bool pdl);
 // Router logits on tensor cores: wcat is [128, 3*hidden] bf16 (the f32 router
