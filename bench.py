@@ -23,6 +23,10 @@ from HBM.
              reference's sources) on the host's cores, rank 0, N=1 only
 --impl reference: the reference CPU path alone, same metric and config.
 
+--workload prefill: T=16384 tokens (seed 2) with a per-expert
+logit bias that skews expert load to Zipf(1.2); the roofline is tensor-bound
+(FLOPs against the measured dense bf16 peak).  --workload stack: config 4.
+
 With N > 1 (torchrun, one rank per GPU) each rank runs the same per-rank workload
 (T tokens of its own) under expert parallelism: rank r holds routed experts
 [r*64/N, (r+1)*64/N) and the shared experts, and every forward exchanges token rows
@@ -47,6 +51,7 @@ if ROOT not in sys.path:
 METRIC = "MoE-layer tokens/s (V2-Lite shape) + % HBM/TC roofline at 1/2/4/8 B200"
 SEED_WEIGHTS = 0
 SEED_TOKENS = 1
+SEED_PREFILL = 2  # config 2: tokens and the Zipf logit bias
 SWEEP = (1, 8, 32, 256)
 FLUSH_BYTES = 256 << 20
 
@@ -65,10 +70,11 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=None,
-                    help="tokens per rank per step (default 32 for decode, 4096 for stack)")
-    ap.add_argument("--workload", choices=["decode", "stack"], default="decode",
-                    help="decode: one MoE layer (BASELINE config 1, headline); stack: 26 x (RMSNorm, MoE, "
-                         "residual) (BASELINE config 4)")
+                    help="tokens per rank per step (default 32 for decode, 16384 for prefill, 4096 for stack)")
+    ap.add_argument("--workload", choices=["decode", "prefill", "stack"], default="decode",
+                    help="decode: one MoE layer (BASELINE config 1, headline); prefill: one layer at 16384 "
+                         "tokens with Zipf expert load (config 2, tensor-bound); stack: 26 x (RMSNorm, MoE, "
+                         "residual) (config 4)")
     ap.add_argument("--layers", type=int, default=26, help="blocks in the stack workload")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-sweep", action="store_true")
@@ -159,6 +165,18 @@ def layer_bytes(shape, touched_experts: int, T: int) -> int:
             + T * shape.hidden * (2 + 4))
 
 
+def layer_flops(shape, T: int) -> int:
+    """Algorithmic FLOPs of one layer forward: router, top-k experts and shared experts."""
+    per_token = 2 * shape.n_routed_experts * shape.hidden + 3 * 2 * shape.inter * shape.hidden * (
+        shape.top_k + shape.n_shared_experts)
+    return per_token * T
+
+
+def gate_up_flops(shape, T: int) -> int:
+    """Algorithmic FLOPs of one gate/up GEMM launch (gate and up rows of the top-k and shared experts)."""
+    return 2 * (2 * shape.inter) * shape.hidden * (shape.top_k + shape.n_shared_experts) * T
+
+
 def gate_up_bytes(shape, touched_experts: int, T: int) -> int:
     """Algorithmic bytes of one gate/up GEMM launch: gate and up of every touched
     expert and of the shared experts, plus the token activations."""
@@ -167,7 +185,7 @@ def gate_up_bytes(shape, touched_experts: int, T: int) -> int:
 
 # ── reference CPU path ────────────────────────────────────────────────────
 
-def cpu_reference_rate(weights, x_f32, seconds: float, min_reps: int = 1, max_reps: int = 1000):
+def cpu_reference_rate(weights, x_f32, seconds: float, min_reps: int = 1, max_reps: int = 1000, bias=None):
     """tokens/s of the reference's own MoE block (oracle/_ref) on all host threads."""
     from oracle.oracle import Reference, RouterConfig
 
@@ -175,10 +193,10 @@ def cpu_reference_rate(weights, x_f32, seconds: float, min_reps: int = 1, max_re
     threads = ref.hardware_threads()
     cfg = RouterConfig()
     T = x_f32.shape[0]
-    ref.moe_layer(x_f32[:1], weights, cfg, 2, threads=threads)  # warm the pool and page in the weights
+    ref.moe_layer(x_f32[:1], weights, cfg, 2, bias=bias, threads=threads)  # warm the pool, page in the weights
     reps, t0 = 0, time.perf_counter()
     while reps < min_reps or (time.perf_counter() - t0 < seconds and reps < max_reps):
-        ref.moe_layer(x_f32, weights, cfg, 2, threads=threads)
+        ref.moe_layer(x_f32, weights, cfg, 2, bias=bias, threads=threads)
         reps += 1
     dt = time.perf_counter() - t0
     return {"value": T * reps / dt, "unit": "tokens/s", "cores": threads, "kind": "reference",
@@ -192,26 +210,31 @@ def run_reference_arm(args, rank: int, world: int) -> None:
     from litemind_b200 import synthetic as syn
 
     W = syn.layer_weights(syn.V2_LITE, seed=SEED_WEIGHTS)
-    x = syn.bf16_to_f32(syn.tokens(syn.V2_LITE, args.tokens, seed=SEED_TOKENS)).reshape(args.tokens, -1)
+    prefill = args.workload == "prefill"
+    # Prefill: each step is a bounded 128-token sample of the 16384-token batch.
+    n = min(args.tokens, 128) if prefill else args.tokens
+    x = syn.bf16_to_f32(syn.tokens(syn.V2_LITE, args.tokens, seed=SEED_PREFILL if prefill else SEED_TOKENS))
+    x = x.reshape(args.tokens, -1)[:n]
+    bias = syn.zipf_bias(syn.V2_LITE, seed=SEED_PREFILL) if prefill else None
     from oracle.oracle import Reference, RouterConfig
 
     ref = Reference()
     threads = ref.hardware_threads()
     for _ in range(max(args.warmup, 0)):
-        ref.moe_layer(x[:1], W, RouterConfig(), 2, threads=threads)
+        ref.moe_layer(x[:1], W, RouterConfig(), 2, bias=bias, threads=threads)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        ref.moe_layer(x, W, RouterConfig(), 2, threads=threads)
+        ref.moe_layer(x, W, RouterConfig(), 2, bias=bias, threads=threads)
         times.append(time.perf_counter() - t0)
     ms = 1e3 * sum(times) / len(times)
-    value = args.tokens / (ms / 1e3)
+    value = n / (ms / 1e3)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(args, world),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
-                         "sample": f"{args.steps} steps of one {args.tokens}-token batch on rank 0's host "
+                         "sample": f"{args.steps} steps of one {n}-token batch on rank 0's host "
                                    f"({ref.kernel_description()})"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -219,8 +242,12 @@ def run_reference_arm(args, rank: int, world: int) -> None:
 
 
 def workload_config(args, world: int) -> dict:
-    return {"workload": "config1-decode: V2-Lite MoE layer, tokens per rank per step", "tokens_per_rank": args.tokens,
-            "global_tokens": args.tokens * world, "seed_weights": SEED_WEIGHTS, "seed_tokens": SEED_TOKENS,
+    prefill = args.workload == "prefill"
+    name = ("config2-prefill: V2-Lite MoE layer, Zipf(1.2) expert load from a per-expert logit bias, tokens per "
+            "rank per step" if prefill else "config1-decode: V2-Lite MoE layer, tokens per rank per step")
+    return {"workload": name, "tokens_per_rank": args.tokens,
+            "global_tokens": args.tokens * world, "seed_weights": SEED_WEIGHTS,
+            "seed_tokens": SEED_PREFILL if prefill else SEED_TOKENS,
             "experts": "64 routed top-6 + 2 shared, hidden 2048, inter 1408",
             "l2": "flushed before every timed step (256 MiB write), outside the step's events",
             "parallelism": "single GPU" if world == 1 else
@@ -229,7 +256,7 @@ def workload_config(args, world: int) -> dict:
 
 # ── our arm ───────────────────────────────────────────────────────────────
 
-def time_forward(layer, x, y, flush, steps: int, torch):
+def time_forward(layer, x, y, flush, steps: int, torch, bias=None):
     """Per-step CUDA-event time (ms) of layer.forward, L2 flushed before each step."""
     total = 0.0
     start = torch.cuda.Event(enable_timing=True)
@@ -237,7 +264,7 @@ def time_forward(layer, x, y, flush, steps: int, torch):
     for _ in range(steps):
         flush.zero_()
         start.record()
-        layer.forward(0, x, y=y)
+        layer.forward(0, x, y=y, bias=bias)
         end.record()
         end.synchronize()
         total += start.elapsed_time(end)
@@ -327,7 +354,7 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> int:
 def main(argv=None) -> int:
     args = parse_args(argv)
     if args.tokens is None:
-        args.tokens = 32 if args.workload == "decode" else 4096
+        args.tokens = {"decode": 32, "prefill": 16384, "stack": 4096}[args.workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -371,13 +398,16 @@ def main(argv=None) -> int:
         dist.broadcast_object_list(uid, src=0)
         layer.ep_init(uid[0], rank, world)
     layer.upload_layer(0, W)
-    x_bits = syn.tokens(shape, T, seed=SEED_TOKENS, stream=rank)
+    prefill = args.workload == "prefill"
+    x_bits = syn.tokens(shape, T, seed=SEED_PREFILL if prefill else SEED_TOKENS, stream=rank)
     x = bf16_tensor(x_bits)
+    bias_np = syn.zipf_bias(shape, seed=SEED_PREFILL) if prefill else None
+    bias = torch.from_numpy(bias_np).cuda() if prefill else None
     y = torch.empty((T, shape.hidden), dtype=torch.float32, device="cuda")
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
 
     for _ in range(max(args.warmup, 3)):
-        layer.forward(0, x, y=y)
+        layer.forward(0, x, y=y, bias=bias)
     layer.sync()
     # Experts whose weights this GPU streams: the touched ones on one GPU; with
     # expert parallelism every local expert (all are hit at >= 32 tokens per rank).
@@ -390,16 +420,16 @@ def main(argv=None) -> int:
     clocks.start()
     t_load = time.perf_counter()
     while time.perf_counter() - t_load < args.clock_window:
-        for _ in range(20):
+        for _ in range(20 if not prefill else 2):
             flush.zero_()
-            layer.forward(0, x, y=y)
+            layer.forward(0, x, y=y, bias=bias)
         torch.cuda.synchronize()
 
     # ── timed region: K steps, barrier + synchronize on both sides ──
     barrier()
     torch.cuda.synchronize()
     wall0 = time.perf_counter()
-    ms = time_forward(layer, x, y, flush, args.steps, torch)
+    ms = time_forward(layer, x, y, flush, args.steps, torch, bias=bias)
     torch.cuda.synchronize()
     barrier()
     wall = time.perf_counter() - wall0
@@ -413,7 +443,7 @@ def main(argv=None) -> int:
     layer.profile_read(reset=True)
     for _ in range(args.steps):
         flush.zero_()
-        layer.forward(0, x, y=y)
+        layer.forward(0, x, y=y, bias=bias)
     prof = layer.profile_read(reset=True)
     layer.profile(False)
     peaks = measured_peaks()
@@ -431,18 +461,32 @@ def main(argv=None) -> int:
     lb = layer_bytes(shape, touched, T)
     layer_roofline = {"bytes": lb, "achieved": lb / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                       "frac": lb / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "touched_experts": touched}
+    if prefill:
+        # Tensor-bound: FLOPs against the measured dense bf16 burst peak (the launch is
+        # timed alone, milliseconds long).
+        gu_f = gate_up_flops(shape, T)
+        tf = gu_f / (gu_avg / 1e3) / 1e12 if gu_avg > 0 else 0.0
+        roofline.update({"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tf / peaks["bf16_tflops"], "peak_source": f"{peaks['source']} (bf16_tflops)",
+                         "flops_per_launch": gu_f, "bytes_per_launch": None})
+        lf = layer_flops(shape, T)
+        layer_roofline = {"flops": lf, "achieved": lf / (ms / 1e3) / 1e12, "peak": peaks["bf16_tflops"],
+                          "unit": "TFLOP/s", "frac": lf / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+                          "expert_rows": [int(v) for v in layer.expert_counts()]}
 
     # ── end to end through the C ABI with host buffers ──
     x_host = torch.from_numpy(x_bits.view(np.int16)).pin_memory()
     y_host = torch.empty((T, shape.hidden), dtype=torch.float32).pin_memory()
-    layer.forward_host_ptr(0, x_host.data_ptr(), T, y_host.data_ptr())
+    bias_host = torch.from_numpy(bias_np).pin_memory() if prefill else None
+    bias_ptr = bias_host.data_ptr() if prefill else None
+    layer.forward_host_ptr(0, x_host.data_ptr(), T, y_host.data_ptr(), bias_ptr)
     e2e_total = 0.0
     barrier()
     for _ in range(args.steps):
         flush.zero_()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        layer.forward_host_ptr(0, x_host.data_ptr(), T, y_host.data_ptr())
+        layer.forward_host_ptr(0, x_host.data_ptr(), T, y_host.data_ptr(), bias_ptr)
         e2e_total += time.perf_counter() - t0
     e2e_ms = max_over_ranks(1e3 * e2e_total / args.steps)
     e2e = {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
@@ -451,7 +495,7 @@ def main(argv=None) -> int:
 
     # ── decode sweep (config 1) ──
     sweep = []
-    if not args.no_sweep and world == 1:
+    if not args.no_sweep and world == 1 and not prefill:
         for t in SWEEP:
             xs = bf16_tensor(syn.tokens(shape, t, seed=SEED_TOKENS, stream=rank))
             ys = torch.empty((t, shape.hidden), dtype=torch.float32, device="cuda")
@@ -467,7 +511,8 @@ def main(argv=None) -> int:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         xf = syn.bf16_to_f32(x_bits).reshape(T, -1)
-        cpu = cpu_reference_rate(W, xf, args.cpu_seconds)
+        # Prefill: a bounded 256-token sample of the same batch, per-token rate.
+        cpu = cpu_reference_rate(W, xf[:256] if prefill else xf, args.cpu_seconds, bias=bias_np)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
