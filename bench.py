@@ -9,9 +9,10 @@ f32, softmax top-6, no renormalisation -- with weights N(0, 0.02) seed 0 and
 activations N(0, 1) bf16 seed 1.  A step is one forward of the layer over T tokens
 (default 32, the decode batch the north star's HBM target names); the sweep
 T in {1, 8, 32, 256} is reported under "sweep".  Weights and activations are
-synthetic (no checkpoint exists on the box).  L2 is flushed (a 256 MiB write)
-before every timed step, outside its events, so each step streams its experts
-from HBM.
+synthetic (no checkpoint exists on the box).  L2 is flushed before every timed
+step, outside its events: a 256 MiB write, then a 256 MiB read of another buffer,
+so each step starts with a cold and clean L2 (no dirty lines of the flush left to
+write back inside the step) and streams its experts from HBM.
 
 --impl ours (default): the CUDA path through liblitemind_b200.so.
   value      tokens/s over all ranks, device time from CUDA events per step
@@ -57,9 +58,12 @@ FLUSH_BYTES = 256 << 20
 
 
 def kernels_per_forward(tokens: int, world: int) -> int:
-    """Our kernel launches in one forward: the fused route (T <= 32) or logits, top-k,
-    scan and place; the row gather; the two grouped GEMMs; and, with expert
-    parallelism, the combine (NCCL's own kernels are not counted)."""
+    """Our kernel launches in one forward.  One GPU, T <= 32: the fused decode kernel
+    alone.  Otherwise: router logits, top-k, scan and place (or, with expert
+    parallelism at T <= 32, the fused route kernel); the row gather; the two grouped
+    GEMMs; and with expert parallelism the combine (NCCL's own kernels not counted)."""
+    if world == 1 and tokens <= 32:
+        return 1
     route = 1 if tokens <= 32 else 4
     return route + 1 + 2 + (1 if world > 1 else 0)
 
@@ -249,12 +253,26 @@ def workload_config(args, world: int) -> dict:
             "global_tokens": args.tokens * world, "seed_weights": SEED_WEIGHTS,
             "seed_tokens": SEED_PREFILL if prefill else SEED_TOKENS,
             "experts": "64 routed top-6 + 2 shared, hidden 2048, inter 1408",
-            "l2": "flushed before every timed step (256 MiB write), outside the step's events",
+            "l2": "flushed before every timed step (256 MiB write, then 256 MiB read of a second buffer: cold, "
+                  "clean L2), outside the step's events",
             "parallelism": "single GPU" if world == 1 else
             f"expert parallel: {64 // world} routed experts per GPU, NCCL all-to-all dispatch/combine"}
 
 
 # ── our arm ───────────────────────────────────────────────────────────────
+
+class L2Flush:
+    """Evicts L2 between steps: writes one buffer larger than L2, then reads another,
+    so the next step starts from a cold L2 that holds no dirty lines."""
+
+    def __init__(self, torch, nbytes: int = FLUSH_BYTES):
+        self.w = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        self.r = torch.zeros(nbytes // 8, dtype=torch.int64, device="cuda")
+
+    def __call__(self):
+        self.w.zero_()
+        self.r.sum()
+
 
 def time_forward(layer, x, y, flush, steps: int, torch, bias=None):
     """Per-step CUDA-event time (ms) of layer.forward, L2 flushed before each step."""
@@ -262,7 +280,7 @@ def time_forward(layer, x, y, flush, steps: int, torch, bias=None):
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     for _ in range(steps):
-        flush.zero_()
+        flush()
         start.record()
         layer.forward(0, x, y=y, bias=bias)
         end.record()
@@ -298,7 +316,7 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> int:
     upload_s = time.perf_counter() - t_up
     x0 = torch.from_numpy(syn.bf16_to_f32(syn.tokens(shape, T, seed=4, stream=rank)).reshape(T, -1)).cuda()
     hidden = x0.clone()
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    flush = L2Flush(torch)
 
     def step():
         hidden.copy_(x0)
@@ -314,7 +332,7 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> int:
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     total = 0.0
     for _ in range(args.steps):
-        flush.zero_()
+        flush()
         start.record()
         step()
         end.record()
@@ -404,7 +422,7 @@ def main(argv=None) -> int:
     bias_np = syn.zipf_bias(shape, seed=SEED_PREFILL) if prefill else None
     bias = torch.from_numpy(bias_np).cuda() if prefill else None
     y = torch.empty((T, shape.hidden), dtype=torch.float32, device="cuda")
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    flush = L2Flush(torch)
 
     for _ in range(max(args.warmup, 3)):
         layer.forward(0, x, y=y, bias=bias)
@@ -421,7 +439,7 @@ def main(argv=None) -> int:
     t_load = time.perf_counter()
     while time.perf_counter() - t_load < args.clock_window:
         for _ in range(20 if not prefill else 2):
-            flush.zero_()
+            flush()
             layer.forward(0, x, y=y, bias=bias)
         torch.cuda.synchronize()
 
@@ -442,21 +460,30 @@ def main(argv=None) -> int:
     layer.profile(True)
     layer.profile_read(reset=True)
     for _ in range(args.steps):
-        flush.zero_()
+        flush()
         layer.forward(0, x, y=y, bias=bias)
     prof = layer.profile_read(reset=True)
     layer.profile(False)
     peaks = measured_peaks()
-    gu_ms, gu_n = prof.get("gemm_gate_up", (0.0, 0))
-    gu_avg = gu_ms / max(gu_n, 1)
-    gu_bytes = gate_up_bytes(shape, touched, T)
-    achieved = gu_bytes / (gu_avg / 1e3) / 1e9 if gu_avg > 0 else 0.0
     total_prof = sum(v[0] for v in prof.values())
-    roofline = {"bound": "hbm", "kernel": "gemm_gate_up (tcgen05 grouped GEMM, gate/up + SiLU epilogue)",
+    if "decode_fused" in prof:
+        # T <= 32 on one GPU: the whole layer is one launch (moe_decode_kernel); its
+        # algorithmic bytes are the layer's.
+        k_ms, k_n = prof["decode_fused"]
+        k_bytes = layer_bytes(shape, touched, T)
+        k_name = "moe_decode_kernel (fused route + tcgen05 gate/up + down + combine, one cooperative launch)"
+        k_traffic = committed_traffic(f"decode_fused_T{T}")
+    else:
+        k_ms, k_n = prof.get("gemm_gate_up", (0.0, 0))
+        k_bytes = gate_up_bytes(shape, touched, T)
+        k_name = "gemm_gate_up (tcgen05 grouped GEMM, gate/up + SiLU epilogue)"
+        k_traffic = committed_traffic(f"gemm_gate_up_T{T}")
+    gu_avg = k_ms / max(k_n, 1)
+    achieved = k_bytes / (gu_avg / 1e3) / 1e9 if gu_avg > 0 else 0.0
+    roofline = {"bound": "hbm", "kernel": k_name,
                 "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} (hbm_gbs)",
-                "bytes_per_launch": gu_bytes, "mean_launch_ms": gu_avg,
-                "traffic": committed_traffic(f"gemm_gate_up_T{T}"),
+                "bytes_per_launch": k_bytes, "mean_launch_ms": gu_avg, "traffic": k_traffic,
                 "share_of_step": {k: round(v[0] / total_prof, 4) for k, v in prof.items()} if total_prof else {}}
     lb = layer_bytes(shape, touched, T)
     layer_roofline = {"bytes": lb, "achieved": lb / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -465,10 +492,14 @@ def main(argv=None) -> int:
         # Tensor-bound: FLOPs against the measured dense bf16 burst peak (the launch is
         # timed alone, milliseconds long).
         gu_f = gate_up_flops(shape, T)
+        gu_ms, gu_n = prof.get("gemm_gate_up", (0.0, 0))
+        gu_avg = gu_ms / max(gu_n, 1)
         tf = gu_f / (gu_avg / 1e3) / 1e12 if gu_avg > 0 else 0.0
         roofline.update({"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": tf / peaks["bf16_tflops"], "peak_source": f"{peaks['source']} (bf16_tflops)",
-                         "flops_per_launch": gu_f, "bytes_per_launch": None})
+                         "flops_per_launch": gu_f, "bytes_per_launch": None, "mean_launch_ms": gu_avg,
+                         "kernel": "gemm_gate_up (tcgen05 CTA-pair grouped GEMM, gate/up + SiLU epilogue)",
+                         "traffic": committed_traffic(f"gemm_gate_up_T{T}")})
         lf = layer_flops(shape, T)
         layer_roofline = {"flops": lf, "achieved": lf / (ms / 1e3) / 1e12, "peak": peaks["bf16_tflops"],
                           "unit": "TFLOP/s", "frac": lf / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
@@ -483,7 +514,7 @@ def main(argv=None) -> int:
     e2e_total = 0.0
     barrier()
     for _ in range(args.steps):
-        flush.zero_()
+        flush()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         layer.forward_host_ptr(0, x_host.data_ptr(), T, y_host.data_ptr(), bias_ptr)

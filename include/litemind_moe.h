@@ -161,13 +161,23 @@ lm_status lm_moe_memory(const lm_moe_ctx* ctx, uint64_t* resident_bytes, uint64_
  * time to a per-slot total: slot 1 routing (the fused kernel for T <= 32, else the
  * router logits), 2 router top-k, 3 dispatch scan, 4 placement, 0 the copy of
  * token rows into expert order, 5 gate/up GEMM, 6 down GEMM, 7 expert-parallel
- * exchange.  lm_moe_profile_read copies LM_PROFILE_SLOTS totals (ms) and launch
+ * exchange, 8 the fused single-launch decode layer (T <= 32 on one GPU).
+ * lm_moe_profile_read copies LM_PROFILE_SLOTS totals (ms) and launch
  * counts to host memory and, when reset != 0, clears them.  No counterpart in the
  * reference, which has no device launches to time.
  */
-#define LM_PROFILE_SLOTS 8
+#define LM_PROFILE_SLOTS 9
 lm_status lm_moe_profile_enable(lm_moe_ctx* ctx, int32_t enable);
 lm_status lm_moe_profile_read(lm_moe_ctx* ctx, double* total_ms, int64_t* launches, int32_t reset);
+/* While profiling, the fused decode kernel (T <= 32 on one GPU) stamps each of its
+ * CTAs' phases with the device's global timer (ns): LM_DECODE_TRACE_SLOTS values
+ * per CTA (0 start, 1 logits written, 2 every CTA's logits seen, 3 schedule built,
+ * 4 gate/up epilogues done, 5 producer saw every h row, 6 producer done, 7 down
+ * epilogues done, 8 MMA done; 0 = not reached).  Copies the last
+ * launch's stamps for up to `ctas` CTAs and sets *ctas_out to the number of CTAs it
+ * ran with (0 if none was traced). */
+#define LM_DECODE_TRACE_SLOTS 16
+lm_status lm_moe_profile_trace(lm_moe_ctx* ctx, uint64_t* stamps, int32_t ctas, int32_t* ctas_out);
 
 /*
  * Expert parallelism over NCCL (NVLink within a node).  Every rank creates its

@@ -20,9 +20,10 @@ LM_ERR_DEVICE_TIMEOUT = 5
 LM_ERR_COMM = 6
 LM_ERR_UNSUPPORTED = 7
 
-LM_PROFILE_SLOTS = 8
+LM_PROFILE_SLOTS = 9
+LM_DECODE_TRACE_SLOTS = 16
 PROFILE_SLOT_NAMES = ["gather_rows", "route", "router_topk", "dispatch_scan", "place", "gemm_gate_up", "gemm_down",
-                      "ep_exchange"]
+                      "ep_exchange", "decode_fused"]
 
 LM_TOPK_GREEDY = 0
 LM_TOPK_GROUP_LIMITED_GREEDY = 1
@@ -75,6 +76,7 @@ SIGNATURES = {
     "lm_moe_ep_plan": (_i32, [_i32, _i32, _vp, _vp, C.POINTER(LmEpPlan)]),
     "lm_moe_profile_enable": (_i32, [_vp, _i32]),
     "lm_moe_profile_read": (_i32, [_vp, _vp, _vp, _i32]),
+    "lm_moe_profile_trace": (_i32, [_vp, _vp, _i32, _vp]),
     "lm_moe_route_static": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp]),
     "lm_gemm_matvec_bf16": (_i32, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "lm_gemm_matvec_bf16_accumulate": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp]),

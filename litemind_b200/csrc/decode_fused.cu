@@ -1,0 +1,776 @@
+// decode_fused.cu -- the whole MoE layer for decode-sized batches (T <= 32 tokens)
+// in one persistent, cooperative launch.
+//
+// At decode sizes the layer is a stream of expert weights (about 139 MB at T=1,
+// 1.1 GB at T=32) and every separate launch costs a ramp-up and a tail in which
+// HBM idles.  Here one CTA per SM runs the layer's steps back to back, each step
+// split evenly over all CTAs ("stream-K": a list's k-block iterations cut into
+// gridDim.x equal ranges), with two grid-wide arrival counters between them:
+//
+//   routing   every CTA: its share of the router logits (src/Gemm.cpp:132-137),
+//             issued before any weight streaming so the router rows see an idle
+//             HBM; after counter 0, every CTA reads all T x E logits into shared
+//             memory once and recomputes the whole routing identically: top-k
+//             (MoeRouter::select, src/MoeRouter.cpp:54-107), the expert histogram
+//             and the expert-sorted row order.  Meanwhile the producer prefetches
+//             the shared experts' gate/up weights (known before routing) into L2.
+//   gate/up   shared experts' tiles, then the routed experts'.  Their token operand
+//             is x itself (all T <= 32 tokens as the MMA's N): at decode sizes the
+//             tensor cores are idle anyway, and it spares a gather of token rows
+//             and a grid-wide wait for it; the epilogue keeps only the expert's own
+//             tokens' columns
+//   down      routed and shared experts.  Their h tiles wait for counter 1 (every
+//             CTA finished gate/up); their weight tiles are loaded before that, so
+//             the switch costs no HBM time
+//
+// Epilogues are the grouped GEMMs' (grouped_gemm.cu): h = silu(gate) * up in bf16
+// for gate/up (src/DeepSeekRunner.cpp:228-240), and the routing-weighted atomic add
+// into y for down (the weighted combine and un-permute of :273-288).  A gate/up tile
+// whose k-blocks two CTAs share is summed deterministically through the split
+// workspace (fixed CTA order); a shared down tile simply adds both parts into y.
+//
+// Warp roles as in the grouped GEMMs: warp 0 TMA producer, warp 1 tcgen05.mma
+// issuer, warps 2-9 routing and then the epilogue.  Every wait -- mbarriers and the
+// grid counters -- is bounded; an expired wait records a status code and the CTA
+// winds down, and CTAs that see a recorded status stop waiting too.
+#include "moe_internal.h"
+#include "ptx.cuh"
+#include "route_device.cuh"
+
+#include <cuda_bf16.h>
+
+namespace lm {
+namespace {
+
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 64 + kEpiThreads;
+constexpr int kBlockM = 128;
+constexpr int kBlockK = 64;
+constexpr int kATile = kBlockM * kBlockK * 2;
+constexpr int kMaxRows = kDecodeMaxTokens * kMaxTopK;
+constexpr int kDynBudget = 186 * 1024;  // leaves room for the static shared arrays below
+constexpr int kMaxPending = 16;
+constexpr int kReduceItems = 4;  // float4 items of a partial-tile reduction per thread (32 rows x 32 / 256)
+constexpr int kReduceParts = 4;  // CTAs' partial sums loaded together
+
+template <int BN>
+struct DCfg {
+    static constexpr int kBTile = BN * kBlockK * 2;
+    static constexpr int kStage = kATile + kBTile;
+    static constexpr int kStaging = BN * 64 * 2;
+    static constexpr int kBar = 1024;
+    static constexpr int kStagesFit = (kDynBudget - 1024 - kStaging - kBar) / kStage;
+    static constexpr int kStages = kStagesFit > 12 ? 12 : kStagesFit;
+    static constexpr int kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
+    static constexpr int kSmem = 1024 + kStages * kStage + kStaging + kBar;
+    static_assert(BN == 16 || BN == 32, "decode token tiles are 16 or 32 wide");
+    static_assert(kStages >= 4 && kStages <= kMaxPending, "pipeline depth");
+    static_assert(kSmem <= kDynBudget, "shared memory");
+};
+
+__device__ __forceinline__ float silu_times(float g, float u) {
+    // src/Gemm.cpp:225-231, with fast exp and divide: the result is rounded to bf16.
+    return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
+
+// One list's stream-K walk: this CTA's equal share of the list's k-block iterations.
+struct ListWalk {
+    int64_t it, end;
+    int num_kb;
+    __device__ void init(int tiles, int num_kb_) {
+        num_kb = num_kb_;
+        const int64_t iters = static_cast<int64_t>(tiles) * num_kb_;
+        it = iters * blockIdx.x / gridDim.x;
+        end = iters * (blockIdx.x + 1) / gridDim.x;
+    }
+    __device__ bool next(int& t, int& kb0, int& kb1) {
+        if (it >= end) return false;
+        t = static_cast<int>(it / num_kb);
+        kb0 = static_cast<int>(it - static_cast<int64_t>(t) * num_kb);
+        const int64_t left = end - it;
+        kb1 = left < num_kb - kb0 ? kb0 + static_cast<int>(left) : num_kb;
+        it += kb1 - kb0;
+        return true;
+    }
+};
+
+// The decoded work unit: which weights, which token tile, where its rows live.
+struct UnitInfo {
+    int a_row;    // tile-major weight row of k-block 0 (the A coordinate is a_row + kb * 128)
+    int b_row;    // first row of the token tile in its B tensor (x for gate/up, h for down)
+    int row0;     // first h row of the unit's expert
+    int rows;     // h rows of the expert (its tokens)
+    int mb;       // 128-row weight block within the expert
+    bool routed;  // routed expert (rows map to tokens through the row maps) or shared (row j = token j)
+};
+
+template <int BN, int EPL>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_decode_kernel(const __grid_constant__ CUtensorMap map_w13, const __grid_constant__ CUtensorMap map_w2,
+                      const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_h,
+                      const __grid_constant__ DecodeArgs args) {
+    using C = DCfg<BN>;
+    constexpr int S = C::kStages;
+    constexpr uint32_t kIdesc = umma_idesc_bf16(kBlockM, BN);
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ float s_logits[kDecodeMaxLogits];  // [t * E + e]
+    __shared__ int s_idx[kMaxRows];               // top-k experts, [t * K + k]
+    __shared__ float s_w[kMaxRows];               // top-k weights
+    __shared__ int s_row_token[kMaxRows];         // expert-sorted row -> token
+    __shared__ float s_row_w[kMaxRows];           // expert-sorted row -> routing weight
+    __shared__ int s_cnt[kMaxExperts];            // rows per expert
+    __shared__ uint32_t s_emask[kMaxExperts];     // tokens of each expert (bit t)
+    __shared__ int s_eoff[kMaxExperts];           // first expert-sorted row of each expert
+    __shared__ int s_seg_e[kMaxExperts];          // active (non-empty) experts, in expert order
+    __shared__ float s_probs[kEpiWarps][kMaxExperts];  // group-limited routing scratch
+    __shared__ RouterParams s_rp;  // read once at entry: a late read of a kernel parameter can miss
+                                   // the constant cache and wait behind the weight stream
+    __shared__ int s_n_act;
+    __shared__ int s_go[2];
+    __shared__ int s_split_last;
+
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem_a = smem;
+    uint8_t* smem_b = smem + S * kATile;
+    uint8_t* staging = smem_b + S * C::kBTile;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + C::kStaging);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + S;
+    uint64_t* tmem_full = bars + 2 * S;
+    uint64_t* tmem_empty = bars + 2 * S + 2;
+    uint64_t* sched_ready = bars + 2 * S + 4;
+    uint64_t* drain_bar = bars + 2 * S + 5;
+    uint64_t* logits_loaded = bars + 2 * S + 6;  // this CTA holds every logit: its HBM reads are done
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int T = args.tokens;
+    const int H = args.hidden;
+    const int I = args.inter;
+    const int E = args.rp.experts;
+    const int K = args.rp.top_k;
+    const int G = gridDim.x;
+    const unsigned long long target = args.epoch * static_cast<unsigned long long>(G);
+    // Lists: 0 = gate/up (shared experts' tiles, then the routed experts'), 1 = down
+    // (routed, then shared).
+    const int mb1 = 2 * I / kBlockM;  // 128-row blocks of interleaved gate/up rows
+    const int nkb1 = H / kBlockK;
+    const int mb2 = H / kBlockM;
+    const int nkb2 = I / kBlockK;
+    const int tiles_sh = args.n_shared * mb1;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tmem_full[i], 1);
+            mbar_init(&tmem_empty[i], kEpiWarps);
+        }
+        mbar_init(sched_ready, 1);
+        mbar_init(drain_bar, 1);
+        mbar_init(logits_loaded, 1);
+        s_rp = args.rp;
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&map_w13);
+        tma_prefetch_desc(&map_w2);
+        tma_prefetch_desc(&map_x);
+        tma_prefetch_desc(&map_h);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::kTmemCols);
+        tmem_relinquish();
+    }
+    // Everything above overlaps the previous kernel's tail (programmatic launch);
+    // x, y and the workspaces are touched only after it has finished.
+    pdl_wait();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    auto stamp = [&](int k) {
+        if (args.trace != nullptr) args.trace[blockIdx.x * kDecodeTraceSlots + k] = global_timer_ns();
+    };
+    if (threadIdx.x == 0) stamp(0);
+
+    // Both lists need the schedule, which exists once `sched_ready` has completed.
+    auto list_tiles = [&](int list) {
+        return list == 0 ? tiles_sh + s_n_act * mb1 : (s_n_act + args.n_shared) * mb2;
+    };
+    // Unit decoding, identical in every role.
+    auto unit_info = [&](int list, int tile) {
+        UnitInfo u;
+        if (list == 0 && tile < tiles_sh) {
+            const int s = tile / mb1;
+            u.mb = tile - s * mb1;
+            u.a_row = ((E + s) * mb1 + u.mb) * nkb1 * kBlockM;
+            u.b_row = 0;
+            u.row0 = args.h_shared_base + s * T;
+            u.rows = T;
+            u.routed = false;
+        } else if (list == 0) {
+            const int a = (tile - tiles_sh) / mb1;
+            const int e = s_seg_e[a];
+            u.mb = tile - tiles_sh - a * mb1;
+            u.a_row = (e * mb1 + u.mb) * nkb1 * kBlockM;
+            u.b_row = 0;
+            u.row0 = s_eoff[e];
+            u.rows = s_cnt[e];
+            u.routed = true;
+        } else {
+            const int g = tile / mb2;
+            u.mb = tile - g * mb2;
+            if (g < s_n_act) {
+                const int e = s_seg_e[g];
+                u.a_row = (e * mb2 + u.mb) * nkb2 * kBlockM;
+                u.row0 = s_eoff[e];
+                u.rows = s_cnt[e];
+                u.routed = true;
+            } else {
+                const int s = g - s_n_act;
+                u.a_row = ((E + s) * mb2 + u.mb) * nkb2 * kBlockM;
+                u.row0 = args.h_shared_base + s * T;
+                u.rows = T;
+                u.routed = false;
+            }
+            u.b_row = u.row0;
+        }
+        return u;
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ── TMA producer ──
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0;
+            uint32_t issued_phase = 0;
+            bool ok = true;
+            // h tiles of list 3 issued before counter 1 opens: (stage, x, y), oldest first.
+            int pend_stage[kMaxPending], pend_y[kMaxPending], pend_x[kMaxPending];
+            int pend_head = 0, pend_n = 0;
+            bool h_ready = false;
+            auto flush = [&](bool block) {
+                if (pend_n == 0) return;
+                if (!h_ready) {
+                    if (block) {
+                        if (!grid_wait(args.grid_bar + 1, target, abort_flag, args.status, kDevTimeoutGrid)) {
+                            ok = false;
+                            return;
+                        }
+                    } else if (ld_acquire_u64(args.grid_bar + 1) < target) {
+                        return;
+                    }
+                    fence_proxy_async_global();
+                    h_ready = true;
+                    stamp(5);
+                }
+                while (pend_n > 0) {
+                    const int st = pend_stage[pend_head];
+                    tma_load_2d(smem_b + st * C::kBTile, &map_h, &full[st], pend_x[pend_head], pend_y[pend_head]);
+                    pend_head = (pend_head + 1) % kMaxPending;
+                    --pend_n;
+                }
+            };
+            // Stay off HBM until the routing is done: under a saturated weight stream
+            // every global access of the routing -- the logits, and the instruction
+            // fetches of code run for the first time -- waits microseconds in the
+            // memory queues, which costs more than streaming early gains.
+            ok = mbar_wait(sched_ready, 0, abort_flag, args.status, kDevTimeoutProducer);
+            for (int list = 0; list <= 1 && ok; ++list) {
+                const int nkb = list == 1 ? nkb2 : nkb1;
+                const CUtensorMap* amap = list == 1 ? &map_w2 : &map_w13;
+                ListWalk walk;
+                walk.init(list_tiles(list), nkb);
+                int tile, kb0, kb1;
+                while (ok && walk.next(tile, kb0, kb1)) {
+                    const UnitInfo u = unit_info(list, tile);
+                    for (int kb = kb0; kb < kb1 && ok; ++kb) {
+                        // A ring of stages all waiting for h tiles drains only once
+                        // every CTA has written its h rows.
+                        flush(pend_n == S);
+                        if (!ok) break;
+                        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status, kDevTimeoutProducer)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&full[stage], kATile + C::kBTile);
+                        tma_load_2d(smem_a + stage * kATile, amap, &full[stage], 0, u.a_row + kb * kBlockM);
+                        if (list == 0) {
+                            tma_load_2d(smem_b + stage * C::kBTile, &map_x, &full[stage], kb * kBlockK, 0);
+                        } else if (h_ready && pend_n == 0) {
+                            tma_load_2d(smem_b + stage * C::kBTile, &map_h, &full[stage], kb * kBlockK, u.b_row);
+                        } else {
+                            const int slot = (pend_head + pend_n) % kMaxPending;
+                            pend_stage[slot] = stage;
+                            pend_x[slot] = kb * kBlockK;
+                            pend_y[slot] = u.b_row;
+                            ++pend_n;
+                            flush(false);
+                        }
+                        issued_mask |= 1u << stage;
+                        issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+                        if (++stage == S) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                }
+            }
+            if (ok) flush(true);
+            stamp(6);
+            if (!ok) {
+                // Loads already issued still land in this CTA's shared memory: wait for
+                // them (bounded) before the CTA can exit.
+                for (int st = 0; st < S; ++st)
+                    if (issued_mask & (1u << st)) mbar_wait_drain(&full[st], (issued_phase >> st) & 1u, 100000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ── MMA issuer ──
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            bool issued_any = false;
+            if (!mbar_wait(sched_ready, 0, abort_flag, args.status, kDevTimeoutMma)) ok = false;
+            for (int list = 0; list <= 1 && ok; ++list) {
+                ListWalk walk;
+                walk.init(list_tiles(list), list == 1 ? nkb2 : nkb1);
+                int tile, kb0, kb1;
+                while (ok && walk.next(tile, kb0, kb1)) {
+                    if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, args.status, kDevTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                    for (int kb = kb0; kb < kb1; ++kb) {
+                        if (!mbar_wait(&full[stage], phase, abort_flag, args.status, kDevTimeoutMma)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint64_t a_desc = umma_desc_sw128(smem_u32(smem_a + stage * kATile));
+                        const uint64_t b_desc = umma_desc_sw128(smem_u32(smem_b + stage * C::kBTile));
+#pragma unroll
+                        for (int kk = 0; kk < kBlockK / 16; ++kk)
+                            umma_bf16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, kIdesc, (kb != kb0) || (kk != 0));
+                        issued_any = true;
+                        umma_commit(&empty[stage]);
+                        if (++stage == S) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    umma_commit(&tmem_full[acc]);
+                    if (++acc == 2) {
+                        acc = 0;
+                        acc_phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok && issued_any) {
+                umma_commit(drain_bar);
+                mbar_wait_drain(drain_bar, 0, 100000000ull);
+            }
+            stamp(8);
+        }
+    } else {
+        // ── Routing, then the epilogue: warps 2..9 ──
+        const int epi_tid = threadIdx.x - 64;
+        const int ew = epi_tid >> 5;
+        const int quad = warp & 3;
+        const int half = (warp - 2) >> 2;
+        bool ok = true;
+        // One thread waits; the named barrier hands the verdict to all eight warps
+        // (the slot alternates so a slow warp never reads the next verdict).
+        int go_slot = 0;
+        auto broadcast = [&](bool v) {
+            if (epi_tid == 0) s_go[go_slot] = v ? 1 : 0;
+            named_bar_sync(2, kEpiThreads);
+            const bool r = s_go[go_slot] != 0;
+            go_slot ^= 1;
+            return r;
+        };
+        auto arrive_grid = [&](int g) {
+            __threadfence();
+            named_bar_sync(2, kEpiThreads);
+            if (epi_tid == 0) red_release_add_u64(args.grid_bar + g, 1ull);
+        };
+
+        // (1) y = 0 when not accumulating; the down epilogues add into it after counter 1.
+        if (args.zero_y) {
+            const int n4 = T * H / 4;
+            const int per = (n4 + G - 1) / G;
+            float4* yz = reinterpret_cast<float4*>(args.y);
+            for (int i = blockIdx.x * per + epi_tid; i < min(n4, (blockIdx.x + 1) * per); i += kEpiThreads)
+                yz[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        for (int e = epi_tid; e < E; e += kEpiThreads) {
+            s_cnt[e] = 0;
+            s_emask[e] = 0u;
+        }
+
+        // (2) Router logits: (token, expert) dot products spread over every warp of the
+        // grid; each lane's loads of a row are all issued before any is used.
+        for (int p = blockIdx.x * kEpiWarps + ew; p < T * E; p += G * kEpiWarps) {
+            const int t = p / E;
+            const int e = p - t * E;
+            const float* wr = args.router + static_cast<size_t>(e) * H;
+            float acc = 0.0f;
+            if (args.x_f32 != nullptr) {
+                const float* xt = args.x_f32 + static_cast<size_t>(t) * H;
+#pragma unroll 8
+                for (int hh = lane * 8; hh < H; hh += 256) {
+                    float xv[8], wv[8];
+                    load8(xt + hh, xv);
+                    load8(wr + hh, wv);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[i], acc);
+                }
+            } else {
+                const uint16_t* xt = args.x + static_cast<size_t>(t) * H;
+#pragma unroll 8
+                for (int hh = lane * 8; hh < H; hh += 256) {
+                    float xv[8], wv[8];
+                    load8(xt + hh, xv);
+                    load8(wr + hh, wv);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[i], acc);
+                }
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(kFull, acc, off);
+            if (lane == 0) args.logits[p] = args.bias != nullptr ? acc + args.bias[e] : acc;
+        }
+        arrive_grid(0);
+        if (epi_tid == 0) stamp(1);
+        ok = broadcast(epi_tid == 0 ? grid_wait(args.grid_bar, target, abort_flag, args.status, kDevTimeoutGrid)
+                                    : true);
+        if (epi_tid == 0) stamp(2);
+
+        if (ok) {
+            // (3) All logits into shared memory in one round trip, then every token's
+            // routing from there (every CTA the same).
+            for (int i = epi_tid; i < T * E; i += kEpiThreads) s_logits[i] = __ldcg(args.logits + i);
+            named_bar_sync(1, kEpiThreads);
+            if (epi_tid == 0) {
+                mbar_arrive(logits_loaded);
+                stamp(10);
+            }
+            for (int t = ew; t < T; t += kEpiWarps) {
+                const Selection sel = route_one_token<EPL, true>(s_logits + t * E, s_rp, s_probs[ew], lane);
+                if (lane < K) {
+                    s_idx[t * K + lane] = sel.idx;
+                    s_w[t * K + lane] = sel.w;
+                    atomicAdd(&s_cnt[sel.idx], 1);
+                    atomicOr(&s_emask[sel.idx], 1u << t);
+                    if (blockIdx.x == 0) {
+                        args.topk_idx[t * K + lane] = sel.idx;
+                        args.topk_w[t * K + lane] = sel.w;
+                    }
+                }
+            }
+            named_bar_sync(1, kEpiThreads);
+            if (epi_tid == 0) stamp(11);
+            // (4) Active experts and their first rows: a warp-wide compaction and scan.
+            if (ew == 0) {
+                int n = 0, off = 0;
+                for (int base = 0; base < E; base += 32) {
+                    const int e = base + lane;
+                    const int c = e < E ? s_cnt[e] : 0;
+                    int incl = c;
+#pragma unroll
+                    for (int d = 1; d < 32; d <<= 1) {
+                        const int v = __shfl_up_sync(kFull, incl, d);
+                        if (lane >= d) incl += v;
+                    }
+                    const uint32_t act = __ballot_sync(kFull, c > 0);
+                    if (c > 0) {
+                        s_seg_e[n + __popc(act & ((1u << lane) - 1u))] = e;
+                        s_eoff[e] = off + incl - c;
+                    }
+                    n += __popc(act);
+                    off += __shfl_sync(kFull, incl, 31);
+                }
+                if (lane == 0) s_n_act = n;
+            }
+            named_bar_sync(1, kEpiThreads);
+            if (epi_tid == 0) stamp(12);
+            // (5) Expert-sorted rows, tokens in order within an expert: a token picks an
+            // expert at most once, so its rank there counts the expert's earlier tokens.
+            const int n_pairs = T * K;
+            for (int q = epi_tid; q < n_pairs; q += kEpiThreads) {
+                const int e = s_idx[q];
+                const int t = q / K;
+                const int row = s_eoff[e] + __popc(s_emask[e] & ((1u << t) - 1u));
+                s_row_token[row] = t;
+                s_row_w[row] = s_w[q];
+            }
+            named_bar_sync(1, kEpiThreads);
+            if (epi_tid == 0) {
+                mbar_arrive(sched_ready);  // producer and MMA may decode lists 2-3
+                stamp(3);
+            }
+            if (blockIdx.x == 0) {
+                for (int r = epi_tid; r < n_pairs; r += kEpiThreads) {
+                    args.row_token[r] = s_row_token[r];
+                    args.row_weight[r] = s_row_w[r];
+                }
+                for (int e = epi_tid; e < E; e += kEpiThreads) args.expert_totals[e] = s_cnt[e];
+            }
+        }
+
+        // (6) Epilogues of both lists, in the order the MMA issuer produced them.
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int list = 0; list <= 1 && ok; ++list) {
+            if (list == 1) {
+                // Every h row this CTA writes is written: publish them for the TMA reads.
+                fence_proxy_async_global();
+                arrive_grid(1);
+                if (epi_tid == 0) stamp(4);
+            }
+            const int tiles = list_tiles(list);
+            const int nkb = list == 1 ? nkb2 : nkb1;
+            ListWalk walk;
+            walk.init(tiles, nkb);
+            int tile, kb0, kb1;
+            bool first_unit = true;
+            while (walk.next(tile, kb0, kb1)) {
+                const UnitInfo u = unit_info(list, tile);
+                ok = broadcast(epi_tid == 0 ? mbar_wait(&tmem_full[acc], acc_phase, abort_flag, args.status,
+                                                        kDevTimeoutEpilogue)
+                                            : true);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t t_row =
+                    tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+                // Gate/up columns are tokens 0..T-1; down columns are the expert's h rows.
+                const int ncols = list == 1 ? u.rows : T;
+                const bool whole = kb0 == 0 && kb1 == nkb;
+                if (list == 0 && !whole) {
+                    // Partial gate/up tile: store the partial sums in this CTA's slot,
+                    // count k-blocks; the CTA completing the tile sums the slots in CTA
+                    // order and applies SiLU.
+                    const int slot = 2 * static_cast<int>(blockIdx.x) + (first_unit ? 0 : 1);
+                    float* wt = args.split_ws + static_cast<size_t>(slot) * (kBlockM * BN);
+                    const int row = quad * 32 + lane;
+#pragma unroll 1
+                    for (int c0 = 16 * half; c0 < BN; c0 += 32) {
+                        if (c0 >= ncols) break;
+                        uint32_t r[16];
+                        tmem_ld16(t_row + c0, r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (c0 + j < ncols) __stcg(wt + (c0 + j) * kBlockM + row, __uint_as_float(r[j]));
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+                    __threadfence();
+                    named_bar_sync(1, kEpiThreads);
+                    const int ticket = tile;
+                    if (epi_tid == 0)
+                        s_split_last = atomicAdd(args.split_ticket + ticket, kb1 - kb0) + (kb1 - kb0) == nkb;
+                    named_bar_sync(1, kEpiThreads);
+                    if (s_split_last) {
+                        __threadfence();
+                        const int64_t iters = static_cast<int64_t>(tiles) * nkb;
+                        const int64_t j0 = static_cast<int64_t>(tile) * nkb;
+                        // CTA owning iteration j: the largest c with iters * c / G <= j.
+                        const int c_lo = static_cast<int>(((j0 + 1) * G + iters - 1) / iters) - 1;
+                        const int c_hi = static_cast<int>(((j0 + nkb) * G + iters - 1) / iters) - 1;
+                        // Items: (h row j, pair of intermediate columns) -> one float4 of
+                        // (gate, up, gate, up); all of a part's loads are in flight together.
+                        const int items = u.rows * 32;
+                        float4 sum[kReduceItems];
+#pragma unroll
+                        for (int k = 0; k < kReduceItems; ++k) sum[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        int col[kReduceItems];
+#pragma unroll
+                        for (int k = 0; k < kReduceItems; ++k) {
+                            const int q = epi_tid + k * kEpiThreads;
+                            const int j = q >> 5;
+                            col[k] = q < items ? (u.routed ? s_row_token[u.row0 + j] : j) : 0;
+                        }
+                        // Parts in batches of kReduceParts, every load of a batch in flight
+                        // at once (under a saturated HBM stream each L2 round trip is long).
+                        for (int cb = c_lo; cb <= c_hi; cb += kReduceParts) {
+                            float4 v[kReduceItems][kReduceParts];
+#pragma unroll
+                            for (int pp = 0; pp < kReduceParts; ++pp) {
+                                const int cta = cb + pp;
+                                const int64_t b = iters * cta / G;
+                                const bool use = cta <= c_hi && iters * (cta + 1) / G != b;  // skip empty ranges
+                                const float* part =
+                                    args.split_ws + static_cast<size_t>(2 * cta + (b >= j0 ? 0 : 1)) * (kBlockM * BN);
+#pragma unroll
+                                for (int k = 0; k < kReduceItems; ++k) {
+                                    const int q = epi_tid + k * kEpiThreads;
+                                    v[k][pp] = (use && q < items) ? __ldcg(reinterpret_cast<const float4*>(
+                                                                        part + col[k] * kBlockM + 4 * (q & 31)))
+                                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                                }
+                            }
+#pragma unroll
+                            for (int k = 0; k < kReduceItems; ++k) {
+#pragma unroll
+                                for (int pp = 0; pp < kReduceParts; ++pp) {
+                                    sum[k].x += v[k][pp].x;
+                                    sum[k].y += v[k][pp].y;
+                                    sum[k].z += v[k][pp].z;
+                                    sum[k].w += v[k][pp].w;
+                                }
+                            }
+                        }
+#pragma unroll
+                        for (int k = 0; k < kReduceItems; ++k) {
+                            const int q = epi_tid + k * kEpiThreads;
+                            if (q < items) {
+                                const int j = q >> 5;
+                                const __nv_bfloat162 hv = __floats2bfloat162_rn(silu_times(sum[k].x, sum[k].y),
+                                                                                silu_times(sum[k].z, sum[k].w));
+                                *reinterpret_cast<__nv_bfloat162*>(args.h + static_cast<size_t>(u.row0 + j) * I +
+                                                                   u.mb * 64 + 2 * (q & 31)) = hv;
+                            }
+                        }
+                        if (epi_tid == 0) args.split_ticket[ticket] = 0;
+                    }
+                } else if (list == 0) {
+                    // Whole gate/up tile: h = silu(gate) * up through a staging tile.
+                    __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(staging);
+                    const int i_local = (quad * 32 + lane) >> 1;
+#pragma unroll 1
+                    for (int c0 = 16 * half; c0 < BN; c0 += 32) {
+                        if (c0 >= ncols) break;
+                        uint32_t r[16];
+                        tmem_ld16(t_row + c0, r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const float mine = __uint_as_float(r[j]);
+                            const float other = __shfl_xor_sync(kFull, mine, 1);
+                            if ((lane & 1) == 0)
+                                st[(c0 + j) * 64 + i_local] = __float2bfloat16_rn(silu_times(mine, other));
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+                    named_bar_sync(1, kEpiThreads);
+                    const uint4* src = reinterpret_cast<const uint4*>(staging);
+                    for (int q = epi_tid; q < u.rows * 8; q += kEpiThreads) {
+                        const int j = q >> 3;
+                        const int part = q & 7;
+                        const int col = u.routed ? s_row_token[u.row0 + j] : j;
+                        uint4* dst =
+                            reinterpret_cast<uint4*>(args.h + static_cast<size_t>(u.row0 + j) * I + u.mb * 64) + part;
+                        *dst = src[col * 8 + part];
+                    }
+                    named_bar_sync(1, kEpiThreads);
+                } else {
+                    // Down: routing weight x output, added into y[token] (128-byte runs).
+                    const int d = u.mb * kBlockM + quad * 32 + lane;
+#pragma unroll 1
+                    for (int c0 = 16 * half; c0 < BN; c0 += 32) {
+                        if (c0 >= ncols) break;
+                        uint32_t r[16];
+                        tmem_ld16(t_row + c0, r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int c = c0 + j;
+                            if (c < ncols) {
+                                const int tok = u.routed ? s_row_token[u.row0 + c] : c;
+                                const float w = u.routed ? s_row_w[u.row0 + c] : 1.0f;
+                                atomicAdd(args.y + static_cast<size_t>(tok) * H + d, w * __uint_as_float(r[j]));
+                            }
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+                }
+                first_unit = false;
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+        }
+        if (epi_tid == 0) stamp(7);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+template <int BN, int EPL>
+cudaError_t launch_t(const CUtensorMap& w13, const CUtensorMap& w2, const CUtensorMap& x, const CUtensorMap& h,
+                     const DecodeArgs& args, int sms, cudaStream_t stream) {
+    using C = DCfg<BN>;
+    auto kernel = moe_decode_kernel<BN, EPL>;
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = stream;
+    // Co-residency of every CTA is what makes the grid counters safe to wait on.
+    // Programmatic serialization lets the launch and the prologue overlap the
+    // previous kernel; the kernel waits for it before touching memory.
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kernel, w13, w2, x, h, args);
+}
+
+}  // namespace
+
+cudaError_t launch_moe_decode(int bn, const CUtensorMap& w13, const CUtensorMap& w2, const CUtensorMap& x,
+                              const CUtensorMap& h, const DecodeArgs& args, int sms, cudaStream_t stream) {
+    if (args.tokens <= 0) return cudaSuccess;
+    if (args.tokens > kDecodeMaxTokens || args.tokens > bn || args.rp.experts > kMaxExperts ||
+        args.rp.top_k > kMaxTopK || args.tokens * args.rp.experts > kDecodeMaxLogits)
+        return cudaErrorInvalidValue;
+    const int need = (args.rp.experts + 31) / 32;
+    const int epl = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : 8;
+#define LM_DECODE(BN_)                                                                \
+    switch (epl) {                                                                    \
+        case 1: return launch_t<BN_, 1>(w13, w2, x, h, args, sms, stream);            \
+        case 2: return launch_t<BN_, 2>(w13, w2, x, h, args, sms, stream);            \
+        case 4: return launch_t<BN_, 4>(w13, w2, x, h, args, sms, stream);            \
+        default: return launch_t<BN_, 8>(w13, w2, x, h, args, sms, stream);           \
+    }
+    if (bn == 16) LM_DECODE(16)
+    if (bn == 32) LM_DECODE(32)
+#undef LM_DECODE
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace lm

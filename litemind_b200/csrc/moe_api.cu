@@ -76,6 +76,10 @@ struct lm_moe_ctx {
     uint16_t* h = nullptr;
     int32_t* status = nullptr;
     int split_max_waves = 4;          // split-K below this many waves of tiles (LITEMIND_B200_SPLIT_WAVES)
+    bool fused_decode = true;         // T <= 32 on one GPU: one cooperative launch (LITEMIND_B200_FUSED_DECODE=0: off)
+    unsigned long long* grid_bar = nullptr;  // the fused decode kernel's arrival counters
+    unsigned long long decode_epoch = 0;     // fused decode launches so far (their counter targets)
+    unsigned long long* decode_trace = nullptr;  // per-CTA phase stamps of the last fused launch (profiling)
     float* split_ws = nullptr;        // gate/up split-K partial tiles
     int32_t* split_ticket = nullptr;  // k-blocks done per split tile, zero between uses
     unsigned int* ticket = nullptr;  // last-CTA ticket of the fused small-T route kernel
@@ -347,6 +351,7 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
     if (prop.major != 10) return LM_ERR_UNSUPPORTED;  // built for sm_100a only
     ctx->sms = prop.multiProcessorCount;
     if (const char* w = std::getenv("LITEMIND_B200_SPLIT_WAVES")) ctx->split_max_waves = std::max(0, std::atoi(w));
+    if (const char* f = std::getenv("LITEMIND_B200_FUSED_DECODE")) ctx->fused_decode = std::atoi(f) != 0;
     ctx->local_experts = c.n_routed_experts;
     ctx->n_seg = ctx->local_experts + c.n_shared_experts;
     ctx->routed_cap = c.max_tokens * c.num_experts_per_tok;
@@ -366,7 +371,8 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
         (st = alloc(p, &p->x_perm, static_cast<size_t>(p->routed_cap) * H)) || (st = alloc(p, &p->h, h_rows * I)) ||
         (st = alloc(p, &p->status, 1)) || (st = alloc(p, &p->ticket, 1)) ||
         (st = alloc(p, &p->split_ws, kSplitWsBytes / sizeof(float))) ||
-        (st = alloc(p, &p->split_ticket, static_cast<size_t>(kSplitTickets)))) {
+        (st = alloc(p, &p->split_ticket, static_cast<size_t>(kSplitTickets))) ||
+        (st = alloc(p, &p->grid_bar, 3))) {
         lm_moe_destroy(ctx.release());
         return st;
     }
@@ -375,7 +381,8 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
         cudaMemset(p->expert_totals, 0, E * sizeof(int32_t)) != cudaSuccess ||
         cudaMemset(p->sched, 0, sizeof(Schedule)) != cudaSuccess ||
         cudaMemset(p->split_ws, 0, kSplitWsBytes) != cudaSuccess ||
-        cudaMemset(p->split_ticket, 0, kSplitTickets * sizeof(int32_t)) != cudaSuccess) {
+        cudaMemset(p->split_ticket, 0, kSplitTickets * sizeof(int32_t)) != cudaSuccess ||
+        cudaMemset(p->grid_bar, 0, 3 * sizeof(unsigned long long)) != cudaSuccess) {
         lm_moe_destroy(ctx.release());
         return LM_ERR_CUDA;
     }
@@ -400,6 +407,7 @@ lm_status lm_moe_destroy(lm_moe_ctx* ctx) {
     if (ctx->bias_stage) cudaFree(ctx->bias_stage);
     if (ctx->norm_f32) cudaFree(ctx->norm_f32);
     if (ctx->norm_bf16) cudaFree(ctx->norm_bf16);
+    if (ctx->decode_trace) cudaFree(ctx->decode_trace);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     if (ctx->comm != nullptr && ctx->nccl != nullptr) ctx->nccl->CommDestroy(ctx->comm);
     if (ctx->host_sched) cudaFreeHost(ctx->host_sched);
@@ -599,6 +607,53 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
     int n_slots = 0;
     const RouterParams rp = router_params(c);
     float* y_zero = accumulate ? nullptr : y;  // the down GEMM adds into y
+    const int fused_bn = T <= 16 ? 16 : 32;
+    const int max_active = std::min(E, T * K);
+    if (ctx->fused_decode && T <= kDecodeMaxTokens && ctx->comm == nullptr && T * E <= kDecodeMaxLogits &&
+        (c.n_shared_experts + max_active) * (2 * I / 128) <= kSplitTickets &&
+        static_cast<size_t>(2) * ctx->sms * 128 * fused_bn * sizeof(float) <= kSplitWsBytes) {
+        // Decode: the whole layer in one cooperative launch.
+        CUtensorMap map_x{};
+        std::string err;
+        if (!encode_tensor_map_bf16(&map_x, x, T, H, fused_bn, 64, err)) return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+        DecodeArgs a{};
+        a.x = x;
+        a.x_f32 = x_f32;
+        a.router = L.router;
+        a.bias = bias;
+        a.y = y;
+        a.zero_y = accumulate ? 0 : 1;
+        a.tokens = T;
+        a.hidden = H;
+        a.inter = I;
+        a.n_shared = c.n_shared_experts;
+        a.rp = rp;
+        a.logits = ctx->logits;
+        a.topk_idx = ctx->topk_idx;
+        a.topk_w = ctx->topk_w;
+        a.expert_totals = ctx->expert_totals;
+        a.row_token = ctx->row_token;
+        a.row_weight = ctx->row_weight;
+        a.h = ctx->h;
+        a.h_shared_base = ctx->routed_cap;
+        a.w13_shared = reinterpret_cast<const uint8_t*>(L.w13 + static_cast<size_t>(ctx->local_experts) * 2 * I * H);
+        a.w13_shared_bytes = static_cast<uint64_t>(c.n_shared_experts) * 2 * I * H * 2;
+        a.split_ws = ctx->split_ws;
+        a.split_ticket = ctx->split_ticket;
+        a.grid_bar = ctx->grid_bar;
+        a.epoch = ++ctx->decode_epoch;
+        a.status = ctx->status;
+        if (ctx->profiling && ctx->decode_trace == nullptr)
+            LM_CUDA(ctx, cudaMalloc(&ctx->decode_trace, static_cast<size_t>(ctx->sms) * kDecodeTraceSlots * 8));
+        if (ctx->profiling) LM_CUDA(ctx, cudaMemsetAsync(ctx->decode_trace, 0, static_cast<size_t>(ctx->sms) *
+                                                                                   kDecodeTraceSlots * 8, s));
+        a.trace = ctx->profiling ? ctx->decode_trace : nullptr;
+        const int fbi = bn_index(fused_bn);
+        LM_CUDA(ctx, launch_moe_decode(fused_bn, L.map_w13, L.map_w2, map_x, ctx->map_h[fbi], a, ctx->sms, s));
+        prof_mark(ctx, 8, s);
+        slots[n_slots++] = 8;
+        return prof_end(ctx, slots, n_slots);
+    }
     if (T <= kRouteTile) {
         // Decode: logits, top-k, counts, schedule and placement in one launch.
         LM_CUDA(ctx, launch_route_small(x, x_f32, L.router, bias, ctx->logits, T, H, rp, ctx->topk_idx, ctx->topk_w,
@@ -913,6 +968,10 @@ lm_status lm_moe_sync(lm_moe_ctx* ctx, void* stream) {
     LM_CUDA(ctx, cudaMemcpy(&status, ctx->status, sizeof(status), cudaMemcpyDeviceToHost));
     if (status != 0) {
         LM_CUDA(ctx, cudaMemset(ctx->status, 0, sizeof(int32_t)));
+        // An aborted fused decode launch leaves its grid counters short: restart them.
+        LM_CUDA(ctx, cudaMemset(ctx->grid_bar, 0, 3 * sizeof(unsigned long long)));
+        LM_CUDA(ctx, cudaMemset(ctx->split_ticket, 0, kSplitTickets * sizeof(int32_t)));
+        ctx->decode_epoch = 0;
         return fail(ctx, LM_ERR_DEVICE_TIMEOUT,
                     "a kernel's bounded wait expired (code " + std::to_string(status) + "); results are invalid");
     }
@@ -957,6 +1016,21 @@ lm_status lm_moe_profile_read(lm_moe_ctx* ctx, double* total_ms, int64_t* launch
             ctx->prof_count[i] = 0;
         }
     }
+    return LM_OK;
+}
+
+lm_status lm_moe_profile_trace(lm_moe_ctx* ctx, uint64_t* stamps, int32_t ctas, int32_t* ctas_out) {
+    if (ctx == nullptr || stamps == nullptr || ctas_out == nullptr || ctas < 0) return LM_ERR_INVALID_ARGUMENT;
+    static_assert(LM_DECODE_TRACE_SLOTS == kDecodeTraceSlots, "trace layout");
+    *ctas_out = 0;
+    if (ctx->decode_trace == nullptr) return LM_OK;
+    lm_status st;
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    const int n = std::min(ctas, ctx->sms);
+    LM_CUDA(ctx, cudaDeviceSynchronize());
+    LM_CUDA(ctx, cudaMemcpy(stamps, ctx->decode_trace, static_cast<size_t>(n) * kDecodeTraceSlots * 8,
+                            cudaMemcpyDeviceToHost));
+    *ctas_out = ctx->sms;
     return LM_OK;
 }
 

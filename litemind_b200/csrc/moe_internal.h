@@ -105,6 +105,48 @@ struct GemmArgs {
     int32_t split_ws_floats;   // capacity of split_ws in floats
     int32_t split_max_waves;   // split when the tiles fill fewer waves of the grid than this (0: never)
 };
+// The fused decode kernel (decode_fused.cu): the whole layer for T <= 32 tokens in
+// one cooperative launch -- routing, dispatch, gate/up, down and the combine.
+constexpr int kDecodeMaxTokens = 32;
+struct DecodeArgs {
+    const uint16_t* x;         // [T, hidden] bf16 tokens (GEMM operand; logits too unless x_f32)
+    const float* x_f32;        // optional [T, hidden] f32 tokens for the router logits
+    const float* router;       // [E, hidden] f32
+    const float* bias;         // [E] per-expert logit bias or null
+    float* y;                  // [T, hidden] f32
+    int32_t zero_y;            // 1: y = MoE(x), 0: y += MoE(x)
+    int32_t tokens;
+    int32_t hidden;
+    int32_t inter;
+    int32_t n_shared;
+    RouterParams rp;
+    float* logits;             // [T, E] (output, also the exchange between CTAs)
+    int32_t* topk_idx;         // [T, k] outputs
+    float* topk_w;
+    int32_t* expert_totals;    // [E]
+    int32_t* row_token;        // [T * k] expert-sorted row -> token
+    float* row_weight;         // [T * k] expert-sorted row -> routing weight
+    uint16_t* h;               // SwiGLU outputs: routed rows, then n_shared blocks of T rows
+    const uint8_t* w13_shared; // the shared experts' gate/up tiles (contiguous), prefetched into L2
+    uint64_t w13_shared_bytes;
+    int32_t h_shared_base;     // first h row of the shared experts
+    float* split_ws;           // gate/up split-K partials: 2 slots of [BN][128] per CTA
+    int32_t* split_ticket;     // per gate/up tile, zero between uses
+    unsigned long long* grid_bar;  // [2] arrival counters (logits, h), monotonic across launches
+    unsigned long long epoch;      // this launch's number (from 1): targets are epoch * gridDim.x
+    int32_t* status;
+    unsigned long long* trace;     // optional: kDecodeTraceSlots global-timer stamps per CTA
+};
+// Phase stamps of the fused decode kernel (profiling only), per CTA:
+//  0 start  1 logits written  2 every CTA's logits seen  3 schedule built
+//  4 gate/up epilogues done  5 producer saw every h row  6 producer issued
+//  everything  7 down epilogues done  8 MMA done
+constexpr int kDecodeTraceSlots = 16;
+// Router logits the fused decode kernel keeps in shared memory (tokens x experts).
+constexpr int kDecodeMaxLogits = 4096;
+cudaError_t launch_moe_decode(int bn, const CUtensorMap& w13, const CUtensorMap& w2, const CUtensorMap& x,
+                              const CUtensorMap& h, const DecodeArgs& args, int sms, cudaStream_t stream);
+
 // Split-K workspace for gate/up partial tiles (bytes) and its ticket count.
 constexpr size_t kSplitWsBytes = size_t(32) << 20;
 constexpr int kSplitTickets = 4096;

@@ -20,6 +20,7 @@ constexpr int kDevTimeoutProducer = 1;
 constexpr int kDevTimeoutMma = 2;
 constexpr int kDevTimeoutEpilogue = 3;
 constexpr int kDevBadTile = 4;
+constexpr int kDevTimeoutGrid = 5;  // a grid-wide arrival counter never reached its target
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -87,9 +88,53 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
     return true;
 }
 
+// ── grid-wide arrival counters (cooperative launches only) ───────────────
+// Counters only grow: launch number n (from 1) of a context waits for n * gridDim.x
+// arrivals, so nothing has to be reset between launches.
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Orders this thread's generic-proxy global writes before later async-proxy (TMA)
+// reads of the same memory, in this CTA or another.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Bounded wait until *ctr >= target.  Gives up when the CTA's abort flag is raised,
+// when another CTA has already recorded an error in the status word, or after
+// kWaitLimitNs (then it records `code`).
+__device__ __forceinline__ bool grid_wait(const unsigned long long* ctr, unsigned long long target,
+                                          volatile int* abort_flag, int* status, int code) {
+    if (ld_acquire_u64(ctr) >= target) return true;
+    const uint64_t start = global_timer_ns();
+    while (true) {
+        if (ld_acquire_u64(ctr) >= target) return true;
+        if (*abort_flag || *reinterpret_cast<volatile int*>(status) != 0) {
+            *abort_flag = 1;
+            return false;
+        }
+        if (global_timer_ns() - start > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicCAS(status, 0, code);
+            return false;
+        }
+        __nanosleep(32);
+    }
+}
+
 // ── TMA ───────────────────────────────────────────────────────────────────
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Hint: bring `bytes` (a multiple of 16) of global memory at `src` (16-byte
+// aligned) into L2.  No completion to wait for.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 // 2-D tile load global -> shared, completing `bytes` on `bar`.  x is the

@@ -222,6 +222,14 @@ class MoeLayer:
         self._check(self.lib.lm_moe_profile_read(self.ctx, _ptr(ms), _ptr(n), int(reset)))
         return {name: (float(ms[i]), int(n[i])) for i, name in enumerate(_lib.PROFILE_SLOT_NAMES) if n[i] > 0}
 
+    def profile_trace(self) -> np.ndarray:
+        """Per-CTA phase stamps (ns) of the last profiled fused decode launch, [ctas, slots]."""
+        cap = 1024
+        out = np.zeros((cap, _lib.LM_DECODE_TRACE_SLOTS), np.uint64)
+        n = C.c_int32(0)
+        self._check(self.lib.lm_moe_profile_trace(self.ctx, _ptr(out), cap, C.byref(n)))
+        return out[: min(n.value, cap)]
+
     def expert_counts(self) -> np.ndarray:
         out = np.zeros(self.config.n_routed_experts, np.int32)
         self._check(self.lib.lm_moe_expert_counts(self.ctx, _ptr(out)))
