@@ -1,0 +1,167 @@
+"""The fused decode kernel (one cooperative launch per layer for T <= 32 on one GPU).
+
+Parity against the oracle across the token counts that change its work split (one
+token, one token-tile boundary, the largest batch it takes), with a logit bias, with
+group-limited and renormalised routing, with accumulation into y, with f32 router
+activations (the block path), and against the grouped multi-launch path it
+replaces.  Its phase trace is checked for ordering.
+"""
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+from litemind_b200 import synthetic as syn  # noqa: E402
+from litemind_b200.moe import MoeConfig, MoeLayer, bf16_tensor  # noqa: E402
+from oracle.oracle import RouterConfig  # noqa: E402
+from tests.parity import MAX_REL, MIN_COS, assert_layer_parity, output_errors  # noqa: E402
+
+V2 = syn.V2_LITE
+# A shape with enough experts for group-limited routing (8 groups of 8).
+GROUPED = syn.MoeShape(hidden=512, inter=256, n_routed_experts=64, n_shared_experts=2, top_k=6)
+
+
+@pytest.fixture(scope="module")
+def v2(v2lite_weights):
+    layer = MoeLayer(MoeConfig(max_tokens=64))
+    layer.upload_layer(0, v2lite_weights)
+    yield layer
+    layer.close()
+
+
+def _oracle(oracle_lib, shape, W, x_bits, cfg=None, bias=None):
+    x = syn.bf16_to_f32(x_bits).reshape(x_bits.shape)
+    cfg = cfg or RouterConfig(shape.n_routed_experts, shape.top_k)
+    return oracle_lib.moe_layer(x, W, cfg, shape.n_shared_experts, bias=bias, threads=0)
+
+
+def _gpu(layer, x_bits, bias=None):
+    x = bf16_tensor(x_bits)
+    b = None if bias is None else torch.from_numpy(bias).cuda()
+    layer.profile(True)
+    layer.profile_read(reset=True)
+    y = layer.forward(0, x, bias=b)
+    prof = layer.profile_read(reset=True)
+    layer.profile(False)
+    idx, w, logits = layer.route(0, x, bias=b)
+    layer.sync()
+    return y.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), logits.cpu().numpy(), prof
+
+
+@pytest.mark.parametrize("T", [1, 2, 15, 16, 17, 31, 32])
+def test_fused_parity_across_token_counts(oracle_lib, v2lite_weights, v2, T):
+    x = syn.tokens(V2, T, seed=50 + T)
+    y, idx, w, _, prof = _gpu(v2, x)
+    assert "decode_fused" in prof and "gemm_gate_up" not in prof, prof
+    ry, ridx, rw, rlog = _oracle(oracle_lib, V2, v2lite_weights, x)
+    assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what=f"fused T={T}")
+
+
+def test_fused_with_zipf_bias(oracle_lib, v2lite_weights, v2):
+    x = syn.tokens(V2, 32, seed=2)
+    bias = syn.zipf_bias(V2, seed=2)
+    y, idx, w, _, _ = _gpu(v2, x, bias)
+    ry, ridx, rw, rlog = _oracle(oracle_lib, V2, v2lite_weights, x, bias=bias)
+    assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what="fused + bias")
+
+
+def test_fused_accumulates(v2):
+    x = bf16_tensor(syn.tokens(V2, 20, seed=9))
+    y0 = v2.forward(0, x)
+    y1 = torch.full_like(y0, 2.0)
+    v2.forward(0, x, y=y1, accumulate=True)
+    v2.sync()
+    torch.testing.assert_close(y1 - 2.0, y0, rtol=1e-5, atol=1e-5)
+
+
+def test_fused_matches_grouped_path(v2lite_weights, v2):
+    """The grouped multi-launch path (LITEMIND_B200_FUSED_DECODE=0) on the same inputs."""
+    old = os.environ.get("LITEMIND_B200_FUSED_DECODE")
+    os.environ["LITEMIND_B200_FUSED_DECODE"] = "0"
+    try:
+        grouped = MoeLayer(MoeConfig(max_tokens=64))
+    finally:
+        if old is None:
+            del os.environ["LITEMIND_B200_FUSED_DECODE"]
+        else:
+            os.environ["LITEMIND_B200_FUSED_DECODE"] = old
+    grouped.upload_layer(0, v2lite_weights)
+    for T in (1, 8, 32):
+        x = syn.tokens(V2, T, seed=70 + T)
+        y, _, _, _, _ = _gpu(v2, x)
+        counts = v2.expert_counts()
+        gy, _, _, _, gprof = _gpu(grouped, x)
+        gcounts = grouped.expert_counts()
+        assert "decode_fused" not in gprof
+        # The two paths sum the router logits in different orders: a near-tie may move
+        # one choice; otherwise both routings and outputs agree.
+        assert np.abs(counts - gcounts).sum() <= 2
+        if np.array_equal(counts, gcounts):
+            rel = np.abs(y - gy).max() / np.abs(gy).max()
+            assert rel < 1e-2, rel
+    grouped.close()
+
+
+@pytest.mark.parametrize("normalize", [False, True])
+def test_fused_group_limited_routing(oracle_lib, normalize):
+    W = syn.layer_weights(GROUPED, seed=21, std=0.05)
+    cfg = MoeConfig.from_shape(GROUPED, max_tokens=32, topk_method="group_limited_greedy", n_group=8,
+                               topk_group=3, norm_topk_prob=normalize, routed_scaling_factor=1.0)
+    layer = MoeLayer(cfg)
+    layer.upload_layer(0, W)
+    x = syn.tokens(GROUPED, 24, seed=22)
+    y, idx, w, _, prof = _gpu(layer, x)
+    assert "decode_fused" in prof
+    rcfg = RouterConfig(64, 6, n_group=8, topk_group=3, group_limited=True, norm_topk_prob=normalize)
+    ry, ridx, rw, rlog = _oracle(oracle_lib, GROUPED, W, x, cfg=rcfg)
+    assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what=f"fused group-limited normalize={normalize}")
+    layer.close()
+
+
+def test_fused_block_forward(oracle_lib):
+    """RMSNorm -> MoE -> residual with the router on the f32 normalised activations."""
+    shape = syn.MoeShape(hidden=512, inter=256, n_routed_experts=16, n_shared_experts=2, top_k=4)
+    W = syn.layer_weights(shape, seed=31, std=0.05)
+    norm = np.linspace(0.5, 1.5, shape.hidden).astype(np.float32)
+    layer = MoeLayer(MoeConfig.from_shape(shape, max_tokens=32))
+    layer.upload_layer(0, W, norm_weight=norm)
+    T = 12
+    hidden0 = np.random.default_rng(32).standard_normal((T, shape.hidden)).astype(np.float32)
+    hidden = torch.from_numpy(hidden0.copy()).cuda()
+    layer.profile(True)
+    layer.profile_read(reset=True)
+    layer.block_forward(0, hidden)
+    prof = layer.profile_read(reset=True)
+    layer.profile(False)
+    layer.sync()
+    assert "decode_fused" in prof
+    xn = np.stack([oracle_lib.rms_norm(row, norm, 1e-6) for row in hidden0])
+    y, idx, _, _ = oracle_lib.moe_layer(xn, W, RouterConfig(shape.n_routed_experts, shape.top_k),
+                                        shape.n_shared_experts, threads=0)
+    counts = layer.expert_counts()
+    ref_counts = np.bincount(idx.reshape(-1), minlength=shape.n_routed_experts)
+    assert np.abs(counts - ref_counts).sum() <= 2
+    if np.array_equal(counts, ref_counts):
+        rel, cos = output_errors(hidden.cpu().numpy() - hidden0, y)
+        assert rel.max() <= MAX_REL and cos.min() >= MIN_COS, (rel.max(), cos.min())
+    layer.close()
+
+
+def test_fused_phase_trace_is_ordered(v2):
+    x = bf16_tensor(syn.tokens(V2, 8, seed=3))
+    v2.profile(True)
+    v2.forward(0, x)
+    tr = v2.profile_trace().astype(np.int64)
+    v2.profile(False)
+    v2.sync()
+    assert tr.shape[0] == torch.cuda.get_device_properties(0).multi_processor_count
+    start, logits, seen, sched, gate_up, down = (tr[:, k] for k in (0, 1, 2, 3, 4, 7))
+    for a, b in ((start, logits), (logits, seen), (seen, sched), (sched, gate_up), (gate_up, down)):
+        assert (a > 0).all() and (b >= a).all()
+    # No CTA leaves routing before the last CTA has written its logits (each CTA
+    # stamps "written" just after its arrival, hence the slack).
+    assert seen.min() >= logits.max() - 2000
