@@ -472,8 +472,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tmem_ld_wait();
 #pragma unroll
                         for (int j = 0; j < 16; ++j)
-                            if (c0 + j < valid)
-                                args.y_rows[static_cast<size_t>(row0 + c0 + j) * args.hidden + d] = __uint_as_float(r[j]);
+                            if (c0 + j < valid) {
+                                const int row = row0 + c0 + j;
+                                const int dst = args.y_rows_map != nullptr ? args.y_rows_map[row] : row;
+                                args.y_rows[static_cast<size_t>(dst) * args.hidden + d] = __uint_as_float(r[j]);
+                            }
                     }
                     tc_fence_before();
                     __syncwarp();

@@ -317,7 +317,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         if (c < valid) {
                             const float v = __uint_as_float(r[j]);
                             if (to_rows)
-                                args.y_rows[static_cast<size_t>(row0 + c) * args.hidden + d] = v;
+                                args.y_rows[static_cast<size_t>(args.y_rows_map != nullptr ? args.y_rows_map[row0 + c]
+                                                                                          : row0 + c) *
+                                                args.hidden +
+                                            d] = v;
                             else
                                 atomicAdd(args.y + static_cast<size_t>(s_ep_tok[iter & 1][c]) * args.hidden + d,
                                           s_ep_w[iter & 1][c] * v);

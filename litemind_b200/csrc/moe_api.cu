@@ -98,6 +98,8 @@ struct lm_moe_ctx {
     ncclComm_t comm = nullptr;
     const lm::NcclApi* nccl = nullptr;
     uint16_t* x_recv = nullptr;    // received token rows, (source rank, local expert) segments
+    uint16_t* x_sorted = nullptr;  // received rows, expert-major (each expert's rows contiguous)
+    int32_t* ep_row_src = nullptr;  // expert-major row -> its source-major row (where its output goes back)
     float* y_ret = nullptr;        // expert outputs of the received rows, returned to their ranks
     float* y_back = nullptr;       // this rank's rows' expert outputs, in send order
     int32_t* recv_counts = nullptr;  // [nranks, local experts] rows received per source and expert
@@ -106,6 +108,7 @@ struct lm_moe_ctx {
     int32_t* host_totals = nullptr;      // pinned [E]
     int32_t* host_recv = nullptr;        // pinned [nranks * local experts]
     CUtensorMap map_xrecv[5]{};
+    CUtensorMap map_xsorted[5]{};
 
     bool profiling = false;
     cudaEvent_t prof_events[LM_PROFILE_SLOTS + 1]{};
@@ -783,9 +786,10 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     const int32_t* recv_cnt = plan.recv_count;
     const int32_t* recv_off = plan.recv_offset;
     const int n_recv = plan.n_recv;
-    // Receiver schedule: segment (source r, local expert e), then the shared splits.
-    const int n_routed = N * El;
-    const int bn = choose_bn(n_recv, 1, n_routed);  // from the mean rows per received segment
+    // Receiver schedule: one segment per local expert (its rows from every source,
+    // made contiguous by ep_sort_rows after the dispatch), then the shared experts.
+    const int n_routed = El;
+    const int bn = choose_bn(n_recv, 1, n_routed);  // from the mean rows per local expert
     const int bi = bn_index(bn);
     Schedule& hs = *ctx->host_sched;
     int p1 = 0, p2 = 0, seg = 0;
@@ -801,12 +805,15 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
         p2 += nb * mb2;
         ++seg;
     };
-    for (int r = 0; r < N; ++r) {
-        int off = recv_off[r];
-        for (int e = 0; e < El; ++e) {
-            add_segment(off, ctx->host_recv[r * El + e], e);
-            off += ctx->host_recv[r * El + e];
+    int max_group = 0;
+    for (int e = 0, off = 0; e < El; ++e) {
+        int cnt = 0;
+        for (int r = 0; r < N; ++r) {
+            cnt += ctx->host_recv[r * El + e];
+            max_group = std::max(max_group, ctx->host_recv[r * El + e]);
         }
+        add_segment(off, cnt, e);
+        off += cnt;
     }
     for (int j = 0; j < c.n_shared_experts; ++j) add_segment(ctx->routed_cap + j * T, T, El + j);
     hs.tiles1[seg] = p1;
@@ -825,6 +832,8 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
                                  ncclBfloat16, d, ctx->comm, s));
     }
     LM_NCCL(ctx, nc.GroupEnd());
+    LM_CUDA(ctx, launch_ep_sort_rows(ctx->x_recv, ctx->x_sorted, ctx->ep_row_src, ctx->recv_counts, N, El, max_group, H,
+                                     s, false));
     prof_mark(ctx, 7, s);
     slots[n_slots++] = 7;
     // 4. Local experts on the received rows, shared experts on this rank's tokens.
@@ -841,6 +850,7 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     args.h = ctx->h;
     args.y = y;
     args.y_rows = ctx->y_ret;
+    args.y_rows_map = ctx->ep_row_src;
     args.row_token = ctx->row_token;
     args.row_weight = ctx->row_weight;
     args.status = ctx->status;
@@ -854,12 +864,12 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     args.split_max_waves = ctx->split_max_waves;
     if (pair) {
         const int hi = bn_index(bn / 2);
-        LM_CUDA(ctx, launch_gemm_gate_up_pair(bn, L.map_w13, ctx->map_xrecv[hi], map_x, args, ctx->sms, s, false));
+        LM_CUDA(ctx, launch_gemm_gate_up_pair(bn, L.map_w13, ctx->map_xsorted[hi], map_x, args, ctx->sms, s, true));
         prof_mark(ctx, 5, s);
         slots[n_slots++] = 5;
         LM_CUDA(ctx, launch_gemm_down_pair(bn, L.map_w2, ctx->map_h[hi], args, ctx->sms, s, true));
     } else {
-        LM_CUDA(ctx, launch_gemm_gate_up(bn, L.map_w13, ctx->map_xrecv[bi], map_x, args, ctx->sms, s, false));
+        LM_CUDA(ctx, launch_gemm_gate_up(bn, L.map_w13, ctx->map_xsorted[bi], map_x, args, ctx->sms, s, true));
         prof_mark(ctx, 5, s);
         slots[n_slots++] = 5;
         LM_CUDA(ctx, launch_gemm_down(bn, L.map_w2, ctx->map_h[bi], args, ctx->sms, s, true));
@@ -1109,7 +1119,8 @@ lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t ra
         }
     if ((st = alloc(ctx, &ctx->h, h_rows * I)) || (st = alloc(ctx, &ctx->x_recv, cap * H)) ||
         (st = alloc(ctx, &ctx->y_ret, cap * H)) || (st = alloc(ctx, &ctx->y_back, T * K * H)) ||
-        (st = alloc(ctx, &ctx->recv_counts, static_cast<size_t>(nranks) * El)) || (st = alloc(ctx, &ctx->sched_ep, 1)))
+        (st = alloc(ctx, &ctx->recv_counts, static_cast<size_t>(nranks) * El)) || (st = alloc(ctx, &ctx->sched_ep, 1)) ||
+        (st = alloc(ctx, &ctx->x_sorted, cap * H)) || (st = alloc(ctx, &ctx->ep_row_src, cap)))
         return st;
     LM_CUDA(ctx, cudaMallocHost(&ctx->host_sched, sizeof(Schedule)));
     LM_CUDA(ctx, cudaMallocHost(&ctx->host_totals, c.n_routed_experts * sizeof(int32_t)));
@@ -1117,6 +1128,7 @@ lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t ra
     std::memset(ctx->host_sched, 0, sizeof(Schedule));
     for (int i = 0; i < 5; ++i) {
         if (!encode_tensor_map_bf16(&ctx->map_xrecv[i], ctx->x_recv, cap, H, kBnChoices[i], 64, err) ||
+            !encode_tensor_map_bf16(&ctx->map_xsorted[i], ctx->x_sorted, cap, H, kBnChoices[i], 64, err) ||
             !encode_tensor_map_bf16(&ctx->map_h[i], ctx->h, h_rows, I, kBnChoices[i], 64, err))
             return fail(ctx, LM_ERR_CUDA, err);
     }

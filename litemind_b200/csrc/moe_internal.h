@@ -68,6 +68,11 @@ cudaError_t launch_place(const int32_t* topk_idx, const float* topk_w, const int
                          float* row_weight, int32_t* slot_row, float* y_zero, cudaStream_t stream, bool pdl);
 cudaError_t launch_ep_combine(float* y, const float* back, const int32_t* slot_row, const float* topk_w, int tokens,
                               int top_k, int hidden, cudaStream_t stream, bool pdl);
+// Expert parallelism: received rows (source-major) -> expert-major, with row_src[row]
+// = the row's source-major index.  max_group_rows: the largest (source, expert) group.
+cudaError_t launch_ep_sort_rows(const uint16_t* x_recv, uint16_t* x_sorted, int32_t* row_src,
+                               const int32_t* recv_counts, int nranks, int local_experts, int max_group_rows,
+                               int hidden, cudaStream_t stream, bool pdl);
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* row_token, int rows, int hidden, uint16_t* x_perm,
                                cudaStream_t stream, bool pdl);
 cudaError_t launch_route_small(const uint16_t* x, const float* x_f32, const float* w, const float* bias,
@@ -90,6 +95,7 @@ struct GemmArgs {
     int32_t hidden;
     int32_t inter;
     float* y_rows;             // when set, routed rows' down outputs are stored here by row, unweighted
+    const int32_t* y_rows_map; // with y_rows: routed row r is stored at row y_rows_map[r] (null: at r)
     float* logits;             // router kind: [T, experts] f32 output
     const float* bias;         // router kind: per-expert logit bias or null
     int32_t experts;           // router kind: experts (<= 128)

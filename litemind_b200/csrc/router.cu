@@ -399,6 +399,47 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(float* __restrict__ y, 
     reinterpret_cast<float4*>(y + static_cast<size_t>(t) * H)[c] = acc;
 }
 
+// Expert parallelism: received rows arrive grouped by source rank, each source's
+// rows grouped by this rank's experts.  The grouped GEMMs want each expert's rows
+// contiguous, so each expert's weights stream once instead of once per source.
+// Block (b, y) with b = (source r, local expert e) copies rows [64 y, 64 y + 64) of
+// its group to their expert-major place and records where each came from, so the
+// down projection can store its output rows back in source-major order.
+constexpr int kSortRows = 64;
+__global__ void __launch_bounds__(256) ep_sort_rows_kernel(const uint16_t* __restrict__ x_recv,
+                                                           uint16_t* __restrict__ x_sorted,
+                                                           int32_t* __restrict__ row_src,
+                                                           const int32_t* __restrict__ recv_counts, int N, int El,
+                                                           int H) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int r = blockIdx.x / El;
+    const int e = blockIdx.x - r * El;
+    __shared__ int s_src, s_dst, s_cnt;
+    if (threadIdx.x == 0) {
+        int src = 0, dst = 0;
+        for (int rr = 0; rr < N; ++rr) {
+            for (int ee = 0; ee < El; ++ee) {
+                const int c = recv_counts[rr * El + ee];
+                if (rr < r || (rr == r && ee < e)) src += c;  // source-major position
+                if (ee < e || (ee == e && rr < r)) dst += c;  // expert-major position
+            }
+        }
+        s_src = src;
+        s_dst = dst;
+        s_cnt = recv_counts[r * El + e];
+    }
+    __syncthreads();
+    const int j0 = blockIdx.y * kSortRows;
+    const int rows = min(kSortRows, s_cnt - j0);
+    if (rows <= 0) return;
+    const int vec = H / 8;
+    const uint4* src = reinterpret_cast<const uint4*>(x_recv) + static_cast<size_t>(s_src + j0) * vec;
+    uint4* dst = reinterpret_cast<uint4*>(x_sorted) + static_cast<size_t>(s_dst + j0) * vec;
+    for (int q = threadIdx.x; q < rows * vec; q += blockDim.x) dst[q] = src[q];
+    for (int j = threadIdx.x; j < rows; j += blockDim.x) row_src[s_dst + j0 + j] = s_src + j0 + j;
+}
+
 // Small T (<= kRouteTile): the whole routing stage in one launch.  CTA b computes
 // expert b's logit for every token (one warp per token) and zeroes a slice of y;
 // the last CTA to finish (an atomic ticket) routes every token (again one warp per
@@ -612,6 +653,15 @@ cudaError_t launch_ep_combine(float* y, const float* back, const int32_t* slot_r
     const int64_t threads = static_cast<int64_t>(tokens) * (hidden / 4);
     return launch_k(ep_combine_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), stream, pdl, y,
                     back, slot_row, topk_w, tokens, top_k, hidden);
+}
+
+cudaError_t launch_ep_sort_rows(const uint16_t* x_recv, uint16_t* x_sorted, int32_t* row_src,
+                               const int32_t* recv_counts, int nranks, int local_experts, int max_group_rows,
+                               int hidden, cudaStream_t stream, bool pdl) {
+    if (max_group_rows <= 0) return cudaSuccess;
+    const dim3 grid(nranks * local_experts, (max_group_rows + kSortRows - 1) / kSortRows);
+    return launch_k(ep_sort_rows_kernel, grid, dim3(256), stream, pdl, x_recv, x_sorted, row_src, recv_counts,
+                    nranks, local_experts, hidden);
 }
 
 template <typename XT, int EPL>
