@@ -100,6 +100,43 @@ lm_status lm_moe_upload_layer(lm_moe_ctx* ctx, int32_t layer, const float* route
                               const uint16_t* shared_gate, const uint16_t* shared_up,
                               const uint16_t* shared_down, const float* norm_weight);
 
+/*
+ * The HBM expert loader: uploads one mixture-of-experts layer straight from
+ * SafeTensors checkpoint shards (the format the reference reads with
+ * SafeTensor::open, src/SafeTensor.cpp:87-152), with the tensor names of
+ * DeepSeekRunner::Impl::resolve_layer (src/DeepSeekRunner.cpp:157-224):
+ *   model.layers.{L}.mlp.gate.weight                     [E, H]  BF16, F16 or F32
+ *   model.layers.{L}.post_attention_layernorm.weight     [H]     BF16, F16 or F32
+ *   model.layers.{L}.mlp.experts.{e}.{gate,up}_proj.weight [I, H] BF16
+ *   model.layers.{L}.mlp.experts.{e}.down_proj.weight    [H, I]  BF16
+ *   model.layers.{L}.mlp.shared_experts.{gate,up}_proj.weight [n_shared * I, H] BF16
+ *   model.layers.{L}.mlp.shared_experts.down_proj.weight [H, n_shared * I] BF16
+ * `layer` is this context's layer slot, `checkpoint_layer` the L in the names.
+ * Tensors may be spread over the shards in any way; each shard is memory-mapped and
+ * only the tensors this device holds are read (under expert parallelism, its own
+ * experts).  Shape and dtype mismatches fail with the reference's messages
+ * (WeightStore::require, src/WeightStore.cpp:119-140) in lm_moe_last_error.
+ */
+lm_status lm_moe_load_safetensors(lm_moe_ctx* ctx, int32_t layer, int32_t checkpoint_layer,
+                                  const char* const* shard_paths, int32_t n_shards);
+
+/*
+ * Header lookup of one tensor in one SafeTensors shard, without a GPU: dtype
+ * (LM_DTYPE_*), rank, up to LM_SAFETENSORS_MAX_DIMS dimensions, file-absolute
+ * payload offset and size.  Returns LM_ERR_INVALID_ARGUMENT for a malformed shard
+ * and LM_ERR_NOT_LOADED when the name is absent, with the reason in `error`
+ * (truncated to error_len bytes; may be null).  No reference counterpart as a C
+ * entry: it exposes SafeTensor::find (src/SafeTensor.cpp:154-157) to tests and tools.
+ */
+#define LM_DTYPE_UNKNOWN 0
+#define LM_DTYPE_BF16 1
+#define LM_DTYPE_F16 2
+#define LM_DTYPE_F32 3
+#define LM_DTYPE_OTHER 4
+#define LM_SAFETENSORS_MAX_DIMS 8
+lm_status lm_safetensors_info(const char* path, const char* name, int32_t* dtype, int32_t* ndim, int64_t* shape,
+                              uint64_t* offset, uint64_t* nbytes, char* error, int32_t error_len);
+
 /* Uploads one routed expert (the unit ExpertCache::touch streams,
  * src/ExpertCache.cpp:9-47): gate, up [inter, hidden], down [hidden, inter]. */
 lm_status lm_moe_upload_expert(lm_moe_ctx* ctx, int32_t layer, int32_t expert,

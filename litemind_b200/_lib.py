@@ -25,6 +25,9 @@ LM_DECODE_TRACE_SLOTS = 16
 PROFILE_SLOT_NAMES = ["gather_rows", "route", "router_topk", "dispatch_scan", "place", "gemm_gate_up", "gemm_down",
                       "ep_exchange", "decode_fused"]
 
+LM_DTYPE_UNKNOWN, LM_DTYPE_BF16, LM_DTYPE_F16, LM_DTYPE_F32, LM_DTYPE_OTHER = 0, 1, 2, 3, 4
+LM_SAFETENSORS_MAX_DIMS = 8
+
 LM_TOPK_GREEDY = 0
 LM_TOPK_GROUP_LIMITED_GREEDY = 1
 
@@ -63,6 +66,8 @@ SIGNATURES = {
     "lm_status_string": (C.c_char_p, [_i32]),
     "lm_moe_upload_layer": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "lm_moe_upload_expert": (_i32, [_vp, _i32, _i32, _vp, _vp, _vp]),
+    "lm_moe_load_safetensors": (_i32, [_vp, _i32, _i32, C.POINTER(C.c_char_p), _i32]),
+    "lm_safetensors_info": (_i32, [C.c_char_p, C.c_char_p, _vp, _vp, _vp, _vp, _vp, _vp, _i32]),
     "lm_moe_route": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _vp]),
     "lm_moe_select": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
     "lm_moe_forward": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp]),

@@ -16,6 +16,7 @@
 // shared FFN of width inter * n_shared, src/DeepSeekRunner.cpp:217-222).
 #include "moe_internal.h"
 #include "nccl_dl.h"
+#include "host/SafeTensors.hpp"
 
 #include <algorithm>
 #include <cstdlib>
@@ -280,6 +281,65 @@ lm_status prof_end(lm_moe_ctx* ctx, const int* slots, int n) {
     return LM_OK;
 }
 
+// The shared experts (gate/up [n_shared * I, H], down [H, n_shared * I]), the f32
+// router [E, H] in its three device forms, and the block's RMSNorm weight (ones
+// when null).
+lm_status upload_shared_and_router(lm_moe_ctx* ctx, LayerWeights& L, const float* router, const uint16_t* shared_gate,
+                                   const uint16_t* shared_up, const uint16_t* shared_down, const float* norm_weight) {
+    const lm_moe_config& c = ctx->cfg;
+    const size_t H = c.hidden_size, I = c.moe_intermediate_size, E = c.n_routed_experts;
+    lm_status st;
+    const size_t S = I * c.n_shared_experts;
+    for (int t = 0; t < c.n_shared_experts; ++t) {
+        if ((st = upload_segment(ctx, L, ctx->local_experts + t, shared_gate + t * I * H, shared_up + t * I * H,
+                                 shared_down + t * I, S)) != LM_OK)
+            return st;
+    }
+    L.shared_loaded = true;
+    std::vector<float> transposed(E * H);
+    for (size_t e = 0; e < E; ++e)
+        for (size_t k = 0; k < H; ++k) transposed[k * E + e] = router[e * H + k];
+    LM_CUDA(ctx, cudaMemcpy(L.router, router, E * H * sizeof(float), cudaMemcpyHostToDevice));
+    // The f32 router as three bf16 parts (each the rounding of what the previous
+    // ones leave), so hi + mid + lo == router exactly and every product with a bf16
+    // token is exact in f32 on the tensor cores.
+    if (E <= 128) {
+        std::vector<uint16_t> cat(128 * 3 * H, 0);
+        auto rne = [](float v) -> uint16_t {
+            uint32_t b;
+            std::memcpy(&b, &v, 4);
+            return static_cast<uint16_t>((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
+        };
+        auto widen = [](uint16_t h) -> float {
+            const uint32_t b = static_cast<uint32_t>(h) << 16;
+            float v;
+            std::memcpy(&v, &b, 4);
+            return v;
+        };
+        for (size_t e = 0; e < E; ++e)
+            for (size_t k = 0; k < H; ++k) {
+                const float w = router[e * H + k];
+                const uint16_t hi = rne(w);
+                const float r1 = w - widen(hi);
+                const uint16_t mid = rne(r1);
+                const float r2 = r1 - widen(mid);
+                cat[e * 3 * H + k] = hi;
+                cat[e * 3 * H + H + k] = mid;
+                cat[e * 3 * H + 2 * H + k] = rne(r2);
+            }
+        LM_CUDA(ctx, cudaMemcpy(L.router_cat, cat.data(), cat.size() * sizeof(uint16_t), cudaMemcpyHostToDevice));
+    }
+    LM_CUDA(ctx, cudaMemcpy(L.router_t, transposed.data(), E * H * sizeof(float), cudaMemcpyHostToDevice));
+    if (norm_weight != nullptr)
+        LM_CUDA(ctx, cudaMemcpy(L.norm, norm_weight, H * sizeof(float), cudaMemcpyHostToDevice));
+    else {
+        std::vector<float> ones(H, 1.0f);
+        LM_CUDA(ctx, cudaMemcpy(L.norm, ones.data(), H * sizeof(float), cudaMemcpyHostToDevice));
+    }
+    ctx->uploaded_bytes += 2 * E * H * 4;
+    L.router_loaded = true;
+    return LM_OK;
+}
 }  // namespace
 }  // namespace lm
 
@@ -443,56 +503,111 @@ lm_status lm_moe_upload_layer(lm_moe_ctx* ctx, int32_t layer, const float* route
             return st;
         L.expert_loaded[s] = 1;
     }
-    const size_t S = I * c.n_shared_experts;
-    for (int t = 0; t < c.n_shared_experts; ++t) {
-        if ((st = upload_segment(ctx, L, ctx->local_experts + t, shared_gate + t * I * H, shared_up + t * I * H,
-                                 shared_down + t * I, S)) != LM_OK)
-            return st;
+    return upload_shared_and_router(ctx, L, router, shared_gate, shared_up, shared_down, norm_weight);
+}
+
+
+lm_status lm_safetensors_info(const char* path, const char* name, int32_t* dtype, int32_t* ndim, int64_t* shape,
+                              uint64_t* offset, uint64_t* nbytes, char* error, int32_t error_len) {
+    auto set_error = [&](const std::string& e) {
+        if (error != nullptr && error_len > 0) {
+            const size_t n = std::min(e.size(), static_cast<size_t>(error_len - 1));
+            std::memcpy(error, e.data(), n);
+            error[n] = '\0';
+        }
+    };
+    set_error("");
+    if (path == nullptr || name == nullptr) {
+        set_error("null path or name");
+        return LM_ERR_INVALID_ARGUMENT;
     }
-    L.shared_loaded = true;
-    std::vector<float> transposed(E * H);
-    for (size_t e = 0; e < E; ++e)
-        for (size_t k = 0; k < H; ++k) transposed[k * E + e] = router[e * H + k];
-    LM_CUDA(ctx, cudaMemcpy(L.router, router, E * H * sizeof(float), cudaMemcpyHostToDevice));
-    // The f32 router as three bf16 parts (each the rounding of what the previous
-    // ones leave), so hi + mid + lo == router exactly and every product with a bf16
-    // token is exact in f32 on the tensor cores.
-    if (E <= 128) {
-        std::vector<uint16_t> cat(128 * 3 * H, 0);
-        auto rne = [](float v) -> uint16_t {
-            uint32_t b;
-            std::memcpy(&b, &v, 4);
-            return static_cast<uint16_t>((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
-        };
-        auto widen = [](uint16_t h) -> float {
-            const uint32_t b = static_cast<uint32_t>(h) << 16;
-            float v;
-            std::memcpy(&v, &b, 4);
-            return v;
-        };
-        for (size_t e = 0; e < E; ++e)
-            for (size_t k = 0; k < H; ++k) {
-                const float w = router[e * H + k];
-                const uint16_t hi = rne(w);
-                const float r1 = w - widen(hi);
-                const uint16_t mid = rne(r1);
-                const float r2 = r1 - widen(mid);
-                cat[e * 3 * H + k] = hi;
-                cat[e * 3 * H + H + k] = mid;
-                cat[e * 3 * H + 2 * H + k] = rne(r2);
-            }
-        LM_CUDA(ctx, cudaMemcpy(L.router_cat, cat.data(), cat.size() * sizeof(uint16_t), cudaMemcpyHostToDevice));
+    host::StShard shard;
+    std::string err;
+    if (!shard.open(path, err)) {
+        set_error(err);
+        return LM_ERR_INVALID_ARGUMENT;
     }
-    LM_CUDA(ctx, cudaMemcpy(L.router_t, transposed.data(), E * H * sizeof(float), cudaMemcpyHostToDevice));
-    if (norm_weight != nullptr)
-        LM_CUDA(ctx, cudaMemcpy(L.norm, norm_weight, H * sizeof(float), cudaMemcpyHostToDevice));
-    else {
-        std::vector<float> ones(H, 1.0f);
-        LM_CUDA(ctx, cudaMemcpy(L.norm, ones.data(), H * sizeof(float), cudaMemcpyHostToDevice));
+    for (const host::StTensor& t : shard.tensors()) {
+        if (t.name != name) continue;
+        if (dtype != nullptr) *dtype = static_cast<int32_t>(t.dtype);
+        if (ndim != nullptr) *ndim = static_cast<int32_t>(t.shape.size());
+        if (shape != nullptr)
+            for (size_t i = 0; i < t.shape.size() && i < LM_SAFETENSORS_MAX_DIMS; ++i) shape[i] = t.shape[i];
+        if (offset != nullptr) *offset = t.offset;
+        if (nbytes != nullptr) *nbytes = t.nbytes;
+        if (t.shape.size() > LM_SAFETENSORS_MAX_DIMS) {
+            set_error("tensor has more than LM_SAFETENSORS_MAX_DIMS dimensions");
+            return LM_ERR_UNSUPPORTED;
+        }
+        return LM_OK;
     }
-    ctx->uploaded_bytes += 2 * E * H * 4;
-    L.router_loaded = true;
-    return LM_OK;
+    set_error(std::string("no tensor named '") + name + "' in " + path);
+    return LM_ERR_NOT_LOADED;
+}
+
+lm_status lm_moe_load_safetensors(lm_moe_ctx* ctx, int32_t layer, int32_t checkpoint_layer,
+                                  const char* const* shard_paths, int32_t n_shards) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= static_cast<int32_t>(ctx->layers.size()))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "layer index out of range");
+    if (shard_paths == nullptr || n_shards <= 0 || checkpoint_layer < 0)
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "need at least one shard path and a checkpoint layer >= 0");
+    std::vector<std::string> paths;
+    for (int i = 0; i < n_shards; ++i) {
+        if (shard_paths[i] == nullptr) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "null shard path");
+        paths.emplace_back(shard_paths[i]);
+    }
+    host::StCheckpoint ck;
+    std::string err;
+    if (!ck.open(paths, err)) return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+    const lm_moe_config& c = ctx->cfg;
+    const int64_t H = c.hidden_size, I = c.moe_intermediate_size, E = c.n_routed_experts;
+    const int64_t S = I * c.n_shared_experts;
+    // Tensor names as DeepSeekRunner::Impl::resolve_layer reads them (src/DeepSeekRunner.cpp:157-224).
+    const std::string prefix = "model.layers." + std::to_string(checkpoint_layer) + ".";
+    std::vector<float> router, norm;
+    if (ck.find(prefix + "mlp.gate.weight") == nullptr && ck.find(prefix + "mlp.gate_proj.weight") != nullptr)
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "checkpoint layer " + std::to_string(checkpoint_layer) +
+                                                      " is a dense feed-forward layer, not a mixture of experts");
+    if (!ck.read_float32(prefix + "mlp.gate.weight", {E, H}, router, err) ||
+        !ck.read_float32(prefix + "post_attention_layernorm.weight", {H}, norm, err))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+    // Payload pointers of a shard whose header length is odd would be misaligned for
+    // 16-bit reads: such tensors are copied out first.
+    std::vector<std::vector<uint16_t>> copies;
+    auto bf16 = [&](const host::StTensor* t) -> const uint16_t* {
+        if ((reinterpret_cast<uintptr_t>(t->data) & 1u) == 0) return reinterpret_cast<const uint16_t*>(t->data);
+        copies.emplace_back(t->nbytes / 2);
+        std::memcpy(copies.back().data(), t->data, t->nbytes);
+        return copies.back().data();
+    };
+    lm_status st;
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    if ((st = ensure_layer_buffers(ctx, layer)) != LM_OK) return st;
+    LayerWeights& L = ctx->layers[layer];
+    for (int s = 0; s < ctx->local_experts; ++s) {
+        const std::string ep = prefix + "mlp.experts." + std::to_string(ctx->first_expert + s) + ".";
+        const host::StTensor* g = ck.require(ep + "gate_proj.weight", {I, H}, host::StDtype::BF16, err);
+        const host::StTensor* u = g ? ck.require(ep + "up_proj.weight", {I, H}, host::StDtype::BF16, err) : nullptr;
+        const host::StTensor* d = u ? ck.require(ep + "down_proj.weight", {H, I}, host::StDtype::BF16, err) : nullptr;
+        if (d == nullptr) return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+        copies.clear();
+        if ((st = upload_segment(ctx, L, s, bf16(g), bf16(u), bf16(d), static_cast<size_t>(I))) != LM_OK) return st;
+        L.expert_loaded[s] = 1;
+    }
+    const uint16_t *sg = nullptr, *su = nullptr, *sd = nullptr;
+    copies.clear();
+    if (c.n_shared_experts > 0) {
+        const std::string sp = prefix + "mlp.shared_experts.";
+        const host::StTensor* g = ck.require(sp + "gate_proj.weight", {S, H}, host::StDtype::BF16, err);
+        const host::StTensor* u = g ? ck.require(sp + "up_proj.weight", {S, H}, host::StDtype::BF16, err) : nullptr;
+        const host::StTensor* d = u ? ck.require(sp + "down_proj.weight", {H, S}, host::StDtype::BF16, err) : nullptr;
+        if (d == nullptr) return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+        sg = bf16(g);
+        su = bf16(u);
+        sd = bf16(d);
+    }
+    return upload_shared_and_router(ctx, L, router.data(), sg, su, sd, norm.data());
 }
 
 lm_status lm_moe_upload_expert(lm_moe_ctx* ctx, int32_t layer, int32_t expert, const uint16_t* gate,

@@ -137,6 +137,13 @@ class MoeLayer:
             self.ctx, layer, _ptr(w["router"]), _ptr(w["gate"]), _ptr(w["up"]), _ptr(w["down"]),
             _ptr(w["shared_gate"]), _ptr(w["shared_up"]), _ptr(w["shared_down"]), _ptr(norm)))
 
+    def load_safetensors(self, layer: int, shard_paths, checkpoint_layer: int | None = None) -> None:
+        """lm_moe_load_safetensors: this context's layer slot from a SafeTensors checkpoint."""
+        paths = [str(p).encode() for p in shard_paths]
+        arr = (C.c_char_p * len(paths))(*paths)
+        self._check(self.lib.lm_moe_load_safetensors(self.ctx, layer, layer if checkpoint_layer is None
+                                                     else checkpoint_layer, arr, len(paths)))
+
     def upload_expert(self, layer: int, expert: int, gate, up, down) -> None:
         g, u, d = (np.ascontiguousarray(a) for a in (gate, up, down))
         self._check(self.lib.lm_moe_upload_expert(self.ctx, layer, expert, _ptr(g), _ptr(u), _ptr(d)))

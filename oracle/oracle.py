@@ -232,10 +232,24 @@ class Reference(_Base):
         L.ref_cache_stats.argtypes = [C.c_void_p, _u64p]
         L.ref_cache_make_key.argtypes = [C.c_uint64, C.c_uint64]
         L.ref_cache_make_key.restype = C.c_uint64
+        L.ref_safetensor_info.argtypes = [C.c_char_p, C.c_char_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_char_p, C.c_int32]
+        L.ref_safetensor_info.restype = C.c_int
         self.threads = 0
         self._matvec_bf16 = lambda w, x, out, r, c: L.ref_matvec_bf16(w, x, out, r, c, self.threads)
         self._matvec_bf16_acc = lambda w, x, out, r, c, s: L.ref_matvec_bf16_accumulate(
             w, x, out, r, c, s, self.threads)
+
+    def safetensor_info(self, path: str, name: str):
+        """SafeTensor::open + find on one shard: (status, dtype, shape, offset, nbytes, error);
+        status 0 found, 1 shard rejected, 2 no such tensor."""
+        dtype, ndim = C.c_int32(0), C.c_int32(0)
+        shape = (C.c_int64 * 8)()
+        offset, nbytes = C.c_uint64(0), C.c_uint64(0)
+        err = C.create_string_buffer(1024)
+        rc = self.lib.ref_safetensor_info(path.encode(), name.encode(), C.byref(dtype), C.byref(ndim), shape,
+                                          C.byref(offset), C.byref(nbytes), err, len(err))
+        return rc, dtype.value, list(shape[: ndim.value]), offset.value, nbytes.value, err.value.decode()
 
     def kerneltest_inputs(self):
         """tests/KernelTest.cpp's seeded 67x253 inputs: (w_f32, w_bf16, x)."""

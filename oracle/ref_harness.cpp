@@ -15,6 +15,7 @@
 #include "ExpertCache.hpp"
 #include "Gemm.hpp"
 #include "MoeRouter.hpp"
+#include "SafeTensor.hpp"
 #include "Tensor.hpp"
 #include "Threading.hpp"
 
@@ -250,6 +251,36 @@ void ref_cache_stats(void* handle, uint64_t* out6) {
 }
 uint64_t ref_cache_make_key(uint64_t layer, uint64_t expert) {
     return ExpertCache::make_key(static_cast<std::size_t>(layer), static_cast<std::size_t>(expert));
+}
+
+// SafeTensor::open + find (src/SafeTensor.cpp:87-157) on one shard: 0 found, 1 the
+// shard was rejected (message in err), 2 no such tensor.  dtype: 1 BF16, 2 F16,
+// 3 F32, 4 any other known type (the codes of lm_safetensors_info).
+int ref_safetensor_info(const char* path, const char* name, int32_t* dtype, int32_t* ndim, int64_t* shape,
+                        uint64_t* offset, uint64_t* nbytes, char* err, int32_t err_len) {
+    SafeTensor shard;
+    std::string error;
+    if (!shard.open(path, error)) {
+        if (err != nullptr && err_len > 0) {
+            const size_t n = std::min(error.size(), static_cast<size_t>(err_len - 1));
+            std::memcpy(err, error.data(), n);
+            err[n] = '\0';
+        }
+        return 1;
+    }
+    const Tensor* t = shard.find(name);
+    if (t == nullptr) return 2;
+    switch (t->data_type()) {
+        case DataType::BFloat16: *dtype = 1; break;
+        case DataType::Float16: *dtype = 2; break;
+        case DataType::Float32: *dtype = 3; break;
+        default: *dtype = 4; break;
+    }
+    *ndim = static_cast<int32_t>(t->shape().size());
+    for (size_t i = 0; i < t->shape().size() && i < 8; ++i) shape[i] = static_cast<int64_t>(t->shape()[i]);
+    *offset = t->offset();
+    *nbytes = t->byte_size();
+    return 0;
 }
 
 }  // extern "C"
