@@ -137,6 +137,25 @@ lm_status lm_moe_load_safetensors(lm_moe_ctx* ctx, int32_t layer, int32_t checkp
 lm_status lm_safetensors_info(const char* path, const char* name, int32_t* dtype, int32_t* ndim, int64_t* shape,
                               uint64_t* offset, uint64_t* nbytes, char* error, int32_t error_len);
 
+/*
+ * Dense feed-forward layers (DeepSeek-V2-Lite's first layer, intermediate 10944:
+ * src/DeepSeekRunner.cpp:270-271, include/Config.hpp:59) on the same grouped GEMM
+ * kernels, as one segment of every token with weight 1.  Dense layers have their
+ * own index space, 0.. per context.  gate/up [inter, hidden], down [hidden, inter]
+ * bf16; inter a multiple of 64; norm_weight [hidden] f32 or NULL (ones).
+ * lm_ffn_forward: y (f32 [T, hidden]) = FFN(x) (or += with accumulate != 0);
+ * lm_ffn_block_forward: hidden += FFN(rms_norm(hidden)).  lm_ffn_load_safetensors
+ * reads model.layers.{L}.mlp.{gate,up,down}_proj.weight and
+ * post_attention_layernorm.weight from SafeTensors shards.
+ */
+lm_status lm_ffn_upload(lm_moe_ctx* ctx, int32_t layer, int32_t intermediate, const uint16_t* gate, const uint16_t* up,
+                        const uint16_t* down, const float* norm_weight);
+lm_status lm_ffn_load_safetensors(lm_moe_ctx* ctx, int32_t layer, int32_t checkpoint_layer, int32_t intermediate,
+                                  const char* const* shard_paths, int32_t n_shards);
+lm_status lm_ffn_forward(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int32_t tokens, float* y,
+                         int32_t accumulate, void* stream);
+lm_status lm_ffn_block_forward(lm_moe_ctx* ctx, int32_t layer, float* hidden, int32_t tokens, void* stream);
+
 /* Uploads one routed expert (the unit ExpertCache::touch streams,
  * src/ExpertCache.cpp:9-47): gate, up [inter, hidden], down [hidden, inter]. */
 lm_status lm_moe_upload_expert(lm_moe_ctx* ctx, int32_t layer, int32_t expert,

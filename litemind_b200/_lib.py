@@ -67,6 +67,10 @@ SIGNATURES = {
     "lm_moe_upload_layer": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "lm_moe_upload_expert": (_i32, [_vp, _i32, _i32, _vp, _vp, _vp]),
     "lm_moe_load_safetensors": (_i32, [_vp, _i32, _i32, C.POINTER(C.c_char_p), _i32]),
+    "lm_ffn_upload": (_i32, [_vp, _i32, _i32, _vp, _vp, _vp, _vp]),
+    "lm_ffn_load_safetensors": (_i32, [_vp, _i32, _i32, _i32, C.POINTER(C.c_char_p), _i32]),
+    "lm_ffn_forward": (_i32, [_vp, _i32, _vp, _i32, _vp, _i32, _vp]),
+    "lm_ffn_block_forward": (_i32, [_vp, _i32, _vp, _i32, _vp]),
     "lm_safetensors_info": (_i32, [C.c_char_p, C.c_char_p, _vp, _vp, _vp, _vp, _vp, _vp, _i32]),
     "lm_moe_route": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _vp]),
     "lm_moe_select": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),

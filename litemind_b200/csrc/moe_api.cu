@@ -47,6 +47,17 @@ struct LayerWeights {
     }
 };
 
+// A dense feed-forward layer (DeepSeek's first layers, src/DeepSeekRunner.cpp:270-271):
+// gate/up [inter, hidden] interleaved tile-major like an expert, down [hidden, inter].
+struct DenseWeights {
+    uint16_t* w13 = nullptr;
+    uint16_t* w2 = nullptr;
+    float* norm = nullptr;
+    int inter = 0;
+    CUtensorMap map_w13{};
+    CUtensorMap map_w2{};
+};
+
 constexpr int kBnChoices[5] = {16, 32, 64, 128, 256};
 
 }  // namespace lm
@@ -81,6 +92,11 @@ struct lm_moe_ctx {
     unsigned long long* grid_bar = nullptr;  // the fused decode kernel's arrival counters
     unsigned long long decode_epoch = 0;     // fused decode launches so far (their counter targets)
     unsigned long long* decode_trace = nullptr;  // per-CTA phase stamps of the last fused launch (profiling)
+    std::vector<lm::DenseWeights> dense;  // dense feed-forward layers (lm_ffn_*)
+    uint16_t* dense_h = nullptr;       // [max_tokens, widest dense inter] SwiGLU outputs
+    int dense_h_inter = 0;
+    CUtensorMap dense_map_h[5]{};
+    lm::Schedule* dense_sched = nullptr;
     float* split_ws = nullptr;        // gate/up split-K partial tiles
     int32_t* split_ticket = nullptr;  // k-blocks done per split tile, zero between uses
     unsigned int* ticket = nullptr;  // last-CTA ticket of the fused small-T route kernel
@@ -608,6 +624,159 @@ lm_status lm_moe_load_safetensors(lm_moe_ctx* ctx, int32_t layer, int32_t checkp
         sd = bf16(d);
     }
     return upload_shared_and_router(ctx, L, router.data(), sg, su, sd, norm.data());
+}
+
+lm_status lm_ffn_upload(lm_moe_ctx* ctx, int32_t layer, int32_t intermediate, const uint16_t* gate, const uint16_t* up,
+                        const uint16_t* down, const float* norm_weight) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    const lm_moe_config& c = ctx->cfg;
+    if (layer < 0 || layer > 4096) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "dense layer index out of range");
+    if (intermediate <= 0 || intermediate % 64 != 0)
+        return fail(ctx, LM_ERR_UNSUPPORTED, "the dense intermediate size must be a positive multiple of 64");
+    if (gate == nullptr || up == nullptr || down == nullptr) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "null weight");
+    lm_status st;
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    if (static_cast<int32_t>(ctx->dense.size()) <= layer) ctx->dense.resize(layer + 1);
+    DenseWeights& D = ctx->dense[layer];
+    const size_t H = c.hidden_size, I = intermediate;
+    if (D.w13 != nullptr && D.inter != intermediate)
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "dense layer was uploaded with another intermediate size");
+    if (D.w13 == nullptr) {
+        if ((st = alloc(ctx, &D.w13, 2 * I * H)) || (st = alloc(ctx, &D.w2, H * I)) || (st = alloc(ctx, &D.norm, H)))
+            return st;
+        D.inter = intermediate;
+        ctx->resident_bytes += 3 * I * H * 2 + H * 4;
+        std::string err;
+        if (!encode_tensor_map_bf16(&D.map_w13, D.w13, 2 * I * H / 64, 64, 128, 64, err) ||
+            !encode_tensor_map_bf16(&D.map_w2, D.w2, H * I / 64, 64, 128, 64, err))
+            return fail(ctx, LM_ERR_CUDA, err);
+    }
+    if (intermediate > ctx->dense_h_inter) {
+        // SwiGLU outputs of the widest dense layer for max_tokens rows.
+        const size_t rows = c.max_tokens;
+        for (auto it = ctx->allocations.begin(); it != ctx->allocations.end(); ++it)
+            if (*it == ctx->dense_h) {
+                cudaFree(*it);
+                ctx->allocations.erase(it);
+                break;
+            }
+        if ((st = alloc(ctx, &ctx->dense_h, rows * I)) != LM_OK) return st;
+        if (ctx->dense_sched == nullptr && (st = alloc(ctx, &ctx->dense_sched, 1)) != LM_OK) return st;
+        ctx->dense_h_inter = intermediate;
+        std::string err;
+        for (int i = 0; i < 5; ++i)
+            if (!encode_tensor_map_bf16(&ctx->dense_map_h[i], ctx->dense_h, rows, I, kBnChoices[i], 64, err))
+                return fail(ctx, LM_ERR_CUDA, err);
+    }
+    std::vector<uint16_t> staging(2 * I * H);
+    tile_major(staging.data(), 2 * I, H, [&](size_t r) { return ((r & 1) ? up : gate) + (r >> 1) * H; });
+    LM_CUDA(ctx, cudaMemcpy(D.w13, staging.data(), 2 * I * H * 2, cudaMemcpyHostToDevice));
+    tile_major(staging.data(), H, I, [&](size_t r) { return down + r * I; });
+    LM_CUDA(ctx, cudaMemcpy(D.w2, staging.data(), H * I * 2, cudaMemcpyHostToDevice));
+    std::vector<float> ones;
+    if (norm_weight == nullptr) ones.assign(H, 1.0f);
+    LM_CUDA(ctx, cudaMemcpy(D.norm, norm_weight != nullptr ? norm_weight : ones.data(), H * 4, cudaMemcpyHostToDevice));
+    ctx->uploaded_bytes += 3 * I * H * 2;
+    return LM_OK;
+}
+
+lm_status lm_ffn_load_safetensors(lm_moe_ctx* ctx, int32_t layer, int32_t checkpoint_layer, int32_t intermediate,
+                                  const char* const* shard_paths, int32_t n_shards) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    if (shard_paths == nullptr || n_shards <= 0 || checkpoint_layer < 0)
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "need at least one shard path and a checkpoint layer >= 0");
+    std::vector<std::string> paths;
+    for (int i = 0; i < n_shards; ++i) {
+        if (shard_paths[i] == nullptr) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "null shard path");
+        paths.emplace_back(shard_paths[i]);
+    }
+    host::StCheckpoint ck;
+    std::string err;
+    if (!ck.open(paths, err)) return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+    const int64_t H = ctx->cfg.hidden_size, I = intermediate;
+    // resolve_feed_forward(prefix + "mlp.", intermediate_size) (src/DeepSeekRunner.cpp:157-177, :193-195).
+    const std::string prefix = "model.layers." + std::to_string(checkpoint_layer) + ".";
+    std::vector<float> norm;
+    const host::StTensor* g = ck.require(prefix + "mlp.gate_proj.weight", {I, H}, host::StDtype::BF16, err);
+    const host::StTensor* u = g ? ck.require(prefix + "mlp.up_proj.weight", {I, H}, host::StDtype::BF16, err) : nullptr;
+    const host::StTensor* d = u ? ck.require(prefix + "mlp.down_proj.weight", {H, I}, host::StDtype::BF16, err) : nullptr;
+    if (d == nullptr || !ck.read_float32(prefix + "post_attention_layernorm.weight", {H}, norm, err))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+    std::vector<std::vector<uint16_t>> copies;
+    auto bf16 = [&](const host::StTensor* t) -> const uint16_t* {
+        if ((reinterpret_cast<uintptr_t>(t->data) & 1u) == 0) return reinterpret_cast<const uint16_t*>(t->data);
+        copies.emplace_back(t->nbytes / 2);
+        std::memcpy(copies.back().data(), t->data, t->nbytes);
+        return copies.back().data();
+    };
+    return lm_ffn_upload(ctx, layer, intermediate, bf16(g), bf16(u), bf16(d), norm.data());
+}
+
+lm_status lm_ffn_forward(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int32_t tokens, float* y,
+                         int32_t accumulate, void* stream) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= static_cast<int32_t>(ctx->dense.size()) || ctx->dense[layer].w13 == nullptr)
+        return fail(ctx, LM_ERR_NOT_LOADED, "dense layer " + std::to_string(layer) + " is not uploaded");
+    if (tokens < 0) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "negative token count");
+    if (tokens > ctx->cfg.max_tokens) return fail(ctx, LM_ERR_TOO_MANY_TOKENS, "tokens exceed max_tokens");
+    if (tokens == 0) return LM_OK;
+    if (x == nullptr || y == nullptr || !aligned16(x) || !aligned16(y))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, "x and y must be 16-byte aligned device pointers");
+    lm_status st;
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    const DenseWeights& D = ctx->dense[layer];
+    const int H = ctx->cfg.hidden_size, I = D.inter, T = tokens;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // One segment of all tokens; 256-wide token tiles would need 256-row weight
+    // blocks, which a dense intermediate size need not divide into.
+    const int bn = std::min(choose_bn(T, 1, 1), 128);
+    const int bi = bn_index(bn);
+    LM_CUDA(ctx, launch_dense_schedule(ctx->dense_sched, T, bn, 2 * I / 128, H / 128, s));
+    if (!accumulate) LM_CUDA(ctx, cudaMemsetAsync(y, 0, static_cast<size_t>(T) * H * sizeof(float), s));
+    CUtensorMap map_x{};
+    std::string err;
+    if (!encode_tensor_map_bf16(&map_x, x, T, H, bn, 64, err)) return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+    GemmArgs args{};
+    args.sched = ctx->dense_sched;
+    args.x = x;
+    args.h = ctx->dense_h;
+    args.y = y;
+    args.status = ctx->status;
+    args.tokens = T;
+    args.hidden = H;
+    args.inter = I;
+    args.n_routed_local = 0;  // the segment reads x, with weight 1, like a shared expert
+    args.split_ws = ctx->split_ws;
+    args.split_ticket = ctx->split_ticket;
+    args.split_ws_floats = static_cast<int32_t>(kSplitWsBytes / sizeof(float));
+    args.split_max_waves = ctx->split_max_waves;
+    LM_CUDA(ctx, launch_gemm_gate_up(bn, D.map_w13, map_x, map_x, args, ctx->sms, s, true));
+    LM_CUDA(ctx, launch_gemm_down(bn, D.map_w2, ctx->dense_map_h[bi], args, ctx->sms, s, true));
+    return LM_OK;
+}
+
+lm_status lm_ffn_block_forward(lm_moe_ctx* ctx, int32_t layer, float* hidden, int32_t tokens, void* stream) {
+    if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    if (layer < 0 || layer >= static_cast<int32_t>(ctx->dense.size()) || ctx->dense[layer].w13 == nullptr)
+        return fail(ctx, LM_ERR_NOT_LOADED, "dense layer " + std::to_string(layer) + " is not uploaded");
+    if (tokens < 0) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "negative token count");
+    if (tokens > ctx->cfg.max_tokens) return fail(ctx, LM_ERR_TOO_MANY_TOKENS, "tokens exceed max_tokens");
+    if (tokens == 0) return LM_OK;
+    if (hidden == nullptr || !aligned16(hidden)) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "hidden must be aligned");
+    lm_status st;
+    if ((st = set_device(ctx)) != LM_OK) return st;
+    const lm_moe_config& c = ctx->cfg;
+    const size_t T = c.max_tokens, H = c.hidden_size;
+    if (ctx->norm_f32 == nullptr) {
+        LM_CUDA(ctx, cudaMalloc(&ctx->norm_f32, T * H * sizeof(float)));
+        LM_CUDA(ctx, cudaMalloc(&ctx->norm_bf16, T * H * sizeof(uint16_t)));
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // rms_norm, the dense feed-forward, the residual add (src/DeepSeekRunner.cpp:265-271, :290),
+    // the add folded into the down projection's accumulation into `hidden`.
+    LM_CUDA(ctx, launch_rms_norm_rows(hidden, ctx->norm_f32, ctx->norm_bf16, ctx->dense[layer].norm, tokens,
+                                      c.hidden_size, c.rms_norm_eps, s));
+    return lm_ffn_forward(ctx, layer, ctx->norm_bf16, tokens, hidden, 1, stream);
 }
 
 lm_status lm_moe_upload_expert(lm_moe_ctx* ctx, int32_t layer, int32_t expert, const uint16_t* gate,

@@ -68,6 +68,7 @@ cudaError_t launch_place(const int32_t* topk_idx, const float* topk_w, const int
                          float* row_weight, int32_t* slot_row, float* y_zero, cudaStream_t stream, bool pdl);
 cudaError_t launch_ep_combine(float* y, const float* back, const int32_t* slot_row, const float* topk_w, int tokens,
                               int top_k, int hidden, cudaStream_t stream, bool pdl);
+cudaError_t launch_dense_schedule(Schedule* sched, int tokens, int bn, int mb1, int mb2, cudaStream_t stream);
 // Expert parallelism: received rows (source-major) -> expert-major, with row_src[row]
 // = the row's source-major index.  max_group_rows: the largest (source, expert) group.
 cudaError_t launch_ep_sort_rows(const uint16_t* x_recv, uint16_t* x_sorted, int32_t* row_src,

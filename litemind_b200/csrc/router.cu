@@ -655,6 +655,28 @@ cudaError_t launch_ep_combine(float* y, const float* back, const int32_t* slot_r
                     back, slot_row, topk_w, tokens, top_k, hidden);
 }
 
+// The dense feed-forward's schedule: one segment of all T tokens (read from x, as a
+// shared expert's are), weight slot 0.
+__global__ void dense_schedule_kernel(Schedule* sched, int T, int bn, int mb1, int mb2) {
+    pdl_wait();
+    pdl_launch_dependents();
+    if (threadIdx.x != 0) return;
+    const int nb = (T + bn - 1) / bn;
+    sched->n_seg = 1;
+    sched->first_expert = 0;
+    sched->seg_off[0] = 0;
+    sched->seg_cnt[0] = T;
+    sched->seg_weight[0] = 0;
+    sched->tiles1[0] = 0;
+    sched->tiles2[0] = 0;
+    sched->tiles1[1] = nb * mb1;
+    sched->tiles2[1] = nb * mb2;
+}
+
+cudaError_t launch_dense_schedule(Schedule* sched, int tokens, int bn, int mb1, int mb2, cudaStream_t stream) {
+    return launch_k(dense_schedule_kernel, dim3(1), dim3(32), stream, false, sched, tokens, bn, mb1, mb2);
+}
+
 cudaError_t launch_ep_sort_rows(const uint16_t* x_recv, uint16_t* x_sorted, int32_t* row_src,
                                const int32_t* recv_counts, int nranks, int local_experts, int max_group_rows,
                                int hidden, cudaStream_t stream, bool pdl) {

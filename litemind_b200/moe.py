@@ -144,6 +144,31 @@ class MoeLayer:
         self._check(self.lib.lm_moe_load_safetensors(self.ctx, layer, layer if checkpoint_layer is None
                                                      else checkpoint_layer, arr, len(paths)))
 
+    # ── dense feed-forward layers (their own index space) ──
+    def ffn_upload(self, layer: int, gate, up, down, norm_weight: np.ndarray | None = None) -> None:
+        """gate/up [inter, hidden], down [hidden, inter] as bf16 bits (numpy uint16)."""
+        g, u, d = (np.ascontiguousarray(a, np.uint16) for a in (gate, up, down))
+        n = None if norm_weight is None else np.ascontiguousarray(norm_weight, np.float32)
+        self._check(self.lib.lm_ffn_upload(self.ctx, layer, g.shape[0], _ptr(g), _ptr(u), _ptr(d), _ptr(n)))
+
+    def ffn_load_safetensors(self, layer: int, shard_paths, intermediate: int, checkpoint_layer: int | None = None):
+        paths = [str(p).encode() for p in shard_paths]
+        arr = (C.c_char_p * len(paths))(*paths)
+        self._check(self.lib.lm_ffn_load_safetensors(self.ctx, layer, layer if checkpoint_layer is None
+                                                     else checkpoint_layer, intermediate, arr, len(paths)))
+
+    def ffn_forward(self, layer: int, x, y=None, accumulate: bool = False, stream=None):
+        T = x.shape[0]
+        if y is None:
+            y = torch.empty((T, self.config.hidden_size), dtype=torch.float32, device=x.device)
+        self._check(self.lib.lm_ffn_forward(self.ctx, layer, _ptr(x) if T else None, T, _ptr(y) if T else None,
+                                            int(accumulate), _stream_ptr(stream)))
+        return y
+
+    def ffn_block_forward(self, layer: int, hidden, stream=None):
+        self._check(self.lib.lm_ffn_block_forward(self.ctx, layer, _ptr(hidden), hidden.shape[0],
+                                                  _stream_ptr(stream)))
+
     def upload_expert(self, layer: int, expert: int, gate, up, down) -> None:
         g, u, d = (np.ascontiguousarray(a) for a in (gate, up, down))
         self._check(self.lib.lm_moe_upload_expert(self.ctx, layer, expert, _ptr(g), _ptr(u), _ptr(d)))
