@@ -124,8 +124,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ int s_epi_go[2];
     __shared__ int s_split_last;
     constexpr int kMapCols = (KIND == Kind::Down) ? BN : 1;
-    __shared__ int s_ep_tok[2][kMapCols];  // down epilogue: this tile's token and routing weight per column
-    __shared__ float s_ep_w[2][kMapCols];
+    __shared__ __align__(16) int s_ep_tok[2][kMapCols];  // down epilogue: this tile's token and routing weight per column
+    __shared__ __align__(16) float s_ep_w[2][kMapCols];
 
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smem_a = smem;
@@ -492,14 +492,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (c0 >= valid) break;
                     uint32_t r[16];
                     tmem_ld16(t_row + c0, r);
+                    // The columns' tokens and weights, read while the TMEM load is in flight.
+                    int tok[16];
+                    float w[16];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int4 t4 = reinterpret_cast<const int4*>(&s_ep_tok[iter & 1][c0])[q];
+                        const float4 w4 = reinterpret_cast<const float4*>(&s_ep_w[iter & 1][c0])[q];
+                        tok[4 * q] = t4.x;
+                        tok[4 * q + 1] = t4.y;
+                        tok[4 * q + 2] = t4.z;
+                        tok[4 * q + 3] = t4.w;
+                        w[4 * q] = w4.x;
+                        w[4 * q + 1] = w4.y;
+                        w[4 * q + 2] = w4.z;
+                        w[4 * q + 3] = w4.w;
+                    }
                     tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int c = c0 + j;
-                        if (c < valid)
-                            atomicAdd(args.y + static_cast<size_t>(s_ep_tok[iter & 1][c]) * args.hidden + d,
-                                      s_ep_w[iter & 1][c] * __uint_as_float(r[j]));
-                    }
+                    for (int j = 0; j < 16; ++j)
+                        if (c0 + j < valid)
+                            atomicAdd(args.y + static_cast<size_t>(tok[j]) * args.hidden + d, w[j] * __uint_as_float(r[j]));
                 }
                 tc_fence_before();
                 __syncwarp();

@@ -43,6 +43,7 @@ struct PCfg {
     static constexpr int kTmemCols = 2 * BN;
     static constexpr int kSmem = 1024 + kStages * kStage + kStaging + kBar;
     static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+    static_assert((BN / 2) % 32 == 0, "epilogue warps drain 32 columns per TMEM wait");
     static_assert(kBTile % 1024 == 0, "token half-tiles must keep 1024-byte alignment");
     static_assert(kStages >= 3, "pipeline depth");
     static_assert(kSmem <= 220 * 1024, "shared memory");
@@ -76,8 +77,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __shared__ int s_n_seg;
     __shared__ int s_epi_go[2];
     constexpr int kMapCols = (KIND == PKind::Down) ? BN : 1;
-    __shared__ int s_ep_tok[2][kMapCols];  // down epilogue: this tile's token and routing weight per column
-    __shared__ float s_ep_w[2][kMapCols];
+    __shared__ __align__(16) int s_ep_tok[2][kMapCols];  // down epilogue: this tile's token and routing weight per column
+    __shared__ __align__(16) float s_ep_w[2][kMapCols];
 
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smem_a = smem;
@@ -239,7 +240,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else {
         // ── Epilogue (both CTAs): this CTA's 128 accumulator rows ──
         const int quad = warp & 3;
-        const int half = (warp - 2) >> 2;  // which 16-column chunks: c0 = 16 * half + 32 k
+        const int half = (warp - 2) >> 2;  // which half of the tile's columns this warp drains
+        const int c_beg = half * (BN / 2);
+        const int c_end = c_beg + BN / 2;
         const int epi_tid = threadIdx.x - 64;  // 0..255
         const uint32_t leader_tmem_empty0 = mapa_shared(smem_u32(&tmem_empty[0]), 0);
         const uint32_t leader_tmem_empty1 = mapa_shared(smem_u32(&tmem_empty[1]), 0);
@@ -276,14 +279,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if constexpr (KIND == PKind::GateUp) {
                 __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(staging);
                 const int i_local = (quad * 32 + lane) >> 1;
+                // 32 columns per TMEM wait: two loads in flight together.
 #pragma unroll 1
-                for (int c0 = 16 * half; c0 < BN; c0 += 32) {
+                for (int c0 = c_beg; c0 < c_end; c0 += 32) {
                     if (c0 >= valid) break;
-                    uint32_t r[16];
-                    tmem_ld16(t_row + c0, r);
+                    uint32_t r[32];
+                    tmem_ld16(t_row + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
+                    tmem_ld16(t_row + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
                     tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
+                    for (int j = 0; j < 32; ++j) {
                         const float mine = __uint_as_float(r[j]);
                         const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
                         if ((lane & 1) == 0) st[(c0 + j) * 64 + i_local] = __float2bfloat16_rn(silu_times(mine, other));
@@ -305,26 +310,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             } else {
                 const int d = block128 * kRows + quad * 32 + lane;
                 const bool to_rows = s < args.n_routed_local && args.y_rows != nullptr;
+                // 32 columns per TMEM wait; the columns' tokens and weights are read
+                // from shared memory while the TMEM loads are in flight.
 #pragma unroll 1
-                for (int c0 = 16 * half; c0 < BN; c0 += 32) {
+                for (int c0 = c_beg; c0 < c_end; c0 += 32) {
                     if (c0 >= valid) break;
-                    uint32_t r[16];
-                    tmem_ld16(t_row + c0, r);
-                    tmem_ld_wait();
+                    uint32_t r[32];
+                    tmem_ld16(t_row + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
+                    tmem_ld16(t_row + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+                    if (to_rows) {
+                        tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int c = c0 + j;
-                        if (c < valid) {
-                            const float v = __uint_as_float(r[j]);
-                            if (to_rows)
+                        for (int j = 0; j < 32; ++j) {
+                            const int c = c0 + j;
+                            if (c < valid)
                                 args.y_rows[static_cast<size_t>(args.y_rows_map != nullptr ? args.y_rows_map[row0 + c]
                                                                                           : row0 + c) *
                                                 args.hidden +
-                                            d] = v;
-                            else
-                                atomicAdd(args.y + static_cast<size_t>(s_ep_tok[iter & 1][c]) * args.hidden + d,
-                                          s_ep_w[iter & 1][c] * v);
+                                            d] = __uint_as_float(r[j]);
                         }
+                    } else {
+                        int tok[32];
+                        float w[32];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const int4 t4 = reinterpret_cast<const int4*>(&s_ep_tok[iter & 1][c0])[q];
+                            const float4 w4 = reinterpret_cast<const float4*>(&s_ep_w[iter & 1][c0])[q];
+                            tok[4 * q] = t4.x;
+                            tok[4 * q + 1] = t4.y;
+                            tok[4 * q + 2] = t4.z;
+                            tok[4 * q + 3] = t4.w;
+                            w[4 * q] = w4.x;
+                            w[4 * q + 1] = w4.y;
+                            w[4 * q + 2] = w4.z;
+                            w[4 * q + 3] = w4.w;
+                        }
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (c0 + j < valid)
+                                atomicAdd(args.y + static_cast<size_t>(tok[j]) * args.hidden + d,
+                                          w[j] * __uint_as_float(r[j]));
                     }
                 }
                 tc_fence_before();
