@@ -475,7 +475,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (c0 + j < valid) {
                                 const int row = row0 + c0 + j;
                                 const int dst = args.y_rows_map != nullptr ? args.y_rows_map[row] : row;
-                                args.y_rows[static_cast<size_t>(dst) * args.hidden + d] = __uint_as_float(r[j]);
+                                reinterpret_cast<__nv_bfloat16*>(args.y_rows)[static_cast<size_t>(dst) * args.hidden + d] =
+                                    __float2bfloat16_rn(__uint_as_float(r[j]));
                             }
                     }
                     tc_fence_before();

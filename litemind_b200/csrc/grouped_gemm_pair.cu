@@ -324,10 +324,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 32; ++j) {
                             const int c = c0 + j;
                             if (c < valid)
-                                args.y_rows[static_cast<size_t>(args.y_rows_map != nullptr ? args.y_rows_map[row0 + c]
-                                                                                          : row0 + c) *
-                                                args.hidden +
-                                            d] = __uint_as_float(r[j]);
+                                reinterpret_cast<__nv_bfloat16*>(args.y_rows)
+                                    [static_cast<size_t>(args.y_rows_map != nullptr ? args.y_rows_map[row0 + c] : row0 + c) *
+                                         args.hidden +
+                                     d] = __float2bfloat16_rn(__uint_as_float(r[j]));
                         }
                     } else {
                         int tok[32];

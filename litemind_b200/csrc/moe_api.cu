@@ -117,8 +117,8 @@ struct lm_moe_ctx {
     uint16_t* x_recv = nullptr;    // received token rows, (source rank, local expert) segments
     uint16_t* x_sorted = nullptr;  // received rows, expert-major (each expert's rows contiguous)
     int32_t* ep_row_src = nullptr;  // expert-major row -> its source-major row (where its output goes back)
-    float* y_ret = nullptr;        // expert outputs of the received rows, returned to their ranks
-    float* y_back = nullptr;       // this rank's rows' expert outputs, in send order
+    uint16_t* y_ret = nullptr;     // expert outputs of the received rows (bf16), returned to their ranks
+    uint16_t* y_back = nullptr;    // this rank's rows' expert outputs (bf16), in send order
     int32_t* recv_counts = nullptr;  // [nranks, local experts] rows received per source and expert
     lm::Schedule* sched_ep = nullptr;
     lm::Schedule* host_sched = nullptr;  // pinned
@@ -1165,10 +1165,10 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     for (int d = 0; d < N; ++d) {
         if (recv_cnt[d] > 0)
             LM_NCCL(ctx, nc.Send(ctx->y_ret + static_cast<size_t>(recv_off[d]) * H, static_cast<size_t>(recv_cnt[d]) * H,
-                                 ncclFloat32, d, ctx->comm, s));
+                                 ncclBfloat16, d, ctx->comm, s));
         if (send_cnt[d] > 0)
             LM_NCCL(ctx, nc.Recv(ctx->y_back + static_cast<size_t>(send_off[d]) * H, static_cast<size_t>(send_cnt[d]) * H,
-                                 ncclFloat32, d, ctx->comm, s));
+                                 ncclBfloat16, d, ctx->comm, s));
     }
     LM_NCCL(ctx, nc.GroupEnd());
     LM_CUDA(ctx, launch_ep_combine(y, ctx->y_back, ctx->slot_row, ctx->topk_w, T, K, H, s, false));

@@ -66,7 +66,7 @@ cudaError_t launch_dispatch_scan(const int32_t* tile_counts, int32_t* tile_base,
 cudaError_t launch_place(const int32_t* topk_idx, const float* topk_w, const int32_t* tile_base, int tokens,
                          int hidden, int top_k, int experts, int first_expert, int local_experts, int32_t* row_token,
                          float* row_weight, int32_t* slot_row, float* y_zero, cudaStream_t stream, bool pdl);
-cudaError_t launch_ep_combine(float* y, const float* back, const int32_t* slot_row, const float* topk_w, int tokens,
+cudaError_t launch_ep_combine(float* y, const uint16_t* back, const int32_t* slot_row, const float* topk_w, int tokens,
                               int top_k, int hidden, cudaStream_t stream, bool pdl);
 cudaError_t launch_dense_schedule(Schedule* sched, int tokens, int bn, int mb1, int mb2, cudaStream_t stream);
 // Expert parallelism: received rows (source-major) -> expert-major, with row_src[row]
@@ -95,7 +95,7 @@ struct GemmArgs {
     int32_t tokens;
     int32_t hidden;
     int32_t inter;
-    float* y_rows;             // when set, routed rows' down outputs are stored here by row, unweighted
+    uint16_t* y_rows;          // when set, routed rows' down outputs are stored here by row, unweighted, bf16
     const int32_t* y_rows_map; // with y_rows: routed row r is stored at row y_rows_map[r] (null: at r)
     float* logits;             // router kind: [T, experts] f32 output
     const float* bias;         // router kind: per-expert logit bias or null

@@ -374,9 +374,10 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
 
 // Expert-parallel combine: y[t] += sum over slots s (in selection order) of
 // w[t, s] * back[slot_row[t, s]], where `back` holds the expert outputs returned
-// by the experts' ranks in this rank's send order.  y already holds the shared
-// experts' output.  One thread per 4 consecutive hidden elements of a token.
-__global__ void __launch_bounds__(256) ep_combine_kernel(float* __restrict__ y, const float* __restrict__ back,
+// by the experts' ranks in this rank's send order, rounded to bf16 for the return
+// trip (half the NVLink bytes; the weighted sum is in f32).  y already holds the
+// shared experts' output.  One thread per 4 consecutive hidden elements of a token.
+__global__ void __launch_bounds__(256) ep_combine_kernel(float* __restrict__ y, const uint16_t* __restrict__ back,
                                                          const int32_t* __restrict__ slot_row,
                                                          const float* __restrict__ topk_w, int T, int K, int H) {
     pdl_wait();
@@ -390,11 +391,11 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(float* __restrict__ y, 
     for (int s = 0; s < K; ++s) {
         const int row = slot_row[t * K + s];
         const float w = topk_w[t * K + s];
-        const float4 v = reinterpret_cast<const float4*>(back + static_cast<size_t>(row) * H)[c];
-        acc.x = fmaf(w, v.x, acc.x);
-        acc.y = fmaf(w, v.y, acc.y);
-        acc.z = fmaf(w, v.z, acc.z);
-        acc.w = fmaf(w, v.w, acc.w);
+        const uint2 b = reinterpret_cast<const uint2*>(back + static_cast<size_t>(row) * H)[c];
+        acc.x = fmaf(w, __uint_as_float(b.x << 16), acc.x);
+        acc.y = fmaf(w, __uint_as_float(b.x & 0xFFFF0000u), acc.y);
+        acc.z = fmaf(w, __uint_as_float(b.y << 16), acc.z);
+        acc.w = fmaf(w, __uint_as_float(b.y & 0xFFFF0000u), acc.w);
     }
     reinterpret_cast<float4*>(y + static_cast<size_t>(t) * H)[c] = acc;
 }
@@ -647,7 +648,7 @@ cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* row_token, int 
     return launch_k(gather_rows_kernel, dim3(blocks), dim3(256), stream, pdl, x, row_token, rows, hidden, x_perm);
 }
 
-cudaError_t launch_ep_combine(float* y, const float* back, const int32_t* slot_row, const float* topk_w, int tokens,
+cudaError_t launch_ep_combine(float* y, const uint16_t* back, const int32_t* slot_row, const float* topk_w, int tokens,
                               int top_k, int hidden, cudaStream_t stream, bool pdl) {
     if (tokens <= 0) return cudaSuccess;
     const int64_t threads = static_cast<int64_t>(tokens) * (hidden / 4);
