@@ -116,6 +116,8 @@ struct lm_moe_ctx {
     const lm::NcclApi* nccl = nullptr;
     uint16_t* x_recv = nullptr;    // received token rows, (source rank, local expert) segments
     uint16_t* x_sorted = nullptr;  // received rows, expert-major (each expert's rows contiguous)
+    int ep_cap = 0;                // > 0: fixed-capacity exchange, rows per (source, destination) block
+    uint16_t* x_send = nullptr;    // fixed-capacity send blocks [nranks][ep_cap][hidden]
     int32_t* ep_row_src = nullptr;  // expert-major row -> its source-major row (where its output goes back)
     uint16_t* y_ret = nullptr;     // expert outputs of the received rows (bf16), returned to their ranks
     uint16_t* y_back = nullptr;    // this rank's rows' expert outputs (bf16), in send order
@@ -1019,6 +1021,79 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
     } while (0)
 
 // Expert-parallel forward.  Every rank runs this same sequence of collectives.
+// Expert parallelism for small batches: every rank pair exchanges a fixed block of
+// ep_cap rows, so the counts travel with the rows in one NCCL group and the receiver
+// plans on the device -- no host round trip per layer.  Steps after routing: pack
+// rows into destination blocks, exchange counts + rows, sort expert-major, schedule,
+// the grouped GEMMs, return the blocks, weighted combine.
+static lm_status forward_ep_fixed(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int32_t T, float* y,
+                                  cudaStream_t s, int* slots, int n_slots) {
+    const lm_moe_config& c = ctx->cfg;
+    const LayerWeights& L = ctx->layers[layer];
+    const int K = c.num_experts_per_tok, E = c.n_routed_experts, H = c.hidden_size, I = c.moe_intermediate_size;
+    const int N = ctx->nranks, El = ctx->local_experts, cap = ctx->ep_cap;
+    const NcclApi& nc = *ctx->nccl;
+    LM_CUDA(ctx, launch_ep_pack(x, ctx->row_token, ctx->expert_totals, ctx->slot_row, ctx->x_send, T, K, E, El, cap, H,
+                                s, true));
+    prof_mark(ctx, 1, s);
+    slots[n_slots++] = 1;
+    const size_t block = static_cast<size_t>(cap) * H;
+    LM_NCCL(ctx, nc.GroupStart());
+    for (int d = 0; d < N; ++d) {
+        LM_NCCL(ctx, nc.Send(ctx->expert_totals + d * El, El, ncclInt32, d, ctx->comm, s));
+        LM_NCCL(ctx, nc.Recv(ctx->recv_counts + d * El, El, ncclInt32, d, ctx->comm, s));
+        LM_NCCL(ctx, nc.Send(ctx->x_send + d * block, block, ncclBfloat16, d, ctx->comm, s));
+        LM_NCCL(ctx, nc.Recv(ctx->x_recv + d * block, block, ncclBfloat16, d, ctx->comm, s));
+    }
+    LM_NCCL(ctx, nc.GroupEnd());
+    // The receiver does not know its row counts on the host: the GEMM tile width
+    // comes from the expected rows per local expert (every rank at T tokens).
+    const int bn = std::min(choose_bn(N * std::max(T, 1), K, E), 128);
+    const int bi = bn_index(bn);
+    LM_CUDA(ctx, launch_ep_sort_rows(ctx->x_recv, ctx->x_sorted, ctx->ep_row_src, ctx->recv_counts, N, El, cap, H, cap,
+                                     s, false));
+    LM_CUDA(ctx, launch_ep_schedule(ctx->recv_counts, ctx->sched_ep, N, El, c.n_shared_experts, T, ctx->routed_cap, bn,
+                                    2 * I / 128, H / 128, s, true));
+    prof_mark(ctx, 7, s);
+    slots[n_slots++] = 7;
+    CUtensorMap map_x{};
+    std::string err;
+    if (!encode_tensor_map_bf16(&map_x, T > 0 ? x : ctx->x_perm, std::max(T, 1), H, bn, 64, err))
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
+    GemmArgs args{};
+    args.sched = ctx->sched_ep;
+    args.x = x;
+    args.h = ctx->h;
+    args.y = y;
+    args.y_rows = ctx->y_ret;
+    args.y_rows_map = ctx->ep_row_src;
+    args.status = ctx->status;
+    args.tokens = T;
+    args.hidden = H;
+    args.inter = I;
+    args.n_routed_local = El;
+    args.split_ws = ctx->split_ws;
+    args.split_ticket = ctx->split_ticket;
+    args.split_ws_floats = static_cast<int32_t>(kSplitWsBytes / sizeof(float));
+    args.split_max_waves = ctx->split_max_waves;
+    LM_CUDA(ctx, launch_gemm_gate_up(bn, L.map_w13, ctx->map_xsorted[bi], map_x, args, ctx->sms, s, true));
+    prof_mark(ctx, 5, s);
+    slots[n_slots++] = 5;
+    LM_CUDA(ctx, launch_gemm_down(bn, L.map_w2, ctx->map_h[bi], args, ctx->sms, s, true));
+    prof_mark(ctx, 6, s);
+    slots[n_slots++] = 6;
+    LM_NCCL(ctx, nc.GroupStart());
+    for (int d = 0; d < N; ++d) {
+        LM_NCCL(ctx, nc.Send(ctx->y_ret + d * block, block, ncclBfloat16, d, ctx->comm, s));
+        LM_NCCL(ctx, nc.Recv(ctx->y_back + d * block, block, ncclBfloat16, d, ctx->comm, s));
+    }
+    LM_NCCL(ctx, nc.GroupEnd());
+    LM_CUDA(ctx, launch_ep_combine(y, ctx->y_back, ctx->slot_row, ctx->topk_w, T, K, H, s, false));
+    prof_mark(ctx, 4, s);
+    slots[n_slots++] = 4;
+    return prof_end(ctx, slots, n_slots);
+}
+
 static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, const float* x_f32, int32_t T,
                             const float* bias, float* y, int32_t accumulate, cudaStream_t s) {
     const lm_moe_config& c = ctx->cfg;
@@ -1049,6 +1124,7 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     } else {
         LM_CUDA(ctx, cudaMemsetAsync(ctx->expert_totals, 0, E * sizeof(int32_t), s));
     }
+    if (ctx->ep_cap > 0) return forward_ep_fixed(ctx, layer, x, T, y, s, slots, n_slots);
     LM_CUDA(ctx, launch_gather_rows(x, ctx->row_token, T * K, H, ctx->x_perm, s, true));
     prof_mark(ctx, 1, s);
     slots[n_slots++] = 1;
@@ -1117,7 +1193,7 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     }
     LM_NCCL(ctx, nc.GroupEnd());
     LM_CUDA(ctx, launch_ep_sort_rows(ctx->x_recv, ctx->x_sorted, ctx->ep_row_src, ctx->recv_counts, N, El, max_group, H,
-                                     s, false));
+                                     0, s, false));
     prof_mark(ctx, 7, s);
     slots[n_slots++] = 7;
     // 4. Local experts on the received rows, shared experts on this rank's tokens.
@@ -1401,8 +1477,14 @@ lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t ra
             ctx->allocations.erase(it);
             break;
         }
+    // Small batches exchange fixed blocks of ep_cap rows per rank pair (no host round
+    // trip): a token sends one rank at most min(k, local experts) rows.
+    const size_t fixed_cap = T * std::min(K, static_cast<size_t>(El));
+    ctx->ep_cap = static_cast<size_t>(nranks) * fixed_cap <= kEpFixedMaxRows ? static_cast<int>(fixed_cap) : 0;
+    const size_t back_rows = std::max(T * K, static_cast<size_t>(nranks) * ctx->ep_cap);
     if ((st = alloc(ctx, &ctx->h, h_rows * I)) || (st = alloc(ctx, &ctx->x_recv, cap * H)) ||
-        (st = alloc(ctx, &ctx->y_ret, cap * H)) || (st = alloc(ctx, &ctx->y_back, T * K * H)) ||
+        (st = alloc(ctx, &ctx->y_ret, cap * H)) || (st = alloc(ctx, &ctx->y_back, back_rows * H)) ||
+        (ctx->ep_cap > 0 && (st = alloc(ctx, &ctx->x_send, static_cast<size_t>(nranks) * ctx->ep_cap * H))) ||
         (st = alloc(ctx, &ctx->recv_counts, static_cast<size_t>(nranks) * El)) || (st = alloc(ctx, &ctx->sched_ep, 1)) ||
         (st = alloc(ctx, &ctx->x_sorted, cap * H)) || (st = alloc(ctx, &ctx->ep_row_src, cap)))
         return st;

@@ -71,9 +71,19 @@ cudaError_t launch_ep_combine(float* y, const uint16_t* back, const int32_t* slo
 cudaError_t launch_dense_schedule(Schedule* sched, int tokens, int bn, int mb1, int mb2, cudaStream_t stream);
 // Expert parallelism: received rows (source-major) -> expert-major, with row_src[row]
 // = the row's source-major index.  max_group_rows: the largest (source, expert) group.
+// src_stride > 0: source r's rows start at r * src_stride (fixed-capacity exchange).
 cudaError_t launch_ep_sort_rows(const uint16_t* x_recv, uint16_t* x_sorted, int32_t* row_src,
                                const int32_t* recv_counts, int nranks, int local_experts, int max_group_rows,
-                               int hidden, cudaStream_t stream, bool pdl);
+                               int hidden, int src_stride, cudaStream_t stream, bool pdl);
+// Fixed-capacity expert parallelism: pack this rank's rows into per-destination
+// blocks of `cap` rows (and point slot_row at them), and build the receiver's
+// schedule on the device from the received counts.
+cudaError_t launch_ep_pack(const uint16_t* x, const int32_t* row_token, const int32_t* expert_totals,
+                           int32_t* slot_row, uint16_t* x_send, int tokens, int top_k, int experts,
+                           int local_experts, int cap, int hidden, cudaStream_t stream, bool pdl);
+cudaError_t launch_ep_schedule(const int32_t* recv_counts, Schedule* sched, int nranks, int local_experts,
+                               int n_shared, int tokens, int shared_base, int bn, int mb1, int mb2,
+                               cudaStream_t stream, bool pdl);
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* row_token, int rows, int hidden, uint16_t* x_perm,
                                cudaStream_t stream, bool pdl);
 cudaError_t launch_route_small(const uint16_t* x, const float* x_f32, const float* w, const float* bias,
@@ -153,6 +163,10 @@ constexpr int kDecodeTraceSlots = 16;
 constexpr int kDecodeMaxLogits = 4096;
 cudaError_t launch_moe_decode(int bn, const CUtensorMap& w13, const CUtensorMap& w2, const CUtensorMap& x,
                               const CUtensorMap& h, const DecodeArgs& args, int sms, cudaStream_t stream);
+
+// Expert parallelism exchanges fixed blocks (no host round trip) while
+// nranks x rows-per-block stays within this many rows.
+constexpr size_t kEpFixedMaxRows = 8192;
 
 // Split-K workspace for gate/up partial tiles (bytes) and its ticket count.
 constexpr size_t kSplitWsBytes = size_t(32) << 20;

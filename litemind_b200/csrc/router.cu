@@ -407,22 +407,25 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(float* __restrict__ y, 
 // its group to their expert-major place and records where each came from, so the
 // down projection can store its output rows back in source-major order.
 constexpr int kSortRows = 64;
+// src_stride > 0: each source's rows sit in a fixed block of src_stride rows
+// (the fixed-capacity exchange) instead of back to back.
 __global__ void __launch_bounds__(256) ep_sort_rows_kernel(const uint16_t* __restrict__ x_recv,
                                                            uint16_t* __restrict__ x_sorted,
                                                            int32_t* __restrict__ row_src,
                                                            const int32_t* __restrict__ recv_counts, int N, int El,
-                                                           int H) {
+                                                           int H, int src_stride) {
     pdl_wait();
     pdl_launch_dependents();
     const int r = blockIdx.x / El;
     const int e = blockIdx.x - r * El;
     __shared__ int s_src, s_dst, s_cnt;
     if (threadIdx.x == 0) {
-        int src = 0, dst = 0;
+        int src = src_stride > 0 ? r * src_stride : 0, dst = 0;
         for (int rr = 0; rr < N; ++rr) {
             for (int ee = 0; ee < El; ++ee) {
                 const int c = recv_counts[rr * El + ee];
-                if (rr < r || (rr == r && ee < e)) src += c;  // source-major position
+                if (src_stride > 0 ? (rr == r && ee < e) : (rr < r || (rr == r && ee < e)))
+                    src += c;  // source-major position
                 if (ee < e || (ee == e && rr < r)) dst += c;  // expert-major position
             }
         }
@@ -680,11 +683,107 @@ cudaError_t launch_dense_schedule(Schedule* sched, int tokens, int bn, int mb1, 
 
 cudaError_t launch_ep_sort_rows(const uint16_t* x_recv, uint16_t* x_sorted, int32_t* row_src,
                                const int32_t* recv_counts, int nranks, int local_experts, int max_group_rows,
-                               int hidden, cudaStream_t stream, bool pdl) {
+                               int hidden, int src_stride, cudaStream_t stream, bool pdl) {
     if (max_group_rows <= 0) return cudaSuccess;
     const dim3 grid(nranks * local_experts, (max_group_rows + kSortRows - 1) / kSortRows);
     return launch_k(ep_sort_rows_kernel, grid, dim3(256), stream, pdl, x_recv, x_sorted, row_src, recv_counts,
-                    nranks, local_experts, hidden);
+                    nranks, local_experts, hidden, src_stride);
+}
+
+// Fixed-capacity expert parallelism (small batches, no host round trip): every
+// rank sends every peer a block of `cap` rows, whatever it holds.  ep_pack puts this
+// rank's expert-sorted rows (sorted by global expert, so by destination) into
+// destination d's block at d * cap, straight from x, and points each (token, slot)
+// at its block position for the combine.  One warp per row.
+__global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict__ x,
+                                                      const int32_t* __restrict__ row_token,
+                                                      const int32_t* __restrict__ expert_totals,
+                                                      int32_t* __restrict__ slot_row, uint16_t* __restrict__ x_send,
+                                                      int T, int K, int E, int El, int cap, int H) {
+    pdl_wait();
+    pdl_launch_dependents();
+    __shared__ int off[kMaxExperts + 1];
+    if (threadIdx.x == 0) {
+        int o = 0;
+        for (int e = 0; e < E; ++e) {
+            off[e] = o;
+            o += expert_totals[e];
+        }
+        off[E] = o;
+    }
+    __syncthreads();
+    const int n_rows = T * K;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int n_warps = (gridDim.x * blockDim.x) >> 5;
+    // Expert-sorted row r -> its destination block position.
+    auto padded = [&](int r) {
+        int lo = 0, hi = E;  // off[lo] <= r < off[hi]
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (off[mid] <= r) lo = mid; else hi = mid;
+        }
+        const int d = lo / El;
+        return d * cap + (r - off[d * El]);
+    };
+    const int vec = H / 8;
+    for (int r = warp; r < n_rows; r += n_warps) {
+        const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row_token[r]) * H);
+        uint4* dst = reinterpret_cast<uint4*>(x_send + static_cast<size_t>(padded(r)) * H);
+        for (int v = lane; v < vec; v += 32) dst[v] = src[v];
+    }
+    for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < n_rows; q += gridDim.x * blockDim.x)
+        if (slot_row[q] >= 0) slot_row[q] = padded(slot_row[q]);
+}
+
+cudaError_t launch_ep_pack(const uint16_t* x, const int32_t* row_token, const int32_t* expert_totals,
+                           int32_t* slot_row, uint16_t* x_send, int tokens, int top_k, int experts,
+                           int local_experts, int cap, int hidden, cudaStream_t stream, bool pdl) {
+    if (tokens <= 0) return cudaSuccess;
+    const int rows = tokens * top_k;
+    const int blocks = std::min((rows + 7) / 8, 1024);
+    return launch_k(ep_pack_kernel, dim3(blocks), dim3(256), stream, pdl, x, row_token, expert_totals, slot_row,
+                    x_send, tokens, top_k, experts, local_experts, cap, hidden);
+}
+
+// The receiver's schedule of a fixed-capacity exchange, on the device: one segment
+// per local expert (its rows from every source, expert-major), then the shared
+// experts over this rank's own T tokens at row shared_base + j * T.
+__global__ void ep_schedule_kernel(const int32_t* __restrict__ recv_counts, Schedule* __restrict__ sched, int N,
+                                   int El, int n_shared, int T, int shared_base, int bn, int mb1, int mb2) {
+    pdl_wait();
+    pdl_launch_dependents();
+    if (threadIdx.x != 0) return;
+    int off = 0, p1 = 0, p2 = 0, seg = 0;
+    auto add = [&](int o, int cnt, int w) {
+        sched->seg_off[seg] = o;
+        sched->seg_cnt[seg] = cnt;
+        sched->seg_weight[seg] = w;
+        sched->tiles1[seg] = p1;
+        sched->tiles2[seg] = p2;
+        const int nb = (cnt + bn - 1) / bn;
+        p1 += nb * mb1;
+        p2 += nb * mb2;
+        ++seg;
+    };
+    for (int e = 0; e < El; ++e) {
+        int cnt = 0;
+        for (int r = 0; r < N; ++r) cnt += recv_counts[r * El + e];
+        add(off, cnt, e);
+        off += cnt;
+    }
+    for (int j = 0; j < n_shared; ++j) add(shared_base + j * T, T, El + j);
+    sched->tiles1[seg] = p1;
+    sched->tiles2[seg] = p2;
+    sched->n_seg = seg;
+    sched->first_expert = 0;
+}
+
+cudaError_t launch_ep_schedule(const int32_t* recv_counts, Schedule* sched, int nranks, int local_experts,
+                               int n_shared, int tokens, int shared_base, int bn, int mb1, int mb2,
+                               cudaStream_t stream, bool pdl) {
+    return launch_k(ep_schedule_kernel, dim3(1), dim3(32), stream, pdl, recv_counts, sched, nranks, local_experts,
+                    n_shared, tokens, shared_base, bn, mb1, mb2);
 }
 
 template <typename XT, int EPL>
