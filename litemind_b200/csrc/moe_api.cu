@@ -830,7 +830,7 @@ static lm_status router_logits(lm_moe_ctx* ctx, const LayerWeights& L, const uin
         return LM_OK;
     }
     LM_CUDA(ctx, launch_router_logits(x, x_f32, L.router, L.router_t, bias, logits, T, c.hidden_size,
-                                      c.n_routed_experts, s, pdl));
+                                      c.n_routed_experts, ctx->split_ws, kSplitWsBytes, s, pdl));
     return LM_OK;
 }
 

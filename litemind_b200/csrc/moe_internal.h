@@ -56,7 +56,7 @@ struct RouterFix {
 // Kernel launchers (router.cu).  All return cudaGetLastError() after launching.
 cudaError_t launch_router_logits(const uint16_t* x, const float* x_f32, const float* w, const float* w_t,
                                  const float* bias, float* logits, int tokens, int hidden, int experts,
-                                 cudaStream_t stream, bool pdl);
+                                 float* split_ws, size_t split_ws_bytes, cudaStream_t stream, bool pdl);
 cudaError_t launch_router_topk(float* logits, int tokens, RouterParams rp, int32_t* topk_idx, float* topk_w,
                                int32_t* tile_counts, cudaStream_t stream, bool pdl, RouterFix fix = RouterFix{});
 cudaError_t launch_dispatch_scan(const int32_t* tile_counts, int32_t* tile_base, int32_t* expert_totals,

@@ -86,8 +86,8 @@ lm_status lm_moe_route_static(const float* router, const uint16_t* x, int32_t to
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // Every logit of this call is written before it is read, so nothing in the
     // scratch needs clearing between calls.
-    cudaError_t e = launch_router_logits(x, nullptr, router, nullptr, logit_bias, scratch, tokens, hidden, experts, s,
-                                         false);
+    cudaError_t e = launch_router_logits(x, nullptr, router, nullptr, logit_bias, scratch, tokens, hidden, experts, nullptr,
+                                         0, s, false);
     if (e == cudaSuccess) e = launch_router_topk(scratch, tokens, rp, topk_idx, topk_w, nullptr, s, false);
     if (e != cudaSuccess) return static_fail(LM_ERR_CUDA, "kernel launch failed");
     return LM_OK;

@@ -73,13 +73,16 @@ __global__ void __launch_bounds__(256) router_logits_warp_kernel(const XT* __res
 }
 
 // Large T: 64 tokens x 64 experts per CTA from smem tiles; w_t is the router
-// transposed to [H, E] so expert vectors are contiguous.
+// transposed to [H, E] so expert vectors are contiguous.  The hidden axis is split
+// over blockIdx.z (k_per elements each) so the grid fills the GPU; with more than
+// one split each CTA writes its partial sums to partial[z][t][e] and
+// router_logits_reduce adds them in z order (deterministic).
 template <typename XT>
 __global__ void __launch_bounds__(256) router_logits_tiled_kernel(const XT* __restrict__ x,
                                                                   const float* __restrict__ w_t,
                                                                   const float* __restrict__ bias,
                                                                   float* __restrict__ logits, int T, int H,
-                                                                  int E) {
+                                                                  int E, int k_per, float* __restrict__ partial) {
     __shared__ __align__(16) float xs[32][68];  // [k][token]
     __shared__ __align__(16) float ws[32][68];  // [k][expert]
     pdl_wait();
@@ -95,7 +98,9 @@ __global__ void __launch_bounds__(256) router_logits_tiled_kernel(const XT* __re
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
 
-    for (int k0 = 0; k0 < H; k0 += 32) {
+    const int k_begin = blockIdx.z * k_per;
+    const int k_end = min(H, k_begin + k_per);
+    for (int k0 = k_begin; k0 < k_end; k0 += 32) {
         {   // x: 64 tokens x 32 k; each thread one 8-wide run of one token
             const int tl = tid >> 2;
             const int kp = (tid & 3) * 8;
@@ -137,9 +142,27 @@ __global__ void __launch_bounds__(256) router_logits_tiled_kernel(const XT* __re
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int e = e0 + tx * 4 + j;
-            if (e < E) logits[static_cast<size_t>(t) * E + e] = bias != nullptr ? acc[i][j] + bias[e] : acc[i][j];
+            if (e >= E) continue;
+            if (partial != nullptr)
+                partial[(static_cast<size_t>(blockIdx.z) * T + t) * E + e] = acc[i][j];
+            else
+                logits[static_cast<size_t>(t) * E + e] = bias != nullptr ? acc[i][j] + bias[e] : acc[i][j];
         }
     }
+}
+
+__global__ void __launch_bounds__(256) router_logits_reduce_kernel(const float* __restrict__ partial,
+                                                                   const float* __restrict__ bias,
+                                                                   float* __restrict__ logits, int T, int E,
+                                                                   int splits) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t n = static_cast<int64_t>(T) * E;
+    if (i >= n) return;
+    float v = 0.0f;
+    for (int z = 0; z < splits; ++z) v += partial[z * n + i];
+    logits[i] = bias != nullptr ? v + bias[i % E] : v;
 }
 
 // Thread 0: segment offsets, counts and both GEMMs' tile prefixes from per-expert
@@ -587,15 +610,28 @@ cudaError_t launch_k(Kernel kernel, dim3 grid, dim3 block, cudaStream_t stream, 
 
 cudaError_t launch_router_logits(const uint16_t* x, const float* x_f32, const float* w, const float* w_t,
                                  const float* bias, float* logits, int tokens, int hidden, int experts,
-                                 cudaStream_t stream, bool pdl) {
+                                 float* split_ws, size_t split_ws_bytes, cudaStream_t stream, bool pdl) {
     if (tokens <= 0) return cudaSuccess;
-    if (tokens >= 2048) {
-        const dim3 grid((tokens + 63) / 64, (experts + 63) / 64);
-        if (x_f32 != nullptr)
-            return launch_k(router_logits_tiled_kernel<float>, grid, dim3(256), stream, pdl, x_f32, w_t, bias,
-                            logits, tokens, hidden, experts);
-        return launch_k(router_logits_tiled_kernel<uint16_t>, grid, dim3(256), stream, pdl, x, w_t, bias, logits,
-                        tokens, hidden, experts);
+    if (tokens >= 2048 && w_t != nullptr) {
+        // Split the hidden axis until the grid has about four CTAs per SM, as far as
+        // the workspace holds the partial sums.
+        const int tiles = ((tokens + 63) / 64) * ((experts + 63) / 64);
+        int splits = 1;
+        while (splits < 8 && tiles * splits < 4 * 148 && hidden % (64 * splits * 2) == 0 &&
+               static_cast<size_t>(splits) * 2 * tokens * experts * sizeof(float) <= split_ws_bytes &&
+               split_ws != nullptr)
+            splits *= 2;
+        const dim3 grid((tokens + 63) / 64, (experts + 63) / 64, splits);
+        float* partial = splits > 1 ? split_ws : nullptr;
+        cudaError_t e = x_f32 != nullptr
+                            ? launch_k(router_logits_tiled_kernel<float>, grid, dim3(256), stream, pdl, x_f32, w_t,
+                                       bias, logits, tokens, hidden, experts, hidden / splits, partial)
+                            : launch_k(router_logits_tiled_kernel<uint16_t>, grid, dim3(256), stream, pdl, x, w_t,
+                                       bias, logits, tokens, hidden, experts, hidden / splits, partial);
+        if (e != cudaSuccess || splits == 1) return e;
+        const int64_t n = static_cast<int64_t>(tokens) * experts;
+        return launch_k(router_logits_reduce_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), stream,
+                        true, static_cast<const float*>(split_ws), bias, logits, tokens, experts, splits);
     }
     const int groups = (experts + 7) / 8;
     const long warps = static_cast<long>(tokens) * groups;

@@ -106,6 +106,24 @@ def test_fused_matches_grouped_path(v2lite_weights, v2):
     grouped.close()
 
 
+def test_group_limited_routing_large_batch(oracle_lib):
+    """Group-limited routing at T >= 2048 takes the CUDA-core tiled router (split over
+    the hidden axis) instead of the tensor-core one; sampled tokens against the oracle."""
+    W = syn.layer_weights(GROUPED, seed=23, std=0.05)
+    cfg = MoeConfig.from_shape(GROUPED, max_tokens=3000, topk_method="group_limited_greedy", n_group=8,
+                               topk_group=3)
+    layer = MoeLayer(cfg)
+    layer.upload_layer(0, W)
+    T = 3000
+    x = syn.tokens(GROUPED, T, seed=24)
+    y, idx, w, _, _ = _gpu(layer, x)
+    sample = np.sort(np.random.default_rng(3).choice(T, 64, replace=False))
+    rcfg = RouterConfig(64, 6, n_group=8, topk_group=3, group_limited=True)
+    ry, ridx, rw, rlog = _oracle(oracle_lib, GROUPED, W, x[sample], cfg=rcfg)
+    assert_layer_parity(y[sample], idx[sample], w[sample], ry, ridx, rw, rlog, what="group-limited T=3000")
+    layer.close()
+
+
 @pytest.mark.parametrize("normalize", [False, True])
 def test_fused_group_limited_routing(oracle_lib, normalize):
     W = syn.layer_weights(GROUPED, seed=21, std=0.05)
