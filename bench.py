@@ -57,15 +57,21 @@ SWEEP = (1, 8, 32, 256)
 FLUSH_BYTES = 256 << 20
 
 
-def kernels_per_forward(tokens: int, world: int) -> int:
-    """Our kernel launches in one forward.  One GPU, T <= 32: the fused decode kernel
-    alone.  Otherwise: router logits, top-k, scan and place (or, with expert
-    parallelism at T <= 32, the fused route kernel); the row gather; the two grouped
-    GEMMs; and with expert parallelism the combine (NCCL's own kernels not counted)."""
-    if world == 1 and tokens <= 32:
-        return 1
+def kernels_per_forward(tokens: int, world: int, experts: int = 64, top_k: int = 6) -> int:
+    """Our kernel launches in one forward (NCCL's own kernels not counted).
+    One GPU: T <= 32 is the fused decode kernel alone; above that router logits,
+    top-k, scan, placement (which also gathers the token rows) and the two grouped
+    GEMMs.  Expert parallel: the routing (fused route kernel for T <= 32, else four
+    kernels), then with the fixed-capacity exchange (small batches) pack, sort,
+    device schedule, two GEMMs and the combine, or with the host-planned exchange
+    the row gather (T <= 32 only), sort, two GEMMs and the combine."""
+    if world == 1:
+        return 1 if tokens <= 32 else 6
     route = 1 if tokens <= 32 else 4
-    return route + 1 + 2 + (1 if world > 1 else 0)
+    fixed = world * tokens * min(top_k, experts // world) <= 8192
+    if fixed:
+        return route + 6
+    return route + (1 if tokens <= 32 else 0) + 4
 
 
 def parse_args(argv=None):

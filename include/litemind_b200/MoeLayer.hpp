@@ -9,6 +9,7 @@
 #include <stdexcept>
 #include <string>
 #include <utility>
+#include <vector>
 
 #include "litemind_moe.h"
 
@@ -64,6 +65,35 @@ public:
     void upload_expert(int32_t layer, int32_t expert, const uint16_t* gate, const uint16_t* up,
                        const uint16_t* down) {
         check(lm_moe_upload_expert(ctx_, layer, expert, gate, up, down));
+    }
+    /** Layer slot `layer` from SafeTensors shards, tensors model.layers.{checkpoint_layer}.* */
+    void load_safetensors(int32_t layer, const std::vector<std::string>& shards, int32_t checkpoint_layer) {
+        std::vector<const char*> paths;
+        paths.reserve(shards.size());
+        for (const std::string& p : shards) paths.push_back(p.c_str());
+        check(lm_moe_load_safetensors(ctx_, layer, checkpoint_layer, paths.data(), static_cast<int32_t>(paths.size())));
+    }
+
+    // Dense feed-forward layers (their own index space): DeepSeek's first layer.
+    void ffn_upload(int32_t layer, int32_t intermediate, const uint16_t* gate, const uint16_t* up,
+                    const uint16_t* down, const float* norm_weight = nullptr) {
+        check(lm_ffn_upload(ctx_, layer, intermediate, gate, up, down, norm_weight));
+    }
+    void ffn_load_safetensors(int32_t layer, const std::vector<std::string>& shards, int32_t checkpoint_layer,
+                              int32_t intermediate) {
+        std::vector<const char*> paths;
+        paths.reserve(shards.size());
+        for (const std::string& p : shards) paths.push_back(p.c_str());
+        check(lm_ffn_load_safetensors(ctx_, layer, checkpoint_layer, intermediate, paths.data(),
+                                      static_cast<int32_t>(paths.size())));
+    }
+    void ffn_forward(int32_t layer, const uint16_t* x, int32_t tokens, float* y, bool accumulate = false,
+                     void* stream = nullptr) {
+        check(lm_ffn_forward(ctx_, layer, x, tokens, y, accumulate ? 1 : 0, stream));
+    }
+    /** hidden (device f32 [T, H]) += FFN(rms_norm(hidden)). */
+    void ffn_block_forward(int32_t layer, float* hidden, int32_t tokens, void* stream = nullptr) {
+        check(lm_ffn_block_forward(ctx_, layer, hidden, tokens, stream));
     }
     /** x device bf16 [T, H] -> y device f32 [T, H] (asynchronous on `stream`). */
     void forward(int32_t layer, const uint16_t* x, int32_t tokens, float* y, bool accumulate = false,

@@ -965,14 +965,18 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
                                           bn, 2 * I / 128, H / 128, s, true));
         prof_mark(ctx, 3, s);
         slots[n_slots++] = 3;
+        // The placement also copies the token rows into expert order.
         LM_CUDA(ctx, launch_place(ctx->topk_idx, ctx->topk_w, ctx->tile_base, T, H, K, E, ctx->first_expert,
-                                  ctx->local_experts, ctx->row_token, ctx->row_weight, ctx->slot_row, y_zero, s, true));
+                                  ctx->local_experts, ctx->row_token, ctx->row_weight, ctx->slot_row, y_zero, x,
+                                  ctx->x_perm, s, true));
         prof_mark(ctx, 4, s);
         slots[n_slots++] = 4;
     }
-    LM_CUDA(ctx, launch_gather_rows(x, ctx->row_token, T * K, H, ctx->x_perm, s, true));
-    prof_mark(ctx, 0, s);
-    slots[n_slots++] = 0;
+    if (T <= kRouteTile) {
+        LM_CUDA(ctx, launch_gather_rows(x, ctx->row_token, T * K, H, ctx->x_perm, s, true));
+        prof_mark(ctx, 0, s);
+        slots[n_slots++] = 0;
+    }
     // Prefill-sized token tiles run on CTA pairs (256-row weight tiles); each CTA
     // loads half of a token tile, so the token maps' boxes are bn/2 rows.
     const bool pair = bn == 256;
@@ -1119,13 +1123,15 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
         LM_CUDA(ctx, launch_router_topk(ctx->logits, T, rp, ctx->topk_idx, ctx->topk_w, ctx->tile_counts, s, true, fix));
         LM_CUDA(ctx, launch_dispatch_scan(ctx->tile_counts, ctx->tile_base, ctx->expert_totals, ctx->sched, T, K, E,
                                           0, 0, E, 0, 16, 1, 1, s, true));
+        // Host-planned exchange: x_perm is the send buffer, filled by the placement.
         LM_CUDA(ctx, launch_place(ctx->topk_idx, ctx->topk_w, ctx->tile_base, T, H, K, E, 0, E, ctx->row_token,
-                                  ctx->row_weight, ctx->slot_row, y_zero, s, true));
+                                  ctx->row_weight, ctx->slot_row, y_zero, x, ctx->ep_cap > 0 ? nullptr : ctx->x_perm,
+                                  s, true));
     } else {
         LM_CUDA(ctx, cudaMemsetAsync(ctx->expert_totals, 0, E * sizeof(int32_t), s));
     }
     if (ctx->ep_cap > 0) return forward_ep_fixed(ctx, layer, x, T, y, s, slots, n_slots);
-    LM_CUDA(ctx, launch_gather_rows(x, ctx->row_token, T * K, H, ctx->x_perm, s, true));
+    if (T > 0 && T <= kRouteTile) LM_CUDA(ctx, launch_gather_rows(x, ctx->row_token, T * K, H, ctx->x_perm, s, true));
     prof_mark(ctx, 1, s);
     slots[n_slots++] = 1;
     // 2. Rows per (destination, expert) to every rank; one host sync to plan.

@@ -63,9 +63,11 @@ cudaError_t launch_dispatch_scan(const int32_t* tile_counts, int32_t* tile_base,
                                  Schedule* sched, int tokens, int top_k, int experts, int n_shared,
                                  int first_expert, int local_experts, int shared_base, int bn, int mb1,
                                  int mb2, cudaStream_t stream, bool pdl);
+// x_perm non-null: also copy each token's row of x to its expert-sorted rows.
 cudaError_t launch_place(const int32_t* topk_idx, const float* topk_w, const int32_t* tile_base, int tokens,
                          int hidden, int top_k, int experts, int first_expert, int local_experts, int32_t* row_token,
-                         float* row_weight, int32_t* slot_row, float* y_zero, cudaStream_t stream, bool pdl);
+                         float* row_weight, int32_t* slot_row, float* y_zero, const uint16_t* x, uint16_t* x_perm,
+                         cudaStream_t stream, bool pdl);
 cudaError_t launch_ep_combine(float* y, const uint16_t* back, const int32_t* slot_row, const float* topk_w, int tokens,
                               int top_k, int hidden, cudaStream_t stream, bool pdl);
 cudaError_t launch_dense_schedule(Schedule* sched, int tokens, int bn, int mb1, int mb2, cudaStream_t stream);

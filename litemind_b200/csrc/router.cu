@@ -321,13 +321,16 @@ __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(const int32
 
 // Permutation maps for one routing tile: each local expert walks the tile in
 // (token, slot) order, so rows are stable in token order and the placement is
-// deterministic.  Also zeroes the tile's rows of y when asked (the combine adds).
+// deterministic.  Also zeroes the tile's rows of y when asked (the combine adds),
+// and, when x_perm is given, copies each token's row to its expert-sorted places
+// (the row gather, reading each token once).
 __global__ void __launch_bounds__(256) place_kernel(const int32_t* __restrict__ topk_idx,
                                                     const float* __restrict__ topk_w,
                                                     const int32_t* __restrict__ tile_base, int T, int H, int K, int E,
                                                     int first_expert, int local_E, int32_t* __restrict__ row_token,
                                                     float* __restrict__ row_weight, int32_t* __restrict__ slot_row,
-                                                    float* __restrict__ y_zero) {
+                                                    float* __restrict__ y_zero, const uint16_t* __restrict__ x,
+                                                    uint16_t* __restrict__ x_perm) {
     __shared__ int s_idx[kRouteTile * kMaxTopK];
     __shared__ int s_row[kRouteTile * kMaxTopK];
     pdl_wait();
@@ -361,6 +364,28 @@ __global__ void __launch_bounds__(256) place_kernel(const int32_t* __restrict__ 
         if (row >= 0) {
             row_token[row] = t0 + q / K;
             row_weight[row] = topk_w[slot];
+        }
+    }
+    if (x_perm == nullptr) return;
+    // One warp per token: its row is read once and written to each of its rows.
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int vec = H / 8;
+    for (int tl = warp; tl < n_tok; tl += blockDim.x >> 5) {
+        const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0 + tl) * H);
+        for (int v0 = 0; v0 < vec; v0 += 128) {
+            uint4 r[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (v0 + u * 32 + lane < vec) r[u] = src[v0 + u * 32 + lane];
+            for (int k = 0; k < K; ++k) {
+                const int row = s_row[tl * K + k];
+                if (row < 0) continue;
+                uint4* dst = reinterpret_cast<uint4*>(x_perm + static_cast<size_t>(row) * H);
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (v0 + u * 32 + lane < vec) dst[v0 + u * 32 + lane] = r[u];
+            }
         }
     }
 }
@@ -672,11 +697,12 @@ cudaError_t launch_dispatch_scan(const int32_t* tile_counts, int32_t* tile_base,
 
 cudaError_t launch_place(const int32_t* topk_idx, const float* topk_w, const int32_t* tile_base, int tokens,
                          int hidden, int top_k, int experts, int first_expert, int local_experts, int32_t* row_token,
-                         float* row_weight, int32_t* slot_row, float* y_zero, cudaStream_t stream, bool pdl) {
+                         float* row_weight, int32_t* slot_row, float* y_zero, const uint16_t* x, uint16_t* x_perm,
+                         cudaStream_t stream, bool pdl) {
     if (tokens <= 0) return cudaSuccess;
     const int tiles = (tokens + kRouteTile - 1) / kRouteTile;
     return launch_k(place_kernel, dim3(tiles), dim3(256), stream, pdl, topk_idx, topk_w, tile_base, tokens, hidden,
-                    top_k, experts, first_expert, local_experts, row_token, row_weight, slot_row, y_zero);
+                    top_k, experts, first_expert, local_experts, row_token, row_weight, slot_row, y_zero, x, x_perm);
 }
 
 cudaError_t launch_gather_rows(const uint16_t* x, const int32_t* row_token, int rows, int hidden, uint16_t* x_perm,

@@ -1,7 +1,7 @@
 """The C++20 host mirror (include/litemind_b200/*.hpp) compiled as a user would:
 g++ against include/ and liblitemind_b200.so.  ExpertCacheTest replays the
-reference's ExpertCache statistics (CPU); MoeRouterTest runs the reference's routing
-checks on the GPU."""
+reference's ExpertCache statistics (CPU); SafeTensorsTest looks up checkpoint tensors
+through the C ABI (CPU); MoeRouterTest runs the reference's routing checks on the GPU."""
 import json
 import os
 import subprocess
@@ -44,3 +44,20 @@ def test_moe_router_mirror_reference_checks(tmp_path):
     exe = _compile("MoeRouterTest", tmp_path)
     res = subprocess.run([exe], capture_output=True, text=True)
     assert res.returncode == 0, res.stdout + res.stderr
+
+
+def test_safetensors_lookup_from_cpp(tmp_path):
+    import numpy as np
+
+    from litemind_b200.checkpoint import write_safetensors
+
+    shard = tmp_path / "shard.safetensors"
+    write_safetensors(shard, {"w": ("BF16", np.arange(48, dtype=np.uint16).reshape(6, 8)),
+                              "b": ("F32", np.ones(4, np.float32))})
+    raw = shard.read_bytes()
+    cut = tmp_path / "cut.safetensors"
+    cut.write_bytes(raw[:-20])
+    exe = _compile("SafeTensorsTest", tmp_path)
+    res = subprocess.run([exe, str(shard), str(cut)], capture_output=True, text=True)
+    assert res.returncode == 0, res.stdout + res.stderr
+
