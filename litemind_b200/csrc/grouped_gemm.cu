@@ -16,15 +16,17 @@
 //             the un-permute in one step.  Lanes of a warp hold 32 consecutive
 //             hidden rows, so every atomic add is a coalesced 128-byte run.
 //
-// One persistent CTA per SM walks the tile list in the device-built Schedule.
-// Warp 0 fills a ring of smem stages by TMA tile loads (128-byte swizzle, each
-// CTA loading its own tiles): weight tiles, and token tiles from the expert-sorted copy x_perm
-// (routed experts) or from x itself (shared experts).  Contiguous rows keep every
-// token tile one TMA request; gathering rows individually (TMA gather4 or cp.async)
-// measured 1.3x (decode) to 2.6x (prefill) slower on B200.  Warp 1 allocates TMEM
-// and issues tcgen05.mma from one thread, warps 2-5 drain the double-buffered
-// TMEM accumulators.  Every mbarrier wait is bounded
-// (ptx.cuh): a stalled pipeline records a status code and the kernel returns.
+// One persistent CTA per SM walks the tile list in the device-built Schedule --
+// whole tiles, or for launches of few tiles an equal share of all tiles' k-blocks
+// ("stream-K").  Warp 0 fills a ring of smem stages by TMA tile loads (128-byte
+// swizzle, each CTA loading its own tiles): weight tiles, and token tiles from the
+// expert-sorted copy x_perm (routed experts) or from x itself (shared experts).
+// Contiguous rows keep every token tile one TMA request; gathering rows
+// individually (TMA gather4 or cp.async) measured 1.3x (decode) to 2.6x (prefill)
+// slower on B200.  Warp 1 allocates TMEM and issues tcgen05.mma from one thread;
+// warps 2-9 drain the double-buffered TMEM accumulators, two warps per TMEM lane
+// quadrant.  Every mbarrier wait is bounded (ptx.cuh): a stalled pipeline records a
+// status code and the kernel returns.
 #include "moe_internal.h"
 #include "ptx.cuh"
 
