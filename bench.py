@@ -295,6 +295,15 @@ def time_forward(layer, x, y, flush, steps: int, torch, bias=None):
     return total / steps
 
 
+def stack_kernels_per_layer(tokens: int, world: int) -> int:
+    """One block: the RMSNorm, then the layer's own launches; the router reads f32
+    activations, so at >= 2048 tokens its logits take the split tiled kernel plus its
+    reduction instead of one launch."""
+    if world == 1 and tokens <= 32:
+        return 1 + 1
+    return 1 + kernels_per_forward(tokens, world) + (1 if tokens >= 2048 else 0)
+
+
 def run_stack(args, rank: int, world: int, local_rank: int) -> int:
     """`layers` x (RMSNorm -> MoE -> residual) over T tokens per rank."""
     import numpy as np
@@ -332,6 +341,12 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> int:
     for _ in range(max(args.warmup, 3)):
         step()
     layer.sync()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    t_load = time.perf_counter()
+    while time.perf_counter() - t_load < args.clock_window:
+        step()
+        torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -344,6 +359,7 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> int:
         end.record()
         end.synchronize()
         total += start.elapsed_time(end)
+    clock_info = clocks.stop()
     ms = total / args.steps
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device="cuda")
@@ -365,7 +381,8 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> int:
                      "frac": flops / (ms / 1e3) / 1e12 / world / peaks["bf16_tflops"],
                      "peak_source": f"{peaks['source']} (bf16_tflops)",
                      "hbm_frac": hbm / world / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "traffic": None},
-        "gpu_launches": None,
+        "clocks": clock_info,
+        "gpu_launches": stack_kernels_per_layer(T, world) * L * args.steps,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
