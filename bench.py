@@ -100,8 +100,9 @@ def measured_peaks() -> dict:
     if os.path.exists(path):
         with open(path) as f:
             d = json.load(f)
-        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 def committed_traffic(workload: str):
@@ -376,10 +377,13 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> int:
                    "layers": L, "seed": 4, "norm_weights": "ones", "resident_weight_gb": hbm / 1e9 / world,
                    "upload_s": upload_s,
                    "parallelism": "single GPU" if world == 1 else f"expert parallel, {64 // world} experts per GPU"},
+        # Timed inside seconds of back-to-back steps under the 1 kW cap: the sustained
+        # GEMM figure is the denominator (the burst one is reported beside it).
         "roofline": {"bound": "tensor", "achieved": flops / (ms / 1e3) / 1e12 / world,
-                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": flops / (ms / 1e3) / 1e12 / world / peaks["bf16_tflops"],
-                     "peak_source": f"{peaks['source']} (bf16_tflops)",
+                     "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": flops / (ms / 1e3) / 1e12 / world / peaks["bf16_tflops_sustained"],
+                     "frac_of_burst": flops / (ms / 1e3) / 1e12 / world / peaks["bf16_tflops"],
+                     "peak_source": f"{peaks['source']} (bf16_tflops_sustained)",
                      "hbm_frac": hbm / world / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "traffic": None},
         "clocks": clock_info,
         "gpu_launches": stack_kernels_per_layer(T, world) * L * args.steps,
@@ -518,14 +522,20 @@ def main(argv=None) -> int:
         gu_ms, gu_n = prof.get("gemm_gate_up", (0.0, 0))
         gu_avg = gu_ms / max(gu_n, 1)
         tf = gu_f / (gu_avg / 1e3) / 1e12 if gu_avg > 0 else 0.0
-        roofline.update({"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": tf / peaks["bf16_tflops"], "peak_source": f"{peaks['source']} (bf16_tflops)",
+        # The prefill step runs after seconds of back-to-back steps (the clock window),
+        # under the 1 kW cap: the sustained GEMM figure is the denominator, the burst
+        # fraction is reported beside it.
+        roofline.update({"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops_sustained"],
+                         "unit": "TFLOP/s", "frac": tf / peaks["bf16_tflops_sustained"],
+                         "frac_of_burst": tf / peaks["bf16_tflops"],
+                         "peak_source": f"{peaks['source']} (bf16_tflops_sustained)",
                          "flops_per_launch": gu_f, "bytes_per_launch": None, "mean_launch_ms": gu_avg,
                          "kernel": "gemm_gate_up (tcgen05 CTA-pair grouped GEMM, gate/up + SiLU epilogue)",
                          "traffic": committed_traffic(f"gemm_gate_up_T{T}")})
         lf = layer_flops(shape, T)
-        layer_roofline = {"flops": lf, "achieved": lf / (ms / 1e3) / 1e12, "peak": peaks["bf16_tflops"],
-                          "unit": "TFLOP/s", "frac": lf / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+        layer_roofline = {"flops": lf, "achieved": lf / (ms / 1e3) / 1e12, "peak": peaks["bf16_tflops_sustained"],
+                          "unit": "TFLOP/s", "frac": lf / (ms / 1e3) / 1e12 / peaks["bf16_tflops_sustained"],
+                          "frac_of_burst": lf / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
                           "expert_rows": [int(v) for v in layer.expert_counts()]}
 
     # ── end to end through the C ABI with host buffers ──
