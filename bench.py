@@ -57,21 +57,23 @@ SWEEP = (1, 8, 32, 256)
 FLUSH_BYTES = 256 << 20
 
 
-def kernels_per_forward(tokens: int, world: int, experts: int = 64, top_k: int = 6) -> int:
+def kernels_per_forward(tokens: int, world: int, experts: int = 64, top_k: int = 6, sms: int = 148) -> int:
     """Our kernel launches in one forward (NCCL's own kernels not counted).
     One GPU: T <= 32 is the fused decode kernel alone; above that router logits,
-    top-k, scan, placement (which also gathers the token rows) and the two grouped
-    GEMMs.  Expert parallel: the routing (fused route kernel for T <= 32, else four
-    kernels), then with the fixed-capacity exchange (small batches) pack, sort,
-    device schedule, two GEMMs and the combine, or with the host-planned exchange
-    the row gather (T <= 32 only), sort, two GEMMs and the combine."""
+    top-k, scan, placement and the two grouped GEMMs, plus a separate row gather
+    unless the placement copies the rows itself (2 T >= 32 x SMs).  Expert parallel:
+    the routing (fused route kernel for T <= 32, else four kernels), then with the
+    fixed-capacity exchange (small batches) pack, sort, device schedule, two GEMMs
+    and the combine, or with the host-planned exchange the row gather (when the
+    placement does not copy), sort, two GEMMs and the combine."""
+    gather = 0 if tokens > 32 and 2 * tokens >= 32 * sms else 1
     if world == 1:
-        return 1 if tokens <= 32 else 6
+        return 1 if tokens <= 32 else 6 + gather
     route = 1 if tokens <= 32 else 4
     fixed = world * tokens * min(top_k, experts // world) <= 8192
     if fixed:
         return route + 6
-    return route + (1 if tokens <= 32 else 0) + 4
+    return route + gather + 4
 
 
 def parse_args(argv=None):
@@ -296,13 +298,17 @@ def time_forward(layer, x, y, flush, steps: int, torch, bias=None):
     return total / steps
 
 
-def stack_kernels_per_layer(tokens: int, world: int) -> int:
+def device_sms(torch) -> int:
+    return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+
+
+def stack_kernels_per_layer(tokens: int, world: int, sms: int = 148) -> int:
     """One block: the RMSNorm, then the layer's own launches; the router reads f32
     activations, so at >= 2048 tokens its logits take the split tiled kernel plus its
     reduction instead of one launch."""
     if world == 1 and tokens <= 32:
         return 1 + 1
-    return 1 + kernels_per_forward(tokens, world) + (1 if tokens >= 2048 else 0)
+    return 1 + kernels_per_forward(tokens, world, sms=sms) + (1 if tokens >= 2048 else 0)
 
 
 def run_stack(args, rank: int, world: int, local_rank: int) -> int:
@@ -386,7 +392,7 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> int:
                      "peak_source": f"{peaks['source']} (bf16_tflops_sustained)",
                      "hbm_frac": hbm / world / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "traffic": None},
         "clocks": clock_info,
-        "gpu_launches": stack_kernels_per_layer(T, world) * L * args.steps,
+        "gpu_launches": stack_kernels_per_layer(T, world, device_sms(torch)) * L * args.steps,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -583,7 +589,8 @@ def main(argv=None) -> int:
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(args, world),
         "roofline": roofline, "layer_roofline": layer_roofline, "cpu_baseline": cpu, "e2e": e2e,
-        "clocks": clock_info, "gpu_launches": kernels_per_forward(T, world) * args.steps, "sweep": sweep,
+        "clocks": clock_info, "gpu_launches": kernels_per_forward(T, world, sms=device_sms(torch)) * args.steps,
+        "sweep": sweep,
         "wall_s_timed_region": wall,
     }
     if rank == 0:

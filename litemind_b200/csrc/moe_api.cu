@@ -188,6 +188,11 @@ int choose_bn(int tokens, int top_k, int experts) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Whether the placement kernel (one CTA per routing tile) also copies the token rows:
+// only past the routed-small path and with at least one tile per two SMs.  Below that
+// the separate gather (a CTA per row) copies faster than the placement's few CTAs.
+bool place_gathers(const lm_moe_ctx* ctx, int T) { return T > kRouteTile && 2 * T >= kRouteTile * ctx->sms; }
+
 lm_status check_layer(lm_moe_ctx* ctx, int32_t layer) {
     if (layer < 0 || layer >= static_cast<int32_t>(ctx->layers.size()))
         return fail(ctx, LM_ERR_INVALID_ARGUMENT, "layer index out of range");
@@ -965,14 +970,16 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
                                           bn, 2 * I / 128, H / 128, s, true));
         prof_mark(ctx, 3, s);
         slots[n_slots++] = 3;
-        // The placement also copies the token rows into expert order.
+        // With enough routing tiles the placement also copies the token rows into
+        // expert order (each token read once); below that its grid is too small to
+        // copy fast and the separate gather runs instead.
         LM_CUDA(ctx, launch_place(ctx->topk_idx, ctx->topk_w, ctx->tile_base, T, H, K, E, ctx->first_expert,
                                   ctx->local_experts, ctx->row_token, ctx->row_weight, ctx->slot_row, y_zero, x,
-                                  ctx->x_perm, s, true));
+                                  place_gathers(ctx, T) ? ctx->x_perm : nullptr, s, true));
         prof_mark(ctx, 4, s);
         slots[n_slots++] = 4;
     }
-    if (T <= kRouteTile) {
+    if (!place_gathers(ctx, T)) {
         LM_CUDA(ctx, launch_gather_rows(x, ctx->row_token, T * K, H, ctx->x_perm, s, true));
         prof_mark(ctx, 0, s);
         slots[n_slots++] = 0;
@@ -1123,15 +1130,17 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
         LM_CUDA(ctx, launch_router_topk(ctx->logits, T, rp, ctx->topk_idx, ctx->topk_w, ctx->tile_counts, s, true, fix));
         LM_CUDA(ctx, launch_dispatch_scan(ctx->tile_counts, ctx->tile_base, ctx->expert_totals, ctx->sched, T, K, E,
                                           0, 0, E, 0, 16, 1, 1, s, true));
-        // Host-planned exchange: x_perm is the send buffer, filled by the placement.
+        // Host-planned exchange: x_perm is the send buffer, filled by the placement
+        // when its grid is large enough (see forward_impl), else by the gather below.
         LM_CUDA(ctx, launch_place(ctx->topk_idx, ctx->topk_w, ctx->tile_base, T, H, K, E, 0, E, ctx->row_token,
-                                  ctx->row_weight, ctx->slot_row, y_zero, x, ctx->ep_cap > 0 ? nullptr : ctx->x_perm,
-                                  s, true));
+                                  ctx->row_weight, ctx->slot_row, y_zero, x,
+                                  ctx->ep_cap == 0 && place_gathers(ctx, T) ? ctx->x_perm : nullptr, s, true));
     } else {
         LM_CUDA(ctx, cudaMemsetAsync(ctx->expert_totals, 0, E * sizeof(int32_t), s));
     }
     if (ctx->ep_cap > 0) return forward_ep_fixed(ctx, layer, x, T, y, s, slots, n_slots);
-    if (T > 0 && T <= kRouteTile) LM_CUDA(ctx, launch_gather_rows(x, ctx->row_token, T * K, H, ctx->x_perm, s, true));
+    if (T > 0 && !place_gathers(ctx, T))
+        LM_CUDA(ctx, launch_gather_rows(x, ctx->row_token, T * K, H, ctx->x_perm, s, true));
     prof_mark(ctx, 1, s);
     slots[n_slots++] = 1;
     // 2. Rows per (destination, expert) to every rank; one host sync to plan.
