@@ -496,6 +496,8 @@ def main(argv=None) -> int:
         flush()
         layer.forward(0, x, y=y, bias=bias)
     prof = layer.profile_read(reset=True)
+    # Chunked expert-parallel exchange: per-step device times of the last profiled step.
+    ep_timeline = layer.profile_ep_timeline() if world > 1 else None
     layer.profile(False)
     peaks = measured_peaks()
     total_prof = sum(v[0] for v in prof.values())
@@ -518,6 +520,10 @@ def main(argv=None) -> int:
                 "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} (hbm_gbs)",
                 "bytes_per_launch": k_bytes, "mean_launch_ms": gu_avg, "traffic": k_traffic,
                 "share_of_step": {k: round(v[0] / total_prof, 4) for k, v in prof.items()} if total_prof else {}}
+    if ep_timeline is not None:
+        roofline["ep_timeline_ms"] = ep_timeline
+        roofline["note"] = ("chunked exchange: the gemm_gate_up slot spans the shared experts' and every chunk's "
+                            "GEMMs, overlapped with the NCCL dispatch and return of other chunks")
     lb = layer_bytes(shape, touched, T)
     layer_roofline = {"bytes": lb, "achieved": lb / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                       "frac": lb / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "touched_experts": touched}

@@ -234,6 +234,16 @@ lm_status lm_moe_profile_read(lm_moe_ctx* ctx, double* total_ms, int64_t* launch
  * ran with (0 if none was traced). */
 #define LM_DECODE_TRACE_SLOTS 16
 lm_status lm_moe_profile_trace(lm_moe_ctx* ctx, uint64_t* stamps, int32_t ctas, int32_t* ctas_out);
+/* While profiling, the chunked expert-parallel exchange (C chunks, see
+ * lm_moe_ep_chunk_plan) times each of its steps on the device from the moment its
+ * rows start to leave.  Copies the last such forward's 4 C + 2 times (ms) -- C ends
+ * of the chunks' dispatches (exchange stream), the end of the shared experts' GEMMs,
+ * C starts of the chunks' GEMMs (their rows in), C ends of the chunks' GEMMs, C ends
+ * of the chunks' returns (exchange stream), the end of the combine -- up to
+ * `capacity` values, and sets *chunks_out to C (0 when no chunked forward was
+ * profiled). */
+#define LM_EP_TIMELINE_MAX 40
+lm_status lm_moe_profile_ep_timeline(lm_moe_ctx* ctx, float* ms, int32_t capacity, int32_t* chunks_out);
 
 /*
  * Expert parallelism over NCCL (NVLink within a node).  Every rank creates its
@@ -244,8 +254,13 @@ lm_status lm_moe_profile_trace(lm_moe_ctx* ctx, uint64_t* stamps, int32_t ctas, 
  * with its own T tokens, T <= max_tokens, possibly 0 -- routes them over all
  * experts, exchanges per-expert row counts, sends the rows to the experts' ranks,
  * runs the local experts, returns their outputs and combines them with the
- * routing weights and the shared experts.  It waits once on the host for the
- * counts.  NCCL is loaded at run time (libnccl.so.2).
+ * routing weights and the shared experts.  Contexts whose nranks x max_tokens x
+ * min(k, E/N) stays within 8192 rows exchange fixed blocks of rows and plan on the
+ * device (no host wait); larger ones wait once on the host for the counts and move
+ * the rows in chunks of local experts overlapped with the GEMMs
+ * (lm_moe_ep_chunk_plan).  The ranks compare their configs here (one small NCCL
+ * exchange) and all fail with LM_ERR_INVALID_ARGUMENT when any differs.  NCCL is
+ * loaded at run time (libnccl.so.2).
  */
 lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t rank,
                          int32_t nranks);
@@ -257,8 +272,9 @@ lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t ra
  * from rank s at row recv_offset[s] of its receive buffer.
  *   send_expert_counts  [E]: this rank's rows per expert (all experts)
  *   recv_expert_counts  [nranks, E/nranks]: rows each rank sends to this rank's experts
- * lm_moe_forward uses exactly this plan; it is exported so callers can size
- * buffers and so the plan can be checked across ranks without a GPU.
+ * lm_moe_forward's host-planned exchange moves exactly these rows (in chunks, see
+ * below); the plan is exported so callers can size buffers and so it can be checked
+ * across ranks without a GPU.
  */
 #define LM_EP_MAX_RANKS 64
 typedef struct lm_ep_plan {
@@ -271,6 +287,24 @@ typedef struct lm_ep_plan {
 } lm_ep_plan;
 lm_status lm_moe_ep_plan(int32_t nranks, int32_t experts, const int32_t* send_expert_counts,
                          const int32_t* recv_expert_counts, lm_ep_plan* plan);
+
+/*
+ * The same exchange in `chunks` pieces: chunk c carries the rows of this rank's
+ * local experts [c El / chunks, (c+1) El / chunks) (El = experts / nranks), so one
+ * chunk's rows can travel while an earlier chunk's experts compute.  Chunk c's plan:
+ * send_count[d] rows to rank d from send_offset[d] of the expert-sorted send buffer
+ * (rank d's chunk-c experts are contiguous there); recv_count[s] rows from rank s at
+ * recv_offset[s] of the receive buffer, which holds all of chunk 0 (by source rank),
+ * then all of chunk 1, and so on.  n_send / n_recv are the chunk's totals.  The
+ * outputs go back with the offsets reversed.  chunks = 1 is lm_moe_ep_plan.
+ * lm_moe_forward uses LITEMIND_B200_EP_CHUNKS chunks (default 2, at most 8 and at
+ * most El) when the context exchanges by host plan, with NCCL capped to
+ * LITEMIND_B200_EP_NCCL_CTAS CTAs (default 32) and the GEMMs leaving it that many
+ * SMs; every rank must use the same (lm_moe_ep_init checks).
+ */
+lm_status lm_moe_ep_chunk_plan(int32_t nranks, int32_t experts, int32_t chunks, int32_t chunk,
+                               const int32_t* send_expert_counts, const int32_t* recv_expert_counts,
+                               lm_ep_plan* plan);
 
 /* A fresh 128-byte ncclUniqueId for lm_moe_ep_init (rank 0 makes it; the caller
  * shares it with the other ranks by any host channel). */

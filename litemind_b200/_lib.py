@@ -83,9 +83,11 @@ SIGNATURES = {
     "lm_moe_ep_init": (_i32, [_vp, _vp, _i32, _i32]),
     "lm_moe_ep_unique_id": (_i32, [_vp]),
     "lm_moe_ep_plan": (_i32, [_i32, _i32, _vp, _vp, C.POINTER(LmEpPlan)]),
+    "lm_moe_ep_chunk_plan": (_i32, [_i32, _i32, _i32, _i32, _vp, _vp, C.POINTER(LmEpPlan)]),
     "lm_moe_profile_enable": (_i32, [_vp, _i32]),
     "lm_moe_profile_read": (_i32, [_vp, _vp, _vp, _i32]),
     "lm_moe_profile_trace": (_i32, [_vp, _vp, _i32, _vp]),
+    "lm_moe_profile_ep_timeline": (_i32, [_vp, _vp, _i32, C.POINTER(C.c_int32)]),
     "lm_moe_route_static": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp]),
     "lm_gemm_matvec_bf16": (_i32, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "lm_gemm_matvec_bf16_accumulate": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp]),

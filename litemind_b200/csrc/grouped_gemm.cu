@@ -29,6 +29,7 @@
 // status code and the kernel returns.
 #include "moe_internal.h"
 #include "ptx.cuh"
+#include "gemm_rows.cuh"
 
 #include <cuda_bf16.h>
 
@@ -476,9 +477,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 16; ++j)
                             if (c0 + j < valid) {
                                 const int row = row0 + c0 + j;
-                                const int dst = args.y_rows_map != nullptr ? args.y_rows_map[row] : row;
-                                reinterpret_cast<__nv_bfloat16*>(args.y_rows)[static_cast<size_t>(dst) * args.hidden + d] =
-                                    __float2bfloat16_rn(__uint_as_float(r[j]));
+                                const int dst = y_row_dst(args, row);
+                                if (dst >= 0)
+                                    reinterpret_cast<__nv_bfloat16*>(args.y_rows)[static_cast<size_t>(dst) * args.hidden +
+                                                                                  d] =
+                                        __float2bfloat16_rn(__uint_as_float(r[j]));
                             }
                     }
                     tc_fence_before();

@@ -16,6 +16,7 @@
 // both CTAs alive until neither touches the other's shared memory or TMEM.
 #include "moe_internal.h"
 #include "ptx.cuh"
+#include "gemm_rows.cuh"
 
 #include <cuda_bf16.h>
 
@@ -323,11 +324,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
                             const int c = c0 + j;
-                            if (c < valid)
-                                reinterpret_cast<__nv_bfloat16*>(args.y_rows)
-                                    [static_cast<size_t>(args.y_rows_map != nullptr ? args.y_rows_map[row0 + c] : row0 + c) *
-                                         args.hidden +
-                                     d] = __float2bfloat16_rn(__uint_as_float(r[j]));
+                            const int dst = c < valid ? y_row_dst(args, row0 + c) : -1;
+                            if (dst >= 0)
+                                reinterpret_cast<__nv_bfloat16*>(args.y_rows)[static_cast<size_t>(dst) * args.hidden +
+                                                                              d] =
+                                    __float2bfloat16_rn(__uint_as_float(r[j]));
                         }
                     } else {
                         int tok[32];

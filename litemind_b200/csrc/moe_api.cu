@@ -16,6 +16,7 @@
 // shared FFN of width inter * n_shared, src/DeepSeekRunner.cpp:217-222).
 #include "moe_internal.h"
 #include "nccl_dl.h"
+#include "ptx.cuh"
 #include "host/SafeTensors.hpp"
 
 #include <algorithm>
@@ -122,8 +123,20 @@ struct lm_moe_ctx {
     uint16_t* y_ret = nullptr;     // expert outputs of the received rows (bf16), returned to their ranks
     uint16_t* y_back = nullptr;    // this rank's rows' expert outputs (bf16), in send order
     int32_t* recv_counts = nullptr;  // [nranks, local experts] rows received per source and expert
-    lm::Schedule* sched_ep = nullptr;
-    lm::Schedule* host_sched = nullptr;  // pinned
+    lm::Schedule* sched_ep = nullptr;    // [kEpMaxChunks + 1]: one per chunk, then the shared experts'
+    lm::Schedule* host_sched = nullptr;  // pinned, same shape
+    int ep_chunks = 2;     // local-expert chunks of the host-planned exchange (LITEMIND_B200_EP_CHUNKS; 1: off)
+    int ep_nccl_ctas = 32;  // NCCL's CTA cap, and the SMs the chunked GEMMs leave it (LITEMIND_B200_EP_NCCL_CTAS)
+    cudaStream_t ep_stream = nullptr;  // the chunked exchange's NCCL stream
+    cudaEvent_t ep_ev_ready = nullptr;
+    cudaEvent_t ep_ev_back = nullptr;
+    cudaEvent_t ep_ev_sent[lm::kEpMaxChunks]{};
+    cudaEvent_t ep_ev_done[lm::kEpMaxChunks]{};
+    // Profiling: timing events of the chunked exchange's last forward (see
+    // lm_moe_profile_ep_timeline) and the times read from them.
+    cudaEvent_t ep_tl_events[LM_EP_TIMELINE_MAX + 1]{};
+    float ep_timeline[LM_EP_TIMELINE_MAX]{};
+    int ep_timeline_chunks = 0;
     int32_t* host_totals = nullptr;      // pinned [E]
     int32_t* host_recv = nullptr;        // pinned [nranks * local experts]
     CUtensorMap map_xrecv[5]{};
@@ -497,6 +510,15 @@ lm_status lm_moe_destroy(lm_moe_ctx* ctx) {
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     if (ctx->comm != nullptr && ctx->nccl != nullptr) ctx->nccl->CommDestroy(ctx->comm);
     if (ctx->host_sched) cudaFreeHost(ctx->host_sched);
+    if (ctx->ep_stream) cudaStreamDestroy(ctx->ep_stream);
+    for (cudaEvent_t e : {ctx->ep_ev_ready, ctx->ep_ev_back})
+        if (e) cudaEventDestroy(e);
+    for (int i = 0; i < kEpMaxChunks; ++i) {
+        if (ctx->ep_ev_sent[i]) cudaEventDestroy(ctx->ep_ev_sent[i]);
+        if (ctx->ep_ev_done[i]) cudaEventDestroy(ctx->ep_ev_done[i]);
+    }
+    for (cudaEvent_t e : ctx->ep_tl_events)
+        if (e) cudaEventDestroy(e);
     if (ctx->host_totals) cudaFreeHost(ctx->host_totals);
     if (ctx->host_recv) cudaFreeHost(ctx->host_recv);
     for (auto& e : ctx->prof_events)
@@ -1062,7 +1084,7 @@ static lm_status forward_ep_fixed(lm_moe_ctx* ctx, int32_t layer, const uint16_t
     const int bn = std::min(choose_bn(N * std::max(T, 1), K, E), 128);
     const int bi = bn_index(bn);
     LM_CUDA(ctx, launch_ep_sort_rows(ctx->x_recv, ctx->x_sorted, ctx->ep_row_src, ctx->recv_counts, N, El, cap, H, cap,
-                                     s, false));
+                                     0, El, s, false));
     LM_CUDA(ctx, launch_ep_schedule(ctx->recv_counts, ctx->sched_ep, N, El, c.n_shared_experts, T, ctx->routed_cap, bn,
                                     2 * I / 128, H / 128, s, true));
     prof_mark(ctx, 7, s);
@@ -1078,6 +1100,7 @@ static lm_status forward_ep_fixed(lm_moe_ctx* ctx, int32_t layer, const uint16_t
     args.y = y;
     args.y_rows = ctx->y_ret;
     args.y_rows_map = ctx->ep_row_src;
+    args.y_rows_cap = ctx->routed_cap;
     args.status = ctx->status;
     args.tokens = T;
     args.hidden = H;
@@ -1153,64 +1176,86 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     LM_CUDA(ctx, cudaMemcpyAsync(ctx->host_totals, ctx->expert_totals, E * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     LM_CUDA(ctx, cudaMemcpyAsync(ctx->host_recv, ctx->recv_counts, N * El * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     LM_CUDA(ctx, cudaStreamSynchronize(s));
-    lm_ep_plan plan;
-    if (lm_moe_ep_plan(N, E, ctx->host_totals, ctx->host_recv, &plan) != LM_OK)
+    lm_ep_plan total;
+    if (lm_moe_ep_plan(N, E, ctx->host_totals, ctx->host_recv, &total) != LM_OK)
         return fail(ctx, LM_ERR_INVALID_ARGUMENT, "invalid expert-parallel plan");
-    const int32_t* send_cnt = plan.send_count;
-    const int32_t* send_off = plan.send_offset;
-    const int32_t* recv_cnt = plan.recv_count;
-    const int32_t* recv_off = plan.recv_offset;
-    const int n_recv = plan.n_recv;
-    // Receiver schedule: one segment per local expert (its rows from every source,
-    // made contiguous by ep_sort_rows after the dispatch), then the shared experts.
-    const int n_routed = El;
-    const int bn = choose_bn(n_recv, 1, n_routed);  // from the mean rows per local expert
+    // The local experts move in C chunks (lm_moe_ep_chunk_plan).  C = 1: one exchange
+    // each way, all on the caller's stream.  C > 1: every chunk's rows go out on the
+    // exchange stream at once; the caller's stream runs the shared experts (they need
+    // no rows from other ranks), then each chunk's sort and GEMMs as its rows arrive,
+    // and each chunk's outputs go back while the next chunk computes.  The GEMMs then
+    // leave ep_nccl_ctas SMs to NCCL's kernels (capped to that many CTAs at init).
+    const int C = ctx->ep_chunks;
+    const bool piped = C > 1;
+    const int gemm_sms = piped ? std::max(2, (ctx->sms - ctx->ep_nccl_ctas) & ~1) : ctx->sms;
+    lm_ep_plan plans[kEpMaxChunks];
+    for (int k = 0; k < C; ++k)
+        if (lm_moe_ep_chunk_plan(N, E, C, k, ctx->host_totals, ctx->host_recv, &plans[k]) != LM_OK)
+            return fail(ctx, LM_ERR_INVALID_ARGUMENT, "invalid expert-parallel plan");
+    // Receiver schedules: one segment per local expert (its rows from every source,
+    // made contiguous by ep_sort_rows after the dispatch; expert-major over all
+    // chunks), then the shared experts -- in chunk 0's schedule when C = 1, else in
+    // a schedule of their own (slot C).
+    const int bn = choose_bn(total.n_recv, 1, El);  // from the mean rows per local expert
     const int bi = bn_index(bn);
-    Schedule& hs = *ctx->host_sched;
-    int p1 = 0, p2 = 0, seg = 0;
     const int mb1 = 2 * I / 128, mb2 = H / 128;
-    auto add_segment = [&](int off, int cnt, int wslot) {
-        hs.seg_off[seg] = off;
-        hs.seg_cnt[seg] = cnt;
-        hs.seg_weight[seg] = wslot;
+    int expert_row[kMaxExperts + 1];  // first expert-major row of each local expert
+    expert_row[0] = 0;
+    for (int e = 0; e < El; ++e) {
+        int cnt = 0;
+        for (int r = 0; r < N; ++r) cnt += ctx->host_recv[r * El + e];
+        expert_row[e + 1] = expert_row[e] + cnt;
+    }
+    auto build = [&](Schedule& hs, int e_lo, int e_hi, bool shared) {
+        int p1 = 0, p2 = 0, seg = 0;
+        auto add_segment = [&](int off, int cnt, int wslot) {
+            hs.seg_off[seg] = off;
+            hs.seg_cnt[seg] = cnt;
+            hs.seg_weight[seg] = wslot;
+            hs.tiles1[seg] = p1;
+            hs.tiles2[seg] = p2;
+            const int nb = (cnt + bn - 1) / bn;
+            p1 += nb * mb1;
+            p2 += nb * mb2;
+            ++seg;
+        };
+        for (int e = e_lo; e < e_hi; ++e) add_segment(expert_row[e], expert_row[e + 1] - expert_row[e], e);
+        if (shared)
+            for (int j = 0; j < c.n_shared_experts; ++j) add_segment(ctx->routed_cap + j * T, T, El + j);
         hs.tiles1[seg] = p1;
         hs.tiles2[seg] = p2;
-        const int nb = (cnt + bn - 1) / bn;
-        p1 += nb * mb1;
-        p2 += nb * mb2;
-        ++seg;
+        hs.n_seg = seg;
+        hs.first_expert = ctx->first_expert;
     };
-    int max_group = 0;
-    for (int e = 0, off = 0; e < El; ++e) {
-        int cnt = 0;
-        for (int r = 0; r < N; ++r) {
-            cnt += ctx->host_recv[r * El + e];
-            max_group = std::max(max_group, ctx->host_recv[r * El + e]);
+    int max_group[kEpMaxChunks];
+    for (int k = 0; k < C; ++k) {
+        const int e_lo = k * El / C, e_hi = (k + 1) * El / C;
+        build(ctx->host_sched[k], e_lo, e_hi, !piped);
+        max_group[k] = 0;
+        for (int r = 0; r < N; ++r)
+            for (int e = e_lo; e < e_hi; ++e) max_group[k] = std::max(max_group[k], ctx->host_recv[r * El + e]);
+    }
+    if (piped) build(ctx->host_sched[C], 0, 0, true);
+    const int n_sched = C + (piped ? 1 : 0);
+    LM_CUDA(ctx, cudaMemcpyAsync(ctx->sched_ep, ctx->host_sched, n_sched * sizeof(Schedule), cudaMemcpyHostToDevice, s));
+    // One NCCL group per chunk and direction: rows out (x_perm -> x_recv) or expert
+    // outputs back (y_ret -> y_back, the same offsets reversed).
+    auto exchange = [&](int k, bool back, cudaStream_t st) -> lm_status {
+        const lm_ep_plan& pk = plans[k];
+        LM_NCCL(ctx, nc.GroupStart());
+        for (int d = 0; d < N; ++d) {
+            uint16_t* out = back ? ctx->y_ret + static_cast<size_t>(pk.recv_offset[d]) * H
+                                 : ctx->x_perm + static_cast<size_t>(pk.send_offset[d]) * H;
+            uint16_t* in = back ? ctx->y_back + static_cast<size_t>(pk.send_offset[d]) * H
+                                : ctx->x_recv + static_cast<size_t>(pk.recv_offset[d]) * H;
+            const size_t n_out = static_cast<size_t>(back ? pk.recv_count[d] : pk.send_count[d]) * H;
+            const size_t n_in = static_cast<size_t>(back ? pk.send_count[d] : pk.recv_count[d]) * H;
+            if (n_out > 0) LM_NCCL(ctx, nc.Send(out, n_out, ncclBfloat16, d, ctx->comm, st));
+            if (n_in > 0) LM_NCCL(ctx, nc.Recv(in, n_in, ncclBfloat16, d, ctx->comm, st));
         }
-        add_segment(off, cnt, e);
-        off += cnt;
-    }
-    for (int j = 0; j < c.n_shared_experts; ++j) add_segment(ctx->routed_cap + j * T, T, El + j);
-    hs.tiles1[seg] = p1;
-    hs.tiles2[seg] = p2;
-    hs.n_seg = seg;
-    hs.first_expert = ctx->first_expert;
-    LM_CUDA(ctx, cudaMemcpyAsync(ctx->sched_ep, &hs, sizeof(Schedule), cudaMemcpyHostToDevice, s));
-    // 3. Dispatch token rows.
-    LM_NCCL(ctx, nc.GroupStart());
-    for (int d = 0; d < N; ++d) {
-        if (send_cnt[d] > 0)
-            LM_NCCL(ctx, nc.Send(ctx->x_perm + static_cast<size_t>(send_off[d]) * H, static_cast<size_t>(send_cnt[d]) * H,
-                                 ncclBfloat16, d, ctx->comm, s));
-        if (recv_cnt[d] > 0)
-            LM_NCCL(ctx, nc.Recv(ctx->x_recv + static_cast<size_t>(recv_off[d]) * H, static_cast<size_t>(recv_cnt[d]) * H,
-                                 ncclBfloat16, d, ctx->comm, s));
-    }
-    LM_NCCL(ctx, nc.GroupEnd());
-    LM_CUDA(ctx, launch_ep_sort_rows(ctx->x_recv, ctx->x_sorted, ctx->ep_row_src, ctx->recv_counts, N, El, max_group, H,
-                                     0, s, false));
-    prof_mark(ctx, 7, s);
-    slots[n_slots++] = 7;
+        LM_NCCL(ctx, nc.GroupEnd());
+        return LM_OK;
+    };
     // 4. Local experts on the received rows, shared experts on this rank's tokens.
     CUtensorMap map_x{};
     std::string err;
@@ -1220,48 +1265,116 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     if (!encode_tensor_map_bf16(&map_x, T > 0 ? x : ctx->x_perm, std::max(T, 1), H, pair ? bn / 2 : bn, 64, err))
         return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
     GemmArgs args{};
-    args.sched = ctx->sched_ep;
     args.x = x;
     args.h = ctx->h;
     args.y = y;
     args.y_rows = ctx->y_ret;
     args.y_rows_map = ctx->ep_row_src;
+    args.y_rows_cap = ctx->routed_cap;
     args.row_token = ctx->row_token;
     args.row_weight = ctx->row_weight;
     args.status = ctx->status;
     args.tokens = T;
     args.hidden = H;
     args.inter = I;
-    args.n_routed_local = n_routed;
+    args.n_routed_local = El;
     args.split_ws = ctx->split_ws;
     args.split_ticket = ctx->split_ticket;
     args.split_ws_floats = static_cast<int32_t>(kSplitWsBytes / sizeof(float));
     args.split_max_waves = ctx->split_max_waves;
-    if (pair) {
-        const int hi = bn_index(bn / 2);
-        LM_CUDA(ctx, launch_gemm_gate_up_pair(bn, L.map_w13, ctx->map_xsorted[hi], map_x, args, ctx->sms, s, true));
-        prof_mark(ctx, 5, s);
-        slots[n_slots++] = 5;
-        LM_CUDA(ctx, launch_gemm_down_pair(bn, L.map_w2, ctx->map_h[hi], args, ctx->sms, s, true));
+    auto gemms = [&](int slot, bool mark) -> lm_status {
+        args.sched = ctx->sched_ep + slot;
+        // The kernels take segments [0, n_routed_local) as routed (rows from x_sorted,
+        // outputs to y_ret) and the rest as shared (rows from x, outputs into y): the
+        // shared experts' own schedule has no routed segment.
+        args.n_routed_local = piped && slot == C ? 0 : El;
+        if (pair) {
+            const int hi = bn_index(bn / 2);
+            LM_CUDA(ctx, launch_gemm_gate_up_pair(bn, L.map_w13, ctx->map_xsorted[hi], map_x, args, gemm_sms, s, true));
+            if (mark) {
+                prof_mark(ctx, 5, s);
+                slots[n_slots++] = 5;
+            }
+            LM_CUDA(ctx, launch_gemm_down_pair(bn, L.map_w2, ctx->map_h[hi], args, gemm_sms, s, true));
+        } else {
+            LM_CUDA(ctx, launch_gemm_gate_up(bn, L.map_w13, ctx->map_xsorted[bi], map_x, args, gemm_sms, s, true));
+            if (mark) {
+                prof_mark(ctx, 5, s);
+                slots[n_slots++] = 5;
+            }
+            LM_CUDA(ctx, launch_gemm_down(bn, L.map_w2, ctx->map_h[bi], args, gemm_sms, s, true));
+        }
+        if (mark) {
+            prof_mark(ctx, 6, s);
+            slots[n_slots++] = 6;
+        }
+        return LM_OK;
+    };
+    auto sort = [&](int k, cudaStream_t st, bool pdl) -> lm_status {
+        LM_CUDA(ctx, launch_ep_sort_rows(ctx->x_recv, ctx->x_sorted, ctx->ep_row_src, ctx->recv_counts, N, El,
+                                         max_group[k], H, 0, k * El / C, (k + 1) * El / C, st, pdl));
+        return LM_OK;
+    };
+    lm_status st;
+    if (!piped) {
+        // 3. Dispatch token rows.
+        if ((st = exchange(0, false, s)) != LM_OK) return st;
+        if ((st = sort(0, s, false)) != LM_OK) return st;
+        prof_mark(ctx, 7, s);
+        slots[n_slots++] = 7;
+        if ((st = gemms(0, true)) != LM_OK) return st;
+        // 5. Outputs back to the tokens' ranks, then the weighted combine.
+        if ((st = exchange(0, true, s)) != LM_OK) return st;
     } else {
-        LM_CUDA(ctx, launch_gemm_gate_up(bn, L.map_w13, ctx->map_xsorted[bi], map_x, args, ctx->sms, s, true));
+        cudaStream_t cs = ctx->ep_stream;
+        // While profiling, timing events mark each step's end (lm_moe_profile_ep_timeline).
+        const bool tl = ctx->profiling;
+        if (tl && ctx->ep_tl_events[0] == nullptr)
+            for (auto& e : ctx->ep_tl_events) LM_CUDA(ctx, cudaEventCreate(&e));
+        auto stamp = [&](int i, cudaStream_t st) -> lm_status {
+            if (tl) LM_CUDA(ctx, cudaEventRecord(ctx->ep_tl_events[i], st));
+            return LM_OK;
+        };
+        if ((st = stamp(LM_EP_TIMELINE_MAX, s)) != LM_OK) return st;  // the origin
+        LM_CUDA(ctx, cudaEventRecord(ctx->ep_ev_ready, s));
+        LM_CUDA(ctx, cudaStreamWaitEvent(cs, ctx->ep_ev_ready, 0));
+        for (int k = 0; k < C; ++k) {
+            if ((st = exchange(k, false, cs)) != LM_OK) return st;
+            LM_CUDA(ctx, cudaEventRecord(ctx->ep_ev_sent[k], cs));
+            if ((st = stamp(k, cs)) != LM_OK) return st;
+        }
+        prof_mark(ctx, 7, s);
+        slots[n_slots++] = 7;
+        if ((st = gemms(C, false)) != LM_OK) return st;  // shared experts
+        if ((st = stamp(C, s)) != LM_OK) return st;
+        for (int k = 0; k < C; ++k) {
+            LM_CUDA(ctx, cudaStreamWaitEvent(s, ctx->ep_ev_sent[k], 0));
+            if ((st = stamp(C + 1 + k, s)) != LM_OK) return st;
+            if ((st = sort(k, s, false)) != LM_OK) return st;
+            if ((st = gemms(k, false)) != LM_OK) return st;
+            LM_CUDA(ctx, cudaEventRecord(ctx->ep_ev_done[k], s));
+            if ((st = stamp(2 * C + 1 + k, s)) != LM_OK) return st;
+            LM_CUDA(ctx, cudaStreamWaitEvent(cs, ctx->ep_ev_done[k], 0));
+            if ((st = exchange(k, true, cs)) != LM_OK) return st;
+            if ((st = stamp(3 * C + 1 + k, cs)) != LM_OK) return st;
+        }
         prof_mark(ctx, 5, s);
         slots[n_slots++] = 5;
-        LM_CUDA(ctx, launch_gemm_down(bn, L.map_w2, ctx->map_h[bi], args, ctx->sms, s, true));
+        LM_CUDA(ctx, cudaEventRecord(ctx->ep_ev_back, cs));
+        LM_CUDA(ctx, cudaStreamWaitEvent(s, ctx->ep_ev_back, 0));
+        LM_CUDA(ctx, launch_ep_combine(y, ctx->y_back, ctx->slot_row, ctx->topk_w, T, K, H, s, false));
+        if ((st = stamp(4 * C + 1, s)) != LM_OK) return st;
+        prof_mark(ctx, 4, s);
+        slots[n_slots++] = 4;
+        if ((st = prof_end(ctx, slots, n_slots)) != LM_OK) return st;
+        if (tl) {
+            for (int i = 0; i <= 4 * C + 1; ++i)
+                LM_CUDA(ctx, cudaEventElapsedTime(&ctx->ep_timeline[i], ctx->ep_tl_events[LM_EP_TIMELINE_MAX],
+                                                  ctx->ep_tl_events[i]));
+            ctx->ep_timeline_chunks = C;
+        }
+        return LM_OK;
     }
-    prof_mark(ctx, 6, s);
-    slots[n_slots++] = 6;
-    // 5. Outputs back to the tokens' ranks, then the weighted combine.
-    LM_NCCL(ctx, nc.GroupStart());
-    for (int d = 0; d < N; ++d) {
-        if (recv_cnt[d] > 0)
-            LM_NCCL(ctx, nc.Send(ctx->y_ret + static_cast<size_t>(recv_off[d]) * H, static_cast<size_t>(recv_cnt[d]) * H,
-                                 ncclBfloat16, d, ctx->comm, s));
-        if (send_cnt[d] > 0)
-            LM_NCCL(ctx, nc.Recv(ctx->y_back + static_cast<size_t>(send_off[d]) * H, static_cast<size_t>(send_cnt[d]) * H,
-                                 ncclBfloat16, d, ctx->comm, s));
-    }
-    LM_NCCL(ctx, nc.GroupEnd());
     LM_CUDA(ctx, launch_ep_combine(y, ctx->y_back, ctx->slot_row, ctx->topk_w, T, K, H, s, false));
     prof_mark(ctx, 4, s);
     slots[n_slots++] = 4;
@@ -1357,8 +1470,12 @@ lm_status lm_moe_sync(lm_moe_ctx* ctx, void* stream) {
         LM_CUDA(ctx, cudaMemset(ctx->grid_bar, 0, 3 * sizeof(unsigned long long)));
         LM_CUDA(ctx, cudaMemset(ctx->split_ticket, 0, kSplitTickets * sizeof(int32_t)));
         ctx->decode_epoch = 0;
+        const char* what = status == kDevBadTile  ? "a tile outside the schedule"
+                           : status == kDevBadRow ? "an output row outside its buffer"
+                                                  : "a bounded wait expired";
         return fail(ctx, LM_ERR_DEVICE_TIMEOUT,
-                    "a kernel's bounded wait expired (code " + std::to_string(status) + "); results are invalid");
+                    std::string("a kernel stopped on ") + what + " (code " + std::to_string(status) +
+                        "); results are invalid");
     }
     return LM_OK;
 }
@@ -1419,26 +1536,53 @@ lm_status lm_moe_profile_trace(lm_moe_ctx* ctx, uint64_t* stamps, int32_t ctas, 
     return LM_OK;
 }
 
+static_assert(4 * kEpMaxChunks + 2 <= LM_EP_TIMELINE_MAX, "timeline layout");
+
+lm_status lm_moe_profile_ep_timeline(lm_moe_ctx* ctx, float* ms, int32_t capacity, int32_t* chunks_out) {
+    if (ctx == nullptr || ms == nullptr || chunks_out == nullptr || capacity < 0) return LM_ERR_INVALID_ARGUMENT;
+    const int C = ctx->ep_timeline_chunks;
+    *chunks_out = C;
+    if (C > 0) std::memcpy(ms, ctx->ep_timeline, std::min(capacity, 4 * C + 2) * sizeof(float));
+    return LM_OK;
+}
+
 lm_status lm_moe_ep_plan(int32_t nranks, int32_t experts, const int32_t* send_expert_counts,
                          const int32_t* recv_expert_counts, lm_ep_plan* plan) {
+    return lm_moe_ep_chunk_plan(nranks, experts, 1, 0, send_expert_counts, recv_expert_counts, plan);
+}
+
+lm_status lm_moe_ep_chunk_plan(int32_t nranks, int32_t experts, int32_t chunks, int32_t chunk,
+                               const int32_t* send_expert_counts, const int32_t* recv_expert_counts,
+                               lm_ep_plan* plan) {
     if (plan == nullptr || send_expert_counts == nullptr || recv_expert_counts == nullptr || nranks < 1 ||
         nranks > LM_EP_MAX_RANKS || experts < 1 || experts % nranks != 0)
         return LM_ERR_INVALID_ARGUMENT;
-    std::memset(plan, 0, sizeof(*plan));
     const int El = experts / nranks;
+    if (chunks < 1 || chunks > El || chunk < 0 || chunk >= chunks) return LM_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < experts; ++i)
+        if (send_expert_counts[i] < 0 || recv_expert_counts[i] < 0) return LM_ERR_INVALID_ARGUMENT;
+    std::memset(plan, 0, sizeof(*plan));
+    const int lo = chunk * El / chunks, hi = (chunk + 1) * El / chunks;
+    // The send buffer is sorted by global expert: rank d's chunk is experts
+    // d * El + [lo, hi).  The receive buffer holds whole chunks one after another.
+    int64_t sent = 0, recv = 0;
+    for (int d = 0; d < nranks; ++d)
+        for (int e = 0; e < lo; ++e) recv += recv_expert_counts[d * El + e];
     for (int d = 0; d < nranks; ++d) {
-        plan->send_offset[d] = plan->n_send;
-        plan->recv_offset[d] = plan->n_recv;
-        for (int e = 0; e < El; ++e) {
-            const int32_t sc = send_expert_counts[d * El + e];
-            const int32_t rc = recv_expert_counts[d * El + e];
-            if (sc < 0 || rc < 0) return LM_ERR_INVALID_ARGUMENT;
-            plan->send_count[d] += sc;
-            plan->recv_count[d] += rc;
+        for (int e = 0; e < lo; ++e) sent += send_expert_counts[d * El + e];
+        plan->send_offset[d] = static_cast<int32_t>(sent);
+        plan->recv_offset[d] = static_cast<int32_t>(recv);
+        for (int e = lo; e < hi; ++e) {
+            plan->send_count[d] += send_expert_counts[d * El + e];
+            plan->recv_count[d] += recv_expert_counts[d * El + e];
         }
+        sent += plan->send_count[d];
+        recv += plan->recv_count[d];
+        for (int e = hi; e < El; ++e) sent += send_expert_counts[d * El + e];
         plan->n_send += plan->send_count[d];
         plan->n_recv += plan->recv_count[d];
     }
+    if (sent > INT32_MAX || recv > INT32_MAX) return LM_ERR_INVALID_ARGUMENT;
     return LM_OK;
 }
 
@@ -1466,14 +1610,33 @@ lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t ra
     std::string err;
     ctx->nccl = nccl_api(err);
     if (ctx->nccl == nullptr) return fail(ctx, LM_ERR_COMM, err);
+    const int El = c.n_routed_experts / nranks;
+    const size_t T = c.max_tokens, K = c.num_experts_per_tok, H = c.hidden_size, I = c.moe_intermediate_size;
+    // Small batches exchange fixed blocks of ep_cap rows per rank pair (no host round
+    // trip): a token sends one rank at most min(k, local experts) rows.
+    const size_t fixed_cap = T * std::min(K, static_cast<size_t>(El));
+    ctx->ep_cap = static_cast<size_t>(nranks) * fixed_cap <= kEpFixedMaxRows ? static_cast<int>(fixed_cap) : 0;
+    // Larger batches plan on the host and move the local experts in chunks, each
+    // chunk's rows on an NCCL stream of its own while earlier chunks compute.
+    if (const char* v = std::getenv("LITEMIND_B200_EP_CHUNKS")) ctx->ep_chunks = std::atoi(v);
+    if (const char* v = std::getenv("LITEMIND_B200_EP_NCCL_CTAS")) ctx->ep_nccl_ctas = std::atoi(v);
+    ctx->ep_chunks = ctx->ep_cap > 0 ? 1 : std::max(1, std::min({ctx->ep_chunks, kEpMaxChunks, El}));
+    ctx->ep_nccl_ctas = std::max(1, std::min(ctx->ep_nccl_ctas, ctx->sms / 2 - 1));
     ncclUniqueId id;
     std::memcpy(&id, nccl_unique_id, sizeof(id));
-    const ncclResult_t r = ctx->nccl->CommInitRank(&ctx->comm, nranks, id, rank);
+    ncclResult_t r;
+    if (ctx->ep_chunks > 1 && ctx->nccl->CommInitRankConfig != nullptr) {
+        // NCCL's kernels run beside the GEMMs: cap their CTAs to the SMs left free.
+        ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+        config.maxCTAs = ctx->ep_nccl_ctas;
+        r = ctx->nccl->CommInitRankConfig(&ctx->comm, nranks, id, rank, &config);
+    } else {
+        r = ctx->nccl->CommInitRank(&ctx->comm, nranks, id, rank);
+    }
     if (r != ncclSuccess) {
         ctx->comm = nullptr;
         return fail(ctx, LM_ERR_COMM, std::string("ncclCommInitRank: ") + ctx->nccl->GetErrorString(r));
     }
-    const int El = c.n_routed_experts / nranks;
     ctx->rank = rank;
     ctx->nranks = nranks;
     ctx->first_expert = rank * El;
@@ -1481,7 +1644,6 @@ lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t ra
     ctx->n_seg = El + c.n_shared_experts;
     // Receive capacity for the worst case (every rank's every slot on this rank),
     // so no rank can overflow mid-exchange and leave its peers waiting.
-    const size_t T = c.max_tokens, K = c.num_experts_per_tok, H = c.hidden_size, I = c.moe_intermediate_size;
     const size_t cap = static_cast<size_t>(nranks) * T * K;
     ctx->routed_cap = static_cast<int>(cap);
     const size_t h_rows = cap + c.n_shared_experts * T;
@@ -1492,21 +1654,65 @@ lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t ra
             ctx->allocations.erase(it);
             break;
         }
-    // Small batches exchange fixed blocks of ep_cap rows per rank pair (no host round
-    // trip): a token sends one rank at most min(k, local experts) rows.
-    const size_t fixed_cap = T * std::min(K, static_cast<size_t>(El));
-    ctx->ep_cap = static_cast<size_t>(nranks) * fixed_cap <= kEpFixedMaxRows ? static_cast<int>(fixed_cap) : 0;
     const size_t back_rows = std::max(T * K, static_cast<size_t>(nranks) * ctx->ep_cap);
     if ((st = alloc(ctx, &ctx->h, h_rows * I)) || (st = alloc(ctx, &ctx->x_recv, cap * H)) ||
         (st = alloc(ctx, &ctx->y_ret, cap * H)) || (st = alloc(ctx, &ctx->y_back, back_rows * H)) ||
         (ctx->ep_cap > 0 && (st = alloc(ctx, &ctx->x_send, static_cast<size_t>(nranks) * ctx->ep_cap * H))) ||
-        (st = alloc(ctx, &ctx->recv_counts, static_cast<size_t>(nranks) * El)) || (st = alloc(ctx, &ctx->sched_ep, 1)) ||
+        (st = alloc(ctx, &ctx->recv_counts, static_cast<size_t>(nranks) * El)) ||
+        (st = alloc(ctx, &ctx->sched_ep, kEpMaxChunks + 1)) ||
         (st = alloc(ctx, &ctx->x_sorted, cap * H)) || (st = alloc(ctx, &ctx->ep_row_src, cap)))
         return st;
-    LM_CUDA(ctx, cudaMallocHost(&ctx->host_sched, sizeof(Schedule)));
+    LM_CUDA(ctx, cudaMallocHost(&ctx->host_sched, (kEpMaxChunks + 1) * sizeof(Schedule)));
     LM_CUDA(ctx, cudaMallocHost(&ctx->host_totals, c.n_routed_experts * sizeof(int32_t)));
     LM_CUDA(ctx, cudaMallocHost(&ctx->host_recv, static_cast<size_t>(nranks) * El * sizeof(int32_t)));
-    std::memset(ctx->host_sched, 0, sizeof(Schedule));
+    std::memset(ctx->host_sched, 0, (kEpMaxChunks + 1) * sizeof(Schedule));
+    if (ctx->ep_chunks > 1) {
+        int lo = 0, hi = 0;
+        LM_CUDA(ctx, cudaDeviceGetStreamPriorityRange(&lo, &hi));
+        LM_CUDA(ctx, cudaStreamCreateWithPriority(&ctx->ep_stream, cudaStreamNonBlocking, hi));
+        LM_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ep_ev_ready, cudaEventDisableTiming));
+        LM_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ep_ev_back, cudaEventDisableTiming));
+        for (int i = 0; i < ctx->ep_chunks; ++i) {
+            LM_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ep_ev_sent[i], cudaEventDisableTiming));
+            LM_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ep_ev_done[i], cudaEventDisableTiming));
+        }
+    }
+    // Every rank must take the same steps in every exchange, and a peer's rows must
+    // fit this rank's buffers: compare the settings that decide both, once.
+    {
+        constexpr int kFields = 8;
+        const int32_t mine[kFields] = {c.hidden_size, c.moe_intermediate_size, c.n_routed_experts,
+                                       c.n_shared_experts, c.num_experts_per_tok, c.max_tokens,
+                                       ctx->ep_cap, ctx->ep_chunks};
+        int32_t* dev = nullptr;
+        if ((st = alloc(ctx, &dev, static_cast<size_t>(kFields) * (nranks + 1))) != LM_OK) return st;
+        std::vector<int32_t> all(static_cast<size_t>(kFields) * nranks);
+        cudaStream_t xs = nullptr;
+        LM_CUDA(ctx, cudaStreamCreateWithFlags(&xs, cudaStreamNonBlocking));
+        cudaError_t ce = cudaMemcpyAsync(dev, mine, sizeof(mine), cudaMemcpyHostToDevice, xs);
+        ncclResult_t nr = ncclSuccess;
+        if (ce == cudaSuccess) {
+            nr = ctx->nccl->GroupStart();
+            for (int d = 0; d < nranks && nr == ncclSuccess; ++d) {
+                nr = ctx->nccl->Send(dev, kFields, ncclInt32, d, ctx->comm, xs);
+                if (nr == ncclSuccess) nr = ctx->nccl->Recv(dev + kFields * (d + 1), kFields, ncclInt32, d, ctx->comm, xs);
+            }
+            const ncclResult_t ne = ctx->nccl->GroupEnd();
+            if (nr == ncclSuccess) nr = ne;
+        }
+        if (ce == cudaSuccess && nr == ncclSuccess)
+            ce = cudaMemcpyAsync(all.data(), dev + kFields, all.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, xs);
+        const cudaError_t cs = cudaStreamSynchronize(xs);
+        cudaStreamDestroy(xs);
+        if (nr != ncclSuccess) return fail(ctx, LM_ERR_COMM, std::string("settings exchange: ") + ctx->nccl->GetErrorString(nr));
+        if (ce != cudaSuccess) return cuda_fail(ctx, ce, "settings exchange");
+        if (cs != cudaSuccess) return cuda_fail(ctx, cs, "settings exchange");
+        for (int d = 0; d < nranks; ++d)
+            if (std::memcmp(all.data() + static_cast<size_t>(kFields) * d, mine, sizeof(mine)) != 0)
+                return fail(ctx, LM_ERR_INVALID_ARGUMENT,
+                            "expert-parallel settings differ between ranks (shape, max_tokens or "
+                            "LITEMIND_B200_EP_CHUNKS): rank " + std::to_string(d));
+    }
     for (int i = 0; i < 5; ++i) {
         if (!encode_tensor_map_bf16(&ctx->map_xrecv[i], ctx->x_recv, cap, H, kBnChoices[i], 64, err) ||
             !encode_tensor_map_bf16(&ctx->map_xsorted[i], ctx->x_sorted, cap, H, kBnChoices[i], 64, err) ||

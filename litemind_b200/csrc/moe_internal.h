@@ -71,12 +71,15 @@ cudaError_t launch_place(const int32_t* topk_idx, const float* topk_w, const int
 cudaError_t launch_ep_combine(float* y, const uint16_t* back, const int32_t* slot_row, const float* topk_w, int tokens,
                               int top_k, int hidden, cudaStream_t stream, bool pdl);
 cudaError_t launch_dense_schedule(Schedule* sched, int tokens, int bn, int mb1, int mb2, cudaStream_t stream);
-// Expert parallelism: received rows (source-major) -> expert-major, with row_src[row]
-// = the row's source-major index.  max_group_rows: the largest (source, expert) group.
-// src_stride > 0: source r's rows start at r * src_stride (fixed-capacity exchange).
+// Expert parallelism: received rows -> expert-major, with row_src[row] = the row's
+// index in the receive buffer.  The receive buffer holds local-expert chunks one after
+// another, each source-major; a launch sorts chunk [e_lo, e_hi) (the whole [0, El) when
+// the exchange is not chunked).  max_group_rows: the largest (source, expert) group in
+// the chunk.  src_stride > 0: source r's rows start at r * src_stride (fixed-capacity
+// exchange, whole range only).
 cudaError_t launch_ep_sort_rows(const uint16_t* x_recv, uint16_t* x_sorted, int32_t* row_src,
                                const int32_t* recv_counts, int nranks, int local_experts, int max_group_rows,
-                               int hidden, int src_stride, cudaStream_t stream, bool pdl);
+                               int hidden, int src_stride, int e_lo, int e_hi, cudaStream_t stream, bool pdl);
 // Fixed-capacity expert parallelism: pack this rank's rows into per-destination
 // blocks of `cap` rows (and point slot_row at them), and build the receiver's
 // schedule on the device from the received counts.
@@ -109,6 +112,8 @@ struct GemmArgs {
     int32_t inter;
     uint16_t* y_rows;          // when set, routed rows' down outputs are stored here by row, unweighted, bf16
     const int32_t* y_rows_map; // with y_rows: routed row r is stored at row y_rows_map[r] (null: at r)
+    int32_t y_rows_cap;        // with y_rows: rows of y_rows and entries of y_rows_map; a row outside is
+                               // skipped and reported (kDevBadRow)
     float* logits;             // router kind: [T, experts] f32 output
     const float* bias;         // router kind: per-expert logit bias or null
     int32_t experts;           // router kind: experts (<= 128)
@@ -169,6 +174,9 @@ cudaError_t launch_moe_decode(int bn, const CUtensorMap& w13, const CUtensorMap&
 // Expert parallelism exchanges fixed blocks (no host round trip) while
 // nranks x rows-per-block stays within this many rows.
 constexpr size_t kEpFixedMaxRows = 8192;
+// The host-planned exchange moves the local experts in at most this many chunks, so
+// that one chunk's rows travel while another chunk's GEMMs run.
+constexpr int kEpMaxChunks = 8;
 
 // Split-K workspace for gate/up partial tiles (bytes) and its ticket count.
 constexpr size_t kSplitWsBytes = size_t(32) << 20;

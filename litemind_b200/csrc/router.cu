@@ -453,27 +453,35 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(float* __restrict__ y, 
 // contiguous, so each expert's weights stream once instead of once per source.
 // Block (b, y) with b = (source r, local expert e) copies rows [64 y, 64 y + 64) of
 // its group to their expert-major place and records where each came from, so the
-// down projection can store its output rows back in source-major order.
+// down projection can store its output rows back in receive order.
+//
+// A pipelined exchange moves the local experts in chunks [e_lo, e_hi): the receive
+// buffer is chunk-major (all rows of earlier chunks first), source-major within a
+// chunk.  One launch sorts one chunk; the whole range [0, El) is the unchunked
+// source-major layout.  The expert-major destination does not depend on chunking.
 constexpr int kSortRows = 64;
 // src_stride > 0: each source's rows sit in a fixed block of src_stride rows
-// (the fixed-capacity exchange) instead of back to back.
+// (the fixed-capacity exchange, one chunk) instead of back to back.
 __global__ void __launch_bounds__(256) ep_sort_rows_kernel(const uint16_t* __restrict__ x_recv,
                                                            uint16_t* __restrict__ x_sorted,
                                                            int32_t* __restrict__ row_src,
                                                            const int32_t* __restrict__ recv_counts, int N, int El,
-                                                           int H, int src_stride) {
+                                                           int H, int src_stride, int e_lo, int e_hi) {
     pdl_wait();
     pdl_launch_dependents();
-    const int r = blockIdx.x / El;
-    const int e = blockIdx.x - r * El;
+    const int ne = e_hi - e_lo;
+    const int r = blockIdx.x / ne;
+    const int e = e_lo + (blockIdx.x - r * ne);
     __shared__ int s_src, s_dst, s_cnt;
     if (threadIdx.x == 0) {
         int src = src_stride > 0 ? r * src_stride : 0, dst = 0;
         for (int rr = 0; rr < N; ++rr) {
             for (int ee = 0; ee < El; ++ee) {
                 const int c = recv_counts[rr * El + ee];
-                if (src_stride > 0 ? (rr == r && ee < e) : (rr < r || (rr == r && ee < e)))
-                    src += c;  // source-major position
+                const bool before = src_stride > 0
+                                        ? (rr == r && ee < e)
+                                        : (ee < e_lo || (ee < e_hi && (rr < r || (rr == r && ee < e))));
+                if (before) src += c;  // chunk-major, then source-major position
                 if (ee < e || (ee == e && rr < r)) dst += c;  // expert-major position
             }
         }
@@ -745,11 +753,13 @@ cudaError_t launch_dense_schedule(Schedule* sched, int tokens, int bn, int mb1, 
 
 cudaError_t launch_ep_sort_rows(const uint16_t* x_recv, uint16_t* x_sorted, int32_t* row_src,
                                const int32_t* recv_counts, int nranks, int local_experts, int max_group_rows,
-                               int hidden, int src_stride, cudaStream_t stream, bool pdl) {
-    if (max_group_rows <= 0) return cudaSuccess;
-    const dim3 grid(nranks * local_experts, (max_group_rows + kSortRows - 1) / kSortRows);
+                               int hidden, int src_stride, int e_lo, int e_hi, cudaStream_t stream, bool pdl) {
+    if (max_group_rows <= 0 || e_hi <= e_lo) return cudaSuccess;
+    if (e_lo < 0 || e_hi > local_experts || (src_stride > 0 && (e_lo != 0 || e_hi != local_experts)))
+        return cudaErrorInvalidValue;
+    const dim3 grid(nranks * (e_hi - e_lo), (max_group_rows + kSortRows - 1) / kSortRows);
     return launch_k(ep_sort_rows_kernel, grid, dim3(256), stream, pdl, x_recv, x_sorted, row_src, recv_counts,
-                    nranks, local_experts, hidden, src_stride);
+                    nranks, local_experts, hidden, src_stride, e_lo, e_hi);
 }
 
 // Fixed-capacity expert parallelism (small batches, no host round trip): every

@@ -70,12 +70,18 @@ class ExpertSelection:
     weight: float
 
 
-def ep_plan(nranks: int, send_expert_counts, recv_expert_counts) -> dict:
-    """lm_moe_ep_plan: send/recv row counts and offsets of one expert-parallel forward."""
+def ep_plan(nranks: int, send_expert_counts, recv_expert_counts, chunks: int = 1, chunk: int = 0) -> dict:
+    """lm_moe_ep_plan (chunks = 1) or lm_moe_ep_chunk_plan: send/recv row counts and
+    offsets of one expert-parallel forward, or of one chunk of its local experts."""
     s = np.ascontiguousarray(send_expert_counts, np.int32)
     r = np.ascontiguousarray(recv_expert_counts, np.int32)
     plan = _lib.LmEpPlan()
-    check(load().lm_moe_ep_plan(nranks, s.size, C.c_void_p(s.ctypes.data), C.c_void_p(r.ctypes.data), C.byref(plan)))
+    if chunks == 1 and chunk == 0:
+        check(load().lm_moe_ep_plan(nranks, s.size, C.c_void_p(s.ctypes.data), C.c_void_p(r.ctypes.data),
+                                    C.byref(plan)))
+    else:
+        check(load().lm_moe_ep_chunk_plan(nranks, s.size, chunks, chunk, C.c_void_p(s.ctypes.data),
+                                          C.c_void_p(r.ctypes.data), C.byref(plan)))
     return {"send_count": list(plan.send_count[:nranks]), "send_offset": list(plan.send_offset[:nranks]),
             "recv_count": list(plan.recv_count[:nranks]), "recv_offset": list(plan.recv_offset[:nranks]),
             "n_send": plan.n_send, "n_recv": plan.n_recv}
@@ -261,6 +267,19 @@ class MoeLayer:
         n = C.c_int32(0)
         self._check(self.lib.lm_moe_profile_trace(self.ctx, _ptr(out), cap, C.byref(n)))
         return out[: min(n.value, cap)]
+
+    def profile_ep_timeline(self) -> dict | None:
+        """Step times (ms) of the last profiled chunked expert-parallel forward, or None."""
+        cap = 40
+        out = np.zeros(cap, np.float32)
+        n = C.c_int32(0)
+        self._check(self.lib.lm_moe_profile_ep_timeline(self.ctx, _ptr(out), cap, C.byref(n)))
+        k = n.value
+        if k == 0:
+            return None
+        v = [round(float(t), 4) for t in out[:4 * k + 2]]
+        return {"dispatched": v[:k], "shared_done": v[k], "gemm_start": v[k + 1:2 * k + 1],
+                "gemm_done": v[2 * k + 1:3 * k + 1], "returned": v[3 * k + 1:4 * k + 1], "combined": v[4 * k + 1]}
 
     def expert_counts(self) -> np.ndarray:
         out = np.zeros(self.config.n_routed_experts, np.int32)

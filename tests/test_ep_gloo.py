@@ -7,7 +7,9 @@ expert (token order within an expert, as the place kernel does), exchanges the
 per-expert counts, asks lm_moe_ep_plan for the send/recv counts and offsets, sends
 the rows with all_to_all_single, computes its local experts, returns the outputs in
 receive order, and combines them by slot with the routing weights, plus the shared
-experts.  No GPU is used.
+experts.  With chunks > 1 the rows move in chunks of local experts planned by
+lm_moe_ep_chunk_plan, as lm_moe_forward's pipelined exchange moves them.  No GPU is
+used.
 """
 import os
 import socket
@@ -37,7 +39,7 @@ def _ffn(gate, up, down, x):
     return h @ down.T
 
 
-def _worker(rank, world, port, token_counts):
+def _worker(rank, world, port, token_counts, chunks):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -71,36 +73,95 @@ def _worker(rank, world, port, token_counts):
         plan = ep_plan(world, counts, recv_counts.numpy())
         assert plan["n_send"] == T * K
         assert plan["send_offset"][0] == 0 and plan["recv_offset"][0] == 0
-        # Rows and their experts to the experts' ranks.
-        recv_x = torch.zeros((plan["n_recv"], H), dtype=torch.float64)
-        dist.all_to_all_single(recv_x, torch.from_numpy(send_rows), plan["recv_count"], plan["send_count"])
-        recv_e = torch.zeros(plan["n_recv"], dtype=torch.int64)
-        dist.all_to_all_single(recv_e, torch.from_numpy(send_expert), plan["recv_count"], plan["send_count"])
-        # Received rows are grouped by source, each source's rows by local expert.
+        # The local experts move in `chunks` exchanges (one when chunks = 1); the
+        # receive buffer holds the chunks one after another, each by source rank.
+        plans = [ep_plan(world, counts, recv_counts.numpy(), chunks, k) for k in range(chunks)]
+        assert sum(p["n_send"] for p in plans) == plan["n_send"]
+        assert sum(p["n_recv"] for p in plans) == plan["n_recv"]
         rc = recv_counts.numpy().reshape(world, El)
-        for src in range(world):
-            seg = recv_e.numpy()[plan["recv_offset"][src]:plan["recv_offset"][src] + plan["recv_count"][src]]
-            assert np.array_equal(seg, np.repeat(rank * El + np.arange(El), rc[src]))
+        recv_x = np.zeros((plan["n_recv"], H))
+        recv_e = np.zeros(plan["n_recv"], np.int64)
+        for k, pk in enumerate(plans):
+            base = pk["recv_offset"][0]
+            assert base == sum(p["n_recv"] for p in plans[:k])
+            assert pk["recv_offset"] == [base + sum(pk["recv_count"][:d]) for d in range(world)]
+            take = np.concatenate([np.arange(pk["send_offset"][d], pk["send_offset"][d] + pk["send_count"][d])
+                                   for d in range(world)]).astype(np.int64)
+            got_x = torch.zeros((pk["n_recv"], H), dtype=torch.float64)
+            dist.all_to_all_single(got_x, torch.from_numpy(send_rows[take].reshape(-1, H)), pk["recv_count"],
+                                   pk["send_count"])
+            got_e = torch.zeros(pk["n_recv"], dtype=torch.int64)
+            dist.all_to_all_single(got_e, torch.from_numpy(send_expert[take]), pk["recv_count"], pk["send_count"])
+            recv_x[base:base + pk["n_recv"]] = got_x.numpy()
+            recv_e[base:base + pk["n_recv"]] = got_e.numpy()
+            # Chunk k carries this rank's local experts [lo, hi), each source's rows by expert.
+            lo, hi = k * El // chunks, (k + 1) * El // chunks
+            for src in range(world):
+                seg = recv_e[pk["recv_offset"][src]:pk["recv_offset"][src] + pk["recv_count"][src]]
+                assert np.array_equal(seg, np.repeat(rank * El + np.arange(lo, hi), rc[src, lo:hi]))
         out = np.zeros((plan["n_recv"], H))
         for r in range(plan["n_recv"]):
             e = int(recv_e[r])
             assert rank * El <= e < (rank + 1) * El
-            out[r] = _ffn(Wf["gate"][e], Wf["up"][e], Wf["down"][e], recv_x[r].numpy()[None])[0]
-        back = torch.zeros((T * K, H), dtype=torch.float64)
-        dist.all_to_all_single(back, torch.from_numpy(out), plan["send_count"], plan["recv_count"])
+            out[r] = _ffn(Wf["gate"][e], Wf["up"][e], Wf["down"][e], recv_x[r][None])[0]
+        # Outputs go back chunk by chunk with the offsets reversed.
+        back = np.zeros((T * K, H))
+        for pk in plans:
+            base = pk["recv_offset"][0]
+            got = torch.zeros((pk["n_send"], H), dtype=torch.float64)
+            dist.all_to_all_single(got, torch.from_numpy(out[base:base + pk["n_recv"]].reshape(-1, H)),
+                                   pk["send_count"], pk["recv_count"])
+            pos = 0
+            for d in range(world):
+                n = pk["send_count"][d]
+                back[pk["send_offset"][d]:pk["send_offset"][d] + n] = got.numpy()[pos:pos + n]
+                pos += n
         y = _ffn(Wf["shared_gate"], Wf["shared_up"], Wf["shared_down"], x.astype(np.float64))
         for t in range(T):
             for s in range(K):
-                y[t] += float(w[t, s]) * back[slot_row[t * K + s]].numpy()
+                y[t] += float(w[t, s]) * back[slot_row[t * K + s]]
         if T > 0:
             np.testing.assert_allclose(y, ref_y, rtol=1e-4, atol=1e-5)
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("token_counts", [(13, 7), (0, 9), (16, 16)])
-def test_ep_protocol_two_gloo_ranks(token_counts):
-    mp.spawn(_worker, args=(2, _free_port(), token_counts), nprocs=2, join=True)
+# chunks > 1: the chunked exchange of lm_moe_ep_chunk_plan (4 local experts per rank
+# here; 3 chunks split them 1 + 1 + 2).
+@pytest.mark.parametrize("token_counts,chunks", [((13, 7), 1), ((0, 9), 1), ((16, 16), 1), ((13, 7), 2),
+                                                 ((16, 16), 3), ((0, 9), 4)])
+def test_ep_protocol_two_gloo_ranks(token_counts, chunks):
+    mp.spawn(_worker, args=(2, _free_port(), token_counts, chunks), nprocs=2, join=True)
+
+
+def test_ep_chunk_plan_layout():
+    """Chunk plans partition the whole plan: per destination, the chunks' send ranges
+    tile the whole send range in order; the receive buffer holds the chunks back to back."""
+    from litemind_b200.moe import ep_plan
+
+    rng = np.random.default_rng(0)
+    world, E = 4, 16
+    El = E // world
+    send = rng.integers(0, 9, E).astype(np.int32)
+    recv = rng.integers(0, 9, E).astype(np.int32)
+    whole = ep_plan(world, send, recv)
+    for chunks in (1, 2, 3, 4):
+        plans = [ep_plan(world, send, recv, chunks, k) for k in range(chunks)]
+        for d in range(world):
+            pos = whole["send_offset"][d]
+            for k, pk in enumerate(plans):
+                assert pk["send_offset"][d] == pos
+                lo, hi = k * El // chunks, (k + 1) * El // chunks
+                assert pk["send_count"][d] == send[d * El + lo:d * El + hi].sum()
+                assert pk["recv_count"][d] == recv[d * El + lo:d * El + hi].sum()
+                pos += pk["send_count"][d]
+            assert pos == whole["send_offset"][d] + whole["send_count"][d]
+        base = 0
+        for pk in plans:
+            assert pk["recv_offset"][0] == base
+            base += pk["n_recv"]
+        assert base == whole["n_recv"]
+    assert ep_plan(world, send, recv, 1, 0) == whole
 
 
 def test_ep_plan_rejects_bad_input():
@@ -111,3 +172,6 @@ def test_ep_plan_rejects_bad_input():
         ep_plan(3, np.zeros(8, np.int32), np.zeros(8, np.int32))  # 3 ranks do not divide 8 experts
     with pytest.raises(LiteMindError):
         ep_plan(2, np.array([1, -1, 0, 0], np.int32), np.zeros(4, np.int32))
+    for chunks, chunk in ((0, 0), (3, 0), (2, 2), (2, -1)):  # 2 local experts: 1 or 2 chunks
+        with pytest.raises(LiteMindError):
+            ep_plan(2, np.zeros(4, np.int32), np.zeros(4, np.int32), chunks, chunk)

@@ -27,8 +27,8 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, shape_name, token_counts):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+def _worker(rank, world, port, shape_name, token_counts, chunks):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LITEMIND_B200_EP_CHUNKS=str(chunks))
     from datetime import timedelta
 
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
@@ -66,12 +66,15 @@ def _worker(rank, world, port, shape_name, token_counts):
 
 
 # Up to max_tokens x min(k, local experts) rows per rank pair, ranks exchange fixed
-# blocks with the plan made on the device; (5000, 4100) exceeds that and takes the
-# host-planned exchange.
-@pytest.mark.parametrize("shape_name,token_counts", [("small", (37, 11)), ("small", (0, 20)),
-                                                     ("small", (300, 300)), ("v2lite", (32, 64)),
-                                                     ("small", (5000, 4100))])
-def test_expert_parallel_two_gpus(shape_name, token_counts):
+# blocks with the plan made on the device; (5000, 4100) and V2-Lite (700, 450) exceed
+# that and take the host-planned exchange: in one piece (chunks 1) or pipelined in
+# chunks of local experts on a second stream (4 chunks of 1 expert, 3 uneven chunks,
+# V2-Lite's 4 chunks of 8 experts).
+@pytest.mark.parametrize("shape_name,token_counts,chunks", [("small", (37, 11), 4), ("small", (0, 20), 4),
+                                                            ("small", (300, 300), 4), ("v2lite", (32, 64), 4),
+                                                            ("small", (5000, 4100), 1), ("small", (5000, 4100), 4),
+                                                            ("small", (3000, 0), 3), ("v2lite", (700, 450), 4)])
+def test_expert_parallel_two_gpus(shape_name, token_counts, chunks):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    mp.spawn(_worker, args=(2, _free_port(), shape_name, token_counts), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), shape_name, token_counts, chunks), nprocs=2, join=True)
