@@ -227,9 +227,10 @@ lm_status lm_moe_profile_enable(lm_moe_ctx* ctx, int32_t enable);
 lm_status lm_moe_profile_read(lm_moe_ctx* ctx, double* total_ms, int64_t* launches, int32_t reset);
 /* While profiling, the fused decode kernel (T <= 32 on one GPU) stamps each of its
  * CTAs' phases with the device's global timer (ns): LM_DECODE_TRACE_SLOTS values
- * per CTA (0 start, 1 logits written, 2 every CTA's logits seen, 3 schedule built,
- * 4 gate/up epilogues done, 5 producer saw every h row, 6 producer done, 7 down
- * epilogues done, 8 MMA done; 0 = not reached).  Copies the last
+ * per CTA (0 start, 1 logits written, 2 every CTA's logits seen, 10 logits in
+ * shared memory, 11 every token routed, 12 active experts compacted, 3 schedule
+ * built, 4 gate/up epilogues done, 5 producer saw every h row, 6 producer done,
+ * 7 down epilogues done, 8 MMA done; 9 and 13-15 unused; 0 = not reached).  Copies the last
  * launch's stamps for up to `ctas` CTAs and sets *ctas_out to the number of CTAs it
  * ran with (0 if none was traced). */
 #define LM_DECODE_TRACE_SLOTS 16
