@@ -27,6 +27,10 @@ write back inside the step) and streams its experts from HBM.
 --workload prefill: T=16384 tokens (seed 2) with a per-expert
 logit bias that skews expert load to Zipf(1.2); the roofline is tensor-bound
 (FLOPs against the measured dense bf16 peak).  --workload stack: config 4.
+--workload ffn: the dense layer-0 feed-forward (intermediate 10944) through
+lm_ffn_forward, with the reference's feed_forward timed on the host beside it.
+--workload load: lm_moe_load_safetensors of one layer (GB/s against a plain pinned
+host -> device copy).
 
 With N > 1 (torchrun, one rank per GPU) each rank runs the same per-rank workload
 (T tokens of its own) under expert parallelism: rank r holds routed experts
@@ -83,10 +87,11 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per rank per step (default 32 for decode, 16384 for prefill, 4096 for stack)")
-    ap.add_argument("--workload", choices=["decode", "prefill", "stack"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "stack", "ffn", "load"], default="decode",
                     help="decode: one MoE layer (BASELINE config 1, headline); prefill: one layer at 16384 "
                          "tokens with Zipf expert load (config 2, tensor-bound); stack: 26 x (RMSNorm, MoE, "
-                         "residual) (config 4)")
+                         "residual) (config 4); ffn: the dense layer-0 feed-forward; load: the SafeTensors "
+                         "-> HBM loader")
     ap.add_argument("--layers", type=int, default=26, help="blocks in the stack workload")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-sweep", action="store_true")
@@ -221,6 +226,27 @@ def run_reference_arm(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     from litemind_b200 import synthetic as syn
+
+    if args.workload == "load":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference has no device loader (its WeightStore "
+                                                              "maps shards and pages weights in on first touch)"}))
+        return
+    if args.workload == "ffn":
+        g, u, d = dense_weights()
+        xf = syn.bf16_to_f32(syn.tokens(syn.V2_LITE, args.tokens, seed=SEED_DENSE)).reshape(args.tokens, -1)
+        per_step = max(args.cpu_seconds / max(args.steps, 1), 0.5)
+        rates = [cpu_dense_rate(g, u, d, xf, per_step) for _ in range(args.steps)]
+        value = statistics.median(r["value"] for r in rates)
+        print(json.dumps({
+            "impl": "reference", "metric": "dense feed-forward tokens/s (V2-Lite layer 0 shape)", "value": value,
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * args.tokens / value, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "dense-ffn: DeepSeek-V2-Lite layer 0 feed-forward (hidden 2048, inter 10944)",
+                       "tokens_per_rank": args.tokens},
+            "cpu_baseline": {**rates[-1], "value": value},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
 
     W = syn.layer_weights(syn.V2_LITE, seed=SEED_WEIGHTS)
     prefill = args.workload == "prefill"
@@ -402,10 +428,234 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> int:
     return 0
 
 
+DENSE_INTER = 10944  # DeepSeek-V2-Lite's dense layer 0 (include/Config.hpp:59)
+SEED_DENSE = 5
+
+
+def dense_weights(seed: int = SEED_DENSE):
+    from litemind_b200 import synthetic as syn
+
+    H, I = syn.V2_LITE.hidden, DENSE_INTER
+    return (syn.normal_bf16(seed, (0,), (I, H), 0.02), syn.normal_bf16(seed, (1,), (I, H), 0.02),
+            syn.normal_bf16(seed, (2,), (H, I), 0.02))
+
+
+def cpu_dense_rate(g, u, d, x_f32, seconds: float) -> dict:
+    """tokens/s of the reference's dense feed-forward (Impl::feed_forward,
+    src/DeepSeekRunner.cpp:228-240: gemm::matvec_bf16 gate and up, silu_multiply,
+    matvec_bf16_accumulate down) on all host threads, one token at a time as the
+    reference runs it."""
+    import numpy as np
+
+    from oracle.oracle import Reference
+
+    ref = Reference()
+    ref.threads = ref.hardware_threads()
+    out = np.zeros(g.shape[1], np.float32)
+
+    def one(x):
+        h = ref.silu_multiply(ref.matvec_bf16(g, x), ref.matvec_bf16(u, x))
+        ref.matvec_bf16_accumulate(d, h, out, 1.0)
+
+    one(x_f32[0])  # page the weights in, start the pool
+    n, t0 = 0, time.perf_counter()
+    while n < 1 or time.perf_counter() - t0 < seconds:
+        one(x_f32[n % x_f32.shape[0]])
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tokens/s", "cores": ref.threads, "kind": "reference",
+            "sample": f"{n} tokens one at a time, {dt:.1f} s, reference gemm:: built from its sources"}
+
+
+def run_ffn(args, rank: int, world: int, local_rank: int) -> int:
+    """The dense feed-forward (DeepSeek-V2-Lite layer 0, intermediate 10944) through
+    lm_ffn_forward: gate/up with the SiLU epilogue, then down, on the grouped tcgen05
+    GEMMs with one all-token segment.  With N > 1 every GPU runs its own replica
+    (the dense layer is not sharded)."""
+    import numpy as np
+
+    import torch
+
+    from litemind_b200 import synthetic as syn
+    from litemind_b200.moe import MoeConfig, MoeLayer, bf16_tensor
+
+    torch.cuda.set_device(local_rank)
+    H, I, T = syn.V2_LITE.hidden, DENSE_INTER, args.tokens
+    g, u, d = dense_weights()
+    layer = MoeLayer(MoeConfig(max_tokens=T), device=local_rank)
+    layer.ffn_upload(0, g, u, d)
+    x_bits = syn.tokens(syn.V2_LITE, T, seed=SEED_DENSE, stream=rank)
+    x = bf16_tensor(x_bits)
+    y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    flush = L2Flush(torch)
+    for _ in range(max(args.warmup, 3)):
+        layer.ffn_forward(0, x, y=y)
+    layer.sync()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    t_load = time.perf_counter()
+    while time.perf_counter() - t_load < args.clock_window:
+        for _ in range(20):
+            flush()
+            layer.ffn_forward(0, x, y=y)
+        torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    total = 0.0
+    for _ in range(args.steps):
+        flush()
+        start.record()
+        layer.ffn_forward(0, x, y=y)
+        end.record()
+        end.synchronize()
+        total += start.elapsed_time(end)
+    clock_info = clocks.stop()
+    ms = total / args.steps
+    # Per-kernel device times of the same steps.
+    layer.profile(True)
+    layer.profile_read(reset=True)
+    for _ in range(args.steps):
+        flush()
+        layer.ffn_forward(0, x, y=y)
+    prof = layer.profile_read(reset=True)
+    layer.profile(False)
+    # End to end: pinned host x in, y out, copies inside the timing.
+    x_host = torch.from_numpy(x_bits.view(np.int16)).pin_memory()
+    y_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    x_dev = torch.empty((T, H), dtype=torch.int16, device="cuda")
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        layer.ffn_forward(0, x_dev.view(torch.bfloat16), y=y)
+        y_host.copy_(y, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_ms = 1e3 * (time.perf_counter() - t0) / args.steps
+    peaks = measured_peaks()
+    weight_bytes = 3 * I * H * 2
+    bytes_step = weight_bytes + T * H * (2 + 4)
+    flops = 6 * I * H * T
+    hbm_bound = flops / bytes_step < peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    gu_ms, gu_n = prof.get("gemm_gate_up", (0.0, 0))
+    gu_avg = gu_ms / max(gu_n, 1)
+    gu_bytes, gu_flops = 2 * I * H * 2 + T * H * 2 + T * I * 2, 4 * I * H * T
+    if hbm_bound:
+        k_achieved = gu_bytes / (gu_avg / 1e3) / 1e9 if gu_avg else 0.0
+        roofline = {"bound": "hbm", "achieved": k_achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": k_achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} (hbm_gbs)",
+                    "layer_achieved": bytes_step / (ms / 1e3) / 1e9,
+                    "layer_frac": bytes_step / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+    else:
+        k_achieved = gu_flops / (gu_avg / 1e3) / 1e12 if gu_avg else 0.0
+        roofline = {"bound": "tensor", "achieved": k_achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                    "frac": k_achieved / peaks["bf16_tflops"], "peak_source": f"{peaks['source']} (bf16_tflops)",
+                    "layer_achieved": flops / (ms / 1e3) / 1e12,
+                    "layer_frac": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"]}
+    total_prof = sum(v[0] for v in prof.values())
+    roofline.update({"kernel": "gemm_gate_up (tcgen05 grouped GEMM, one all-token segment, SiLU epilogue)",
+                     "bytes_per_launch": gu_bytes, "flops_per_launch": gu_flops, "mean_launch_ms": gu_avg,
+                     "traffic": None,
+                     "share_of_step": {k: round(v[0] / total_prof, 4) for k, v in prof.items()} if total_prof else {}})
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        xf = syn.bf16_to_f32(x_bits).reshape(T, H)
+        cpu = cpu_dense_rate(g, u, d, xf, args.cpu_seconds)
+    line = {
+        "metric": "dense feed-forward tokens/s (V2-Lite layer 0 shape)", "value": T * world / (ms / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "dense-ffn: DeepSeek-V2-Lite layer 0 feed-forward (hidden 2048, inter 10944)",
+                   "tokens_per_rank": T, "seed": SEED_DENSE, "weights": "N(0, 0.02) bf16",
+                   "l2": "flushed before every timed step (weights 134.5 MB also exceed L2)",
+                   "parallelism": "single GPU" if world == 1 else "replicas (the dense layer is not sharded)"},
+        "roofline": roofline, "cpu_baseline": cpu,
+        "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4,
+                "how": "pinned host x copied in, lm_ffn_forward, y copied out, synchronised, wall clock per step"},
+        "clocks": clock_info, "gpu_launches": 3 * args.steps,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    layer.close()
+    return 0
+
+
+def run_load(args, rank: int, world: int, local_rank: int) -> int:
+    """The SafeTensors -> HBM loader: one V2-Lite MoE layer (64 experts, shared experts,
+    router, norm; DeepSeek tensor names) written to a shard in a temporary directory,
+    then lm_moe_load_safetensors (mmap, header parse, name lookup, bf16 repack into the
+    tile-major GEMM layout, host -> device copies) timed per call.  The shard was just
+    written, so it is read from the page cache: this measures the loader, not the disk."""
+    import numpy as np
+
+    import shutil
+
+    import torch
+
+    from litemind_b200 import synthetic as syn
+    from litemind_b200.checkpoint import layer_tensors, write_safetensors
+    from litemind_b200.moe import MoeConfig, MoeLayer
+
+    torch.cuda.set_device(local_rank)
+    shape = syn.V2_LITE
+    W = syn.layer_weights(shape, seed=SEED_WEIGHTS)
+    tensors = layer_tensors(W, 0, shape.n_shared_experts)
+    nbytes = sum(np.asarray(a).nbytes for _, a in tensors.values())
+    tmp = tempfile.mkdtemp(prefix="lm_load_")
+    try:
+        path = os.path.join(tmp, "model-00001-of-00001.safetensors")
+        write_safetensors(path, tensors)
+        del tensors
+        layer = MoeLayer(MoeConfig(max_tokens=32), device=local_rank)
+        for _ in range(max(args.warmup, 1)):
+            layer.load_safetensors(0, [path], checkpoint_layer=0)
+        layer.sync()
+        times = []
+        for _ in range(args.steps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            layer.load_safetensors(0, [path], checkpoint_layer=0)
+            layer.sync()
+            times.append(time.perf_counter() - t0)
+        # The copy bound: a plain pinned host -> device copy of the same size.
+        src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        dst.copy_(src)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(3):
+            dst.copy_(src, non_blocking=True)
+        torch.cuda.synchronize()
+        h2d = 3 * nbytes / (time.perf_counter() - t0) / 1e9
+        layer.close()
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    sec = statistics.median(times)
+    gbs = nbytes / sec / 1e9
+    line = {
+        "metric": "SafeTensors -> HBM load GB/s (one V2-Lite MoE layer)", "value": gbs, "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "load: lm_moe_load_safetensors of one layer from a fresh shard in the page cache",
+                   "tensor_bytes": nbytes, "tensors": 3 * shape.n_routed_experts + 6,
+                   "parallelism": "single GPU"},
+        "roofline": {"bound": "h2d", "achieved": gbs, "peak": h2d, "unit": "GB/s", "frac": gbs / h2d,
+                     "peak_source": "pinned host -> device copy of the same bytes, measured in this run",
+                     "traffic": None},
+        "cpu_baseline": None,
+        "cpu_baseline_note": "the reference has no device loader: WeightStore maps the shard and the CPU kernels "
+                             "page weights in as they touch them",
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
     if args.tokens is None:
-        args.tokens = {"decode": 32, "prefill": 16384, "stack": 4096}[args.workload]
+        args.tokens = {"decode": 32, "prefill": 16384, "stack": 4096, "ffn": 32, "load": 32}[args.workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -414,6 +664,10 @@ def main(argv=None) -> int:
         return 0
     if args.workload == "stack":
         return run_stack(args, rank, world, local_rank)
+    if args.workload == "ffn":
+        return run_ffn(args, rank, world, local_rank)
+    if args.workload == "load":
+        return run_load(args, rank, world, local_rank)
 
     import numpy as np
     import torch

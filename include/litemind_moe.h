@@ -217,7 +217,8 @@ lm_status lm_moe_memory(const lm_moe_ctx* ctx, uint64_t* resident_bytes, uint64_
  * time to a per-slot total: slot 1 routing (the fused kernel for T <= 32, else the
  * router logits), 2 router top-k, 3 dispatch scan, 4 placement, 0 the copy of
  * token rows into expert order, 5 gate/up GEMM, 6 down GEMM, 7 expert-parallel
- * exchange, 8 the fused single-launch decode layer (T <= 32 on one GPU).
+ * exchange, 8 the fused single-launch decode layer (T <= 32 on one GPU).  A dense
+ * feed-forward (lm_ffn_forward) records its schedule in slot 3 and its GEMMs in 5 / 6.
  * lm_moe_profile_read copies LM_PROFILE_SLOTS totals (ms) and launch
  * counts to host memory and, when reset != 0, clears them.  No counterpart in the
  * reference, which has no device launches to time.

@@ -10,6 +10,8 @@
 #include "litemind_moe.h"
 #include "moe_internal.h"
 
+#include <algorithm>
+
 namespace lm {
 namespace {
 
@@ -110,6 +112,28 @@ __global__ void add_kernel(float* __restrict__ dst, const float* __restrict__ sr
     if (i < n) dst[i] += src[i];
 }
 
+// Weight packing on upload: row-major gate and up [I, H] and down [H, I] into the
+// grouped GEMMs' tile-major layout -- 128-row x 64-column tiles, tile (rb, cb) at
+// (rb * (cols / 64) + cb) * 8192 elements -- with gate rows on the even rows of w13
+// and up rows on the odd ones.  One thread moves 16 bytes; reads run along rows.
+__global__ void __launch_bounds__(256) pack_swiglu_kernel(const uint16_t* __restrict__ gate,
+                                                          const uint16_t* __restrict__ up,
+                                                          const uint16_t* __restrict__ down, int I, int H,
+                                                          uint16_t* __restrict__ w13, uint16_t* __restrict__ w2) {
+    const int64_t n13 = int64_t(2) * I * H / 8, n2 = int64_t(H) * I / 8;
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    for (int64_t v = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; v < n13 + n2; v += stride) {
+        const bool first = v < n13;
+        const int cols = first ? H : I;
+        const int64_t q = first ? v : v - n13;
+        const int64_t r = q / (cols / 8);
+        const int c = static_cast<int>(q - r * (cols / 8)) * 8;
+        const uint16_t* src = first ? ((r & 1) ? up : gate) + (r >> 1) * int64_t(H) + c : down + r * int64_t(I) + c;
+        const int64_t dst = ((r / 128 * (cols / 64) + c / 64) * 128 + r % 128) * 64 + c % 64;
+        *reinterpret_cast<uint4*>((first ? w13 : w2) + dst) = *reinterpret_cast<const uint4*>(src);
+    }
+}
+
 thread_local std::string g_last_error;
 
 lm_status finish(cudaError_t e) {
@@ -136,6 +160,15 @@ cudaError_t launch_rms_norm_rows(const float* in, float* out_f32, uint16_t* out_
 cudaError_t launch_add_rows(float* dst, const float* src, int64_t count, cudaStream_t stream) {
     if (count <= 0) return cudaSuccess;
     add_kernel<<<blocks_for(count, 256), 256, 0, stream>>>(dst, src, count);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pack_swiglu(const uint16_t* gate, const uint16_t* up, const uint16_t* down, int inter, int hidden,
+                               uint16_t* w13, uint16_t* w2, int sms, cudaStream_t stream) {
+    if (inter <= 0 || hidden <= 0 || inter % 64 != 0 || hidden % 128 != 0) return cudaErrorInvalidValue;
+    const int64_t vectors = int64_t(3) * inter * hidden / 8;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>((vectors + 255) / 256, int64_t(sms) * 8));
+    pack_swiglu_kernel<<<grid, 256, 0, stream>>>(gate, up, down, inter, hidden, w13, w2);
     return cudaGetLastError();
 }
 

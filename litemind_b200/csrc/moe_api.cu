@@ -17,6 +17,7 @@
 #include "moe_internal.h"
 #include "nccl_dl.h"
 #include "ptx.cuh"
+#include "host/CopyPool.hpp"
 #include "host/SafeTensors.hpp"
 
 #include <algorithm>
@@ -25,6 +26,7 @@
 #include <cstring>
 #include <memory>
 #include <string>
+#include <thread>
 #include <vector>
 
 namespace lm {
@@ -103,6 +105,16 @@ struct lm_moe_ctx {
     unsigned int* ticket = nullptr;  // last-CTA ticket of the fused small-T route kernel
     CUtensorMap map_xperm[5]{};
     CUtensorMap map_h[5]{};
+
+    // Weight upload: rows staged in two pinned buffers, then on the device before
+    // packing; the copy threads, the stream and each pinned buffer's DMA event.
+    uint16_t* upload_raw = nullptr;
+    size_t upload_raw_elems = 0;
+    uint16_t* upload_pinned[2]{};
+    cudaEvent_t upload_free[2]{};
+    int upload_next = 0;
+    cudaStream_t upload_stream = nullptr;
+    std::unique_ptr<lm::CopyPool> copy_pool;
 
     // Host-API staging and the decoder sub-layer's normalised activations.
     uint16_t* x_stage = nullptr;
@@ -255,18 +267,80 @@ lm_status ensure_layer_buffers(lm_moe_ctx* ctx, int32_t layer) {
     return LM_OK;
 }
 
-// Copies a logical row-major [rows, cols] matrix into tile-major order: 128 x 64
-// tiles, tile (rb, cb) at ((rb * (cols / 64)) + cb) * 8192 elements.  `row(r)`
-// returns the source row r.
-template <typename RowFn>
-void tile_major(uint16_t* dst, size_t rows, size_t cols, RowFn row) {
-    const size_t cb_n = cols / 64;
-    for (size_t r = 0; r < rows; ++r) {
-        const uint16_t* src = row(r);
-        const size_t rb = r / 128, rr = r % 128;
-        for (size_t cb = 0; cb < cb_n; ++cb)
-            std::memcpy(dst + ((rb * cb_n + cb) * 128 + rr) * 64, src + cb * 64, 64 * sizeof(uint16_t));
+// One SwiGLU block from host memory into the tile-major w13 / w2.  The host threads
+// of a CopyPool copy the three matrices' rows into one of two pinned buffers (down
+// rows read with their pitch), one DMA moves the buffer to the device, and
+// launch_pack_swiglu reorders the rows there -- the host does no per-element work,
+// and the next block's host copy overlaps this one's DMA.  The source is fully read
+// on return; the device work completes by finish_uploads.
+lm_status pack_upload(lm_moe_ctx* ctx, uint16_t* w13, uint16_t* w2, const uint16_t* gate, const uint16_t* up,
+                      const uint16_t* down, size_t I, size_t H, size_t down_pitch) {
+    const size_t need = 3 * I * H;
+    if (ctx->upload_stream == nullptr) {
+        LM_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->upload_stream, cudaStreamNonBlocking));
+        for (cudaEvent_t& e : ctx->upload_free) LM_CUDA(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        const unsigned hw = std::thread::hardware_concurrency();
+        ctx->copy_pool = std::make_unique<CopyPool>(static_cast<int>(std::clamp(hw, 1u, 8u)));
     }
+    cudaStream_t s = ctx->upload_stream;
+    if (need > ctx->upload_raw_elems) {
+        LM_CUDA(ctx, cudaStreamSynchronize(s));
+        if (ctx->upload_raw != nullptr) cudaFree(ctx->upload_raw);
+        for (uint16_t*& p : ctx->upload_pinned)
+            if (p != nullptr) cudaFreeHost(p), p = nullptr;
+        ctx->upload_raw = nullptr;
+        ctx->upload_raw_elems = 0;
+        LM_CUDA(ctx, cudaMalloc(&ctx->upload_raw, need * sizeof(uint16_t)));
+        for (uint16_t*& p : ctx->upload_pinned) LM_CUDA(ctx, cudaMallocHost(&p, need * sizeof(uint16_t)));
+        ctx->upload_raw_elems = need;
+    }
+    const int k = ctx->upload_next;
+    ctx->upload_next ^= 1;
+    // The buffer's previous DMA must be done before it is refilled.
+    LM_CUDA(ctx, cudaEventSynchronize(ctx->upload_free[k]));
+    uint16_t* pin = ctx->upload_pinned[k];
+    struct Rows {
+        uint16_t* dst;
+        const uint16_t* src;
+        size_t rows, width, pitch;
+    };
+    const Rows mats[3] = {{pin, gate, I, H, H}, {pin + I * H, up, I, H, H}, {pin + 2 * I * H, down, H, I, down_pitch}};
+    // About 1 MiB per piece.
+    size_t per[3], pieces[3], total = 0;
+    for (int m = 0; m < 3; ++m) {
+        per[m] = std::max<size_t>(1, (size_t(1) << 19) / mats[m].width);
+        pieces[m] = (mats[m].rows + per[m] - 1) / per[m];
+        total += pieces[m];
+    }
+    ctx->copy_pool->run(static_cast<int>(total), [&](int i) {
+        int m = 0;
+        size_t j = static_cast<size_t>(i);
+        while (j >= pieces[m]) j -= pieces[m++];
+        const Rows& R = mats[m];
+        const size_t r0 = j * per[m], r1 = std::min(R.rows, r0 + per[m]);
+        if (R.pitch == R.width) {
+            std::memcpy(R.dst + r0 * R.width, R.src + r0 * R.pitch, (r1 - r0) * R.width * sizeof(uint16_t));
+        } else {
+            for (size_t r = r0; r < r1; ++r)
+                std::memcpy(R.dst + r * R.width, R.src + r * R.pitch, R.width * sizeof(uint16_t));
+        }
+    });
+    LM_CUDA(ctx, cudaMemcpyAsync(ctx->upload_raw, pin, need * sizeof(uint16_t), cudaMemcpyHostToDevice, s));
+    LM_CUDA(ctx, cudaEventRecord(ctx->upload_free[k], s));
+    uint16_t* rg = ctx->upload_raw;
+    LM_CUDA(ctx, launch_pack_swiglu(rg, rg + I * H, rg + 2 * I * H, static_cast<int>(I), static_cast<int>(H), w13, w2,
+                                    ctx->sms, s));
+    return LM_OK;
+}
+
+// Waits for the uploads pack_upload queued (every public upload entry point ends
+// here, so weights are in place when it returns); `st` passes through unless it is
+// LM_OK and the device work failed.
+lm_status finish_uploads(lm_moe_ctx* ctx, lm_status st) {
+    if (ctx == nullptr || ctx->upload_stream == nullptr) return st;
+    const cudaError_t e = cudaStreamSynchronize(ctx->upload_stream);
+    if (st == LM_OK && e != cudaSuccess) return cuda_fail(ctx, e, "weight upload");
+    return st;
 }
 
 // One SwiGLU block into segment `seg`: gate rows to the even rows of w13, up rows
@@ -275,14 +349,9 @@ void tile_major(uint16_t* dst, size_t rows, size_t cols, RowFn row) {
 lm_status upload_segment(lm_moe_ctx* ctx, LayerWeights& L, int seg, const uint16_t* gate, const uint16_t* up,
                          const uint16_t* down, size_t down_pitch) {
     const size_t H = ctx->cfg.hidden_size, I = ctx->cfg.moe_intermediate_size;
-    static thread_local std::vector<uint16_t> staging;
-    staging.resize(2 * I * H);
-    tile_major(staging.data(), 2 * I, H, [&](size_t r) { return ((r & 1) ? up : gate) + (r >> 1) * H; });
-    LM_CUDA(ctx, cudaMemcpy(L.w13 + static_cast<size_t>(seg) * 2 * I * H, staging.data(), 2 * I * H * 2,
-                            cudaMemcpyHostToDevice));
-    tile_major(staging.data(), H, I, [&](size_t r) { return down + r * down_pitch; });
-    LM_CUDA(ctx, cudaMemcpy(L.w2 + static_cast<size_t>(seg) * H * I, staging.data(), H * I * 2,
-                            cudaMemcpyHostToDevice));
+    lm_status st = pack_upload(ctx, L.w13 + static_cast<size_t>(seg) * 2 * I * H, L.w2 + static_cast<size_t>(seg) * H * I,
+                               gate, up, down, I, H, down_pitch);
+    if (st != LM_OK) return st;
     ctx->uploaded_bytes += 3 * I * H * 2;
     return LM_OK;
 }
@@ -508,6 +577,13 @@ lm_status lm_moe_destroy(lm_moe_ctx* ctx) {
     if (ctx->norm_bf16) cudaFree(ctx->norm_bf16);
     if (ctx->decode_trace) cudaFree(ctx->decode_trace);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    if (ctx->upload_stream) cudaStreamSynchronize(ctx->upload_stream);
+    if (ctx->upload_raw) cudaFree(ctx->upload_raw);
+    for (uint16_t* p : ctx->upload_pinned)
+        if (p) cudaFreeHost(p);
+    for (cudaEvent_t e : ctx->upload_free)
+        if (e) cudaEventDestroy(e);
+    if (ctx->upload_stream) cudaStreamDestroy(ctx->upload_stream);
     if (ctx->comm != nullptr && ctx->nccl != nullptr) ctx->nccl->CommDestroy(ctx->comm);
     if (ctx->host_sched) cudaFreeHost(ctx->host_sched);
     if (ctx->ep_stream) cudaStreamDestroy(ctx->ep_stream);
@@ -527,7 +603,7 @@ lm_status lm_moe_destroy(lm_moe_ctx* ctx) {
     return LM_OK;
 }
 
-lm_status lm_moe_upload_layer(lm_moe_ctx* ctx, int32_t layer, const float* router, const uint16_t* gate,
+static lm_status upload_layer_body(lm_moe_ctx* ctx, int32_t layer, const float* router, const uint16_t* gate,
                               const uint16_t* up, const uint16_t* down, const uint16_t* shared_gate,
                               const uint16_t* shared_up, const uint16_t* shared_down, const float* norm_weight) {
     if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
@@ -549,6 +625,13 @@ lm_status lm_moe_upload_layer(lm_moe_ctx* ctx, int32_t layer, const float* route
         L.expert_loaded[s] = 1;
     }
     return upload_shared_and_router(ctx, L, router, shared_gate, shared_up, shared_down, norm_weight);
+}
+
+lm_status lm_moe_upload_layer(lm_moe_ctx* ctx, int32_t layer, const float* router, const uint16_t* gate,
+                              const uint16_t* up, const uint16_t* down, const uint16_t* shared_gate,
+                              const uint16_t* shared_up, const uint16_t* shared_down, const float* norm_weight) {
+    return finish_uploads(
+        ctx, upload_layer_body(ctx, layer, router, gate, up, down, shared_gate, shared_up, shared_down, norm_weight));
 }
 
 
@@ -590,7 +673,7 @@ lm_status lm_safetensors_info(const char* path, const char* name, int32_t* dtype
     return LM_ERR_NOT_LOADED;
 }
 
-lm_status lm_moe_load_safetensors(lm_moe_ctx* ctx, int32_t layer, int32_t checkpoint_layer,
+static lm_status load_safetensors_body(lm_moe_ctx* ctx, int32_t layer, int32_t checkpoint_layer,
                                   const char* const* shard_paths, int32_t n_shards) {
     if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
     if (layer < 0 || layer >= static_cast<int32_t>(ctx->layers.size()))
@@ -655,7 +738,12 @@ lm_status lm_moe_load_safetensors(lm_moe_ctx* ctx, int32_t layer, int32_t checkp
     return upload_shared_and_router(ctx, L, router.data(), sg, su, sd, norm.data());
 }
 
-lm_status lm_ffn_upload(lm_moe_ctx* ctx, int32_t layer, int32_t intermediate, const uint16_t* gate, const uint16_t* up,
+lm_status lm_moe_load_safetensors(lm_moe_ctx* ctx, int32_t layer, int32_t checkpoint_layer,
+                                  const char* const* shard_paths, int32_t n_shards) {
+    return finish_uploads(ctx, load_safetensors_body(ctx, layer, checkpoint_layer, shard_paths, n_shards));
+}
+
+static lm_status ffn_upload_body(lm_moe_ctx* ctx, int32_t layer, int32_t intermediate, const uint16_t* gate, const uint16_t* up,
                         const uint16_t* down, const float* norm_weight) {
     if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
     const lm_moe_config& c = ctx->cfg;
@@ -697,11 +785,7 @@ lm_status lm_ffn_upload(lm_moe_ctx* ctx, int32_t layer, int32_t intermediate, co
             if (!encode_tensor_map_bf16(&ctx->dense_map_h[i], ctx->dense_h, rows, I, kBnChoices[i], 64, err))
                 return fail(ctx, LM_ERR_CUDA, err);
     }
-    std::vector<uint16_t> staging(2 * I * H);
-    tile_major(staging.data(), 2 * I, H, [&](size_t r) { return ((r & 1) ? up : gate) + (r >> 1) * H; });
-    LM_CUDA(ctx, cudaMemcpy(D.w13, staging.data(), 2 * I * H * 2, cudaMemcpyHostToDevice));
-    tile_major(staging.data(), H, I, [&](size_t r) { return down + r * I; });
-    LM_CUDA(ctx, cudaMemcpy(D.w2, staging.data(), H * I * 2, cudaMemcpyHostToDevice));
+    if ((st = pack_upload(ctx, D.w13, D.w2, gate, up, down, I, H, I)) != LM_OK) return st;
     std::vector<float> ones;
     if (norm_weight == nullptr) ones.assign(H, 1.0f);
     LM_CUDA(ctx, cudaMemcpy(D.norm, norm_weight != nullptr ? norm_weight : ones.data(), H * 4, cudaMemcpyHostToDevice));
@@ -709,7 +793,12 @@ lm_status lm_ffn_upload(lm_moe_ctx* ctx, int32_t layer, int32_t intermediate, co
     return LM_OK;
 }
 
-lm_status lm_ffn_load_safetensors(lm_moe_ctx* ctx, int32_t layer, int32_t checkpoint_layer, int32_t intermediate,
+lm_status lm_ffn_upload(lm_moe_ctx* ctx, int32_t layer, int32_t intermediate, const uint16_t* gate, const uint16_t* up,
+                        const uint16_t* down, const float* norm_weight) {
+    return finish_uploads(ctx, ffn_upload_body(ctx, layer, intermediate, gate, up, down, norm_weight));
+}
+
+static lm_status ffn_load_safetensors_body(lm_moe_ctx* ctx, int32_t layer, int32_t checkpoint_layer, int32_t intermediate,
                                   const char* const* shard_paths, int32_t n_shards) {
     if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
     if (shard_paths == nullptr || n_shards <= 0 || checkpoint_layer < 0)
@@ -741,6 +830,12 @@ lm_status lm_ffn_load_safetensors(lm_moe_ctx* ctx, int32_t layer, int32_t checkp
     return lm_ffn_upload(ctx, layer, intermediate, bf16(g), bf16(u), bf16(d), norm.data());
 }
 
+lm_status lm_ffn_load_safetensors(lm_moe_ctx* ctx, int32_t layer, int32_t checkpoint_layer, int32_t intermediate,
+                                  const char* const* shard_paths, int32_t n_shards) {
+    return finish_uploads(ctx,
+                          ffn_load_safetensors_body(ctx, layer, checkpoint_layer, intermediate, shard_paths, n_shards));
+}
+
 lm_status lm_ffn_forward(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int32_t tokens, float* y,
                          int32_t accumulate, void* stream) {
     if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
@@ -760,8 +855,10 @@ lm_status lm_ffn_forward(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int3
     // blocks, which a dense intermediate size need not divide into.
     const int bn = std::min(choose_bn(T, 1, 1), 128);
     const int bi = bn_index(bn);
+    prof_begin(ctx, s);
     LM_CUDA(ctx, launch_dense_schedule(ctx->dense_sched, T, bn, 2 * I / 128, H / 128, s));
     if (!accumulate) LM_CUDA(ctx, cudaMemsetAsync(y, 0, static_cast<size_t>(T) * H * sizeof(float), s));
+    prof_mark(ctx, 3, s);
     CUtensorMap map_x{};
     std::string err;
     if (!encode_tensor_map_bf16(&map_x, x, T, H, bn, 64, err)) return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
@@ -780,8 +877,11 @@ lm_status lm_ffn_forward(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int3
     args.split_ws_floats = static_cast<int32_t>(kSplitWsBytes / sizeof(float));
     args.split_max_waves = ctx->split_max_waves;
     LM_CUDA(ctx, launch_gemm_gate_up(bn, D.map_w13, map_x, map_x, args, ctx->sms, s, true));
+    prof_mark(ctx, 5, s);
     LM_CUDA(ctx, launch_gemm_down(bn, D.map_w2, ctx->dense_map_h[bi], args, ctx->sms, s, true));
-    return LM_OK;
+    prof_mark(ctx, 6, s);
+    const int slots[3] = {3, 5, 6};
+    return prof_end(ctx, slots, 3);
 }
 
 lm_status lm_ffn_block_forward(lm_moe_ctx* ctx, int32_t layer, float* hidden, int32_t tokens, void* stream) {
@@ -808,7 +908,7 @@ lm_status lm_ffn_block_forward(lm_moe_ctx* ctx, int32_t layer, float* hidden, in
     return lm_ffn_forward(ctx, layer, ctx->norm_bf16, tokens, hidden, 1, stream);
 }
 
-lm_status lm_moe_upload_expert(lm_moe_ctx* ctx, int32_t layer, int32_t expert, const uint16_t* gate,
+static lm_status upload_expert_body(lm_moe_ctx* ctx, int32_t layer, int32_t expert, const uint16_t* gate,
                                const uint16_t* up, const uint16_t* down) {
     if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
     if (layer < 0 || layer >= static_cast<int32_t>(ctx->layers.size()))
@@ -824,6 +924,11 @@ lm_status lm_moe_upload_expert(lm_moe_ctx* ctx, int32_t layer, int32_t expert, c
     if ((st = upload_segment(ctx, L, s, gate, up, down, ctx->cfg.moe_intermediate_size)) != LM_OK) return st;
     L.expert_loaded[s] = 1;
     return LM_OK;
+}
+
+lm_status lm_moe_upload_expert(lm_moe_ctx* ctx, int32_t layer, int32_t expert, const uint16_t* gate,
+                               const uint16_t* up, const uint16_t* down) {
+    return finish_uploads(ctx, upload_expert_body(ctx, layer, expert, gate, up, down));
 }
 
 // Router logits: on the tensor cores for large batches of bf16 tokens, else the

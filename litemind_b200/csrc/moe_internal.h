@@ -202,6 +202,11 @@ cudaError_t launch_gemm_down_pair(int bn, const CUtensorMap& w2, const CUtensorM
 cudaError_t launch_rms_norm_rows(const float* in, float* out_f32, uint16_t* out_bf16, const float* weight,
                                  int rows, int count, float eps, cudaStream_t stream);
 cudaError_t launch_add_rows(float* dst, const float* src, int64_t count, cudaStream_t stream);
+// Row-major gate/up [inter, hidden] and down [hidden, inter] (device) into the
+// tile-major w13 (gate and up rows interleaved) and w2 the grouped GEMMs read.
+// inter must be a multiple of 64, hidden of 128.
+cudaError_t launch_pack_swiglu(const uint16_t* gate, const uint16_t* up, const uint16_t* down, int inter, int hidden,
+                               uint16_t* w13, uint16_t* w2, int sms, cudaStream_t stream);
 const std::string& context_free_error();
 
 // Host-side TMA descriptor encoding (tensor_map.cpp).
