@@ -1,7 +1,9 @@
 """The C++20 host mirror (include/litemind_b200/*.hpp) compiled as a user would:
 g++ against include/ and liblitemind_b200.so.  ExpertCacheTest replays the
 reference's ExpertCache statistics (CPU); SafeTensorsTest looks up checkpoint tensors
-through the C ABI (CPU); MoeRouterTest runs the reference's routing checks on the GPU."""
+through the C ABI (CPU); MoeRouterTest runs the reference's routing checks on the GPU.
+CopyPoolTest checks the weight upload's host copy threads (CPU, built from source
+under ThreadSanitizer)."""
 import json
 import os
 import subprocess
@@ -61,3 +63,14 @@ def test_safetensors_lookup_from_cpp(tmp_path):
     res = subprocess.run([exe, str(shard), str(cut)], capture_output=True, text=True)
     assert res.returncode == 0, res.stdout + res.stderr
 
+
+
+def test_copy_pool_threads(tmp_path):
+    exe = tmp_path / "CopyPoolTest"
+    host = os.path.join(ROOT, "litemind_b200", "csrc", "host")
+    cmd = ["g++", "-std=c++20", "-O1", "-g", "-Wall", "-Wextra", "-pthread", "-fsanitize=thread", f"-I{host}", f"-I{CPP}",
+           os.path.join(CPP, "CopyPoolTest.cpp"), os.path.join(host, "CopyPool.cpp"), "-o", str(exe)]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "CopyPoolTest: all checks passed" in res.stdout
