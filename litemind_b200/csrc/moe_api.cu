@@ -856,8 +856,8 @@ lm_status lm_ffn_forward(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int3
     const int bn = std::min(choose_bn(T, 1, 1), 128);
     const int bi = bn_index(bn);
     prof_begin(ctx, s);
-    LM_CUDA(ctx, launch_dense_schedule(ctx->dense_sched, T, bn, 2 * I / 128, H / 128, s));
-    if (!accumulate) LM_CUDA(ctx, cudaMemsetAsync(y, 0, static_cast<size_t>(T) * H * sizeof(float), s));
+    LM_CUDA(ctx, launch_dense_schedule(ctx->dense_sched, T, bn, 2 * I / 128, H / 128, accumulate ? nullptr : y,
+                                       static_cast<int64_t>(T) * H, ctx->sms, s));
     prof_mark(ctx, 3, s);
     CUtensorMap map_x{};
     std::string err;

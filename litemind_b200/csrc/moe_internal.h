@@ -70,7 +70,10 @@ cudaError_t launch_place(const int32_t* topk_idx, const float* topk_w, const int
                          cudaStream_t stream, bool pdl);
 cudaError_t launch_ep_combine(float* y, const uint16_t* back, const int32_t* slot_row, const float* topk_w, int tokens,
                               int top_k, int hidden, cudaStream_t stream, bool pdl);
-cudaError_t launch_dense_schedule(Schedule* sched, int tokens, int bn, int mb1, int mb2, cudaStream_t stream);
+// The dense feed-forward's one-segment schedule; also zeroes y_count floats of y_zero
+// (16-byte aligned, a multiple of 4) unless it is null.
+cudaError_t launch_dense_schedule(Schedule* sched, int tokens, int bn, int mb1, int mb2, float* y_zero,
+                                  int64_t y_count, int sms, cudaStream_t stream);
 // Expert parallelism: received rows -> expert-major, with row_src[row] = the row's
 // index in the receive buffer.  The receive buffer holds local-expert chunks one after
 // another, each source-major; a launch sorts chunk [e_lo, e_hi) (the whole [0, El) when

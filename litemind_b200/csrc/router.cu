@@ -729,12 +729,18 @@ cudaError_t launch_ep_combine(float* y, const uint16_t* back, const int32_t* slo
                     back, slot_row, topk_w, tokens, top_k, hidden);
 }
 
-// The dense feed-forward's schedule: one segment of all T tokens (read from x, as a
-// shared expert's are), weight slot 0.
-__global__ void dense_schedule_kernel(Schedule* sched, int T, int bn, int mb1, int mb2) {
+// The dense feed-forward's schedule -- one segment of all T tokens (read from x, as a
+// shared expert's are), weight slot 0 -- and, unless the call accumulates, y zeroed
+// for the down GEMM's adds: one launch, which the gate/up GEMM follows
+// programmatically (its prologue overlaps this kernel).
+__global__ void dense_schedule_kernel(Schedule* sched, int T, int bn, int mb1, int mb2, float4* __restrict__ y,
+                                      int64_t y_vec4) {
     pdl_wait();
     pdl_launch_dependents();
-    if (threadIdx.x != 0) return;
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < y_vec4; i += stride)
+        y[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (blockIdx.x != 0 || threadIdx.x != 0) return;
     const int nb = (T + bn - 1) / bn;
     sched->n_seg = 1;
     sched->first_expert = 0;
@@ -747,8 +753,13 @@ __global__ void dense_schedule_kernel(Schedule* sched, int T, int bn, int mb1, i
     sched->tiles2[1] = nb * mb2;
 }
 
-cudaError_t launch_dense_schedule(Schedule* sched, int tokens, int bn, int mb1, int mb2, cudaStream_t stream) {
-    return launch_k(dense_schedule_kernel, dim3(1), dim3(32), stream, false, sched, tokens, bn, mb1, mb2);
+cudaError_t launch_dense_schedule(Schedule* sched, int tokens, int bn, int mb1, int mb2, float* y_zero,
+                                  int64_t y_count, int sms, cudaStream_t stream) {
+    const int64_t vec4 = y_zero != nullptr ? y_count / 4 : 0;
+    if (vec4 * 4 != (y_zero != nullptr ? y_count : 0)) return cudaErrorInvalidValue;
+    const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((vec4 + 255) / 256, 4 * sms)));
+    return launch_k(dense_schedule_kernel, dim3(grid), dim3(256), stream, false, sched, tokens, bn, mb1, mb2,
+                    reinterpret_cast<float4*>(y_zero), vec4);
 }
 
 cudaError_t launch_ep_sort_rows(const uint16_t* x_recv, uint16_t* x_sorted, int32_t* row_src,
