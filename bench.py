@@ -36,7 +36,9 @@ With N > 1 (torchrun, one rank per GPU) each rank runs the same per-rank workloa
 (T tokens of its own) under expert parallelism: rank r holds routed experts
 [r*64/N, (r+1)*64/N) and the shared experts, and every forward exchanges token rows
 and expert outputs with NCCL all-to-all over NVLink (BASELINE config 3's scheme;
-config 3's own size is --tokens 8192).  Scaling is weak: tokens per GPU fixed.
+config 3's own size is --tokens 8192, where the exchange runs in chunks of local
+experts overlapped with the GEMMs and roofline.ep_timeline_ms shows the overlap).
+Scaling is weak: tokens per GPU fixed.
 """
 from __future__ import annotations
 
