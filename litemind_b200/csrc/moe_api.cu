@@ -1083,6 +1083,14 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
                                         ctx->local_experts, ctx->routed_cap, bn, 2 * I / 128, H / 128, s, false));
         prof_mark(ctx, 1, s);
         slots[n_slots++] = 1;
+    } else if (T <= kRouteMidTokens) {
+        // Mid-size batches: the same single launch, over several token blocks.
+        LM_CUDA(ctx, launch_route_mid(x, x_f32, L.router, bias, ctx->logits, T, H, rp, ctx->topk_idx, ctx->topk_w,
+                                      ctx->expert_totals, ctx->sched, ctx->row_token, ctx->row_weight,
+                                      ctx->slot_row, y_zero, ctx->ticket, c.n_shared_experts, ctx->first_expert,
+                                      ctx->local_experts, ctx->routed_cap, bn, 2 * I / 128, H / 128, s, false));
+        prof_mark(ctx, 1, s);
+        slots[n_slots++] = 1;
     } else {
         lm_status rst;
         RouterFix fix;

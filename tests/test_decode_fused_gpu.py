@@ -4,7 +4,8 @@ Parity against the oracle across the token counts that change its work split (on
 token, one token-tile boundary, the largest batch it takes), with a logit bias, with
 group-limited and renormalised routing, with accumulation into y, with f32 router
 activations (the block path), and against the grouped multi-launch path it
-replaces.  Its phase trace is checked for ordering.
+replaces.  Its phase trace is checked for ordering.  Mid-size batches (33-128
+tokens) route in one launch too, checked here the same way.
 """
 import os
 
@@ -137,6 +138,29 @@ def test_fused_group_limited_routing(oracle_lib, normalize):
     rcfg = RouterConfig(64, 6, n_group=8, topk_group=3, group_limited=True, norm_topk_prob=normalize)
     ry, ridx, rw, rlog = _oracle(oracle_lib, GROUPED, W, x, cfg=rcfg)
     assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what=f"fused group-limited normalize={normalize}")
+    layer.close()
+
+
+@pytest.mark.parametrize("T,normalize", [(33, False), (100, True), (128, False)])
+def test_mid_batch_single_launch_routing(oracle_lib, T, normalize):
+    """32 < T <= 128 routes in one launch (logits over token blocks of 128, top-k,
+    counts, schedule, rows), then the grouped GEMMs: group-limited routing with a
+    logit bias, and the forward's own expert histogram against the oracle's."""
+    W = syn.layer_weights(GROUPED, seed=41, std=0.05)
+    cfg = MoeConfig.from_shape(GROUPED, max_tokens=256, topk_method="group_limited_greedy", n_group=8,
+                               topk_group=3, norm_topk_prob=normalize, routed_scaling_factor=1.0)
+    layer = MoeLayer(cfg)
+    layer.upload_layer(0, W)
+    x = syn.tokens(GROUPED, T, seed=42 + T)
+    bias = np.linspace(-0.5, 0.5, GROUPED.n_routed_experts).astype(np.float32)
+    y, idx, w, _, prof = _gpu(layer, x, bias=bias)
+    assert "route" in prof and "router_topk" not in prof and "decode_fused" not in prof, prof
+    rcfg = RouterConfig(64, 6, n_group=8, topk_group=3, group_limited=True, norm_topk_prob=normalize)
+    ry, ridx, rw, rlog = _oracle(oracle_lib, GROUPED, W, x, cfg=rcfg, bias=bias)
+    assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what=f"mid-batch route T={T}")
+    counts = layer.expert_counts()
+    ref_counts = np.bincount(ridx.reshape(-1), minlength=GROUPED.n_routed_experts)
+    assert np.abs(counts - ref_counts).sum() <= 2, (counts, ref_counts)
     layer.close()
 
 
