@@ -286,8 +286,10 @@ lm_status pack_upload(lm_moe_ctx* ctx, uint16_t* w13, uint16_t* w2, const uint16
     if (need > ctx->upload_raw_elems) {
         LM_CUDA(ctx, cudaStreamSynchronize(s));
         if (ctx->upload_raw != nullptr) cudaFree(ctx->upload_raw);
-        for (uint16_t*& p : ctx->upload_pinned)
-            if (p != nullptr) cudaFreeHost(p), p = nullptr;
+        for (uint16_t*& p : ctx->upload_pinned) {
+            if (p != nullptr) cudaFreeHost(p);
+            p = nullptr;
+        }
         ctx->upload_raw = nullptr;
         ctx->upload_raw_elems = 0;
         LM_CUDA(ctx, cudaMalloc(&ctx->upload_raw, need * sizeof(uint16_t)));
