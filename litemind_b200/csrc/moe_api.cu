@@ -14,6 +14,8 @@
 // where segments = the routed experts held on this device + n_shared_experts
 // shared splits of width inter (sum over the splits == the reference's one
 // shared FFN of width inter * n_shared, src/DeepSeekRunner.cpp:217-222).
+// Uploads copy each segment's row-major rows into pinned staging on host threads,
+// move them with one DMA and reorder them into tiles on the device (pack_upload).
 #include "moe_internal.h"
 #include "nccl_dl.h"
 #include "ptx.cuh"
