@@ -65,7 +65,7 @@ FLUSH_BYTES = 256 << 20
 
 def kernels_per_forward(tokens: int, world: int, experts: int = 64, top_k: int = 6, sms: int = 148) -> int:
     """Our kernel launches in one forward (NCCL's own kernels not counted).
-    One GPU: T <= 32 is the fused decode kernel alone; 32 < T <= 128 the single-launch
+    One GPU: T <= 32 is the fused decode kernel alone; 32 < T <= 256 the single-launch
     routing kernel, the row gather and the two grouped GEMMs; above that router
     logits, top-k, scan, placement and the two grouped GEMMs, plus a separate row
     gather unless the placement copies the rows itself (2 T >= 32 x SMs).  Expert parallel:
@@ -75,7 +75,7 @@ def kernels_per_forward(tokens: int, world: int, experts: int = 64, top_k: int =
     placement does not copy), sort, two GEMMs and the combine."""
     gather = 0 if tokens > 32 and 2 * tokens >= 32 * sms else 1
     if world == 1:
-        return 1 if tokens <= 32 else 4 if tokens <= 128 else 6 + gather
+        return 1 if tokens <= 32 else 4 if tokens <= 256 else 6 + gather
     route = 1 if tokens <= 32 else 4
     fixed = world * tokens * min(top_k, experts // world) <= 8192
     if fixed:

@@ -104,7 +104,7 @@ struct lm_moe_ctx {
     lm::Schedule* dense_sched = nullptr;
     float* split_ws = nullptr;        // gate/up split-K partial tiles
     int32_t* split_ticket = nullptr;  // k-blocks done per split tile, zero between uses
-    unsigned int* ticket = nullptr;  // last-CTA ticket of the fused small-T route kernel
+    unsigned int* ticket = nullptr;  // [kRouteTickets] last-CTA tickets of the single-launch route kernels
     CUtensorMap map_xperm[5]{};
     CUtensorMap map_h[5]{};
 
@@ -541,7 +541,7 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
         (st = alloc(p, &p->sched, 1)) || (st = alloc(p, &p->row_token, static_cast<size_t>(p->routed_cap))) ||
         (st = alloc(p, &p->row_weight, static_cast<size_t>(p->routed_cap))) || (st = alloc(p, &p->slot_row, T * K)) ||
         (st = alloc(p, &p->x_perm, static_cast<size_t>(p->routed_cap) * H)) || (st = alloc(p, &p->h, h_rows * I)) ||
-        (st = alloc(p, &p->status, 1)) || (st = alloc(p, &p->ticket, 1)) ||
+        (st = alloc(p, &p->status, 1)) || (st = alloc(p, &p->ticket, kRouteTickets)) ||
         (st = alloc(p, &p->split_ws, kSplitWsBytes / sizeof(float))) ||
         (st = alloc(p, &p->split_ticket, static_cast<size_t>(kSplitTickets))) ||
         (st = alloc(p, &p->grid_bar, 3))) {
@@ -549,7 +549,7 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
         return st;
     }
     if (cudaMemset(p->status, 0, sizeof(int32_t)) != cudaSuccess ||
-        cudaMemset(p->ticket, 0, sizeof(unsigned int)) != cudaSuccess ||
+        cudaMemset(p->ticket, 0, kRouteTickets * sizeof(unsigned int)) != cudaSuccess ||
         cudaMemset(p->expert_totals, 0, E * sizeof(int32_t)) != cudaSuccess ||
         cudaMemset(p->sched, 0, sizeof(Schedule)) != cudaSuccess ||
         cudaMemset(p->split_ws, 0, kSplitWsBytes) != cudaSuccess ||
@@ -1091,8 +1091,10 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
         // Mid-size batches: the same single launch, over several token blocks.
         LM_CUDA(ctx, launch_route_mid(x, x_f32, L.router, bias, ctx->logits, T, H, rp, ctx->topk_idx, ctx->topk_w,
                                       ctx->expert_totals, ctx->sched, ctx->row_token, ctx->row_weight,
-                                      ctx->slot_row, y_zero, ctx->ticket, c.n_shared_experts, ctx->first_expert,
-                                      ctx->local_experts, ctx->routed_cap, bn, 2 * I / 128, H / 128, s, false));
+                                      ctx->slot_row, y_zero, ctx->ticket + 1,
+                                      reinterpret_cast<uint32_t*>(ctx->tile_counts), c.n_shared_experts,
+                                      ctx->first_expert, ctx->local_experts, ctx->routed_cap, bn, 2 * I / 128, H / 128,
+                                      s, false));
         prof_mark(ctx, 1, s);
         slots[n_slots++] = 1;
     } else {

@@ -17,7 +17,8 @@ constexpr int kMaxShared = 8;             // shared-expert splits (n_shared_expe
 constexpr int kMaxSegments = kMaxExperts + kMaxShared;
 constexpr int kMaxTopK = 16;
 constexpr int kRouteTile = 32;            // tokens per routing tile (one warp per token)
-constexpr int kRouteMidTokens = 128;      // largest batch routed by the single-launch mid-size kernel
+constexpr int kRouteMidTokens = 256;      // largest batch routed by the single-launch mid-size kernel
+constexpr int kRouteTickets = 16;         // [0] route_small's ticket, [1, ...] route_mid's block + final tickets
 
 // Per-call schedule read by the grouped GEMMs: written on the device by the
 // routing kernels (one GPU: segment s is local expert s, then the shared splits),
@@ -103,13 +104,15 @@ cudaError_t launch_route_small(const uint16_t* x, const float* x_f32, const floa
                                int mb2, cudaStream_t stream, bool pdl);
 
 // kRouteTile < T <= kRouteMidTokens: the same single-launch routing stage (logits,
-// top-k, counts, schedule, placement; E <= kMaxExperts).
+// top-k, counts, schedule, placement; E <= kMaxExperts), routed per 32-token block.
+// tickets: kRouteMidTokens / 32 + 1 zeroed counters (re-armed by the kernel);
+// blk_mask: [blocks, E] scratch.
 cudaError_t launch_route_mid(const uint16_t* x, const float* x_f32, const float* w, const float* bias,
                              float* logits, int tokens, int hidden, RouterParams rp, int32_t* topk_idx,
                              float* topk_w, int32_t* expert_totals, Schedule* sched, int32_t* row_token,
-                             float* row_weight, int32_t* slot_row, float* y_zero, unsigned int* ticket,
-                             int n_shared, int first_expert, int local_experts, int shared_base, int bn, int mb1,
-                             int mb2, cudaStream_t stream, bool pdl);
+                             float* row_weight, int32_t* slot_row, float* y_zero, unsigned int* tickets,
+                             uint32_t* blk_mask, int n_shared, int first_expert, int local_experts, int shared_base,
+                             int bn, int mb1, int mb2, cudaStream_t stream, bool pdl);
 
 // Grouped SwiGLU GEMMs (grouped_gemm.cu).
 struct GemmArgs {

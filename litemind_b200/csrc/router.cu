@@ -624,18 +624,18 @@ __global__ void __launch_bounds__(kSmallThreads) route_small_kernel(
     }
 }
 
-// Mid-size batches (kRouteTile < T <= kRouteMidTokens): the same single-launch
-// routing stage.  CTA (e, part) computes expert e's logits for tokens
-// [128 part, 128 part + 128) and zeroes a slice of y; the last CTA in routes every
-// token (a warp per token), keeps per expert a token bit mask and a count, builds the
+// Mid-size batches (kRouteTile < T <= kRouteMidTokens): the routing stage in one
+// launch, routed in parallel per 32-token block.  CTA (e, b) computes expert e's
+// logits for block b's tokens (a warp per token) and zeroes a slice of y.  The last
+// CTA of each block (a ticket per block) routes the block's tokens (a warp per
+// token) and publishes, per expert, the block's token bit mask; the last block
+// router (one more ticket) sums the masks into the expert counts, builds the
 // schedule, and places each (token, slot) pair at its expert's first row plus the
-// number of earlier tokens in that expert's mask -- rows in (expert, token) order,
-// as the placement kernel orders them (a token picks an expert at most once).  The
-// last CTA's routing is serial in tokens per warp: at 256 tokens (8 per warp) the
-// launch took as long as the four-kernel route it replaces (45 us on a B200), at 64
-// half as long, so the limit is 128.
-constexpr int kMidTokensPerCta = 128;
-constexpr int kMidMaskWords = kRouteMidTokens / 32;
+// number of earlier tokens in that expert's masks -- rows in (expert, token) order,
+// as the placement kernel orders them (a token picks an expert at most once) -- and
+// re-arms the tickets.  tickets: kMidBlocks block tickets, then the final one.
+constexpr int kMidBlocks = kRouteMidTokens / kRouteTile;
+static_assert(kMidBlocks + 2 <= kRouteTickets, "route_small's ticket, the block tickets and the final one");
 
 template <typename XT, int EPL>
 __global__ void __launch_bounds__(kSmallThreads) route_mid_kernel(
@@ -643,19 +643,19 @@ __global__ void __launch_bounds__(kSmallThreads) route_mid_kernel(
     int T, int H, RouterParams rp, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
     int32_t* __restrict__ expert_totals, Schedule* __restrict__ sched, int32_t* __restrict__ row_token,
     float* __restrict__ row_weight, int32_t* __restrict__ slot_row, float* __restrict__ y_zero,
-    unsigned int* __restrict__ ticket, int n_shared, int first_expert, int local_E, int shared_base, int bn, int mb1,
-    int mb2) {
+    unsigned int* __restrict__ tickets, uint32_t* __restrict__ blk_mask, int n_shared, int first_expert, int local_E,
+    int shared_base, int bn, int mb1, int mb2) {
     __shared__ float probs[kSmallThreads / 32][kMaxExperts];
-    __shared__ uint32_t s_mask[kMaxExperts][kMidMaskWords];
+    __shared__ uint32_t s_mask[kMaxExperts];
     __shared__ int totals[kMaxExperts];
     __shared__ int seg_off_s[kMaxExperts];
     __shared__ int s_last;
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
-    constexpr int kWarps = kSmallThreads / 32;
     const int E = rp.experts;
     const int K = rp.top_k;
+    const int nblk = (T + kRouteTile - 1) / kRouteTile;
     pdl_wait();
     pdl_launch_dependents();
 
@@ -667,73 +667,82 @@ __global__ void __launch_bounds__(kSmallThreads) route_mid_kernel(
             yz[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
 
-    // Logits of this CTA's expert for its tokens; the unrolled loop keeps each lane's
-    // loads of x and of the router row in flight together.
-    const int parts = (T + kMidTokensPerCta - 1) / kMidTokensPerCta;
-    const int e = blockIdx.x / parts;
-    const int part = blockIdx.x - e * parts;
-    const int t_end = min(T, (part + 1) * kMidTokensPerCta);
-    if (e < E) {
+    // Logits of this CTA's expert for its block: a warp per token; the unrolled loop
+    // keeps each lane's loads of x and of the router row in flight together.
+    const int e = blockIdx.x / nblk;
+    const int b = blockIdx.x - e * nblk;
+    const int t = b * kRouteTile + warp;
+    if (t < T) {
         const float* we = w + static_cast<size_t>(e) * H;
-        for (int t = part * kMidTokensPerCta + warp; t < t_end; t += kWarps) {
-            float acc = 0.0f;
-            const XT* xt = x + static_cast<size_t>(t) * H;
+        const XT* xt = x + static_cast<size_t>(t) * H;
+        float acc = 0.0f;
 #pragma unroll 8
-            for (int h = lane * 8; h < H; h += 256) {
-                float xv[8], wv[8];
-                load8(xt + h, xv);
-                load8(we + h, wv);
+        for (int h = lane * 8; h < H; h += 256) {
+            float xv[8], wv[8];
+            load8(xt + h, xv);
+            load8(we + h, wv);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[i], acc);
-            }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(kFull, acc, off);
-            if (lane == 0) logits[static_cast<size_t>(t) * E + e] = bias != nullptr ? acc + bias[e] : acc;
+            for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[i], acc);
         }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(kFull, acc, off);
+        if (lane == 0) logits[static_cast<size_t>(t) * E + e] = bias != nullptr ? acc + bias[e] : acc;
     }
 
-    // Last CTA in: route, count, schedule, place.
+    // Last CTA of the block: route its tokens and publish the block's expert masks.
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(ticket, 1u) == gridDim.x - 1) ? 1 : 0;
+    if (tid == 0) s_last = (atomicAdd(&tickets[b], 1u) == static_cast<unsigned>(E - 1)) ? 1 : 0;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int i = tid; i < E; i += blockDim.x) {
-        totals[i] = 0;
-        seg_off_s[i] = 0;
-    }
-    for (int i = tid; i < E * kMidMaskWords; i += blockDim.x) s_mask[i / kMidMaskWords][i % kMidMaskWords] = 0u;
+    for (int i = tid; i < E; i += blockDim.x) s_mask[i] = 0u;
     __syncthreads();
-    for (int t = warp; t < T; t += kWarps) {
+    if (t < T) {
         const Selection sel = route_one_token<EPL>(logits + static_cast<size_t>(t) * E, rp, probs[warp], lane);
         if (lane < K) {
             topk_idx[static_cast<size_t>(t) * K + lane] = sel.idx;
             topk_w[static_cast<size_t>(t) * K + lane] = sel.w;
-            atomicAdd(&totals[sel.idx], 1);
-            atomicOr(&s_mask[sel.idx][t >> 5], 1u << (t & 31));
+            atomicOr(&s_mask[sel.idx], 1u << warp);
         }
     }
     __syncthreads();
-    for (int i = tid; i < E; i += blockDim.x) expert_totals[i] = totals[i];
+    for (int i = tid; i < E; i += blockDim.x) blk_mask[static_cast<size_t>(b) * E + i] = s_mask[i];
+
+    // Last block router: counts, schedule, rows; then re-arm every ticket.
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(&tickets[kMidBlocks], 1u) == static_cast<unsigned>(nblk - 1)) ? 1 : 0;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int i = tid; i < E; i += blockDim.x) {
+        int c = 0;
+        for (int bb = 0; bb < nblk; ++bb) c += __popc(__ldcg(blk_mask + static_cast<size_t>(bb) * E + i));
+        totals[i] = c;
+        seg_off_s[i] = 0;
+        expert_totals[i] = c;
+    }
+    __syncthreads();
     if (tid == 0) {
         build_schedule(sched, totals, T, n_shared, first_expert, local_E, shared_base, bn, mb1, mb2, seg_off_s);
-        *ticket = 0u;  // every CTA has taken its ticket: re-arm for the next launch
+        for (int i = 0; i <= kMidBlocks; ++i) tickets[i] = 0u;  // every CTA has taken its tickets
     }
     __syncthreads();
     const int n_pairs = T * K;
     for (int q = tid; q < n_pairs; q += blockDim.x) {
-        const int t = q / K;
-        const int eq = topk_idx[q];  // this CTA's own writes, ordered by the barrier
+        const int tq = q / K;
+        const int eq = __ldcg(topk_idx + q);  // written by the block routers, published by the ticket
         if (eq < first_expert || eq >= first_expert + local_E) {
             if (slot_row != nullptr) slot_row[q] = -1;
             continue;
         }
-        int rank = __popc(s_mask[eq][t >> 5] & ((1u << (t & 31)) - 1u));
-        for (int wd = 0; wd < (t >> 5); ++wd) rank += __popc(s_mask[eq][wd]);
+        const int bq = tq / kRouteTile;
+        int rank = __popc(__ldcg(blk_mask + static_cast<size_t>(bq) * E + eq) & ((1u << (tq % kRouteTile)) - 1u));
+        for (int bb = 0; bb < bq; ++bb) rank += __popc(__ldcg(blk_mask + static_cast<size_t>(bb) * E + eq));
         const int row = seg_off_s[eq] + rank;
-        row_token[row] = t;
-        row_weight[row] = topk_w[q];
+        row_token[row] = tq;
+        row_weight[row] = __ldcg(topk_w + q);
         if (slot_row != nullptr) slot_row[q] = row;
     }
 }
@@ -1020,25 +1029,27 @@ template <typename XT, int EPL>
 cudaError_t launch_route_mid_t(const XT* x, const float* w, const float* bias, float* logits, int tokens, int hidden,
                                RouterParams rp, int32_t* topk_idx, float* topk_w, int32_t* expert_totals,
                                Schedule* sched, int32_t* row_token, float* row_weight, int32_t* slot_row,
-                               float* y_zero, unsigned int* ticket, int n_shared, int first_expert, int local_experts,
-                               int shared_base, int bn, int mb1, int mb2, cudaStream_t stream, bool pdl) {
-    const int parts = (tokens + kMidTokensPerCta - 1) / kMidTokensPerCta;
-    const dim3 grid(static_cast<unsigned>(rp.experts * parts));
+                               float* y_zero, unsigned int* tickets, uint32_t* blk_mask, int n_shared,
+                               int first_expert, int local_experts, int shared_base, int bn, int mb1, int mb2,
+                               cudaStream_t stream, bool pdl) {
+    const int nblk = (tokens + kRouteTile - 1) / kRouteTile;
+    const dim3 grid(static_cast<unsigned>(rp.experts * nblk));
     return launch_k(route_mid_kernel<XT, EPL>, grid, dim3(kSmallThreads), stream, pdl, x, w, bias, logits, tokens,
                     hidden, rp, topk_idx, topk_w, expert_totals, sched, row_token, row_weight, slot_row, y_zero,
-                    ticket, n_shared, first_expert, local_experts, shared_base, bn, mb1, mb2);
+                    tickets, blk_mask, n_shared, first_expert, local_experts, shared_base, bn, mb1, mb2);
 }
 
 template <typename XT>
 cudaError_t route_mid_dispatch(const XT* x, const float* w, const float* bias, float* logits, int tokens, int hidden,
                                RouterParams rp, int32_t* topk_idx, float* topk_w, int32_t* expert_totals,
                                Schedule* sched, int32_t* row_token, float* row_weight, int32_t* slot_row,
-                               float* y_zero, unsigned int* ticket, int n_shared, int first_expert, int local_experts,
-                               int shared_base, int bn, int mb1, int mb2, cudaStream_t stream, bool pdl) {
+                               float* y_zero, unsigned int* tickets, uint32_t* blk_mask, int n_shared,
+                               int first_expert, int local_experts, int shared_base, int bn, int mb1, int mb2,
+                               cudaStream_t stream, bool pdl) {
 #define LM_ROUTE_MID(EPL)                                                                                        \
     launch_route_mid_t<XT, EPL>(x, w, bias, logits, tokens, hidden, rp, topk_idx, topk_w, expert_totals, sched, \
-                                row_token, row_weight, slot_row, y_zero, ticket, n_shared, first_expert,        \
-                                local_experts, shared_base, bn, mb1, mb2, stream, pdl)
+                                row_token, row_weight, slot_row, y_zero, tickets, blk_mask, n_shared,           \
+                                first_expert, local_experts, shared_base, bn, mb1, mb2, stream, pdl)
     switch (experts_per_lane(rp.experts)) {
         case 1: return LM_ROUTE_MID(1);
         case 2: return LM_ROUTE_MID(2);
@@ -1051,18 +1062,18 @@ cudaError_t route_mid_dispatch(const XT* x, const float* w, const float* bias, f
 cudaError_t launch_route_mid(const uint16_t* x, const float* x_f32, const float* w, const float* bias, float* logits,
                              int tokens, int hidden, RouterParams rp, int32_t* topk_idx, float* topk_w,
                              int32_t* expert_totals, Schedule* sched, int32_t* row_token, float* row_weight,
-                             int32_t* slot_row, float* y_zero, unsigned int* ticket, int n_shared, int first_expert,
-                             int local_experts, int shared_base, int bn, int mb1, int mb2, cudaStream_t stream,
-                             bool pdl) {
+                             int32_t* slot_row, float* y_zero, unsigned int* tickets, uint32_t* blk_mask,
+                             int n_shared, int first_expert, int local_experts, int shared_base, int bn, int mb1,
+                             int mb2, cudaStream_t stream, bool pdl) {
     if (tokens <= 0) return cudaSuccess;
     if (tokens > kRouteMidTokens || rp.experts > kMaxExperts || rp.top_k > kMaxTopK || hidden % 8 != 0)
         return cudaErrorInvalidValue;
     if (x_f32 != nullptr)
         return route_mid_dispatch<float>(x_f32, w, bias, logits, tokens, hidden, rp, topk_idx, topk_w, expert_totals,
-                                         sched, row_token, row_weight, slot_row, y_zero, ticket, n_shared,
+                                         sched, row_token, row_weight, slot_row, y_zero, tickets, blk_mask, n_shared,
                                          first_expert, local_experts, shared_base, bn, mb1, mb2, stream, pdl);
     return route_mid_dispatch<uint16_t>(x, w, bias, logits, tokens, hidden, rp, topk_idx, topk_w, expert_totals,
-                                        sched, row_token, row_weight, slot_row, y_zero, ticket, n_shared,
+                                        sched, row_token, row_weight, slot_row, y_zero, tickets, blk_mask, n_shared,
                                         first_expert, local_experts, shared_base, bn, mb1, mb2, stream, pdl);
 }
 

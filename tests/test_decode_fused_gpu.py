@@ -4,7 +4,7 @@ Parity against the oracle across the token counts that change its work split (on
 token, one token-tile boundary, the largest batch it takes), with a logit bias, with
 group-limited and renormalised routing, with accumulation into y, with f32 router
 activations (the block path), and against the grouped multi-launch path it
-replaces.  Its phase trace is checked for ordering.  Mid-size batches (33-128
+replaces.  Its phase trace is checked for ordering.  Mid-size batches (33-256
 tokens) route in one launch too, checked here the same way.
 """
 import os
@@ -141,11 +141,11 @@ def test_fused_group_limited_routing(oracle_lib, normalize):
     layer.close()
 
 
-@pytest.mark.parametrize("T,normalize", [(33, False), (100, True), (128, False)])
+@pytest.mark.parametrize("T,normalize", [(33, False), (100, True), (128, False), (256, True)])
 def test_mid_batch_single_launch_routing(oracle_lib, T, normalize):
-    """32 < T <= 128 routes in one launch (logits over token blocks of 128, top-k,
-    counts, schedule, rows), then the grouped GEMMs: group-limited routing with a
-    logit bias, and the forward's own expert histogram against the oracle's."""
+    """32 < T <= 256 routes in one launch (logits and routing per 32-token block,
+    then counts, schedule and rows), then the grouped GEMMs: group-limited routing
+    with a logit bias, and the forward's own expert histogram against the oracle's."""
     W = syn.layer_weights(GROUPED, seed=41, std=0.05)
     cfg = MoeConfig.from_shape(GROUPED, max_tokens=256, topk_method="group_limited_greedy", n_group=8,
                                topk_group=3, norm_topk_prob=normalize, routed_scaling_factor=1.0)
