@@ -72,15 +72,20 @@ def kernels_per_forward(tokens: int, world: int, experts: int = 64, top_k: int =
     the routing (fused route kernel for T <= 32, else four kernels), then with the
     fixed-capacity exchange (small batches) pack, sort, device schedule, two GEMMs
     and the combine, or with the host-planned exchange the row gather (when the
-    placement does not copy), sort, two GEMMs and the combine."""
+    placement does not copy), a sort and two GEMMs per chunk of local experts (plus
+    the shared experts' two GEMMs when chunked) and the combine."""
     gather = 0 if tokens > 32 and 2 * tokens >= 32 * sms else 1
     if world == 1:
         return 1 if tokens <= 32 else 4 if tokens <= 256 else 6 + gather
     route = 1 if tokens <= 32 else 4
-    fixed = world * tokens * min(top_k, experts // world) <= 8192
+    local = experts // world
+    fixed = world * tokens * min(top_k, local) <= 8192
     if fixed:
         return route + 6
-    return route + gather + 4
+    # Host-planned: per chunk of local experts a sort and two GEMMs; with more than one
+    # chunk the shared experts get GEMMs of their own.
+    chunks = max(1, min(int(os.environ.get("LITEMIND_B200_EP_CHUNKS", "2")), 8, local))
+    return route + gather + 3 * chunks + (2 if chunks > 1 else 0) + 1
 
 
 def parse_args(argv=None):
