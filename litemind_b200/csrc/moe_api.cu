@@ -1588,6 +1588,7 @@ lm_status lm_moe_sync(lm_moe_ctx* ctx, void* stream) {
         // An aborted fused decode launch leaves its grid counters short: restart them.
         LM_CUDA(ctx, cudaMemset(ctx->grid_bar, 0, 3 * sizeof(unsigned long long)));
         LM_CUDA(ctx, cudaMemset(ctx->split_ticket, 0, kSplitTickets * sizeof(int32_t)));
+        LM_CUDA(ctx, cudaMemset(ctx->ticket, 0, kRouteTickets * sizeof(unsigned int)));
         ctx->decode_epoch = 0;
         const char* what = status == kDevBadTile  ? "a tile outside the schedule"
                            : status == kDevBadRow ? "an output row outside its buffer"
