@@ -134,6 +134,12 @@ def test_ep_protocol_two_gloo_ranks(token_counts, chunks):
     mp.spawn(_worker, args=(2, _free_port(), token_counts, chunks), nprocs=2, join=True)
 
 
+# Four ranks of 2 local experts each, in one piece and in 2 chunks of one expert.
+@pytest.mark.parametrize("chunks", [1, 2])
+def test_ep_protocol_four_gloo_ranks(chunks):
+    mp.spawn(_worker, args=(4, _free_port(), (11, 0, 6, 19), chunks), nprocs=4, join=True)
+
+
 def test_ep_chunk_plan_layout():
     """Chunk plans partition the whole plan: per destination, the chunks' send ranges
     tile the whole send range in order; the receive buffer holds the chunks back to back."""
