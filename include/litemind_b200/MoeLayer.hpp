@@ -116,7 +116,38 @@ public:
     void ep_init(const void* nccl_unique_id, int32_t rank, int32_t nranks) {
         check(lm_moe_ep_init(ctx_, nccl_unique_id, rank, nranks));
     }
+    /** A fresh 128-byte NCCL id for ep_init (rank 0 makes it and shares it). */
+    static std::vector<char> ep_unique_id() {
+        std::vector<char> id(128);
+        const lm_status st = lm_moe_ep_unique_id(id.data());
+        if (st != LM_OK) throw Error(st, std::string("lm_moe_ep_unique_id: ") + lm_status_string(st));
+        return id;
+    }
     void sync(void* stream = nullptr) { check(lm_moe_sync(ctx_, stream)); }
+
+    /** Tokens routed to each of the `experts` experts by the last route or forward. */
+    [[nodiscard]] std::vector<int32_t> expert_counts(int32_t experts) const {
+        std::vector<int32_t> counts(static_cast<size_t>(experts));
+        check(lm_moe_expert_counts(ctx_, counts.data()));
+        return counts;
+    }
+    /** Per-slot device time (ms) and launch counts while profiling (lm_moe_profile_*). */
+    void profile(bool enable) { check(lm_moe_profile_enable(ctx_, enable ? 1 : 0)); }
+    std::vector<double> profile_read(bool reset = true, std::vector<int64_t>* launches = nullptr) {
+        std::vector<double> ms(LM_PROFILE_SLOTS);
+        std::vector<int64_t> n(LM_PROFILE_SLOTS);
+        check(lm_moe_profile_read(ctx_, ms.data(), n.data(), reset ? 1 : 0));
+        if (launches != nullptr) *launches = std::move(n);
+        return ms;
+    }
+    /** Step times of the last profiled chunked expert-parallel forward (empty if none). */
+    std::vector<float> profile_ep_timeline() {
+        std::vector<float> ms(LM_EP_TIMELINE_MAX);
+        int32_t chunks = 0;
+        check(lm_moe_profile_ep_timeline(ctx_, ms.data(), LM_EP_TIMELINE_MAX, &chunks));
+        ms.resize(chunks > 0 ? static_cast<size_t>(4 * chunks + 2) : 0);
+        return ms;
+    }
 
     [[nodiscard]] lm_moe_ctx* handle() const noexcept { return ctx_; }
 
@@ -131,5 +162,20 @@ private:
 
     lm_moe_ctx* ctx_{nullptr};
 };
+
+/** The exchange plan of one expert-parallel forward, or of one chunk of it (host only;
+ *  lm_moe_ep_plan / lm_moe_ep_chunk_plan).  send counts: [E] this rank's rows per
+ *  expert; recv counts: [nranks, E / nranks] rows each rank sends to this rank's experts. */
+inline lm_ep_plan ep_plan(int32_t nranks, const std::vector<int32_t>& send_expert_counts,
+                          const std::vector<int32_t>& recv_expert_counts, int32_t chunks = 1, int32_t chunk = 0) {
+    lm_ep_plan plan{};
+    if (send_expert_counts.size() != recv_expert_counts.size())
+        throw Error(LM_ERR_INVALID_ARGUMENT, "ep_plan: send and receive counts differ in length");
+    const auto experts = static_cast<int32_t>(send_expert_counts.size());
+    const lm_status st = lm_moe_ep_chunk_plan(nranks, experts, chunks, chunk, send_expert_counts.data(),
+                                              recv_expert_counts.data(), &plan);
+    if (st != LM_OK) throw Error(st, std::string("lm_moe_ep_chunk_plan: ") + lm_status_string(st));
+    return plan;
+}
 
 }  // namespace litemind::b200

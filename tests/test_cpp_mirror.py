@@ -3,7 +3,7 @@ g++ against include/ and liblitemind_b200.so.  ExpertCacheTest replays the
 reference's ExpertCache statistics (CPU); SafeTensorsTest looks up checkpoint tensors
 through the C ABI (CPU); MoeRouterTest runs the reference's routing checks on the GPU.
 CopyPoolTest checks the weight upload's host copy threads (CPU, built from source
-under ThreadSanitizer)."""
+under ThreadSanitizer); EpPlanTest the expert-parallel plans through MoeLayer.hpp (CPU)."""
 import json
 import os
 import subprocess
@@ -74,3 +74,9 @@ def test_copy_pool_threads(tmp_path):
     res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert res.returncode == 0, res.stdout + res.stderr
     assert "CopyPoolTest: all checks passed" in res.stdout
+
+
+def test_ep_plan_from_cpp(tmp_path):
+    exe = _compile("EpPlanTest", tmp_path)
+    res = subprocess.run([exe], capture_output=True, text=True, timeout=60)
+    assert res.returncode == 0, res.stdout + res.stderr
