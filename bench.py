@@ -3,42 +3,44 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
 
-Workload: one DeepSeek-V2-Lite MoE layer -- 64 routed experts
-(gate/up [1408, 2048], down [2048, 1408] bf16), 2 shared experts, router [64, 2048]
-f32, softmax top-6, no renormalisation -- with weights N(0, 0.02) seed 0 and
-activations N(0, 1) bf16 seed 1.  A step is one forward of the layer over T tokens
-(default 32, the decode batch the north star's HBM target names); the sweep
-T in {1, 8, 32, 256} is reported under "sweep".  Weights and activations are
-synthetic (no checkpoint exists on the box).  L2 is flushed before every timed
-step, outside its events: a 256 MiB write, then a 256 MiB read of another buffer,
-so each step starts with a cold and clean L2 (no dirty lines of the flush left to
-write back inside the step) and streams its experts from HBM.
+The layer: 64 routed experts (gate/up [1408, 2048], down [2048, 1408] bf16), 2 shared
+experts, router [64, 2048] f32, softmax top-6, no renormalisation, scaling 1.0, with
+weights N(0, 0.02) and activations N(0, 1) rounded to bf16 -- synthetic and seeded,
+as no checkpoint exists on the box.  A step is one forward of the layer over a batch
+of T tokens already resident in HBM.  L2 is flushed before every timed step, outside
+its events (a 256 MiB write, then a 256 MiB read of another buffer), so each step
+starts cold and clean and streams its experts from HBM.
+
+One GPU (the default): the headline is the 128-token layer (weights seed 0, tokens
+seed 0), HBM-bound.  The same line carries
+  sweep      the decode sizes T in {1, 8, 32, 256} (tokens seed 1), HBM GB/s each
+  prefill    16384 tokens (seed 2) whose expert load is skewed to Zipf(1.2) by a
+             per-expert logit bias: tensor-bound, TFLOP/s against the measured
+             dense bf16 burst peak (the launches are milliseconds long)
+  ep_base    the expert-parallel per-rank workload (8192 tokens, weights and tokens
+             seed 3) on this one GPU: the base of the weak-scaling series
+  parity     sampled tokens of the headline batch against the CPU oracle
+N > 1 GPUs (torchrun, one rank per GPU): expert parallelism, rank r holding routed
+experts [r*64/N, (r+1)*64/N) and the shared experts; every rank forwards 8192 tokens
+of its own per step (weights and tokens seed 3; random router, so near-uniform
+routing), exchanging token rows and expert outputs with NCCL over NVLink.  Scaling is
+weak (tokens per GPU fixed).  Every rank checks sampled tokens against the oracle
+and the line reports the worst over ranks.
 
 --impl ours (default): the CUDA path through liblitemind_b200.so.
   value      tokens/s over all ranks, device time from CUDA events per step
   e2e        tokens/s through lm_moe_forward_host from pinned host buffers
              (host->device copy of x, device->host copy of y, inside the timing)
-  roofline   the dominant kernel (the gate/up grouped GEMM): algorithmic bytes
-             per launch / its mean CUDA-event duration, against MEASURED_PEAKS.json
+  roofline   the dominant kernel: algorithmic bytes per launch / its mean device
+             time, against MEASURED_PEAKS.json
   cpu_baseline  the reference's own CPU code (oracle/_ref, built from the
              reference's sources) on the host's cores, rank 0, N=1 only
---impl reference: the reference CPU path alone, same metric and config.
+--impl reference: the reference CPU path alone (rank 0), same metric and workload,
+a bounded sample of the batch per step.
 
---workload prefill: T=16384 tokens (seed 2) with a per-expert
-logit bias that skews expert load to Zipf(1.2); the roofline is tensor-bound
-(FLOPs against the measured dense bf16 peak).  --workload stack: config 4.
---workload ffn: the dense layer-0 feed-forward (intermediate 10944) through
-lm_ffn_forward, with the reference's feed_forward timed on the host beside it.
---workload load: lm_moe_load_safetensors of one layer (GB/s against a plain pinned
-host -> device copy).
-
-With N > 1 (torchrun, one rank per GPU) each rank runs the same per-rank workload
-(T tokens of its own) under expert parallelism: rank r holds routed experts
-[r*64/N, (r+1)*64/N) and the shared experts, and every forward exchanges token rows
-and expert outputs with NCCL all-to-all over NVLink (BASELINE config 3's scheme;
-config 3's own size is --tokens 8192, where the exchange runs in chunks of local
-experts overlapped with the GEMMs and roofline.ep_timeline_ms shows the overlap).
-Scaling is weak: tokens per GPU fixed.
+Other workloads: --workload prefill (the 16384-token Zipf batch as the headline),
+stack (26 x (RMSNorm, MoE layer, residual) at 4096 tokens, seed 4), ffn (the dense
+layer-0 feed-forward), load (the SafeTensors -> HBM loader).
 """
 from __future__ import annotations
 
@@ -57,9 +59,15 @@ if ROOT not in sys.path:
 
 METRIC = "MoE-layer tokens/s (V2-Lite shape) + % HBM/TC roofline at 1/2/4/8 B200"
 SEED_WEIGHTS = 0
-SEED_TOKENS = 1
-SEED_PREFILL = 2  # config 2: tokens and the Zipf logit bias
+SEED_HEADLINE = 0   # the 128-token headline batch
+SEED_SWEEP = 1      # the decode sweep's batches
+SEED_PREFILL = 2    # the prefill batch and its Zipf logit bias
+SEED_EP = 3         # the expert-parallel workload: weights and every rank's tokens
+HEADLINE_TOKENS = 128
 SWEEP = (1, 8, 32, 256)
+PREFILL_TOKENS = 16384
+EP_TOKENS = 8192
+PARITY_SAMPLES = 8
 FLUSH_BYTES = 256 << 20
 
 
@@ -94,15 +102,19 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=None,
-                    help="tokens per rank per step (default 32 for decode, 16384 for prefill, 4096 for stack)")
+                    help="tokens per rank per step (default: 128 on one GPU, 8192 per rank on several; 16384 "
+                         "for prefill, 4096 for stack)")
     ap.add_argument("--workload", choices=["decode", "prefill", "stack", "ffn", "load"], default="decode",
-                    help="decode: one MoE layer (BASELINE config 1, headline); prefill: one layer at 16384 "
-                         "tokens with Zipf expert load (config 2, tensor-bound); stack: 26 x (RMSNorm, MoE, "
-                         "residual) (config 4); ffn: the dense layer-0 feed-forward; load: the SafeTensors "
-                         "-> HBM loader")
+                    help="decode: one MoE layer (the headline; expert parallel on several GPUs); prefill: one "
+                         "layer at 16384 tokens with Zipf expert load (tensor-bound); stack: 26 x (RMSNorm, "
+                         "MoE, residual); ffn: the dense layer-0 feed-forward; load: the SafeTensors -> HBM "
+                         "loader")
     ap.add_argument("--layers", type=int, default=26, help="blocks in the stack workload")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill object of the one-GPU line")
+    ap.add_argument("--no-ep-base", action="store_true", help="skip the one-GPU expert-parallel base")
+    ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--clock-window", type=float, default=1.5,
@@ -256,13 +268,13 @@ def run_reference_arm(args, rank: int, world: int) -> None:
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         return
 
-    W = syn.layer_weights(syn.V2_LITE, seed=SEED_WEIGHTS)
-    prefill = args.workload == "prefill"
-    # Prefill: each step is a bounded 128-token sample of the 16384-token batch.
-    n = min(args.tokens, 128) if prefill else args.tokens
-    x = syn.bf16_to_f32(syn.tokens(syn.V2_LITE, args.tokens, seed=SEED_PREFILL if prefill else SEED_TOKENS))
+    wl = layer_workload(args, world)
+    W = syn.layer_weights(syn.V2_LITE, seed=wl["seed_weights"])
+    # Each step is a bounded sample of the batch: the reference runs a token at a time.
+    n = min(args.tokens, 128)
+    x = syn.bf16_to_f32(syn.tokens(syn.V2_LITE, args.tokens, seed=wl["seed_tokens"]))
     x = x.reshape(args.tokens, -1)[:n]
-    bias = syn.zipf_bias(syn.V2_LITE, seed=SEED_PREFILL) if prefill else None
+    bias = syn.zipf_bias(syn.V2_LITE, seed=SEED_PREFILL) if wl["bias"] else None
     from oracle.oracle import Reference, RouterConfig
 
     ref = Reference()
@@ -279,27 +291,38 @@ def run_reference_arm(args, rank: int, world: int) -> None:
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(args, world),
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": wl["config"],
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
-                         "sample": f"{args.steps} steps of one {n}-token batch on rank 0's host "
+                         "sample": f"{args.steps} steps of the first {n} tokens of the {args.tokens}-token batch "
+                                   f"on rank 0's host, one host for all {world} rank(s) "
                                    f"({ref.kernel_description()})"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def workload_config(args, world: int) -> dict:
-    prefill = args.workload == "prefill"
-    name = ("config2-prefill: V2-Lite MoE layer, Zipf(1.2) expert load from a per-expert logit bias, tokens per "
-            "rank per step" if prefill else "config1-decode: V2-Lite MoE layer, tokens per rank per step")
-    return {"workload": name, "tokens_per_rank": args.tokens,
-            "global_tokens": args.tokens * world, "seed_weights": SEED_WEIGHTS,
-            "seed_tokens": SEED_PREFILL if prefill else SEED_TOKENS,
-            "experts": "64 routed top-6 + 2 shared, hidden 2048, inter 1408",
-            "l2": "flushed before every timed step (256 MiB write, then 256 MiB read of a second buffer: cold, "
-                  "clean L2), outside the step's events",
-            "parallelism": "single GPU" if world == 1 else
-            f"expert parallel: {64 // world} routed experts per GPU, NCCL all-to-all dispatch/combine"}
+def layer_workload(args, world: int) -> dict:
+    """Seeds, bias and description of the layer workload both arms run."""
+    if args.workload == "prefill":
+        sw, st, bias = SEED_WEIGHTS, SEED_PREFILL, True
+        name = "prefill: V2-Lite MoE layer, Zipf(1.2) expert load from a per-expert logit bias"
+    elif world > 1:
+        sw, st, bias = SEED_EP, SEED_EP, False
+        name = ("expert-parallel: V2-Lite MoE layer, 64/N routed experts per GPU, NCCL all-to-all dispatch and "
+                "return, random router (near-uniform routing)")
+    else:
+        sw, st, bias = SEED_WEIGHTS, (SEED_HEADLINE if args.tokens == HEADLINE_TOKENS else SEED_SWEEP), False
+        name = "moe-layer: V2-Lite MoE layer on one GPU, HBM-bound batch"
+    config = {"workload": name, "tokens_per_rank": args.tokens, "global_tokens": args.tokens * world,
+              "seed_weights": sw, "seed_tokens": st,
+              "experts": "64 routed top-6 + 2 shared, hidden 2048, inter 1408",
+              "l2": "flushed before every timed step (256 MiB write, then 256 MiB read of a second buffer: cold, "
+                    "clean L2), outside the step's events",
+              "parallelism": "single GPU" if world == 1 else
+              f"expert parallel: {64 // world} routed experts per GPU, NCCL all-to-all dispatch/combine"}
+    if world > 1:
+        config["tokens_seed_stream"] = "rank"
+    return {"seed_weights": sw, "seed_tokens": st, "bias": bias, "config": config}
 
 
 # ── our arm ───────────────────────────────────────────────────────────────
@@ -315,21 +338,6 @@ class L2Flush:
     def __call__(self):
         self.w.zero_()
         self.r.sum()
-
-
-def time_forward(layer, x, y, flush, steps: int, torch, bias=None):
-    """Per-step CUDA-event time (ms) of layer.forward, L2 flushed before each step."""
-    total = 0.0
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    for _ in range(steps):
-        flush()
-        start.record()
-        layer.forward(0, x, y=y, bias=bias)
-        end.record()
-        end.synchronize()
-        total += start.elapsed_time(end)
-    return total / steps
 
 
 def device_sms(torch) -> int:
@@ -660,13 +668,142 @@ def run_load(args, rank: int, world: int, local_rank: int) -> int:
     return 0
 
 
+def sampled_parity(y, x_bits, W, rows, bias=None) -> dict:
+    """Output parity of sampled tokens, checked after the timed region by the test
+    suite's oracle checker (tests/parity.py)."""
+    from tests.parity import sampled_oracle_parity
+
+    return sampled_oracle_parity(y, x_bits, W, rows, bias=bias)
+
+
+def kernel_roofline(prof: dict, ms_per_step: float, layer_b: int, gate_up_b: int, peaks: dict) -> dict:
+    """The dominant kernel's roofline from the profiled per-launch device times.  A
+    one-launch step is timed by the step's own events (the kernel is the step); a
+    kernel of a several-launch step by its profiling events, capped at the step time."""
+    total = sum(v[0] for v in prof.values())
+    share = {k: round(v[0] / total, 4) for k, v in prof.items()} if total else {}
+    if "decode_fused" in prof:
+        k_bytes, name, mean = layer_b, ("moe_decode_kernel (fused routing, gathers, tcgen05 gate/up and down, "
+                                        "weighted combine: the whole layer in one cooperative launch)"), ms_per_step
+        how = "one launch per step: the step's CUDA events time the kernel"
+    else:
+        ms, n = prof.get("gemm_gate_up", (0.0, 0))
+        k_bytes, name = gate_up_b, "gemm_gate_up (tcgen05 grouped GEMM, gate/up + SiLU epilogue)"
+        mean = min(ms / max(n, 1), ms_per_step)
+        how = "profiling events around the launch in the same steps, capped at the step time"
+    achieved = k_bytes / (mean / 1e3) / 1e9 if mean > 0 else 0.0
+    return {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} (hbm_gbs)",
+            "bytes_per_launch": k_bytes, "mean_launch_ms": mean, "timing": how, "share_of_step": share}
+
+
+def time_steps(layer, x, y, flush, steps, torch, bias=None, slot=0):
+    """Per-step CUDA-event time (ms) of layer.forward on layer slot `slot`, L2 flushed before each."""
+    total = 0.0
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    for _ in range(steps):
+        flush()
+        start.record()
+        layer.forward(slot, x, y=y, bias=bias)
+        end.record()
+        end.synchronize()
+        total += start.elapsed_time(end)
+    return total / steps
+
+
+def measure_prefill(layer, W, flush, args, torch, peaks) -> dict:
+    """The 16384-token Zipf(1.2) batch on one GPU: tensor-bound, against the burst peak."""
+    import numpy as np
+
+    from litemind_b200 import synthetic as syn
+    from litemind_b200.moe import bf16_tensor
+
+    shape, T = syn.V2_LITE, PREFILL_TOKENS
+    x_bits = syn.tokens(shape, T, seed=SEED_PREFILL)
+    x = bf16_tensor(x_bits)
+    bias_np = syn.zipf_bias(shape, seed=SEED_PREFILL)
+    bias = torch.from_numpy(bias_np).cuda()
+    y = torch.empty((T, shape.hidden), dtype=torch.float32, device="cuda")
+    for _ in range(max(args.warmup, 3)):
+        layer.forward(0, x, y=y, bias=bias)
+    layer.sync()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < args.clock_window:
+        for _ in range(2):
+            flush()
+            layer.forward(0, x, y=y, bias=bias)
+        torch.cuda.synchronize()
+    ms = time_steps(layer, x, y, flush, args.steps, torch, bias=bias)
+    clock_info = clocks.stop()
+    layer.profile(True)
+    layer.profile_read(reset=True)
+    for _ in range(args.steps):
+        flush()
+        layer.forward(0, x, y=y, bias=bias)
+    prof = layer.profile_read(reset=True)
+    layer.profile(False)
+    counts = [int(v) for v in layer.expert_counts()]
+    lf = layer_flops(shape, T)
+    gu_f = gate_up_flops(shape, T)
+    gu_ms, gu_n = prof.get("gemm_gate_up", (0.0, 0))
+    gu_avg = min(gu_ms / max(gu_n, 1), ms)
+    dn_ms, dn_n = prof.get("gemm_down", (0.0, 0))
+    dn_avg = min(dn_ms / max(dn_n, 1), ms)
+    dn_f = 2 * shape.hidden * shape.inter * (shape.top_k + shape.n_shared_experts) * T
+    total = sum(v[0] for v in prof.values())
+    burst, sus = peaks["bf16_tflops"], peaks["bf16_tflops_sustained"]
+    layer_tf = lf / (ms / 1e3) / 1e12
+    out = {
+        "tokens": T, "seed_tokens": SEED_PREFILL, "seed_weights": SEED_WEIGHTS,
+        "expert_load": "Zipf(1.2) from a per-expert logit bias b_e = -1.2 ln(rank_e) over a seeded permutation",
+        "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
+        "roofline": {"bound": "tensor", "achieved": layer_tf, "peak": burst, "unit": "TFLOP/s",
+                     "frac": layer_tf / burst, "peak_source": f"{peaks['source']} (bf16_tflops, burst)",
+                     "frac_of_sustained": layer_tf / sus, "flops_per_step": lf},
+        "kernels": {
+            "gemm_gate_up": {"mean_ms": gu_avg, "tflops": gu_f / (gu_avg / 1e3) / 1e12 if gu_avg else 0.0,
+                             "frac": gu_f / (gu_avg / 1e3) / 1e12 / burst if gu_avg else 0.0},
+            "gemm_down": {"mean_ms": dn_avg, "tflops": dn_f / (dn_avg / 1e3) / 1e12 if dn_avg else 0.0,
+                          "frac": dn_f / (dn_avg / 1e3) / 1e12 / burst if dn_avg else 0.0},
+            "share_of_step": {k: round(v[0] / total, 4) for k, v in prof.items()} if total else {}},
+        "expert_rows": counts, "clocks": clock_info,
+        "gpu_launches_per_step": kernels_per_forward(T, 1),
+    }
+    if not args.no_parity:
+        rows = np.linspace(0, T - 1, PARITY_SAMPLES).astype(int)
+        out["parity"] = sampled_parity(y.cpu().numpy(), x_bits, W, rows, bias=bias_np)
+    return out
+
+
+def measure_ep_base(layer, flush, args, torch) -> dict:
+    """The expert-parallel per-rank workload (8192 tokens, seed 3) on this one GPU:
+    what each rank of the N-GPU runs computes, with every expert local."""
+    from litemind_b200 import synthetic as syn
+    from litemind_b200.moe import bf16_tensor
+
+    shape, T = syn.V2_LITE, EP_TOKENS
+    x = bf16_tensor(syn.tokens(shape, T, seed=SEED_EP, stream=0))
+    y = torch.empty((T, shape.hidden), dtype=torch.float32, device="cuda")
+    for _ in range(3):
+        layer.forward(1, x, y=y)
+    layer.sync()
+    ms = time_steps(layer, x, y, flush, max(5, args.steps // 2), torch, slot=1)
+    return {"tokens": T, "seed": SEED_EP, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
+            "note": "the expert-parallel runs' per-rank workload on one GPU (weights and rank-0 tokens of seed 3): "
+                    "the base of the weak-scaling series"}
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
-    if args.tokens is None:
-        args.tokens = {"decode": 32, "prefill": 16384, "stack": 4096, "ffn": 32, "load": 32}[args.workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.tokens is None:
+        args.tokens = {"decode": HEADLINE_TOKENS if world == 1 else EP_TOKENS, "prefill": PREFILL_TOKENS,
+                       "stack": 4096, "ffn": 32, "load": 32}[args.workload]
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
         return 0
@@ -676,7 +813,10 @@ def main(argv=None) -> int:
         return run_ffn(args, rank, world, local_rank)
     if args.workload == "load":
         return run_load(args, rank, world, local_rank)
+    return run_layer(args, rank, world, local_rank)
 
+
+def run_layer(args, rank: int, world: int, local_rank: int) -> int:
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -703,19 +843,24 @@ def main(argv=None) -> int:
 
     shape = syn.V2_LITE
     T = args.tokens
-    W = syn.layer_weights(shape, seed=SEED_WEIGHTS)
-    max_tokens = max([T] + ([] if args.no_sweep else list(SWEEP)))
-    layer = MoeLayer(MoeConfig(max_tokens=max_tokens), device=local_rank)
+    wl = layer_workload(args, world)
+    prefill = args.workload == "prefill"
+    extras = world == 1 and not prefill  # sweep, prefill and ep_base ride on the one-GPU headline line
+    W = syn.layer_weights(shape, seed=wl["seed_weights"])
+    max_tokens = max([T] + (list(SWEEP) if extras and not args.no_sweep else [])
+                     + ([PREFILL_TOKENS] if extras and not args.no_prefill else [])
+                     + ([EP_TOKENS] if extras and not args.no_ep_base else []))
+    n_slots = 2 if extras and not args.no_ep_base else 1
+    layer = MoeLayer(MoeConfig(max_tokens=max_tokens, num_layers=n_slots), device=local_rank)
     if world > 1:
         uid = [MoeLayer.ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         layer.ep_init(uid[0], rank, world)
     layer.upload_layer(0, W)
-    prefill = args.workload == "prefill"
-    x_bits = syn.tokens(shape, T, seed=SEED_PREFILL if prefill else SEED_TOKENS, stream=rank)
+    x_bits = syn.tokens(shape, T, seed=wl["seed_tokens"], stream=rank)
     x = bf16_tensor(x_bits)
-    bias_np = syn.zipf_bias(shape, seed=SEED_PREFILL) if prefill else None
-    bias = torch.from_numpy(bias_np).cuda() if prefill else None
+    bias_np = syn.zipf_bias(shape, seed=SEED_PREFILL) if wl["bias"] else None
+    bias = torch.from_numpy(bias_np).cuda() if wl["bias"] else None
     y = torch.empty((T, shape.hidden), dtype=torch.float32, device="cuda")
     flush = L2Flush(torch)
 
@@ -733,7 +878,7 @@ def main(argv=None) -> int:
     clocks.start()
     t_load = time.perf_counter()
     while time.perf_counter() - t_load < args.clock_window:
-        for _ in range(20 if not prefill else 2):
+        for _ in range(20 if T <= 1024 else 2):
             flush()
             layer.forward(0, x, y=y, bias=bias)
         torch.cuda.synchronize()
@@ -742,7 +887,7 @@ def main(argv=None) -> int:
     barrier()
     torch.cuda.synchronize()
     wall0 = time.perf_counter()
-    ms = time_forward(layer, x, y, flush, args.steps, torch, bias=bias)
+    ms = time_steps(layer, x, y, flush, args.steps, torch, bias=bias)
     torch.cuda.synchronize()
     barrier()
     wall = time.perf_counter() - wall0
@@ -750,6 +895,7 @@ def main(argv=None) -> int:
     layer.sync()
     ms = max_over_ranks(ms)
     value = T * world / (ms / 1e3)
+    y_host = y.cpu().numpy()
 
     # ── per-launch device times for the roofline (same workload, instrumented) ──
     layer.profile(True)
@@ -758,109 +904,122 @@ def main(argv=None) -> int:
         flush()
         layer.forward(0, x, y=y, bias=bias)
     prof = layer.profile_read(reset=True)
-    # Chunked expert-parallel exchange: per-step device times of the last profiled step.
     ep_timeline = layer.profile_ep_timeline() if world > 1 else None
     layer.profile(False)
     peaks = measured_peaks()
-    total_prof = sum(v[0] for v in prof.values())
-    if "decode_fused" in prof:
-        # T <= 32 on one GPU: the whole layer is one launch (moe_decode_kernel); its
-        # algorithmic bytes are the layer's.
-        k_ms, k_n = prof["decode_fused"]
-        k_bytes = layer_bytes(shape, touched, T)
-        k_name = "moe_decode_kernel (fused route + tcgen05 gate/up + down + combine, one cooperative launch)"
-        k_traffic = committed_traffic(f"decode_fused_T{T}")
-    else:
-        k_ms, k_n = prof.get("gemm_gate_up", (0.0, 0))
-        k_bytes = gate_up_bytes(shape, touched, T)
-        k_name = "gemm_gate_up (tcgen05 grouped GEMM, gate/up + SiLU epilogue)"
-        k_traffic = committed_traffic(f"gemm_gate_up_T{T}")
-    gu_avg = k_ms / max(k_n, 1)
-    achieved = k_bytes / (gu_avg / 1e3) / 1e9 if gu_avg > 0 else 0.0
-    roofline = {"bound": "hbm", "kernel": k_name,
-                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} (hbm_gbs)",
-                "bytes_per_launch": k_bytes, "mean_launch_ms": gu_avg, "traffic": k_traffic,
-                "share_of_step": {k: round(v[0] / total_prof, 4) for k, v in prof.items()} if total_prof else {}}
+    lb = layer_bytes(shape, touched, T)
+    roofline = kernel_roofline(prof, ms, lb, gate_up_bytes(shape, touched, T), peaks)
+    roofline["traffic"] = committed_traffic(("decode_fused_T" if "decode_fused" in prof else "gemm_gate_up_T")
+                                            + str(T))
     if ep_timeline is not None:
         roofline["ep_timeline_ms"] = ep_timeline
         roofline["note"] = ("chunked exchange: the gemm_gate_up slot spans the shared experts' and every chunk's "
                             "GEMMs, overlapped with the NCCL dispatch and return of other chunks")
-    lb = layer_bytes(shape, touched, T)
     layer_roofline = {"bytes": lb, "achieved": lb / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                       "frac": lb / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "touched_experts": touched}
-    if prefill:
-        # Tensor-bound: FLOPs against the measured dense bf16 burst peak (the launch is
-        # timed alone, milliseconds long).
-        gu_f = gate_up_flops(shape, T)
-        gu_ms, gu_n = prof.get("gemm_gate_up", (0.0, 0))
-        gu_avg = gu_ms / max(gu_n, 1)
-        tf = gu_f / (gu_avg / 1e3) / 1e12 if gu_avg > 0 else 0.0
-        # The prefill step runs after seconds of back-to-back steps (the clock window),
-        # under the 1 kW cap: the sustained GEMM figure is the denominator, the burst
-        # fraction is reported beside it.
-        roofline.update({"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops_sustained"],
-                         "unit": "TFLOP/s", "frac": tf / peaks["bf16_tflops_sustained"],
-                         "frac_of_burst": tf / peaks["bf16_tflops"],
-                         "peak_source": f"{peaks['source']} (bf16_tflops_sustained)",
-                         "flops_per_launch": gu_f, "bytes_per_launch": None, "mean_launch_ms": gu_avg,
-                         "kernel": "gemm_gate_up (tcgen05 CTA-pair grouped GEMM, gate/up + SiLU epilogue)",
-                         "traffic": committed_traffic(f"gemm_gate_up_T{T}")})
+    if prefill or world > 1:
+        # Tensor-bound batches: FLOPs against the dense bf16 burst peak (the launches
+        # are milliseconds long), the sustained figure beside it.
         lf = layer_flops(shape, T)
-        layer_roofline = {"flops": lf, "achieved": lf / (ms / 1e3) / 1e12, "peak": peaks["bf16_tflops_sustained"],
-                          "unit": "TFLOP/s", "frac": lf / (ms / 1e3) / 1e12 / peaks["bf16_tflops_sustained"],
-                          "frac_of_burst": lf / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
-                          "expert_rows": [int(v) for v in layer.expert_counts()]}
+        tf = lf / (ms / 1e3) / 1e12
+        layer_roofline = {"flops": lf, "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                          "frac": tf / peaks["bf16_tflops"], "peak_source": f"{peaks['source']} (bf16_tflops, burst)",
+                          "frac_of_sustained": tf / peaks["bf16_tflops_sustained"], "hbm_bytes": lb}
+        if prefill:
+            layer_roofline["expert_rows"] = [int(v) for v in layer.expert_counts()]
+            gu_ms, gu_n = prof.get("gemm_gate_up", (0.0, 0))
+            gu_avg = min(gu_ms / max(gu_n, 1), ms)
+            gu_tf = gate_up_flops(shape, T) / (gu_avg / 1e3) / 1e12 if gu_avg > 0 else 0.0
+            roofline.update({"bound": "tensor", "kernel": "gemm_gate_up (tcgen05 CTA-pair grouped GEMM, gate/up + "
+                                                          "SiLU epilogue)",
+                             "achieved": gu_tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": gu_tf / peaks["bf16_tflops"],
+                             "peak_source": f"{peaks['source']} (bf16_tflops, burst)",
+                             "flops_per_launch": gate_up_flops(shape, T), "bytes_per_launch": None,
+                             "mean_launch_ms": gu_avg})
+        else:
+            # Expert parallel: the step is routing, two exchanges and the grouped GEMMs
+            # overlapped in chunks; the per-rank step is the unit.
+            roofline.update({"bound": "tensor", "kernel": "the expert-parallel step (per rank: routing, NCCL "
+                                                          "dispatch/return overlapped with the tcgen05 grouped GEMMs, "
+                                                          "combine)",
+                             "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": tf / peaks["bf16_tflops"],
+                             "peak_source": f"{peaks['source']} (bf16_tflops, burst)",
+                             "flops_per_launch": lf, "bytes_per_launch": None, "mean_launch_ms": ms,
+                             "timing": "the step's CUDA events, max over ranks"})
 
     # ── end to end through the C ABI with host buffers ──
     x_host = torch.from_numpy(x_bits.view(np.int16)).pin_memory()
-    y_host = torch.empty((T, shape.hidden), dtype=torch.float32).pin_memory()
-    bias_host = torch.from_numpy(bias_np).pin_memory() if prefill else None
-    bias_ptr = bias_host.data_ptr() if prefill else None
-    layer.forward_host_ptr(0, x_host.data_ptr(), T, y_host.data_ptr(), bias_ptr)
+    y_pinned = torch.empty((T, shape.hidden), dtype=torch.float32).pin_memory()
+    bias_host = torch.from_numpy(bias_np).pin_memory() if wl["bias"] else None
+    bias_ptr = bias_host.data_ptr() if wl["bias"] else None
+    layer.forward_host_ptr(0, x_host.data_ptr(), T, y_pinned.data_ptr(), bias_ptr)
     e2e_total = 0.0
     barrier()
     for _ in range(args.steps):
         flush()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        layer.forward_host_ptr(0, x_host.data_ptr(), T, y_host.data_ptr(), bias_ptr)
+        layer.forward_host_ptr(0, x_host.data_ptr(), T, y_pinned.data_ptr(), bias_ptr)
         e2e_total += time.perf_counter() - t0
     e2e_ms = max_over_ranks(1e3 * e2e_total / args.steps)
     e2e = {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
            "h2d_bytes_per_step": T * shape.hidden * 2, "d2h_bytes_per_step": T * shape.hidden * 4,
-           "how": "lm_moe_forward_host from pinned host memory, wall clock per call (copies + sync inside)"}
+           "how": "lm_moe_forward_host from pinned host memory, wall clock per call (copies, status read-back "
+                  "and one synchronisation inside)"}
 
-    # ── decode sweep (config 1) ──
-    sweep = []
-    if not args.no_sweep and world == 1 and not prefill:
+    # ── parity of sampled tokens against the oracle (every rank its own tokens) ──
+    parity = None
+    if not args.no_parity:
+        rows = np.linspace(0, T - 1, min(PARITY_SAMPLES, T)).astype(int)
+        par = sampled_parity(y_host, x_bits, W, rows, bias=bias_np)
+        if world > 1:
+            t = torch.tensor([par["max_rel"], -par["min_cos"], float(not par["pass"])], dtype=torch.float64,
+                             device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            par.update({"max_rel": float(t[0]), "min_cos": float(-t[1]), "pass": bool(t[2] == 0),
+                        "tokens": par["tokens"] * world, "ranks": world,
+                        "exempt_near_ties": "rank 0: " + str(par["exempt_near_ties"])})
+        parity = par
+
+    # ── one-GPU extras: the decode sweep, the prefill batch, the expert-parallel base ──
+    sweep, prefill_obj, ep_base = [], None, None
+    if extras and not args.no_sweep:
         for t in SWEEP:
-            xs = bf16_tensor(syn.tokens(shape, t, seed=SEED_TOKENS, stream=rank))
+            xs = bf16_tensor(syn.tokens(shape, t, seed=SEED_SWEEP))
             ys = torch.empty((t, shape.hidden), dtype=torch.float32, device="cuda")
             for _ in range(3):
                 layer.forward(0, xs, y=ys)
             layer.sync()
             tt = int((layer.expert_counts() > 0).sum())
-            m = max_over_ranks(time_forward(layer, xs, ys, flush, max(5, args.steps // 2), torch))
+            m = time_steps(layer, xs, ys, flush, max(5, args.steps // 2), torch)
             b = layer_bytes(shape, tt, t)
-            sweep.append({"tokens": t, "tokens_per_s": t * world / (m / 1e3), "ms": m, "touched_experts": tt,
-                          "layer_gbs": b / (m / 1e3) / 1e9, "frac_hbm": b / (m / 1e3) / 1e9 / peaks["hbm_gbs"]})
+            sweep.append({"tokens": t, "seed_tokens": SEED_SWEEP, "tokens_per_s": t / (m / 1e3), "ms": m,
+                          "touched_experts": tt, "layer_gbs": b / (m / 1e3) / 1e9,
+                          "frac_hbm": b / (m / 1e3) / 1e9 / peaks["hbm_gbs"]})
+    if extras and not args.no_prefill:
+        prefill_obj = measure_prefill(layer, W, flush, args, torch, peaks)
+    if extras and not args.no_ep_base:
+        layer.upload_layer(1, syn.layer_weights(shape, seed=SEED_EP))
+        ep_base = measure_ep_base(layer, flush, args, torch)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         xf = syn.bf16_to_f32(x_bits).reshape(T, -1)
-        # Prefill: a bounded 256-token sample of the same batch, per-token rate.
-        cpu = cpu_reference_rate(W, xf[:256] if prefill else xf, args.cpu_seconds, bias=bias_np)
+        # A bounded sample (at most 256 tokens) of the same batch, per-token rate.
+        cpu = cpu_reference_rate(W, xf[:256], args.cpu_seconds, bias=bias_np)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(args, world),
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": wl["config"],
         "roofline": roofline, "layer_roofline": layer_roofline, "cpu_baseline": cpu, "e2e": e2e,
         "clocks": clock_info, "gpu_launches": kernels_per_forward(T, world, sms=device_sms(torch)) * args.steps,
-        "sweep": sweep,
-        "wall_s_timed_region": wall,
+        "parity": parity, "wall_s_timed_region": wall,
     }
+    if extras:
+        line.update({"sweep": sweep, "prefill": prefill_obj, "ep_base": ep_base})
     if rank == 0:
         print(json.dumps(line), flush=True)
     layer.close()

@@ -50,9 +50,11 @@ public:
     ~MoeLayer() { lm_moe_destroy(ctx_); }
     MoeLayer(const MoeLayer&) = delete;
     MoeLayer& operator=(const MoeLayer&) = delete;
-    MoeLayer(MoeLayer&& o) noexcept : ctx_(std::exchange(o.ctx_, nullptr)) {}
+    MoeLayer(MoeLayer&& o) noexcept
+        : ctx_(std::exchange(o.ctx_, nullptr)), routed_experts_(std::exchange(o.routed_experts_, 0)) {}
     MoeLayer& operator=(MoeLayer&& o) noexcept {
         std::swap(ctx_, o.ctx_);
+        std::swap(routed_experts_, o.routed_experts_);
         return *this;
     }
 
@@ -125,12 +127,13 @@ public:
     }
     void sync(void* stream = nullptr) { check(lm_moe_sync(ctx_, stream)); }
 
-    /** Tokens routed to each of the `experts` experts by the last route or forward. */
-    [[nodiscard]] std::vector<int32_t> expert_counts(int32_t experts) const {
-        std::vector<int32_t> counts(static_cast<size_t>(experts));
-        check(lm_moe_expert_counts(ctx_, counts.data()));
+    /** Tokens routed to each routed expert by the last route or forward. */
+    [[nodiscard]] std::vector<int32_t> expert_counts() const {
+        std::vector<int32_t> counts(static_cast<size_t>(routed_experts_));
+        check(lm_moe_expert_counts(ctx_, counts.data(), routed_experts_));
         return counts;
     }
+    [[nodiscard]] int32_t routed_experts() const noexcept { return routed_experts_; }
     /** Per-slot device time (ms) and launch counts while profiling (lm_moe_profile_*). */
     void profile(bool enable) { check(lm_moe_profile_enable(ctx_, enable ? 1 : 0)); }
     std::vector<double> profile_read(bool reset = true, std::vector<int64_t>* launches = nullptr) {
@@ -155,12 +158,14 @@ private:
     void create(const lm_moe_config& cfg, int device) {
         const lm_status st = lm_moe_create(&cfg, device, &ctx_);
         if (st != LM_OK) throw Error(st, std::string("lm_moe_create: ") + lm_status_string(st));
+        routed_experts_ = cfg.n_routed_experts;
     }
     void check(lm_status st) const {
         if (st != LM_OK) throw Error(st, lm_moe_last_error(ctx_));
     }
 
     lm_moe_ctx* ctx_{nullptr};
+    int32_t routed_experts_{0};
 };
 
 /** The exchange plan of one expert-parallel forward, or of one chunk of it (host only;

@@ -201,12 +201,28 @@ lm_status lm_moe_block_forward(lm_moe_ctx* ctx, int32_t layer, float* hidden, in
                                void* stream);
 
 /* Waits for the stream and reports a device-side timeout recorded since the last
- * call (then clears it). */
+ * call (then clears it and re-arms the kernels' counters, so the context stays usable). */
 lm_status lm_moe_sync(lm_moe_ctx* ctx, void* stream);
 
-/* Tokens routed to each expert by the last route/forward (host int32 [E]); the
- * per-expert token histogram.  Waits for the device. */
-lm_status lm_moe_expert_counts(lm_moe_ctx* ctx, int32_t* counts);
+/*
+ * Testing hooks for the failure-detection path; production code leaves them at 0.
+ *   LM_DEBUG_GRID_EXTRA     arrivals the fused decode kernel's grid-wide waits expect
+ *                           beyond its own grid (at most 1024).  Nothing provides them,
+ *                           so the waits run out: the kernel records a status code and
+ *                           returns, and lm_moe_sync / lm_moe_forward_host report
+ *                           LM_ERR_DEVICE_TIMEOUT.  0 = off.
+ *   LM_DEBUG_WAIT_LIMIT_NS  bound of those grid-wide waits in ns (0 = the 2 s default,
+ *                           which is also the maximum).
+ * No GPU fault is involved: the kernel only stops waiting.
+ */
+enum { LM_DEBUG_GRID_EXTRA = 1, LM_DEBUG_WAIT_LIMIT_NS = 2 };
+lm_status lm_moe_debug_set(lm_moe_ctx* ctx, int32_t knob, int64_t value);
+
+/* Tokens routed to each expert by the last route/forward: the per-expert token
+ * histogram, written to host int32 counts[0 .. E-1].  `capacity` is the number of
+ * int32 slots at `counts`; a capacity below the context's n_routed_experts is
+ * refused with LM_ERR_INVALID_ARGUMENT and nothing is written.  Waits for the device. */
+lm_status lm_moe_expert_counts(lm_moe_ctx* ctx, int32_t* counts, int32_t capacity);
 
 /* Bytes of weights resident on the device, and bytes uploaded so far. */
 lm_status lm_moe_memory(const lm_moe_ctx* ctx, uint64_t* resident_bytes, uint64_t* uploaded_bytes);
@@ -262,7 +278,9 @@ lm_status lm_moe_profile_ep_timeline(lm_moe_ctx* ctx, float* ms, int32_t capacit
  * the rows in chunks of local experts overlapped with the GEMMs
  * (lm_moe_ep_chunk_plan).  The ranks compare their configs here (one small NCCL
  * exchange) and all fail with LM_ERR_INVALID_ARGUMENT when any differs.  NCCL is
- * loaded at run time (libnccl.so.2).
+ * loaded at run time (libnccl.so.2).  NCCL's copy-engine peer transfers
+ * (NCCL_P2P_USE_CUDA_MEMCPY set to non-zero) are refused with LM_ERR_UNSUPPORTED
+ * before NCCL is touched.
  */
 lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t rank,
                          int32_t nranks);
@@ -327,6 +345,8 @@ lm_status lm_moe_ep_unique_id(void* nccl_unique_id_out);
  * GPU that loads it until the process exits), so: T <= 2047 and T * E <= 262144,
  * else LM_ERR_TOO_MANY_TOKENS.  The first call on a device looks up that array's
  * address (cudaGetSymbolAddress); make that first call before any stream capture.
+ * After a reset of the device (cudaDeviceReset) the next call looks it up again,
+ * so that call too should come before any capture.
  * All calls share the array: calls whose kernels overlap on the GPU (different
  * streams without ordering) race on it and give wrong results.  Errors are
  * status codes only; lm_moe_last_error does not describe them.

@@ -30,6 +30,8 @@ LM_SAFETENSORS_MAX_DIMS = 8
 
 LM_TOPK_GREEDY = 0
 LM_TOPK_GROUP_LIMITED_GREEDY = 1
+LM_DEBUG_GRID_EXTRA = 1
+LM_DEBUG_WAIT_LIMIT_NS = 2
 
 # Every symbol include/litemind_moe.h declares, with (restype, argtypes).
 _vp, _i32, _i64, _f32, _u64p = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.POINTER(C.c_uint64)
@@ -78,7 +80,8 @@ SIGNATURES = {
     "lm_moe_forward_host": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp]),
     "lm_moe_block_forward": (_i32, [_vp, _i32, _vp, _i32, _vp]),
     "lm_moe_sync": (_i32, [_vp, _vp]),
-    "lm_moe_expert_counts": (_i32, [_vp, _vp]),
+    "lm_moe_debug_set": (_i32, [_vp, _i32, _i64]),
+    "lm_moe_expert_counts": (_i32, [_vp, _vp, _i32]),
     "lm_moe_memory": (_i32, [_vp, _u64p, _u64p]),
     "lm_moe_ep_init": (_i32, [_vp, _vp, _i32, _i32]),
     "lm_moe_ep_unique_id": (_i32, [_vp]),

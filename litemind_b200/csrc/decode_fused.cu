@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int E = args.rp.experts;
     const int K = args.rp.top_k;
     const int G = gridDim.x;
-    const unsigned long long target = args.epoch * static_cast<unsigned long long>(G);
+    const unsigned long long target = static_cast<unsigned long long>(G) + args.grid_extra;
     // Lists: 0 = gate/up (shared experts' tiles, then the routed experts'), 1 = down
     // (routed, then shared).
     const int mb1 = 2 * I / kBlockM;  // 128-row blocks of interleaved gate/up rows
@@ -260,7 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (pend_n == 0) return;
                 if (!h_ready) {
                     if (block) {
-                        if (!grid_wait(args.grid_bar + 1, target, abort_flag, args.status, kDevTimeoutGrid)) {
+                        if (!grid_wait(args.grid_bar + 1, target, abort_flag, args.status, kDevTimeoutGrid,
+                                       args.wait_limit_ns)) {
                             ok = false;
                             return;
                         }
@@ -455,7 +456,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         arrive_grid(0);
         if (epi_tid == 0) stamp(1);
-        ok = broadcast(epi_tid == 0 ? grid_wait(args.grid_bar, target, abort_flag, args.status, kDevTimeoutGrid)
+        ok = broadcast(epi_tid == 0 ? grid_wait(args.grid_bar, target, abort_flag, args.status, kDevTimeoutGrid,
+                                                args.wait_limit_ns)
                                     : true);
         if (epi_tid == 0) stamp(2);
 
@@ -719,6 +721,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem_base, C::kTmemCols);
     }
+    // Every wait of this CTA is over.  The last CTA to get here has seen every CTA
+    // finish waiting, so it re-arms the counters for the next launch.
+    if (threadIdx.x == 0 &&
+        atom_acq_rel_add_u64(args.grid_bar + 2, 1ull) == static_cast<unsigned long long>(G) - 1ull) {
+        args.grid_bar[0] = 0ull;
+        args.grid_bar[1] = 0ull;
+        args.grid_bar[2] = 0ull;
+        __threadfence();
+    }
 }
 
 template <int BN, int EPL>
@@ -726,12 +737,8 @@ cudaError_t launch_t(const CUtensorMap& w13, const CUtensorMap& w2, const CUtens
                      const DecodeArgs& args, int sms, cudaStream_t stream) {
     using C = DCfg<BN>;
     auto kernel = moe_decode_kernel<BN, EPL>;
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    static std::atomic<uint64_t> configured{0};  // devices whose limit is raised
+    if (const cudaError_t e = set_smem_limit_once(kernel, C::kSmem, configured); e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sms);
     cfg.blockDim = dim3(kThreads);

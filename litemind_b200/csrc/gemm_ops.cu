@@ -24,16 +24,60 @@ __device__ __forceinline__ float widen<uint16_t>(uint16_t v) { return bf16_bits_
 template <>
 __device__ __forceinline__ float widen<float>(float v) { return v; }
 
+// Sixteen bytes of weights widened to f32, multiplied by the matching x values.
+__device__ __forceinline__ float dot16(const uint16_t* w, const float* x, float acc) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(w));
+    const float4 x0 = __ldg(reinterpret_cast<const float4*>(x));
+    const float4 x1 = __ldg(reinterpret_cast<const float4*>(x) + 1);
+    const uint32_t p[4] = {v.x, v.y, v.z, v.w};
+    const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        acc = fmaf(__uint_as_float(p[i] << 16), xs[2 * i], acc);
+        acc = fmaf(__uint_as_float(p[i] & 0xffff0000u), xs[2 * i + 1], acc);
+    }
+    return acc;
+}
+__device__ __forceinline__ float dot16(const float* w, const float* x, float acc) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(w));
+    const float4 xv = __ldg(reinterpret_cast<const float4*>(x));
+    acc = fmaf(v.x, xv.x, acc);
+    acc = fmaf(v.y, xv.y, acc);
+    acc = fmaf(v.z, xv.z, acc);
+    return fmaf(v.w, xv.w, acc);
+}
+
 // One warp per output row; out[r] = (accumulate ? fmaf(scale, dot, out[r]) : dot).
+// A row that starts on a 16-byte boundary (with x aligned too) is read 16 bytes per
+// lane per load -- 512 contiguous bytes per warp instruction, four loads in flight --
+// and its last cols % (16 / sizeof(W)) elements one by one; a row that does not
+// (a ragged width such as 253) is read one element per lane per step, still
+// contiguous across the warp.
 template <typename W>
-__global__ void matvec_kernel(const W* __restrict__ w, const float* __restrict__ x, float* __restrict__ out,
-                              int64_t rows, int64_t cols, float scale, int accumulate) {
+__global__ void __launch_bounds__(256) matvec_kernel(const W* __restrict__ w, const float* __restrict__ x,
+                                                     float* __restrict__ out, int64_t rows, int64_t cols, float scale,
+                                                     int accumulate) {
+    constexpr int V = 16 / static_cast<int>(sizeof(W));
     const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
     const W* wr = w + row * cols;
     float acc = 0.0f;
-    for (int64_t c = lane; c < cols; c += 32) acc = fmaf(widen(wr[c]), x[c], acc);
+    const bool vec = ((reinterpret_cast<uintptr_t>(wr) | reinterpret_cast<uintptr_t>(x)) & 15u) == 0;
+    int64_t c0 = 0;
+    if (vec) {
+        const int64_t nv = cols / V;  // whole vectors in the row
+        int64_t v = lane;
+        float a[4] = {0.f, 0.f, 0.f, 0.f};
+        for (; v + 96 < nv; v += 128) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) a[u] = dot16(wr + (v + 32 * u) * V, x + (v + 32 * u) * V, a[u]);
+        }
+        for (; v < nv; v += 32) a[0] = dot16(wr + v * V, x + v * V, a[0]);
+        acc = (a[0] + a[1]) + (a[2] + a[3]);
+        c0 = nv * V;
+    }
+    for (int64_t c = c0 + lane; c < cols; c += 32) acc = fmaf(widen(wr[c]), x[c], acc);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
     if (lane == 0) out[row] = accumulate ? fmaf(scale, acc, out[row]) : acc;

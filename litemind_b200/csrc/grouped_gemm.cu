@@ -544,12 +544,8 @@ cudaError_t launch_one(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
                        int sms, cudaStream_t stream, bool pdl) {
     using C = Cfg<BN, KIND>;
     auto kernel = moe_gemm_kernel<BN, KIND>;
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    static std::atomic<uint64_t> configured{0};  // devices whose limit is raised
+    if (const cudaError_t e = set_smem_limit_once(kernel, C::kSmemBytes, configured); e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sms);
     cfg.blockDim = dim3(kThreads);

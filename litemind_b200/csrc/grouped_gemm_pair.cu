@@ -379,12 +379,8 @@ cudaError_t launch_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtens
                         int sms, cudaStream_t stream, bool pdl) {
     using C = PCfg<BN, KIND>;
     auto kernel = moe_gemm_pair_kernel<BN, KIND>;
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    static std::atomic<uint64_t> configured{0};  // devices whose limit is raised
+    if (const cudaError_t e = set_smem_limit_once(kernel, C::kSmem, configured); e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sms & ~1);
     cfg.blockDim = dim3(kThreads);

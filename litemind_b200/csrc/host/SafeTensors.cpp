@@ -7,6 +7,7 @@
 #include <unistd.h>
 
 #include <cmath>
+#include <cstdint>
 #include <cstring>
 #include <memory>
 #include <utility>
@@ -322,26 +323,35 @@ bool StShard::open(const std::string& path, std::string& error) {
         if (t.dtype == StDtype::Unknown) return bad("uses an unsupported dtype '" + t.dtype_text + "'.");
         const JValue* sh = entry.get("shape");
         if (sh == nullptr || sh->kind != JValue::Array) return bad("has no shape array.");
+        // Every number below is a JSON double: it must be a non-negative integer no
+        // larger than the shard (2^53 bounds what a double holds exactly), checked
+        // before any cast; products are checked against overflow.
+        constexpr double kExact = 9007199254740992.0;  // 2^53
+        auto whole = [](const JValue& v) {
+            return v.kind == JValue::Number && v.number >= 0 && v.number == std::floor(v.number) && v.number <= kExact;
+        };
         uint64_t count = 1;
         for (const JValue& d : sh->items) {
-            if (d.kind != JValue::Number || d.number < 0 || d.number != std::floor(d.number))
-                return bad("has a non-numeric dimension.");
-            t.shape.push_back(static_cast<int64_t>(d.number));
-            count *= static_cast<uint64_t>(d.number);
+            if (!whole(d)) return bad("has a non-numeric dimension.");
+            const uint64_t dim = static_cast<uint64_t>(d.number);
+            t.shape.push_back(static_cast<int64_t>(dim));
+            if (dim != 0 && count > UINT64_MAX / dim) return bad("has a shape whose element count overflows.");
+            count *= dim;
         }
         const JValue* off = entry.get("data_offsets");
-        if (off == nullptr || off->kind != JValue::Array || off->items.size() != 2 ||
-            off->items[0].kind != JValue::Number || off->items[1].kind != JValue::Number)
+        if (off == nullptr || off->kind != JValue::Array || off->items.size() != 2 || !whole(off->items[0]) ||
+            !whole(off->items[1]))
             return bad("has a malformed data_offsets pair.");
         const uint64_t b = static_cast<uint64_t>(off->items[0].number);
         const uint64_t e = static_cast<uint64_t>(off->items[1].number);
         if (e < b) return bad("has data_offsets in descending order.");
+        if (payload > size_ || e > size_ - payload) return bad("extends past the end of the shard.");
+        if (count > UINT64_MAX / elem) return bad("has a shape whose byte size overflows.");
         t.offset = payload + b;
         t.nbytes = count * elem;
         if (t.nbytes != e - b)
             return bad("declares " + std::to_string(e - b) + " payload bytes but its shape and dtype need " +
                        std::to_string(t.nbytes) + ".");
-        if (t.offset > size_ || t.nbytes > size_ - t.offset) return bad("extends past the end of the shard.");
         t.data = map_ + t.offset;
         tensors_.push_back(std::move(t));
     }

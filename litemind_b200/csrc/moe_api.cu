@@ -94,8 +94,11 @@ struct lm_moe_ctx {
     int32_t* status = nullptr;
     int split_max_waves = 4;          // split-K below this many waves of tiles (LITEMIND_B200_SPLIT_WAVES)
     bool fused_decode = true;         // T <= 32 on one GPU: one cooperative launch (LITEMIND_B200_FUSED_DECODE=0: off)
-    unsigned long long* grid_bar = nullptr;  // the fused decode kernel's arrival counters
-    unsigned long long decode_epoch = 0;     // fused decode launches so far (their counter targets)
+    unsigned long long* grid_bar = nullptr;  // the fused decode kernel's arrival counters (self-resetting)
+    // Testing only (lm_moe_debug_set): arrivals the fused kernel's grid waits expect
+    // beyond the grid (so the waits run out), and the bound of those waits (0: 2 s).
+    uint32_t debug_grid_extra = 0;
+    uint64_t debug_wait_limit_ns = 0;
     unsigned long long* decode_trace = nullptr;  // per-CTA phase stamps of the last fused launch (profiling)
     std::vector<lm::DenseWeights> dense;  // dense feed-forward layers (lm_ffn_*)
     uint16_t* dense_h = nullptr;       // [max_tokens, widest dense inter] SwiGLU outputs
@@ -122,6 +125,7 @@ struct lm_moe_ctx {
     uint16_t* x_stage = nullptr;
     float* y_stage = nullptr;
     float* bias_stage = nullptr;
+    int32_t* status_host = nullptr;  // pinned: the status word read back with y, one sync per host call
     float* norm_f32 = nullptr;
     uint16_t* norm_bf16 = nullptr;
     cudaStream_t own_stream = nullptr;
@@ -449,6 +453,25 @@ lm_status upload_shared_and_router(lm_moe_ctx* ctx, LayerWeights& L, const float
     L.router_loaded = true;
     return LM_OK;
 }
+
+// A status word the device recorded (already read back): on an error, clear it and
+// re-arm every counter an aborted launch may have left short, then report it.
+lm_status settle_status(lm_moe_ctx* ctx, int32_t status) {
+    if (status != 0) {
+        LM_CUDA(ctx, cudaMemset(ctx->status, 0, sizeof(int32_t)));
+        // An aborted fused decode launch leaves its grid counters short: restart them.
+        LM_CUDA(ctx, cudaMemset(ctx->grid_bar, 0, 3 * sizeof(unsigned long long)));
+        LM_CUDA(ctx, cudaMemset(ctx->split_ticket, 0, kSplitTickets * sizeof(int32_t)));
+        LM_CUDA(ctx, cudaMemset(ctx->ticket, 0, kRouteTickets * sizeof(unsigned int)));
+        const char* what = status == kDevBadTile  ? "a tile outside the schedule"
+                           : status == kDevBadRow ? "an output row outside its buffer"
+                                                  : "a bounded wait expired";
+        return fail(ctx, LM_ERR_DEVICE_TIMEOUT,
+                    std::string("a kernel stopped on ") + what + " (code " + std::to_string(status) +
+                        "); results are invalid");
+    }
+    return LM_OK;
+}
 }  // namespace
 }  // namespace lm
 
@@ -577,6 +600,7 @@ lm_status lm_moe_destroy(lm_moe_ctx* ctx) {
     if (ctx->x_stage) cudaFree(ctx->x_stage);
     if (ctx->y_stage) cudaFree(ctx->y_stage);
     if (ctx->bias_stage) cudaFree(ctx->bias_stage);
+    if (ctx->status_host) cudaFreeHost(ctx->status_host);
     if (ctx->norm_f32) cudaFree(ctx->norm_f32);
     if (ctx->norm_bf16) cudaFree(ctx->norm_bf16);
     if (ctx->decode_trace) cudaFree(ctx->decode_trace);
@@ -1066,7 +1090,8 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
         a.split_ws = ctx->split_ws;
         a.split_ticket = ctx->split_ticket;
         a.grid_bar = ctx->grid_bar;
-        a.epoch = ++ctx->decode_epoch;
+        a.grid_extra = ctx->debug_grid_extra;
+        a.wait_limit_ns = ctx->debug_wait_limit_ns != 0 ? ctx->debug_wait_limit_ns : kWaitLimitNs;
         a.status = ctx->status;
         if (ctx->profiling && ctx->decode_trace == nullptr)
             LM_CUDA(ctx, cudaMalloc(&ctx->decode_trace, static_cast<size_t>(ctx->sms) * kDecodeTraceSlots * 8));
@@ -1532,6 +1557,7 @@ lm_status lm_moe_forward_host(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x_
         LM_CUDA(ctx, cudaMalloc(&ctx->x_stage, T * H * sizeof(uint16_t)));
         LM_CUDA(ctx, cudaMalloc(&ctx->y_stage, T * H * sizeof(float)));
         LM_CUDA(ctx, cudaMalloc(&ctx->bias_stage, static_cast<size_t>(c.n_routed_experts) * sizeof(float)));
+        LM_CUDA(ctx, cudaMallocHost(&ctx->status_host, sizeof(int32_t)));
         LM_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking));
     }
     cudaStream_t s = ctx->own_stream;
@@ -1546,8 +1572,12 @@ lm_status lm_moe_forward_host(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x_
     st = ctx->nranks > 1 ? forward_ep(ctx, layer, ctx->x_stage, nullptr, tokens, bias, ctx->y_stage, 0, s)
                          : forward_impl(ctx, layer, ctx->x_stage, nullptr, tokens, bias, ctx->y_stage, 0, s);
     if (st != LM_OK) return st;
+    // y and the status word come back in the same stream order: one synchronisation
+    // covers both.
     LM_CUDA(ctx, cudaMemcpyAsync(y_host, ctx->y_stage, n * sizeof(float), cudaMemcpyDeviceToHost, s));
-    return lm_moe_sync(ctx, s);
+    LM_CUDA(ctx, cudaMemcpyAsync(ctx->status_host, ctx->status, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    LM_CUDA(ctx, cudaStreamSynchronize(s));
+    return settle_status(ctx, *ctx->status_host);
 }
 
 lm_status lm_moe_block_forward(lm_moe_ctx* ctx, int32_t layer, float* hidden, int32_t tokens, void* stream) {
@@ -1583,25 +1613,32 @@ lm_status lm_moe_sync(lm_moe_ctx* ctx, void* stream) {
     LM_CUDA(ctx, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
     int32_t status = 0;
     LM_CUDA(ctx, cudaMemcpy(&status, ctx->status, sizeof(status), cudaMemcpyDeviceToHost));
-    if (status != 0) {
-        LM_CUDA(ctx, cudaMemset(ctx->status, 0, sizeof(int32_t)));
-        // An aborted fused decode launch leaves its grid counters short: restart them.
-        LM_CUDA(ctx, cudaMemset(ctx->grid_bar, 0, 3 * sizeof(unsigned long long)));
-        LM_CUDA(ctx, cudaMemset(ctx->split_ticket, 0, kSplitTickets * sizeof(int32_t)));
-        LM_CUDA(ctx, cudaMemset(ctx->ticket, 0, kRouteTickets * sizeof(unsigned int)));
-        ctx->decode_epoch = 0;
-        const char* what = status == kDevBadTile  ? "a tile outside the schedule"
-                           : status == kDevBadRow ? "an output row outside its buffer"
-                                                  : "a bounded wait expired";
-        return fail(ctx, LM_ERR_DEVICE_TIMEOUT,
-                    std::string("a kernel stopped on ") + what + " (code " + std::to_string(status) +
-                        "); results are invalid");
-    }
-    return LM_OK;
+    return settle_status(ctx, status);
 }
 
-lm_status lm_moe_expert_counts(lm_moe_ctx* ctx, int32_t* counts) {
+lm_status lm_moe_debug_set(lm_moe_ctx* ctx, int32_t knob, int64_t value) {
+    if (ctx == nullptr || value < 0) return LM_ERR_INVALID_ARGUMENT;
+    switch (knob) {
+        case LM_DEBUG_GRID_EXTRA:
+            if (value > 1024) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "LM_DEBUG_GRID_EXTRA above 1024");
+            ctx->debug_grid_extra = static_cast<uint32_t>(value);
+            return LM_OK;
+        case LM_DEBUG_WAIT_LIMIT_NS:
+            if (value > static_cast<int64_t>(kWaitLimitNs))
+                return fail(ctx, LM_ERR_INVALID_ARGUMENT, "LM_DEBUG_WAIT_LIMIT_NS above the 2 s default");
+            ctx->debug_wait_limit_ns = static_cast<uint64_t>(value);
+            return LM_OK;
+        default:
+            return fail(ctx, LM_ERR_INVALID_ARGUMENT, "unknown debug knob " + std::to_string(knob));
+    }
+}
+
+lm_status lm_moe_expert_counts(lm_moe_ctx* ctx, int32_t* counts, int32_t capacity) {
     if (ctx == nullptr || counts == nullptr) return LM_ERR_INVALID_ARGUMENT;
+    if (capacity < ctx->cfg.n_routed_experts)
+        return fail(ctx, LM_ERR_INVALID_ARGUMENT,
+                    "counts holds " + std::to_string(capacity) + " slots; the context has " +
+                        std::to_string(ctx->cfg.n_routed_experts) + " routed experts");
     lm_status st;
     if ((st = set_device(ctx)) != LM_OK) return st;
     LM_CUDA(ctx, cudaDeviceSynchronize());
@@ -1725,6 +1762,15 @@ lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t ra
     if (ctx->comm != nullptr) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "expert parallelism is already initialised");
     for (const LayerWeights& L : ctx->layers)
         if (L.w13 != nullptr) return fail(ctx, LM_ERR_INVALID_ARGUMENT, "call lm_moe_ep_init before uploading weights");
+    // NCCL's copy-engine mode for peer transfers makes NCCL's kernel on the caller's
+    // stream wait for copies that NCCL's host proxy thread issues.  When the caller's
+    // stream is the legacy default stream, a copy the driver orders behind that stream
+    // waits for the very kernel that waits for it; an exchange in this mode once made
+    // no progress until its process was killed.  Refused rather than risked.
+    if (const char* v = std::getenv("NCCL_P2P_USE_CUDA_MEMCPY"); v != nullptr && std::atoi(v) != 0)
+        return fail(ctx, LM_ERR_UNSUPPORTED,
+                    "NCCL_P2P_USE_CUDA_MEMCPY is set: the expert-parallel exchange does not support NCCL's "
+                    "copy-engine peer transfers (unset it, or set it to 0)");
     lm_status st;
     if ((st = set_device(ctx)) != LM_OK) return st;
     std::string err;

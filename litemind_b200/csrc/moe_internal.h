@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <string>
 #include <vector>
@@ -172,8 +173,10 @@ struct DecodeArgs {
     int32_t h_shared_base;     // first h row of the shared experts
     float* split_ws;           // gate/up split-K partials: 2 slots of [BN][128] per CTA
     int32_t* split_ticket;     // per gate/up tile, zero between uses
-    unsigned long long* grid_bar;  // [2] arrival counters (logits, h), monotonic across launches
-    unsigned long long epoch;      // this launch's number (from 1): targets are epoch * gridDim.x
+    unsigned long long* grid_bar;  // [3] arrival counters: logits, h, and CTAs finished (the last
+                                   // CTA to finish zeroes all three for the next launch)
+    uint32_t grid_extra;           // testing only: arrivals each grid wait expects beyond gridDim.x
+    uint64_t wait_limit_ns;        // bound of the grid waits
     int32_t* status;
     unsigned long long* trace;     // optional: kDecodeTraceSlots global-timer stamps per CTA
 };
@@ -224,6 +227,22 @@ cudaError_t launch_add_rows(float* dst, const float* src, int64_t count, cudaStr
 cudaError_t launch_pack_swiglu(const uint16_t* gate, const uint16_t* up, const uint16_t* down, int inter, int hidden,
                                uint16_t* w13, uint16_t* w2, int sms, cudaStream_t stream);
 const std::string& context_free_error();
+
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current device.
+// The attribute belongs to the device's context, so it is set once per device
+// (`done` is the caller's per-kernel bit set of devices; ordinals >= 64 set it on
+// every launch).  Setting it twice from racing threads is harmless.
+template <typename Kernel>
+cudaError_t set_smem_limit_once(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = (dev >= 0 && dev < 64) ? (uint64_t{1} << dev) : 0;
+    if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit != 0) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
 
 // Host-side TMA descriptor encoding (tensor_map.cpp).
 bool encode_tensor_map_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,

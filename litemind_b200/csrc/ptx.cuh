@@ -90,8 +90,9 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
 }
 
 // ── grid-wide arrival counters (cooperative launches only) ───────────────
-// Counters only grow: launch number n (from 1) of a context waits for n * gridDim.x
-// arrivals, so nothing has to be reset between launches.
+// A launch waits for gridDim.x arrivals on each counter; the last CTA to leave the
+// kernel sets the counters back to zero, so every launch (a CUDA graph replay too)
+// starts from zero without any host-side bookkeeping.
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -100,6 +101,11 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 __device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+__device__ __forceinline__ unsigned long long atom_acq_rel_add_u64(unsigned long long* p, unsigned long long v) {
+    unsigned long long old;
+    asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+    return old;
+}
 // Orders this thread's generic-proxy global writes before later async-proxy (TMA)
 // reads of the same memory, in this CTA or another.
 __device__ __forceinline__ void fence_proxy_async_global() {
@@ -107,9 +113,10 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 }
 // Bounded wait until *ctr >= target.  Gives up when the CTA's abort flag is raised,
 // when another CTA has already recorded an error in the status word, or after
-// kWaitLimitNs (then it records `code`).
+// limit_ns (then it records `code`).
 __device__ __forceinline__ bool grid_wait(const unsigned long long* ctr, unsigned long long target,
-                                          volatile int* abort_flag, int* status, int code) {
+                                          volatile int* abort_flag, int* status, int code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
     if (ld_acquire_u64(ctr) >= target) return true;
     const uint64_t start = global_timer_ns();
     while (true) {
@@ -118,7 +125,7 @@ __device__ __forceinline__ bool grid_wait(const unsigned long long* ctr, unsigne
             *abort_flag = 1;
             return false;
         }
-        if (global_timer_ns() - start > kWaitLimitNs) {
+        if (global_timer_ns() - start > limit_ns) {
             *abort_flag = 1;
             atomicCAS(status, 0, code);
             return false;

@@ -9,6 +9,8 @@
 // device memory through its own pool and forbids the plugin from calling the
 // CUDA allocator, and latency-critical paths that must not risk an allocation
 // that synchronises the device.
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "moe_internal.h"
@@ -24,30 +26,72 @@ constexpr int kMaxDevices = 64;
 // device address: it must go through cudaGetSymbolAddress before any kernel sees it.
 static __device__ __align__(256) float g_route_scratch[kStaticLogitsFloats];
 
+// The resolved address of the scratch on each device, with the unique id of the
+// context it belongs to: after a device reset the module is loaded again into a new
+// context (with a new id), and the address is looked up again.
+struct ScratchSlot {
+    unsigned long long ctx_id = 0;
+    float* ptr = nullptr;
+};
 std::mutex g_setup_mutex;
-float* g_scratch_ptr[kMaxDevices] = {};
+ScratchSlot g_scratch[kMaxDevices];
 
 // Failures are reported by status code only (see include/litemind_moe.h): the
 // entry point keeps no message state of its own.
 lm_status static_fail(lm_status code, const char* /*why*/) { return code; }
 
-// Once per device, with that device current: resolve the device address of the
-// scratch array.  The first call on a device does this; it should come before
-// any stream capture on that device.
+// cuCtxGetCurrent and cuCtxGetId, fetched through the runtime (the library does not
+// link the driver API directly).
+struct CtxApi {
+    PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+    PFN_cuCtxGetId_v12000 get_id = nullptr;
+};
+const CtxApi& ctx_api() {
+    static CtxApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            api.get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            api.get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+    });
+    return api;
+}
+
+// Unique id of this thread's current context, 0 when none is current yet.
+unsigned long long current_ctx_id() {
+    const CtxApi& api = ctx_api();
+    CUcontext cur = nullptr;
+    unsigned long long id = 0;
+    if (api.get_current == nullptr || api.get_id == nullptr || api.get_current(&cur) != CUDA_SUCCESS ||
+        cur == nullptr || api.get_id(cur, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
+
+// Set-up, once per device (and again after a reset of that device), with the device
+// current: resolve the device address of the scratch array.  The first call on a
+// device does this; it should come before any stream capture on that device.
 lm_status scratch_for_current_device(float** out) {
     int device = -1;
     cudaError_t e = cudaGetDevice(&device);
     if (e != cudaSuccess) return static_fail(LM_ERR_CUDA, "cudaGetDevice failed");
     if (device < 0 || device >= kMaxDevices) return static_fail(LM_ERR_UNSUPPORTED, "device ordinal out of range");
+    const unsigned long long id = current_ctx_id();
     std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (g_scratch_ptr[device] == nullptr) {
+    ScratchSlot& slot = g_scratch[device];
+    if (slot.ptr == nullptr || id == 0 || slot.ctx_id != id) {
         void* ptr = nullptr;
-        e = cudaGetSymbolAddress(&ptr, g_route_scratch);
-        if (e != cudaSuccess || ptr == nullptr)
-            return static_fail(LM_ERR_CUDA, "cudaGetSymbolAddress failed");
-        g_scratch_ptr[device] = static_cast<float*>(ptr);
+        e = cudaGetSymbolAddress(&ptr, g_route_scratch);  // makes the device's context current if needed
+        if (e != cudaSuccess || ptr == nullptr) return static_fail(LM_ERR_CUDA, "cudaGetSymbolAddress failed");
+        slot.ptr = static_cast<float*>(ptr);
+        slot.ctx_id = current_ctx_id();
     }
-    *out = g_scratch_ptr[device];
+    *out = slot.ptr;
     return LM_OK;
 }
 

@@ -251,6 +251,10 @@ class MoeLayer:
     def sync(self, stream=None) -> None:
         self._check(self.lib.lm_moe_sync(self.ctx, _stream_ptr(stream)))
 
+    def debug_set(self, knob: int, value: int) -> None:
+        """Testing hooks of the failure-detection path (lm_moe_debug_set)."""
+        self._check(self.lib.lm_moe_debug_set(self.ctx, knob, value))
+
     def profile(self, enable: bool) -> None:
         self._check(self.lib.lm_moe_profile_enable(self.ctx, int(enable)))
 
@@ -283,7 +287,7 @@ class MoeLayer:
 
     def expert_counts(self) -> np.ndarray:
         out = np.zeros(self.config.n_routed_experts, np.int32)
-        self._check(self.lib.lm_moe_expert_counts(self.ctx, _ptr(out)))
+        self._check(self.lib.lm_moe_expert_counts(self.ctx, _ptr(out), out.size))
         return out
 
 

@@ -23,7 +23,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libmoe_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libref_litemind.so")
-REFERENCE_DIR = "/root/reference"
+# The reference checkout: LITEMIND_REFERENCE_DIR, else a directory named `reference`
+# beside this repository's root.
+REFERENCE_DIR = os.environ.get("LITEMIND_REFERENCE_DIR") or os.path.join(
+    os.path.dirname(os.path.dirname(HERE)), "reference")
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")

@@ -65,3 +65,28 @@ def assert_layer_parity(y, idx, w, ref_y, ref_idx, ref_w, ref_logits, what=""):
     assert rel.max(initial=0.0) <= MAX_REL, f"{what}: max relative error {rel.max():.3e} > {MAX_REL}"
     assert cos.min(initial=1.0) >= MIN_COS, f"{what}: min cosine {cos.min():.7f} < {MIN_COS}"
     return {"exempt": len(exempt), "max_rel": float(rel.max(initial=0.0)), "min_cos": float(cos.min(initial=1.0))}
+
+
+def sampled_oracle_parity(y, x_bits, W, rows, bias=None) -> dict:
+    """Sampled tokens of a V2-Lite-shaped batch against the CPU oracle (the
+    reference's MoE block restated in C): per token max |y - y_ref| / max |y_ref| and
+    cosine, leaving out tokens whose 6th and 7th router probabilities lie within
+    ROUTE_TIE (either expert is a correct choice there).  y: [T, H] f32 output of
+    the GPU path; x_bits: [T, H] bf16 bits of its input; W: its weights."""
+    from litemind_b200 import synthetic as syn
+    from oracle.oracle import Oracle, RouterConfig
+
+    rows = np.asarray(rows)
+    xs = syn.bf16_to_f32(x_bits[rows]).reshape(len(rows), -1)
+    n_shared = W["shared_gate"].shape[0] // W["gate"].shape[1]
+    cfg = RouterConfig(W["router"].shape[0], 6)
+    ry, _, _, rlog = Oracle().moe_layer(xs, W, cfg, n_shared, bias=bias)
+    p = np.sort(softmax64(rlog), axis=1)[:, ::-1]
+    k = cfg.num_experts_per_tok
+    tie = (p[:, k - 1] - p[:, k]) <= ROUTE_TIE
+    rel, cos = output_errors(y[rows][~tie], ry[~tie])
+    return {"tokens": int(len(rows)), "exempt_near_ties": int(tie.sum()),
+            "max_rel": float(rel.max(initial=0.0)), "min_cos": float(cos.min(initial=1.0)),
+            "pass": bool(rel.max(initial=0.0) <= MAX_REL and cos.min(initial=1.0) >= MIN_COS),
+            "criteria": f"max_rel <= {MAX_REL}, cosine >= {MIN_COS} (fp32 accumulate); oracle = the reference's "
+                        "MoE block restated in C"}

@@ -86,6 +86,13 @@ def test_null_context_and_arguments(lib):
     assert lib.lm_gemm_axpy(1.0, None, None, 5, None) == _lib.LM_ERR_INVALID_ARGUMENT
 
 
+def test_new_entry_points_check_their_arguments(lib):
+    assert lib.lm_moe_debug_set(None, _lib.LM_DEBUG_GRID_EXTRA, 0) == _lib.LM_ERR_INVALID_ARGUMENT
+    assert lib.lm_moe_expert_counts(None, None, 64) == _lib.LM_ERR_INVALID_ARGUMENT
+    buf = C.create_string_buffer(128)
+    assert lib.lm_moe_ep_init(None, buf, 0, 1) == _lib.LM_ERR_INVALID_ARGUMENT
+
+
 def test_status_strings(lib):
     for code in range(8):
         assert lib.lm_status_string(code)

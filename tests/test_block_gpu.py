@@ -1,4 +1,4 @@
-"""Stacked decoder feed-forward sub-layers against the oracle.
+"""Stacked decoder feed-forward sub-layers (RMSNorm, MoE layer, residual add) against the oracle.
 
 Each block is DeepSeekRunner::Impl::forward's feed-forward half
 (src/DeepSeekRunner.cpp:264-290): normalised = rms_norm(hidden, weight) with the sum

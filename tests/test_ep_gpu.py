@@ -1,6 +1,6 @@
 """Expert parallelism on two B200s: each rank holds half of the routed experts,
 runs lm_moe_forward on its own tokens over NCCL, and its outputs must match the
-oracle's single-process MoE block for those tokens.  Needs 2 GPUs (gpurun --gpus 2);
+oracle's single-process MoE block for those tokens.  Needs 2 GPUs on one machine;
 gloo carries only the NCCL unique id.
 """
 import os

@@ -121,7 +121,7 @@ def v2_layer(v2lite_weights):
 
 @pytest.mark.parametrize("T,seed", [(1, 1), (8, 1), (32, 1), (128, 0), (256, 1)])
 def test_v2lite_decode_parity(oracle_lib, v2lite_weights, v2_layer, T, seed):
-    """BASELINE configs 0 (T=128, seed 0) and 1 (T in 1/8/32/256, seed 1)."""
+    """The V2-Lite layer at T=128 (token seed 0) and at decode sizes T in 1/8/32/256 (token seed 1)."""
     x = syn.tokens(syn.V2_LITE, T, seed=seed)
     y, idx, w, _ = run_gpu(v2_layer, x)
     ry, ridx, rw, rlog = run_oracle(oracle_lib, syn.V2_LITE, v2lite_weights, x)
@@ -131,7 +131,7 @@ def test_v2lite_decode_parity(oracle_lib, v2lite_weights, v2_layer, T, seed):
 
 @pytest.mark.parametrize("T,zipf", [(2048, False), (16384, True)])
 def test_v2lite_prefill_sampled_parity(oracle_lib, v2lite_weights, v2_layer, T, zipf):
-    """BASELINE config 2 (T=16384, Zipf(1.2) expert load) and a 2048-token prefill."""
+    """Prefill: T=16384 with a Zipf(1.2) expert load, and a 2048-token batch."""
     x = syn.tokens(syn.V2_LITE, T, seed=2)
     bias = syn.zipf_bias(syn.V2_LITE, seed=2) if zipf else None
     y, idx, w, _ = run_gpu(v2_layer, x, bias)

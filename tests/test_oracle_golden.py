@@ -148,3 +148,23 @@ def test_expert_cache_golden(oracle_lib):
         assert [c.resident_bytes, c.count, c.loads, c.hits, c.evictions, c.bytes_streamed] == want
     lib.orc_cache_clear(C.byref(c))
     assert [c.resident_bytes, c.count, c.loads, c.hits, c.evictions, c.bytes_streamed] == g["after_clear"]
+
+
+def test_sampled_parity_checker_accepts_the_oracle_and_rejects_a_perturbation():
+    """The bench's parity leg (tests/parity.py) on CPU: the oracle's own output passes,
+    an output with one expert's contribution dropped does not."""
+    import numpy as np
+
+    from litemind_b200 import synthetic as syn
+    from oracle.oracle import Oracle, RouterConfig
+    from tests.parity import sampled_oracle_parity
+
+    shape = syn.MoeShape(hidden=256, inter=128, n_routed_experts=16, n_shared_experts=2, top_k=6)
+    W = syn.layer_weights(shape, seed=3, std=0.05)
+    xb = syn.tokens(shape, 12, seed=5)
+    y, idx, w, _ = Oracle().moe_layer(syn.bf16_to_f32(xb).reshape(12, -1), W, RouterConfig(16, 6), 2)
+    ok = sampled_oracle_parity(y, xb, W, [0, 3, 11])
+    assert ok["pass"] and ok["max_rel"] == 0.0 and ok["tokens"] == 3
+    bad = y.copy()
+    bad[3] *= 1.05
+    assert not sampled_oracle_parity(bad, xb, W, [0, 3, 11])["pass"]

@@ -102,6 +102,30 @@ def test_malformed_shards_are_rejected_as_the_reference_rejects_them(tmp_path, r
     assert str(path) in ref_error and str(path) in str(err.value)
 
 
+# Numbers the JSON header can hold but no shard can: rejected before any cast or
+# product could wrap (a negative or fractional offset, an offset far past the end,
+# a shape whose element count overflows 64 bits).
+OUT_OF_RANGE = {
+    "negative offset": _shard({"a": {"dtype": "F32", "shape": [1], "data_offsets": [-4, 0]}}, payload=b"\0" * 4),
+    "fractional offset": _shard({"a": {"dtype": "F32", "shape": [1], "data_offsets": [0.5, 4.5]}},
+                                payload=b"\0" * 8),
+    "offset wraps": _shard({"a": {"dtype": "F32", "shape": [1], "data_offsets": [2 ** 64 - 2, 2 ** 64 + 2]}},
+                           payload=b"\0" * 4),
+    "shape overflows": _shard({"a": {"dtype": "F32", "shape": [2 ** 32, 2 ** 32, 4], "data_offsets": [0, 0]}},
+                              payload=b"\0" * 4),
+}
+
+
+@pytest.mark.parametrize("case", sorted(OUT_OF_RANGE))
+def test_out_of_range_numbers_are_rejected(tmp_path, case):
+    path = tmp_path / "bad.safetensors"
+    path.write_bytes(OUT_OF_RANGE[case])
+    with pytest.raises(_lib.LiteMindError) as err:
+        safetensors_info(path, "a")
+    assert err.value.status == _lib.LM_ERR_INVALID_ARGUMENT
+    assert str(path) in str(err.value)
+
+
 def test_missing_tensor(tmp_path, reference_lib):
     path = tmp_path / "shard.safetensors"
     write_safetensors(path, _tensors())

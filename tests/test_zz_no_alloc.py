@@ -3,10 +3,11 @@
 Some callers cannot allocate: code inside a CUDA graph capture, plugins whose host
 application owns every device allocation, paths that must not trigger an
 allocation's synchronisation.  lm_moe_route_static serves them with a fixed scratch
-array inside the library.  This test calls it through the C ABI and checks that it
-routes exactly as the context-based entry point lm_moe_route does, on two calls in
-a row (the second call reuses the scratch the first one left behind), and that a
-batch beyond the scratch's capacity is refused.  It lives in its own file, collected
+array inside the library.  This test calls it through the C ABI and checks, on two calls in
+a row (the second call reuses the scratch the first one left behind), that it
+routes as the context-based entry point lm_moe_route does and as the CPU oracle
+(the reference's gemm::matvec_f32 + MoeRouter::select, restated in C) does, and
+that a batch beyond the scratch's capacity is refused.  It lives in its own file, collected
 last, and needs nothing from the other tests.
 """
 import ctypes as C
@@ -20,6 +21,7 @@ torch = pytest.importorskip("torch")
 
 from litemind_b200 import _lib, synthetic as syn  # noqa: E402
 from litemind_b200.moe import MoeConfig, MoeLayer, bf16_tensor  # noqa: E402
+from oracle.oracle import Oracle, RouterConfig  # noqa: E402
 from tests.parity import routing_mismatches  # noqa: E402
 
 SHAPE = syn.MoeShape(hidden=512, inter=128, n_routed_experts=64, n_shared_experts=1, top_k=6)
@@ -60,6 +62,22 @@ def test_static_route_matches_context_route():
         keep = np.ones(T, bool)
         keep[exempt] = False
         np.testing.assert_allclose(w[keep], ref_w[keep], rtol=W_RTOL, atol=1e-8, err_msg=f"call {call}")
+        # The oracle: per token, f32 logits (+ bias), then the reference's selection.
+        orc = Oracle()
+        xf = syn.bf16_to_f32(x.view(torch.int16).cpu().numpy().view(np.uint16)).reshape(T, -1)
+        bias_np = None if b is None else b.cpu().numpy()
+        o_logits = np.stack([orc.matvec_f32(W["router"], xf[t]) for t in range(T)])
+        if bias_np is not None:
+            o_logits = o_logits + bias_np
+        cfg = RouterConfig(SHAPE.n_routed_experts, SHAPE.top_k)
+        sel = [orc.router_select(o_logits[t], cfg) for t in range(T)]
+        o_idx = np.stack([i for i, _ in sel]).astype(np.int32)
+        o_w = np.stack([v for _, v in sel])
+        exempt, bad = routing_mismatches(idx, o_idx, o_logits)
+        assert not bad, f"call {call}: routing differs from the oracle beyond near-ties for tokens {bad[:10]}"
+        keep = np.ones(T, bool)
+        keep[exempt] = False
+        np.testing.assert_allclose(w[keep], o_w[keep], rtol=W_RTOL, atol=1e-8, err_msg=f"call {call} vs oracle")
     layer.close()
 
 
