@@ -73,7 +73,7 @@ FLUSH_BYTES = 256 << 20
 
 def kernels_per_forward(tokens: int, world: int, experts: int = 64, top_k: int = 6, sms: int = 148) -> int:
     """Our kernel launches in one forward (NCCL's own kernels not counted).
-    One GPU: T <= 32 is the fused decode kernel alone; 32 < T <= 256 the single-launch
+    One GPU: T <= 128 is the fused decode kernel alone; 128 < T <= 256 the single-launch
     routing kernel, the row gather and the two grouped GEMMs; above that router
     logits, top-k, scan, placement and the two grouped GEMMs, plus a separate row
     gather unless the placement copies the rows itself (2 T >= 32 x SMs).  Expert parallel:
@@ -84,7 +84,7 @@ def kernels_per_forward(tokens: int, world: int, experts: int = 64, top_k: int =
     the shared experts' two GEMMs when chunked) and the combine."""
     gather = 0 if tokens > 32 and 2 * tokens >= 32 * sms else 1
     if world == 1:
-        return 1 if tokens <= 32 else 4 if tokens <= 256 else 6 + gather
+        return 1 if tokens <= 128 else 4 if tokens <= 256 else 6 + gather
     route = 1 if tokens <= 32 else 4
     local = experts // world
     fixed = world * tokens * min(top_k, local) <= 8192
@@ -348,7 +348,7 @@ def stack_kernels_per_layer(tokens: int, world: int, sms: int = 148) -> int:
     """One block: the RMSNorm, then the layer's own launches; the router reads f32
     activations, so at >= 2048 tokens its logits take the split tiled kernel plus its
     reduction instead of one launch."""
-    if world == 1 and tokens <= 32:
+    if world == 1 and tokens <= 128:
         return 1 + 1
     return 1 + kernels_per_forward(tokens, world, sms=sms) + (1 if tokens >= 2048 else 0)
 

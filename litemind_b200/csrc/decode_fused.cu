@@ -1,27 +1,35 @@
-// decode_fused.cu -- the whole MoE layer for decode-sized batches (T <= 32 tokens)
+// decode_fused.cu -- the whole MoE layer for decode-sized batches (T <= 128 tokens)
 // in one persistent, cooperative launch.
 //
-// At decode sizes the layer is a stream of expert weights (about 139 MB at T=1,
-// 1.1 GB at T=32) and every separate launch costs a ramp-up and a tail in which
-// HBM idles.  Here one CTA per SM runs the layer's steps back to back, each step
-// split evenly over all CTAs ("stream-K": a list's k-block iterations cut into
-// gridDim.x equal ranges), with two grid-wide arrival counters between them:
+// At these sizes the layer is a stream of expert weights (about 139 MB at T=1,
+// 1.1 GB from T=32 on) and every separate launch costs a ramp-up and a tail in
+// which HBM idles.  Here one CTA per SM runs the layer's steps back to back, each
+// step split evenly over all CTAs ("stream-K": a list's k-block iterations cut into
+// gridDim.x equal ranges), with grid-wide arrival counters between them.
 //
-//   routing   every CTA: its share of the router logits (src/Gemm.cpp:132-137),
-//             issued before any weight streaming so the router rows see an idle
-//             HBM; after counter 0, every CTA reads all T x E logits into shared
-//             memory once and recomputes the whole routing identically: top-k
-//             (MoeRouter::select, src/MoeRouter.cpp:54-107), the expert histogram
-//             and the expert-sorted row order.  Meanwhile the producer prefetches
-//             the shared experts' gate/up weights (known before routing) into L2.
-//   gate/up   shared experts' tiles, then the routed experts'.  Their token operand
-//             is x itself (all T <= 32 tokens as the MMA's N): at decode sizes the
-//             tensor cores are idle anyway, and it spares a gather of token rows
-//             and a grid-wide wait for it; the epilogue keeps only the expert's own
-//             tokens' columns
-//   down      routed and shared experts.  Their h tiles wait for counter 1 (every
-//             CTA finished gate/up); their weight tiles are loaded before that, so
-//             the switch costs no HBM time
+// Routing (src/Gemm.cpp:132-137, MoeRouter::select src/MoeRouter.cpp:54-107) comes
+// first, before any weight is streamed: under a saturated weight stream every
+// global access of the routing waits microseconds in the memory queues.  Two modes:
+//
+//   direct  (T <= 32)  router dot products spread over every warp of the grid;
+//           after counter 0 every CTA reads all T x E logits into shared memory and
+//           recomputes the whole routing identically (top-k, histogram, row order).
+//           Every expert's token operand is x itself (all T tokens as the MMA's N):
+//           the tensor cores are idle at these sizes anyway, and it spares a gather
+//           and a grid-wide wait; the epilogue keeps the expert's own tokens.
+//   gather  (T > 32)   router logits as (expert, 8 tokens) warp tasks; after counter
+//           0 each token's top-k is computed once in the grid (one warp per token)
+//           and published; after counter 3 every CTA reads all T x k selections and
+//           builds the histogram and row order; each CTA then copies its share of
+//           token rows into expert order (x_perm) and arrives on counter 2.  Every
+//           expert's rows are tiled 32 at a time (column tiles); the shared
+//           experts' tiles read x directly, so they stream while the rows gather.
+//
+// Then two lists of tiles, each spread over all CTAs:
+//   gate/up   shared experts' tiles, then the routed experts'
+//   down      routed experts' tiles, then the shared experts'.  Their h tiles wait for
+//             counter 1 (every CTA finished gate/up); their weight tiles are loaded
+//             before that, so the switch costs no HBM time.
 //
 // Epilogues are the grouped GEMMs' (grouped_gemm.cu): h = silu(gate) * up in bf16
 // for gate/up (src/DeepSeekRunner.cpp:228-240), and the routing-weighted atomic add
@@ -30,9 +38,11 @@
 // workspace (fixed CTA order); a shared down tile simply adds both parts into y.
 //
 // Warp roles as in the grouped GEMMs: warp 0 TMA producer, warp 1 tcgen05.mma
-// issuer, warps 2-9 routing and then the epilogue.  Every wait -- mbarriers and the
-// grid counters -- is bounded; an expired wait records a status code and the CTA
-// winds down, and CTAs that see a recorded status stop waiting too.
+// issuer, warps 2-9 routing and then the epilogue.  The routing's scratch lives in
+// the pipeline ring, which no TMA load touches before the schedule exists.  Every
+// wait -- mbarriers and the grid counters -- is bounded; an expired wait records a
+// status code and the CTA winds down, and CTAs that see a recorded status stop
+// waiting too.
 #include "moe_internal.h"
 #include "ptx.cuh"
 #include "route_device.cuh"
@@ -48,11 +58,21 @@ constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;
 constexpr int kATile = kBlockM * kBlockK * 2;
-constexpr int kMaxRows = kDecodeMaxTokens * kMaxTopK;
-constexpr int kDynBudget = 186 * 1024;  // leaves room for the static shared arrays below
+constexpr int kMaskWords = kDecodeMaxTokens / 32;  // token bit set per expert
+constexpr int kMaxGroups = kMaxExperts + kMaxShared;
+constexpr int kDynBudget = 210 * 1024;  // leaves room for the static shared arrays below
 constexpr int kMaxPending = 16;
 constexpr int kReduceItems = 4;  // float4 items of a partial-tile reduction per thread (32 rows x 32 / 256)
 constexpr int kReduceParts = 4;  // CTAs' partial sums loaded together
+constexpr int kLogitTokens = 8;  // gather mode: tokens per router-logit warp task
+
+// Grid counters (DecodeArgs::grid_bar).
+constexpr int kCtrLogits = 0;
+constexpr int kCtrH = 1;
+constexpr int kCtrXperm = 2;
+constexpr int kCtrTopk = 3;
+constexpr int kCtrExit = 4;
+static_assert(kCtrExit + 1 == kDecodeCounters, "counter count");
 
 template <int BN>
 struct DCfg {
@@ -68,6 +88,17 @@ struct DCfg {
     static_assert(kStages >= 4 && kStages <= kMaxPending, "pipeline depth");
     static_assert(kSmem <= kDynBudget, "shared memory");
 };
+
+// Routing scratch, placed at the start of the pipeline ring (unused until the
+// schedule is built).
+struct RouteScratch {
+    float logits[kDecodeMaxLogits];           // direct mode: [t * E + e]
+    int idx[kDecodeMaxRows];                  // top-k experts, [t * K + k]
+    float w[kDecodeMaxRows];                  // top-k weights
+    uint32_t emask[kMaxExperts][kMaskWords];  // tokens of each expert (bit t)
+    float probs[kEpiWarps][kMaxExperts];      // group-limited routing scratch
+};
+static_assert(sizeof(RouteScratch) <= 4 * kATile, "routing scratch fits in the first pipeline stages");
 
 __device__ __forceinline__ float silu_times(float g, float u) {
     // src/Gemm.cpp:225-231, with fast exp and divide: the result is rounded to bf16.
@@ -95,36 +126,40 @@ struct ListWalk {
     }
 };
 
-// The decoded work unit: which weights, which token tile, where its rows live.
+// Token operand of a unit.
+constexpr int kBx = 0;      // x (direct mode: all T tokens; gather mode: a shared expert's column tile)
+constexpr int kBxperm = 1;  // x_perm rows (gather mode, routed gate/up)
+constexpr int kBh = 2;      // h rows (down)
+
+// The decoded work unit: which weights, which token rows, where its outputs go.
 struct UnitInfo {
-    int a_row;    // tile-major weight row of k-block 0 (the A coordinate is a_row + kb * 128)
-    int b_row;    // first row of the token tile in its B tensor (x for gate/up, h for down)
-    int row0;     // first h row of the unit's expert
-    int rows;     // h rows of the expert (its tokens)
-    int mb;       // 128-row weight block within the expert
-    bool routed;  // routed expert (rows map to tokens through the row maps) or shared (row j = token j)
+    int a_row;      // tile-major weight row of k-block 0 (the A coordinate is a_row + kb * 128)
+    int bmap;       // kBx, kBxperm or kBh
+    int b_row;      // first row of the token tile in its B tensor
+    int hrow0;      // h row of output column 0 (gate/up: row written; down: row read)
+    int nout;       // valid output columns
+    int tok0;       // shared experts: token of column 0
+    int mb;         // 128-row weight block within the expert
+    bool routed;    // routed expert (rows map to tokens through the row maps) or shared
+    bool by_token;  // direct-mode routed gate/up: column c is token c, output row j takes column row_token[j]
 };
 
 template <int BN, int EPL>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_decode_kernel(const __grid_constant__ CUtensorMap map_w13, const __grid_constant__ CUtensorMap map_w2,
-                      const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_h,
-                      const __grid_constant__ DecodeArgs args) {
+                      const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_xperm,
+                      const __grid_constant__ CUtensorMap map_h, const __grid_constant__ DecodeArgs args) {
     using C = DCfg<BN>;
     constexpr int S = C::kStages;
     constexpr uint32_t kIdesc = umma_idesc_bf16(kBlockM, BN);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    __shared__ float s_logits[kDecodeMaxLogits];  // [t * E + e]
-    __shared__ int s_idx[kMaxRows];               // top-k experts, [t * K + k]
-    __shared__ float s_w[kMaxRows];               // top-k weights
-    __shared__ int s_row_token[kMaxRows];         // expert-sorted row -> token
-    __shared__ float s_row_w[kMaxRows];           // expert-sorted row -> routing weight
+    __shared__ int s_row_token[kDecodeMaxRows];   // expert-sorted row -> token
+    __shared__ float s_row_w[kDecodeMaxRows];     // expert-sorted row -> routing weight
     __shared__ int s_cnt[kMaxExperts];            // rows per expert
-    __shared__ uint32_t s_emask[kMaxExperts];     // tokens of each expert (bit t)
     __shared__ int s_eoff[kMaxExperts];           // first expert-sorted row of each expert
     __shared__ int s_seg_e[kMaxExperts];          // active (non-empty) experts, in expert order
-    __shared__ float s_probs[kEpiWarps][kMaxExperts];  // group-limited routing scratch
+    __shared__ int s_tp[2][kMaxGroups + 1];       // per list: first tile of each group (prefix)
     __shared__ RouterParams s_rp;  // read once at entry: a late read of a kernel parameter can miss
                                    // the constant cache and wait behind the weight stream
     __shared__ int s_n_act;
@@ -142,9 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tmem_empty = bars + 2 * S + 2;
     uint64_t* sched_ready = bars + 2 * S + 4;
     uint64_t* drain_bar = bars + 2 * S + 5;
-    uint64_t* logits_loaded = bars + 2 * S + 6;  // this CTA holds every logit: its HBM reads are done
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    RouteScratch& rs = *reinterpret_cast<RouteScratch*>(smem_a);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -154,14 +189,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int E = args.rp.experts;
     const int K = args.rp.top_k;
     const int G = gridDim.x;
+    const bool gather = args.gather != 0;
     const unsigned long long target = static_cast<unsigned long long>(G) + args.grid_extra;
-    // Lists: 0 = gate/up (shared experts' tiles, then the routed experts'), 1 = down
-    // (routed, then shared).
     const int mb1 = 2 * I / kBlockM;  // 128-row blocks of interleaved gate/up rows
     const int nkb1 = H / kBlockK;
     const int mb2 = H / kBlockM;
     const int nkb2 = I / kBlockK;
-    const int tiles_sh = args.n_shared * mb1;
+    const int nsh = args.n_shared;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
@@ -174,13 +208,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(sched_ready, 1);
         mbar_init(drain_bar, 1);
-        mbar_init(logits_loaded, 1);
         s_rp = args.rp;
         *abort_flag = 0;
         fence_mbar_init();
         tma_prefetch_desc(&map_w13);
         tma_prefetch_desc(&map_w2);
         tma_prefetch_desc(&map_x);
+        tma_prefetch_desc(&map_xperm);
         tma_prefetch_desc(&map_h);
     }
     if (warp == 1) {
@@ -200,46 +234,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) stamp(0);
 
     // Both lists need the schedule, which exists once `sched_ready` has completed.
-    auto list_tiles = [&](int list) {
-        return list == 0 ? tiles_sh + s_n_act * mb1 : (s_n_act + args.n_shared) * mb2;
-    };
-    // Unit decoding, identical in every role.
+    // Groups: list 0 = shared experts, then active routed experts; list 1 = active
+    // routed experts, then shared experts.  Each group has one or more column tiles
+    // (32 token rows each in gather mode, one in direct mode) of mb weight blocks,
+    // ordered (group, weight block, column tile).
+    auto n_groups = [&]() { return nsh + s_n_act; };
+    auto list_tiles = [&](int list) { return s_tp[list][n_groups()]; };
     auto unit_info = [&](int list, int tile) {
+        const int* tp = s_tp[list];
+        int lo = 0, hi = n_groups() - 1;  // the group g with tp[g] <= tile < tp[g + 1]
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (tp[mid] <= tile) lo = mid;
+            else hi = mid - 1;
+        }
+        const int g = lo;
+        const bool shared = list == 0 ? g < nsh : g >= s_n_act;
+        const int s = list == 0 ? g : g - s_n_act;
+        const int e = shared ? 0 : s_seg_e[list == 0 ? g - nsh : g];
+        const int rows = shared ? T : s_cnt[e];
+        const int nct = gather ? (rows + kDecodeColTile - 1) / kDecodeColTile : 1;
+        const int local = tile - tp[g];
         UnitInfo u;
-        if (list == 0 && tile < tiles_sh) {
-            const int s = tile / mb1;
-            u.mb = tile - s * mb1;
-            u.a_row = ((E + s) * mb1 + u.mb) * nkb1 * kBlockM;
-            u.b_row = 0;
-            u.row0 = args.h_shared_base + s * T;
-            u.rows = T;
-            u.routed = false;
-        } else if (list == 0) {
-            const int a = (tile - tiles_sh) / mb1;
-            const int e = s_seg_e[a];
-            u.mb = tile - tiles_sh - a * mb1;
-            u.a_row = (e * mb1 + u.mb) * nkb1 * kBlockM;
-            u.b_row = 0;
-            u.row0 = s_eoff[e];
-            u.rows = s_cnt[e];
-            u.routed = true;
+        u.mb = local / nct;
+        const int ct = local - u.mb * nct;
+        const int slot = shared ? E + s : e;
+        u.a_row = list == 0 ? ((slot * mb1 + u.mb) * nkb1) * kBlockM : ((slot * mb2 + u.mb) * nkb2) * kBlockM;
+        u.routed = !shared;
+        const int base = shared ? args.h_shared_base + s * T : s_eoff[e];
+        u.hrow0 = base + ct * kDecodeColTile;
+        u.nout = gather ? min(kDecodeColTile, rows - ct * kDecodeColTile) : rows;
+        u.tok0 = shared ? ct * kDecodeColTile : 0;
+        u.by_token = !gather && !shared && list == 0;
+        if (list == 1) {
+            u.bmap = kBh;
+            u.b_row = u.hrow0;
+        } else if (shared || !gather) {
+            u.bmap = kBx;
+            u.b_row = gather ? ct * kDecodeColTile : 0;
         } else {
-            const int g = tile / mb2;
-            u.mb = tile - g * mb2;
-            if (g < s_n_act) {
-                const int e = s_seg_e[g];
-                u.a_row = (e * mb2 + u.mb) * nkb2 * kBlockM;
-                u.row0 = s_eoff[e];
-                u.rows = s_cnt[e];
-                u.routed = true;
-            } else {
-                const int s = g - s_n_act;
-                u.a_row = ((E + s) * mb2 + u.mb) * nkb2 * kBlockM;
-                u.row0 = args.h_shared_base + s * T;
-                u.rows = T;
-                u.routed = false;
-            }
-            u.b_row = u.row0;
+            u.bmap = kBxperm;
+            u.b_row = u.hrow0;
         }
         return u;
     };
@@ -252,29 +287,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t issued_mask = 0;
             uint32_t issued_phase = 0;
             bool ok = true;
-            // h tiles of list 3 issued before counter 1 opens: (stage, x, y), oldest first.
-            int pend_stage[kMaxPending], pend_y[kMaxPending], pend_x[kMaxPending];
+            // Token tiles whose rows are not written yet (x_perm before counter 2, h
+            // before counter 1), oldest first: every x_perm entry precedes every h one.
+            int pend_stage[kMaxPending], pend_map[kMaxPending], pend_y[kMaxPending], pend_x[kMaxPending];
             int pend_head = 0, pend_n = 0;
-            bool h_ready = false;
+            bool ready[2] = {!gather, false};  // [0] x_perm, [1] h
             auto flush = [&](bool block) {
-                if (pend_n == 0) return;
-                if (!h_ready) {
-                    if (block) {
-                        if (!grid_wait(args.grid_bar + 1, target, abort_flag, args.status, kDevTimeoutGrid,
-                                       args.wait_limit_ns)) {
-                            ok = false;
+                while (pend_n > 0) {
+                    const int m = pend_map[pend_head];
+                    if (!ready[m]) {
+                        unsigned long long* ctr = args.grid_bar + (m == 0 ? kCtrXperm : kCtrH);
+                        if (block) {
+                            if (!grid_wait(ctr, target, abort_flag, args.status, kDevTimeoutGrid,
+                                           args.wait_limit_ns)) {
+                                ok = false;
+                                return;
+                            }
+                        } else if (ld_acquire_u64(ctr) < target) {
                             return;
                         }
-                    } else if (ld_acquire_u64(args.grid_bar + 1) < target) {
-                        return;
+                        fence_proxy_async_global();
+                        ready[m] = true;
+                        stamp(m == 0 ? 15 : 5);
                     }
-                    fence_proxy_async_global();
-                    h_ready = true;
-                    stamp(5);
-                }
-                while (pend_n > 0) {
                     const int st = pend_stage[pend_head];
-                    tma_load_2d(smem_b + st * C::kBTile, &map_h, &full[st], pend_x[pend_head], pend_y[pend_head]);
+                    tma_load_2d(smem_b + st * C::kBTile, m == 0 ? &map_xperm : &map_h, &full[st], pend_x[pend_head],
+                                pend_y[pend_head]);
                     pend_head = (pend_head + 1) % kMaxPending;
                     --pend_n;
                 }
@@ -293,8 +331,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 while (ok && walk.next(tile, kb0, kb1)) {
                     const UnitInfo u = unit_info(list, tile);
                     for (int kb = kb0; kb < kb1 && ok; ++kb) {
-                        // A ring of stages all waiting for h tiles drains only once
-                        // every CTA has written its h rows.
+                        // A ring of stages all waiting for token rows drains only once
+                        // every CTA has written them.
                         flush(pend_n == S);
                         if (!ok) break;
                         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status, kDevTimeoutProducer)) {
@@ -303,17 +341,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         mbar_arrive_expect_tx(&full[stage], kATile + C::kBTile);
                         tma_load_2d(smem_a + stage * kATile, amap, &full[stage], 0, u.a_row + kb * kBlockM);
-                        if (list == 0) {
-                            tma_load_2d(smem_b + stage * C::kBTile, &map_x, &full[stage], kb * kBlockK, 0);
-                        } else if (h_ready && pend_n == 0) {
-                            tma_load_2d(smem_b + stage * C::kBTile, &map_h, &full[stage], kb * kBlockK, u.b_row);
+                        if (u.bmap == kBx) {
+                            tma_load_2d(smem_b + stage * C::kBTile, &map_x, &full[stage], kb * kBlockK, u.b_row);
                         } else {
-                            const int slot = (pend_head + pend_n) % kMaxPending;
-                            pend_stage[slot] = stage;
-                            pend_x[slot] = kb * kBlockK;
-                            pend_y[slot] = u.b_row;
-                            ++pend_n;
-                            flush(false);
+                            const int m = u.bmap == kBxperm ? 0 : 1;
+                            if (ready[m] && pend_n == 0) {
+                                tma_load_2d(smem_b + stage * C::kBTile, m == 0 ? &map_xperm : &map_h, &full[stage],
+                                            kb * kBlockK, u.b_row);
+                            } else {
+                                const int slot = (pend_head + pend_n) % kMaxPending;
+                                pend_stage[slot] = stage;
+                                pend_map[slot] = m;
+                                pend_x[slot] = kb * kBlockK;
+                                pend_y[slot] = u.b_row;
+                                ++pend_n;
+                                flush(false);
+                            }
                         }
                         issued_mask |= 1u << stage;
                         issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
@@ -408,6 +451,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_bar_sync(2, kEpiThreads);
             if (epi_tid == 0) red_release_add_u64(args.grid_bar + g, 1ull);
         };
+        auto wait_grid = [&](int g) {
+            return broadcast(epi_tid == 0 ? grid_wait(args.grid_bar + g, target, abort_flag, args.status,
+                                                      kDevTimeoutGrid, args.wait_limit_ns)
+                                          : true);
+        };
 
         // (1) y = 0 when not accumulating; the down epilogues add into it after counter 1.
         if (args.zero_y) {
@@ -419,72 +467,163 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int e = epi_tid; e < E; e += kEpiThreads) {
             s_cnt[e] = 0;
-            s_emask[e] = 0u;
+#pragma unroll
+            for (int w = 0; w < kMaskWords; ++w) rs.emask[e][w] = 0u;
         }
 
-        // (2) Router logits: (token, expert) dot products spread over every warp of the
-        // grid; each lane's loads of a row are all issued before any is used.
-        for (int p = blockIdx.x * kEpiWarps + ew; p < T * E; p += G * kEpiWarps) {
-            const int t = p / E;
-            const int e = p - t * E;
-            const float* wr = args.router + static_cast<size_t>(e) * H;
-            float acc = 0.0f;
-            if (args.x_f32 != nullptr) {
-                const float* xt = args.x_f32 + static_cast<size_t>(t) * H;
+        if (!gather) {
+            // (2) Router logits: (token, expert) dot products spread over every warp of
+            // the grid; each lane's loads of a row are all issued before any is used.
+            for (int p = blockIdx.x * kEpiWarps + ew; p < T * E; p += G * kEpiWarps) {
+                const int t = p / E;
+                const int e = p - t * E;
+                const float* wr = args.router + static_cast<size_t>(e) * H;
+                float acc = 0.0f;
+                if (args.x_f32 != nullptr) {
+                    const float* xt = args.x_f32 + static_cast<size_t>(t) * H;
 #pragma unroll 8
-                for (int hh = lane * 8; hh < H; hh += 256) {
-                    float xv[8], wv[8];
-                    load8(xt + hh, xv);
-                    load8(wr + hh, wv);
+                    for (int hh = lane * 8; hh < H; hh += 256) {
+                        float xv[8], wv[8];
+                        load8(xt + hh, xv);
+                        load8(wr + hh, wv);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[i], acc);
-                }
-            } else {
-                const uint16_t* xt = args.x + static_cast<size_t>(t) * H;
+                        for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[i], acc);
+                    }
+                } else {
+                    const uint16_t* xt = args.x + static_cast<size_t>(t) * H;
 #pragma unroll 8
-                for (int hh = lane * 8; hh < H; hh += 256) {
-                    float xv[8], wv[8];
-                    load8(xt + hh, xv);
-                    load8(wr + hh, wv);
+                    for (int hh = lane * 8; hh < H; hh += 256) {
+                        float xv[8], wv[8];
+                        load8(xt + hh, xv);
+                        load8(wr + hh, wv);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[i], acc);
+                        for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[i], acc);
+                    }
                 }
-            }
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(kFull, acc, off);
-            if (lane == 0) args.logits[p] = args.bias != nullptr ? acc + args.bias[e] : acc;
-        }
-        arrive_grid(0);
-        if (epi_tid == 0) stamp(1);
-        ok = broadcast(epi_tid == 0 ? grid_wait(args.grid_bar, target, abort_flag, args.status, kDevTimeoutGrid,
-                                                args.wait_limit_ns)
-                                    : true);
-        if (epi_tid == 0) stamp(2);
-
-        if (ok) {
-            // (3) All logits into shared memory in one round trip, then every token's
-            // routing from there (every CTA the same).
-            for (int i = epi_tid; i < T * E; i += kEpiThreads) s_logits[i] = __ldcg(args.logits + i);
-            named_bar_sync(1, kEpiThreads);
-            if (epi_tid == 0) {
-                mbar_arrive(logits_loaded);
-                stamp(10);
+                for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(kFull, acc, off);
+                if (lane == 0) args.logits[p] = args.bias != nullptr ? acc + args.bias[e] : acc;
             }
-            for (int t = ew; t < T; t += kEpiWarps) {
-                const Selection sel = route_one_token<EPL, true>(s_logits + t * E, s_rp, s_probs[ew], lane);
-                if (lane < K) {
-                    s_idx[t * K + lane] = sel.idx;
-                    s_w[t * K + lane] = sel.w;
-                    atomicAdd(&s_cnt[sel.idx], 1);
-                    atomicOr(&s_emask[sel.idx], 1u << t);
-                    if (blockIdx.x == 0) {
+            arrive_grid(kCtrLogits);
+            if (epi_tid == 0) stamp(1);
+            ok = wait_grid(kCtrLogits);
+            if (epi_tid == 0) stamp(2);
+            if (ok) {
+                // (3) All logits into shared memory in one round trip, then every token's
+                // routing from there (every CTA the same).
+                for (int i = epi_tid; i < T * E; i += kEpiThreads) rs.logits[i] = __ldcg(args.logits + i);
+                named_bar_sync(1, kEpiThreads);
+                if (epi_tid == 0) stamp(10);
+                for (int t = ew; t < T; t += kEpiWarps) {
+                    const Selection sel = route_one_token<EPL, true>(rs.logits + t * E, s_rp, rs.probs[ew], lane);
+                    if (lane < K) {
+                        rs.idx[t * K + lane] = sel.idx;
+                        rs.w[t * K + lane] = sel.w;
+                        atomicAdd(&s_cnt[sel.idx], 1);
+                        atomicOr(&rs.emask[sel.idx][t >> 5], 1u << (t & 31));
+                        if (blockIdx.x == 0) {
+                            args.topk_idx[t * K + lane] = sel.idx;
+                            args.topk_w[t * K + lane] = sel.w;
+                        }
+                    }
+                }
+                named_bar_sync(1, kEpiThreads);
+                if (epi_tid == 0) stamp(11);
+            }
+        } else {
+            // (2g) Router logits as warp tasks of (expert e, 8 tokens): the warp streams
+            // the router row once for its 8 tokens.  Consecutive warps take consecutive
+            // experts of the same tokens, so a CTA's token rows stay in L1.
+            const int ntg = (T + kLogitTokens - 1) / kLogitTokens;
+            for (int p = blockIdx.x * kEpiWarps + ew; p < E * ntg; p += G * kEpiWarps) {
+                const int tg = p / E;
+                const int e = p - tg * E;
+                const int t0 = tg * kLogitTokens;
+                const int nt = min(kLogitTokens, T - t0);
+                const float* wr = args.router + static_cast<size_t>(e) * H;
+                float acc[kLogitTokens];
+#pragma unroll
+                for (int j = 0; j < kLogitTokens; ++j) acc[j] = 0.0f;
+                // Every load of a step is issued before any is used (a load under a
+                // token-count branch would wait out its own round trip): tokens past the
+                // batch re-read its last row and are never stored.
+                if (args.x_f32 != nullptr) {
+                    for (int hh = lane * 8; hh < H; hh += 256) {
+                        float wv[8];
+                        load8(wr + hh, wv);
+#pragma unroll
+                        for (int j = 0; j < kLogitTokens; ++j) {
+                            float xv[8];
+                            load8(args.x_f32 + static_cast<size_t>(min(t0 + j, T - 1)) * H + hh, xv);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) acc[j] = fmaf(xv[i], wv[i], acc[j]);
+                        }
+                    }
+                } else {
+#pragma unroll 2
+                    for (int hh = lane * 8; hh < H; hh += 256) {
+                        float wv[8];
+                        load8(wr + hh, wv);
+                        uint4 raw[kLogitTokens];
+#pragma unroll
+                        for (int j = 0; j < kLogitTokens; ++j)
+                            raw[j] = *reinterpret_cast<const uint4*>(args.x + static_cast<size_t>(min(t0 + j, T - 1)) * H + hh);
+#pragma unroll
+                        for (int j = 0; j < kLogitTokens; ++j) {
+                            const uint32_t words[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                acc[j] = fmaf(__uint_as_float(words[i] << 16), wv[2 * i], acc[j]);
+                                acc[j] = fmaf(__uint_as_float(words[i] & 0xFFFF0000u), wv[2 * i + 1], acc[j]);
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < kLogitTokens; ++j) {
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) acc[j] += __shfl_xor_sync(kFull, acc[j], off);
+                }
+                float v = acc[0];
+#pragma unroll
+                for (int j = 1; j < kLogitTokens; ++j)
+                    if (lane == j) v = acc[j];
+                if (lane < nt) args.logits[(t0 + lane) * E + e] = args.bias != nullptr ? v + args.bias[e] : v;
+            }
+            arrive_grid(kCtrLogits);
+            if (epi_tid == 0) stamp(1);
+            ok = wait_grid(kCtrLogits);
+            if (epi_tid == 0) stamp(2);
+            if (ok) {
+                // (3g) Each token's top-k once in the grid: token t on warp t / G of CTA t % G.
+                for (int t = blockIdx.x + G * ew; t < T; t += G * kEpiWarps) {
+                    const Selection sel = route_one_token<EPL, false>(args.logits + t * E, s_rp, rs.probs[ew], lane);
+                    if (lane < K) {
                         args.topk_idx[t * K + lane] = sel.idx;
                         args.topk_w[t * K + lane] = sel.w;
                     }
                 }
+                arrive_grid(kCtrTopk);
+                if (epi_tid == 0) stamp(9);
+                ok = wait_grid(kCtrTopk);
+                if (epi_tid == 0) stamp(13);
             }
-            named_bar_sync(1, kEpiThreads);
-            if (epi_tid == 0) stamp(11);
+            if (ok) {
+                // (4g) Every CTA reads all selections and builds the same histogram.
+                for (int q = epi_tid; q < T * K; q += kEpiThreads) {
+                    const int e = __ldcg(args.topk_idx + q);
+                    const int t = q / K;
+                    rs.idx[q] = e;
+                    rs.w[q] = __ldcg(args.topk_w + q);
+                    atomicAdd(&s_cnt[e], 1);
+                    atomicOr(&rs.emask[e][t >> 5], 1u << (t & 31));
+                }
+                named_bar_sync(1, kEpiThreads);
+                if (epi_tid == 0) stamp(11);
+            }
+        }
+
+        if (ok) {
             // (4) Active experts and their first rows: a warp-wide compaction and scan.
             if (ew == 0) {
                 int n = 0, off = 0;
@@ -513,15 +652,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             // expert at most once, so its rank there counts the expert's earlier tokens.
             const int n_pairs = T * K;
             for (int q = epi_tid; q < n_pairs; q += kEpiThreads) {
-                const int e = s_idx[q];
+                const int e = rs.idx[q];
                 const int t = q / K;
-                const int row = s_eoff[e] + __popc(s_emask[e] & ((1u << t) - 1u));
+                int r = 0;
+                for (int w = 0; w < (t >> 5); ++w) r += __popc(rs.emask[e][w]);
+                r += __popc(rs.emask[e][t >> 5] & ((1u << (t & 31)) - 1u));
+                const int row = s_eoff[e] + r;
                 s_row_token[row] = t;
-                s_row_w[row] = s_w[q];
+                s_row_w[row] = rs.w[q];
+            }
+            // (6) The two lists' tile prefixes (warps 1 and 2 of the epilogue).
+            if (ew == 1 || ew == 2) {
+                const int list = ew - 1;
+                const int ng = nsh + s_n_act;
+                const int mbn = list == 0 ? mb1 : mb2;
+                int run = 0;
+                if (lane == 0) s_tp[list][0] = 0;
+                for (int base = 0; base < ng; base += 32) {
+                    const int g = base + lane;
+                    int v = 0;
+                    if (g < ng) {
+                        const bool shared = list == 0 ? g < nsh : g >= s_n_act;
+                        const int rows = shared ? T : s_cnt[s_seg_e[list == 0 ? g - nsh : g]];
+                        v = (gather ? (rows + kDecodeColTile - 1) / kDecodeColTile : 1) * mbn;
+                    }
+                    int incl = v;
+#pragma unroll
+                    for (int d = 1; d < 32; d <<= 1) {
+                        const int o = __shfl_up_sync(kFull, incl, d);
+                        if (lane >= d) incl += o;
+                    }
+                    if (g < ng) s_tp[list][g + 1] = run + incl;
+                    run += __shfl_sync(kFull, incl, 31);
+                }
             }
             named_bar_sync(1, kEpiThreads);
             if (epi_tid == 0) {
-                mbar_arrive(sched_ready);  // producer and MMA may decode lists 2-3
+                mbar_arrive(sched_ready);  // producer and MMA may decode the lists
                 stamp(3);
             }
             if (blockIdx.x == 0) {
@@ -531,16 +698,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 for (int e = epi_tid; e < E; e += kEpiThreads) args.expert_totals[e] = s_cnt[e];
             }
+            if (gather) {
+                // (7g) This CTA's share of the token rows into expert order.
+                const int q0 = static_cast<int>(static_cast<int64_t>(n_pairs) * blockIdx.x / G);
+                const int q1 = static_cast<int>(static_cast<int64_t>(n_pairs) * (blockIdx.x + 1) / G);
+                const int vec = H / 8;
+                for (int q = q0; q < q1; ++q) {
+                    const uint4* src = reinterpret_cast<const uint4*>(args.x + static_cast<size_t>(s_row_token[q]) * H);
+                    uint4* dst = reinterpret_cast<uint4*>(args.x_perm + static_cast<size_t>(q) * H);
+                    for (int i = epi_tid; i < vec; i += kEpiThreads) dst[i] = src[i];
+                }
+                fence_proxy_async_global();
+                arrive_grid(kCtrXperm);
+                if (epi_tid == 0) stamp(14);
+            }
         }
 
-        // (6) Epilogues of both lists, in the order the MMA issuer produced them.
+        // (8) Epilogues of both lists, in the order the MMA issuer produced them.
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int list = 0; list <= 1 && ok; ++list) {
             if (list == 1) {
                 // Every h row this CTA writes is written: publish them for the TMA reads.
                 fence_proxy_async_global();
-                arrive_grid(1);
+                arrive_grid(kCtrH);
                 if (epi_tid == 0) stamp(4);
             }
             const int tiles = list_tiles(list);
@@ -558,8 +739,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t t_row =
                     tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-                // Gate/up columns are tokens 0..T-1; down columns are the expert's h rows.
-                const int ncols = list == 1 ? u.rows : T;
+                // TMEM columns holding results: direct-mode routed gate/up has every token
+                // as a column; otherwise the unit's own rows.
+                const int ncols = u.by_token ? T : u.nout;
                 const bool whole = kb0 == 0 && kb1 == nkb;
                 if (list == 0 && !whole) {
                     // Partial gate/up tile: store the partial sums in this CTA's slot,
@@ -594,9 +776,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // CTA owning iteration j: the largest c with iters * c / G <= j.
                         const int c_lo = static_cast<int>(((j0 + 1) * G + iters - 1) / iters) - 1;
                         const int c_hi = static_cast<int>(((j0 + nkb) * G + iters - 1) / iters) - 1;
-                        // Items: (h row j, pair of intermediate columns) -> one float4 of
+                        // Items: (output row j, pair of intermediate columns) -> one float4 of
                         // (gate, up, gate, up); all of a part's loads are in flight together.
-                        const int items = u.rows * 32;
+                        const int items = u.nout * 32;
                         float4 sum[kReduceItems];
 #pragma unroll
                         for (int k = 0; k < kReduceItems; ++k) sum[k] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -605,7 +787,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int k = 0; k < kReduceItems; ++k) {
                             const int q = epi_tid + k * kEpiThreads;
                             const int j = q >> 5;
-                            col[k] = q < items ? (u.routed ? s_row_token[u.row0 + j] : j) : 0;
+                            col[k] = q < items ? (u.by_token ? s_row_token[u.hrow0 + j] : j) : 0;
                         }
                         // Parts in batches of kReduceParts, every load of a batch in flight
                         // at once (under a saturated HBM stream each L2 round trip is long).
@@ -644,7 +826,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 const int j = q >> 5;
                                 const __nv_bfloat162 hv = __floats2bfloat162_rn(silu_times(sum[k].x, sum[k].y),
                                                                                 silu_times(sum[k].z, sum[k].w));
-                                *reinterpret_cast<__nv_bfloat162*>(args.h + static_cast<size_t>(u.row0 + j) * I +
+                                *reinterpret_cast<__nv_bfloat162*>(args.h + static_cast<size_t>(u.hrow0 + j) * I +
                                                                    u.mb * 64 + 2 * (q & 31)) = hv;
                             }
                         }
@@ -673,12 +855,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (lane == 0) mbar_arrive(&tmem_empty[acc]);
                     named_bar_sync(1, kEpiThreads);
                     const uint4* src = reinterpret_cast<const uint4*>(staging);
-                    for (int q = epi_tid; q < u.rows * 8; q += kEpiThreads) {
+                    for (int q = epi_tid; q < u.nout * 8; q += kEpiThreads) {
                         const int j = q >> 3;
                         const int part = q & 7;
-                        const int col = u.routed ? s_row_token[u.row0 + j] : j;
+                        const int col = u.by_token ? s_row_token[u.hrow0 + j] : j;
                         uint4* dst =
-                            reinterpret_cast<uint4*>(args.h + static_cast<size_t>(u.row0 + j) * I + u.mb * 64) + part;
+                            reinterpret_cast<uint4*>(args.h + static_cast<size_t>(u.hrow0 + j) * I + u.mb * 64) + part;
                         *dst = src[col * 8 + part];
                     }
                     named_bar_sync(1, kEpiThreads);
@@ -695,8 +877,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 16; ++j) {
                             const int c = c0 + j;
                             if (c < ncols) {
-                                const int tok = u.routed ? s_row_token[u.row0 + c] : c;
-                                const float w = u.routed ? s_row_w[u.row0 + c] : 1.0f;
+                                const int tok = u.routed ? s_row_token[u.hrow0 + c] : u.tok0 + c;
+                                const float w = u.routed ? s_row_w[u.hrow0 + c] : 1.0f;
                                 atomicAdd(args.y + static_cast<size_t>(tok) * H + d, w * __uint_as_float(r[j]));
                             }
                         }
@@ -724,17 +906,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Every wait of this CTA is over.  The last CTA to get here has seen every CTA
     // finish waiting, so it re-arms the counters for the next launch.
     if (threadIdx.x == 0 &&
-        atom_acq_rel_add_u64(args.grid_bar + 2, 1ull) == static_cast<unsigned long long>(G) - 1ull) {
-        args.grid_bar[0] = 0ull;
-        args.grid_bar[1] = 0ull;
-        args.grid_bar[2] = 0ull;
+        atom_acq_rel_add_u64(args.grid_bar + kCtrExit, 1ull) == static_cast<unsigned long long>(G) - 1ull) {
+        for (int i = 0; i < kDecodeCounters; ++i) args.grid_bar[i] = 0ull;
         __threadfence();
     }
 }
 
 template <int BN, int EPL>
-cudaError_t launch_t(const CUtensorMap& w13, const CUtensorMap& w2, const CUtensorMap& x, const CUtensorMap& h,
-                     const DecodeArgs& args, int sms, cudaStream_t stream) {
+cudaError_t launch_t(const CUtensorMap& w13, const CUtensorMap& w2, const CUtensorMap& x, const CUtensorMap& xperm,
+                     const CUtensorMap& h, const DecodeArgs& args, int sms, cudaStream_t stream) {
     using C = DCfg<BN>;
     auto kernel = moe_decode_kernel<BN, EPL>;
     static std::atomic<uint64_t> configured{0};  // devices whose limit is raised
@@ -754,25 +934,28 @@ cudaError_t launch_t(const CUtensorMap& w13, const CUtensorMap& w2, const CUtens
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kernel, w13, w2, x, h, args);
+    return cudaLaunchKernelEx(&cfg, kernel, w13, w2, x, xperm, h, args);
 }
 
 }  // namespace
 
 cudaError_t launch_moe_decode(int bn, const CUtensorMap& w13, const CUtensorMap& w2, const CUtensorMap& x,
-                              const CUtensorMap& h, const DecodeArgs& args, int sms, cudaStream_t stream) {
+                              const CUtensorMap& xperm, const CUtensorMap& h, const DecodeArgs& args, int sms,
+                              cudaStream_t stream) {
     if (args.tokens <= 0) return cudaSuccess;
-    if (args.tokens > kDecodeMaxTokens || args.tokens > bn || args.rp.experts > kMaxExperts ||
-        args.rp.top_k > kMaxTopK || args.tokens * args.rp.experts > kDecodeMaxLogits)
+    const bool gather = args.gather != 0;
+    if (args.tokens > kDecodeMaxTokens || args.rp.experts > kMaxExperts || args.rp.top_k > kMaxTopK ||
+        args.tokens * args.rp.top_k > kDecodeMaxRows || args.n_shared > kMaxShared ||
+        (gather ? bn != kDecodeColTile : (args.tokens > bn || args.tokens * args.rp.experts > kDecodeMaxLogits)))
         return cudaErrorInvalidValue;
     const int need = (args.rp.experts + 31) / 32;
     const int epl = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : 8;
 #define LM_DECODE(BN_)                                                                \
     switch (epl) {                                                                    \
-        case 1: return launch_t<BN_, 1>(w13, w2, x, h, args, sms, stream);            \
-        case 2: return launch_t<BN_, 2>(w13, w2, x, h, args, sms, stream);            \
-        case 4: return launch_t<BN_, 4>(w13, w2, x, h, args, sms, stream);            \
-        default: return launch_t<BN_, 8>(w13, w2, x, h, args, sms, stream);           \
+        case 1: return launch_t<BN_, 1>(w13, w2, x, xperm, h, args, sms, stream);     \
+        case 2: return launch_t<BN_, 2>(w13, w2, x, xperm, h, args, sms, stream);     \
+        case 4: return launch_t<BN_, 4>(w13, w2, x, xperm, h, args, sms, stream);     \
+        default: return launch_t<BN_, 8>(w13, w2, x, xperm, h, args, sms, stream);    \
     }
     if (bn == 16) LM_DECODE(16)
     if (bn == 32) LM_DECODE(32)

@@ -93,7 +93,10 @@ struct lm_moe_ctx {
     uint16_t* h = nullptr;
     int32_t* status = nullptr;
     int split_max_waves = 4;          // split-K below this many waves of tiles (LITEMIND_B200_SPLIT_WAVES)
-    bool fused_decode = true;         // T <= 32 on one GPU: one cooperative launch (LITEMIND_B200_FUSED_DECODE=0: off)
+    bool fused_decode = true;         // decode sizes on one GPU: one cooperative launch (LITEMIND_B200_FUSED_DECODE=0: off)
+    int fused_max_tokens = lm::kDecodeMaxTokens;    // largest batch for it (LITEMIND_B200_FUSED_MAX_TOKENS)
+    int fused_gather_from = lm::kDecodeDirectTokens + 1;  // smallest batch it gathers rows for
+                                                          // (LITEMIND_B200_FUSED_GATHER_FROM)
     unsigned long long* grid_bar = nullptr;  // the fused decode kernel's arrival counters (self-resetting)
     // Testing only (lm_moe_debug_set): arrivals the fused kernel's grid waits expect
     // beyond the grid (so the waits run out), and the bound of those waits (0: 2 s).
@@ -460,7 +463,7 @@ lm_status settle_status(lm_moe_ctx* ctx, int32_t status) {
     if (status != 0) {
         LM_CUDA(ctx, cudaMemset(ctx->status, 0, sizeof(int32_t)));
         // An aborted fused decode launch leaves its grid counters short: restart them.
-        LM_CUDA(ctx, cudaMemset(ctx->grid_bar, 0, 3 * sizeof(unsigned long long)));
+        LM_CUDA(ctx, cudaMemset(ctx->grid_bar, 0, kDecodeCounters * sizeof(unsigned long long)));
         LM_CUDA(ctx, cudaMemset(ctx->split_ticket, 0, kSplitTickets * sizeof(int32_t)));
         LM_CUDA(ctx, cudaMemset(ctx->ticket, 0, kRouteTickets * sizeof(unsigned int)));
         const char* what = status == kDevBadTile  ? "a tile outside the schedule"
@@ -547,6 +550,9 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
     ctx->sms = prop.multiProcessorCount;
     if (const char* w = std::getenv("LITEMIND_B200_SPLIT_WAVES")) ctx->split_max_waves = std::max(0, std::atoi(w));
     if (const char* f = std::getenv("LITEMIND_B200_FUSED_DECODE")) ctx->fused_decode = std::atoi(f) != 0;
+    if (const char* f = std::getenv("LITEMIND_B200_FUSED_MAX_TOKENS")) ctx->fused_max_tokens = std::atoi(f);
+    if (const char* f = std::getenv("LITEMIND_B200_FUSED_GATHER_FROM"))
+        ctx->fused_gather_from = std::max(1, std::atoi(f));
     ctx->local_experts = c.n_routed_experts;
     ctx->n_seg = ctx->local_experts + c.n_shared_experts;
     ctx->routed_cap = c.max_tokens * c.num_experts_per_tok;
@@ -567,7 +573,7 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
         (st = alloc(p, &p->status, 1)) || (st = alloc(p, &p->ticket, kRouteTickets)) ||
         (st = alloc(p, &p->split_ws, kSplitWsBytes / sizeof(float))) ||
         (st = alloc(p, &p->split_ticket, static_cast<size_t>(kSplitTickets))) ||
-        (st = alloc(p, &p->grid_bar, 3))) {
+        (st = alloc(p, &p->grid_bar, kDecodeCounters))) {
         lm_moe_destroy(ctx.release());
         return st;
     }
@@ -577,7 +583,7 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
         cudaMemset(p->sched, 0, sizeof(Schedule)) != cudaSuccess ||
         cudaMemset(p->split_ws, 0, kSplitWsBytes) != cudaSuccess ||
         cudaMemset(p->split_ticket, 0, kSplitTickets * sizeof(int32_t)) != cudaSuccess ||
-        cudaMemset(p->grid_bar, 0, 3 * sizeof(unsigned long long)) != cudaSuccess) {
+        cudaMemset(p->grid_bar, 0, kDecodeCounters * sizeof(unsigned long long)) != cudaSuccess) {
         lm_moe_destroy(ctx.release());
         return LM_ERR_CUDA;
     }
@@ -1056,12 +1062,20 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
     int n_slots = 0;
     const RouterParams rp = router_params(c);
     float* y_zero = accumulate ? nullptr : y;  // the down GEMM adds into y
-    const int fused_bn = T <= 16 ? 16 : 32;
+    // Decode sizes: the whole layer in one cooperative launch.  Up to
+    // kDecodeDirectTokens tokens every expert reads x itself; above, routed token rows
+    // are gathered in the kernel and tiled 32 at a time.
+    const bool gather = T >= ctx->fused_gather_from;
+    const int fused_bn = gather ? kDecodeColTile : T <= 16 ? 16 : 32;
     const int max_active = std::min(E, T * K);
-    if (ctx->fused_decode && T <= kDecodeMaxTokens && ctx->comm == nullptr && T * E <= kDecodeMaxLogits &&
-        (c.n_shared_experts + max_active) * (2 * I / 128) <= kSplitTickets &&
+    const int fused_tiles =
+        gather ? (c.n_shared_experts * ((T + kDecodeColTile - 1) / kDecodeColTile) + max_active +
+                  (T * K + kDecodeColTile - 1) / kDecodeColTile) * (2 * I / 128)
+               : (c.n_shared_experts + max_active) * (2 * I / 128);
+    if (ctx->fused_decode && T <= ctx->fused_max_tokens && T <= kDecodeMaxTokens && T * K <= kDecodeMaxRows &&
+        ctx->comm == nullptr && (gather || (T <= kDecodeDirectTokens && T * E <= kDecodeMaxLogits)) &&
+        fused_tiles <= kSplitTickets &&
         static_cast<size_t>(2) * ctx->sms * 128 * fused_bn * sizeof(float) <= kSplitWsBytes) {
-        // Decode: the whole layer in one cooperative launch.
         CUtensorMap map_x{};
         std::string err;
         if (!encode_tensor_map_bf16(&map_x, x, T, H, fused_bn, 64, err)) return fail(ctx, LM_ERR_INVALID_ARGUMENT, err);
@@ -1077,16 +1091,16 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
         a.inter = I;
         a.n_shared = c.n_shared_experts;
         a.rp = rp;
+        a.gather = gather ? 1 : 0;
         a.logits = ctx->logits;
         a.topk_idx = ctx->topk_idx;
         a.topk_w = ctx->topk_w;
         a.expert_totals = ctx->expert_totals;
         a.row_token = ctx->row_token;
         a.row_weight = ctx->row_weight;
+        a.x_perm = ctx->x_perm;
         a.h = ctx->h;
         a.h_shared_base = ctx->routed_cap;
-        a.w13_shared = reinterpret_cast<const uint8_t*>(L.w13 + static_cast<size_t>(ctx->local_experts) * 2 * I * H);
-        a.w13_shared_bytes = static_cast<uint64_t>(c.n_shared_experts) * 2 * I * H * 2;
         a.split_ws = ctx->split_ws;
         a.split_ticket = ctx->split_ticket;
         a.grid_bar = ctx->grid_bar;
@@ -1099,7 +1113,8 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
                                                                                    kDecodeTraceSlots * 8, s));
         a.trace = ctx->profiling ? ctx->decode_trace : nullptr;
         const int fbi = bn_index(fused_bn);
-        LM_CUDA(ctx, launch_moe_decode(fused_bn, L.map_w13, L.map_w2, map_x, ctx->map_h[fbi], a, ctx->sms, s));
+        LM_CUDA(ctx, launch_moe_decode(fused_bn, L.map_w13, L.map_w2, map_x, ctx->map_xperm[bn_index(kDecodeColTile)],
+                                       ctx->map_h[fbi], a, ctx->sms, s));
         prof_mark(ctx, 8, s);
         slots[n_slots++] = 8;
         return prof_end(ctx, slots, n_slots);

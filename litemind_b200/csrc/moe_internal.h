@@ -146,9 +146,12 @@ struct GemmArgs {
     int32_t split_ws_floats;   // capacity of split_ws in floats
     int32_t split_max_waves;   // split when the tiles fill fewer waves of the grid than this (0: never)
 };
-// The fused decode kernel (decode_fused.cu): the whole layer for T <= 32 tokens in
+// The fused decode kernel (decode_fused.cu): the whole layer for T <= 128 tokens in
 // one cooperative launch -- routing, dispatch, gate/up, down and the combine.
-constexpr int kDecodeMaxTokens = 32;
+constexpr int kDecodeMaxTokens = 128;
+constexpr int kDecodeMaxRows = 1024;        // tokens x top-k
+constexpr int kDecodeDirectTokens = 32;     // up to this many tokens: x itself is every expert's token operand
+constexpr int kDecodeColTile = 32;          // token rows per column tile above that (gather mode)
 struct DecodeArgs {
     const uint16_t* x;         // [T, hidden] bf16 tokens (GEMM operand; logits too unless x_f32)
     const float* x_f32;        // optional [T, hidden] f32 tokens for the router logits
@@ -161,34 +164,39 @@ struct DecodeArgs {
     int32_t inter;
     int32_t n_shared;
     RouterParams rp;
+    int32_t gather;            // 1: routed token rows are gathered into x_perm and tiled 32 at a time
     float* logits;             // [T, E] (output, also the exchange between CTAs)
-    int32_t* topk_idx;         // [T, k] outputs
+    int32_t* topk_idx;         // [T, k] outputs (gather mode: also the exchange between CTAs)
     float* topk_w;
     int32_t* expert_totals;    // [E]
     int32_t* row_token;        // [T * k] expert-sorted row -> token
     float* row_weight;         // [T * k] expert-sorted row -> routing weight
+    uint16_t* x_perm;          // gather mode: [T * k, hidden] expert-sorted token rows
     uint16_t* h;               // SwiGLU outputs: routed rows, then n_shared blocks of T rows
-    const uint8_t* w13_shared; // the shared experts' gate/up tiles (contiguous), prefetched into L2
-    uint64_t w13_shared_bytes;
     int32_t h_shared_base;     // first h row of the shared experts
     float* split_ws;           // gate/up split-K partials: 2 slots of [BN][128] per CTA
     int32_t* split_ticket;     // per gate/up tile, zero between uses
-    unsigned long long* grid_bar;  // [3] arrival counters: logits, h, and CTAs finished (the last
-                                   // CTA to finish zeroes all three for the next launch)
+    unsigned long long* grid_bar;  // [kDecodeCounters] arrival counters: logits, h, x_perm, top-k, and
+                                   // CTAs finished (the last CTA to finish zeroes all of them)
     uint32_t grid_extra;           // testing only: arrivals each grid wait expects beyond gridDim.x
     uint64_t wait_limit_ns;        // bound of the grid waits
     int32_t* status;
     unsigned long long* trace;     // optional: kDecodeTraceSlots global-timer stamps per CTA
 };
+constexpr int kDecodeCounters = 5;
 // Phase stamps of the fused decode kernel (profiling only), per CTA:
 //  0 start  1 logits written  2 every CTA's logits seen  3 schedule built
 //  4 gate/up epilogues done  5 producer saw every h row  6 producer issued
-//  everything  7 down epilogues done  8 MMA done
+//  everything  7 down epilogues done  8 MMA done  9 top-k written (gather mode)
+//  10 logits loaded (direct mode)  11 routed  12 experts scanned
+//  13 every CTA's top-k seen  14 rows gathered  15 producer saw every gathered row
 constexpr int kDecodeTraceSlots = 16;
-// Router logits the fused decode kernel keeps in shared memory (tokens x experts).
+// Router logits the fused decode kernel keeps in shared memory in direct mode
+// (tokens x experts).
 constexpr int kDecodeMaxLogits = 4096;
 cudaError_t launch_moe_decode(int bn, const CUtensorMap& w13, const CUtensorMap& w2, const CUtensorMap& x,
-                              const CUtensorMap& h, const DecodeArgs& args, int sms, cudaStream_t stream);
+                              const CUtensorMap& xperm, const CUtensorMap& h, const DecodeArgs& args, int sms,
+                              cudaStream_t stream);
 
 // Expert parallelism exchanges fixed blocks (no host round trip) while
 // nranks x rows-per-block stays within this many rows.
