@@ -14,8 +14,9 @@
 
 #include <cstddef>
 #include <cstdint>
-#include <list>
+#include <map>
 #include <unordered_map>
+#include <vector>
 
 namespace litemind::b200 {
 
@@ -52,7 +53,7 @@ public:
     [[nodiscard]] bool enabled() const noexcept { return budget_bytes_ != 0U; }
     [[nodiscard]] std::uint64_t budget_bytes() const noexcept { return budget_bytes_; }
     [[nodiscard]] std::uint64_t resident_bytes() const noexcept { return resident_bytes_; }
-    [[nodiscard]] std::size_t resident_experts() const noexcept { return entries_.size(); }
+    [[nodiscard]] std::size_t resident_experts() const noexcept { return slot_of_.size(); }
     [[nodiscard]] std::uint64_t loads() const noexcept { return loads_; }
     [[nodiscard]] std::uint64_t hits() const noexcept { return hits_; }
     [[nodiscard]] std::uint64_t evictions() const noexcept { return evictions_; }
@@ -64,18 +65,25 @@ public:
     }
 
 private:
-    struct Entry final {
+    // The residency ledger: one slot per resident expert in a flat vector (slots of
+    // evicted experts are reused), the key -> slot index, and the slots ordered by
+    // the tick of their last touch -- the smallest tick is the least recently used.
+    struct Slot final {
+        std::uint64_t key{};
         std::uint64_t bytes{};
-        std::list<std::uint64_t>::iterator position;
+        std::uint64_t last_touch{};
     };
 
-    void evict_oldest();
+    void drop_least_recent();
 
     MoeLayer* layer_{nullptr};
     std::uint64_t budget_bytes_{};
     std::uint64_t resident_bytes_{};
-    std::list<std::uint64_t> recency_;  ///< Most recently used first.
-    std::unordered_map<std::uint64_t, Entry> entries_;
+    std::uint64_t clock_{};
+    std::vector<Slot> slots_;
+    std::vector<std::uint32_t> free_slots_;
+    std::unordered_map<std::uint64_t, std::uint32_t> slot_of_;
+    std::map<std::uint64_t, std::uint32_t> by_last_touch_;
     std::uint64_t loads_{};
     std::uint64_t hits_{};
     std::uint64_t evictions_{};

@@ -8,26 +8,25 @@
 #include <vector>
 
 #include "CopyPool.hpp"
-#include "TestSupport.hpp"
-
-using test_support::check;
+#include "Expect.hpp"
 
 int main() {
+    Expect expect("CopyPoolTest");
     lm::CopyPool pool(8);
-    check(pool.threads() == 8, "thread count");
+    expect(pool.threads() == 8, "thread count");
     for (int rep = 0; rep < 500; ++rep) {
         const int n = 1 + rep % 97;
         std::vector<int> hits(static_cast<size_t>(n), 0);
         pool.run(n, [&](int i) { hits[static_cast<size_t>(i)] += 1; });
         bool once = true;
         for (int v : hits) once = once && v == 1;
-        check(once, "every index exactly once");
-        pool.run(0, [&](int) { check(false, "empty run calls nothing"); });
+        expect(once, "every index exactly once");
+        pool.run(0, [&](int) { expect(false, "empty run calls nothing"); });
     }
     lm::CopyPool single(1);
     int sum = 0;
     single.run(10, [&](int i) { sum += i; });  // caller only: no race on sum
-    check(sum == 45, "one-thread pool");
+    expect(sum == 45, "one-thread pool");
     // Pieces of 1 KiB copied in parallel reassemble a 1 MiB buffer.
     std::vector<uint16_t> src(1 << 19), dst(1 << 19, 0);
     std::iota(src.begin(), src.end(), uint16_t{7});
@@ -36,6 +35,6 @@ int main() {
         std::memcpy(dst.data() + static_cast<size_t>(i) * piece, src.data() + static_cast<size_t>(i) * piece,
                     piece * sizeof(uint16_t));
     });
-    check(src == dst, "parallel pieces reassemble the source");
-    return test_support::report("CopyPoolTest");
+    expect(src == dst, "parallel pieces reassemble the source");
+    return expect.finish();
 }

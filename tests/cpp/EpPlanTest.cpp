@@ -5,13 +5,12 @@
 #include <random>
 #include <vector>
 
-#include "TestSupport.hpp"
+#include "Expect.hpp"
 #include "litemind_b200/MoeLayer.hpp"
 
 using litemind::b200::ep_plan;
-using test_support::check;
-
 int main() {
+    Expect expect("EpPlanTest");
     constexpr int32_t world = 4, experts = 32, local = experts / world;
     std::mt19937 gen(7);
     std::uniform_int_distribution<int32_t> dist(0, 9);
@@ -24,21 +23,21 @@ int main() {
         for (int32_t k = 0; k < chunks; ++k) plans.push_back(ep_plan(world, send, recv, chunks, k));
         int32_t base = 0;
         for (const lm_ep_plan& p : plans) {
-            check(p.recv_offset[0] == base, "chunks stack in the receive buffer");
+            expect(p.recv_offset[0] == base, "chunks stack in the receive buffer");
             base += p.n_recv;
         }
-        check(base == whole.n_recv, "chunks receive every row");
+        expect(base == whole.n_recv, "chunks receive every row");
         for (int32_t d = 0; d < world; ++d) {
             int32_t pos = whole.send_offset[d];
             for (int32_t k = 0; k < chunks; ++k) {
                 const int32_t lo = k * local / chunks, hi = (k + 1) * local / chunks;
                 int32_t want = 0;
                 for (int32_t e = lo; e < hi; ++e) want += send[static_cast<size_t>(d * local + e)];
-                check(plans[static_cast<size_t>(k)].send_offset[d] == pos, "send ranges in order");
-                check(plans[static_cast<size_t>(k)].send_count[d] == want, "send count of the chunk");
+                expect(plans[static_cast<size_t>(k)].send_offset[d] == pos, "send ranges in order");
+                expect(plans[static_cast<size_t>(k)].send_count[d] == want, "send count of the chunk");
                 pos += want;
             }
-            check(pos == whole.send_offset[d] + whole.send_count[d], "chunks send every row");
+            expect(pos == whole.send_offset[d] + whole.send_count[d], "chunks send every row");
         }
     }
     bool threw = false;
@@ -47,6 +46,6 @@ int main() {
     } catch (const litemind::b200::Error& e) {
         threw = e.status() == LM_ERR_INVALID_ARGUMENT;
     }
-    check(threw, "too many chunks is an error");
-    return test_support::report("EpPlanTest");
+    expect(threw, "too many chunks is an error");
+    return expect.finish();
 }
