@@ -8,10 +8,14 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <string>
 
 #include "litemind_moe.h"
 
 namespace litemind::b200::gemm {
+
+/** Which kernels this build runs, for logs (the reference's gemm::kernel_description). */
+inline std::string kernel_description() { return lm_kernel_description(); }
 
 /** out = weights * input, weights row-major [out_dim, in_dim] bf16. */
 inline lm_status matvec_bf16(const std::uint16_t* weights, const float* input, float* out, std::size_t out_dim,

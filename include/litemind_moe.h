@@ -357,6 +357,10 @@ lm_status lm_moe_route_static(const float* router, const uint16_t* x, int32_t to
 
 /* ── gemm:: kernels on device memory (include/Gemm.hpp:23-72) ──────────────── */
 
+/* gemm::kernel_description (src/Gemm.cpp:108-123): which kernels this build runs, for
+ * logs.  A static string; needs no GPU. */
+const char* lm_kernel_description(void);
+
 /* gemm::matvec_bf16 (src/Gemm.cpp:139-154): out = W x, W [rows, cols] bf16. */
 lm_status lm_gemm_matvec_bf16(const uint16_t* weights, const float* input, float* out,
                               int64_t rows, int64_t cols, void* stream);

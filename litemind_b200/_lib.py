@@ -92,6 +92,7 @@ SIGNATURES = {
     "lm_moe_profile_trace": (_i32, [_vp, _vp, _i32, _vp]),
     "lm_moe_profile_ep_timeline": (_i32, [_vp, _vp, _i32, C.POINTER(C.c_int32)]),
     "lm_moe_route_static": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp]),
+    "lm_kernel_description": (C.c_char_p, []),
     "lm_gemm_matvec_bf16": (_i32, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "lm_gemm_matvec_bf16_accumulate": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp]),
     "lm_gemm_matvec_f32": (_i32, [_vp, _vp, _vp, _i64, _i64, _vp]),

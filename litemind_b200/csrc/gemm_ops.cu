@@ -223,6 +223,14 @@ using lm::finish;
 
 extern "C" {
 
+const char* lm_kernel_description(void) {
+    // The device code of this library is compiled for sm_100a only (no PTX for JIT),
+    // so the description is fixed at build time, as the reference's is.
+    return "sm_100a kernels: tcgen05/TMEM tensor cores fed by TMA -- the whole MoE layer in one cooperative "
+           "launch up to 128 tokens, grouped SwiGLU GEMMs (1-CTA and CTA-pair) above, warp-per-token router; "
+           "bf16 weights, f32 accumulate";
+}
+
 lm_status lm_gemm_matvec_bf16(const uint16_t* weights, const float* input, float* out, int64_t rows, int64_t cols,
                               void* stream) {
     if (rows < 0 || cols < 0 || (rows > 0 && (weights == nullptr || input == nullptr || out == nullptr)))

@@ -93,6 +93,11 @@ def test_new_entry_points_check_their_arguments(lib):
     assert lib.lm_moe_ep_init(None, buf, 0, 1) == _lib.LM_ERR_INVALID_ARGUMENT
 
 
+def test_kernel_description_names_the_b200_kernels(lib):
+    text = lib.lm_kernel_description().decode()
+    assert "sm_100a" in text and "tcgen05" in text
+
+
 def test_status_strings(lib):
     for code in range(8):
         assert lib.lm_status_string(code)
