@@ -8,8 +8,10 @@ per-expert counts, asks lm_moe_ep_plan for the send/recv counts and offsets, sen
 the rows with all_to_all_single, computes its local experts, returns the outputs in
 receive order, and combines them by slot with the routing weights, plus the shared
 experts.  With chunks > 1 the rows move in chunks of local experts planned by
-lm_moe_ep_chunk_plan, as lm_moe_forward's pipelined exchange moves them.  No GPU is
-used.
+lm_moe_ep_chunk_plan, as lm_moe_forward's pipelined exchange moves them.  The
+small-batch fixed-block exchange (one block of rows per rank pair, planned on the
+device) runs the same way through a restatement of its kernels' index math.  No GPU
+is used.
 """
 import os
 import socket
@@ -124,6 +126,101 @@ def _worker(rank, world, port, token_counts, chunks):
             np.testing.assert_allclose(y, ref_y, rtol=1e-4, atol=1e-5)
     finally:
         dist.destroy_process_group()
+
+
+def _worker_fixed(rank, world, port, token_counts, max_tokens):
+    """The fixed-block exchange (small batches, no host round trip): every rank sends
+    every peer one block of `cap` = max_tokens x min(k, local experts) rows with the
+    per-expert counts beside it.  The index math restates the device kernels: the
+    pack into destination blocks (ep_pack_kernel), the receiver's expert-major sort
+    with its row map (ep_sort_rows_kernel with a fixed source stride), the receiver's
+    schedule (ep_schedule_kernel), outputs stored back at their receive positions
+    (the down epilogue's y_rows_map), the blocks returned and the slot-ordered
+    weighted combine (ep_combine_kernel)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle.oracle import Oracle, RouterConfig
+
+        orc = Oracle()
+        W = syn.layer_weights(SHAPE, seed=5, std=0.1)
+        Wf = {k: (syn.bf16_to_f32(v).reshape(v.shape).astype(np.float64) if v.dtype == np.uint16 else v)
+              for k, v in W.items()}
+        E, K, H = SHAPE.n_routed_experts, SHAPE.top_k, SHAPE.hidden
+        El = E // world
+        cap = max_tokens * min(K, El)
+        T = token_counts[rank]
+        x = syn.bf16_to_f32(syn.tokens(SHAPE, max(T, 1), seed=20 + rank)).reshape(-1, H)[:T]
+        if T > 0:
+            ref_y, idx, w, _ = orc.moe_layer(x, W, RouterConfig(E, K), SHAPE.n_shared_experts)
+        else:
+            ref_y, idx, w = np.zeros((0, H), np.float32), np.zeros((0, K), np.int64), np.zeros((0, K), np.float32)
+        # Expert-sorted rows (token order within an expert) and each slot's row.
+        pairs = [(int(idx[t, s]), t) for t in range(T) for s in range(K)]
+        order = sorted(range(len(pairs)), key=lambda i: (pairs[i][0], i))
+        row_token = np.array([pairs[i][1] for i in order], np.int64)
+        slot_row = np.zeros(T * K, np.int64)
+        for row, i in enumerate(order):
+            slot_row[i] = row
+        counts = np.bincount(idx.reshape(-1), minlength=E).astype(np.int64)
+        off = np.concatenate([[0], np.cumsum(counts)])
+        # ep_pack: row r of expert e goes to destination d = e // El, at d * cap + its
+        # rank among the rows bound for d.
+        def padded(r):
+            e = int(np.searchsorted(off, r, side="right") - 1)
+            d = e // El
+            assert r - off[d * El] < cap, "a destination's rows exceed the fixed block"
+            return d * cap + (r - off[d * El])
+        x_send = np.zeros((world * cap, H))
+        for r in range(T * K):
+            x_send[padded(r)] = x[row_token[r]]
+        slot_row = np.array([padded(int(r)) for r in slot_row], np.int64)
+        # One exchange of counts and blocks.
+        recv_counts = torch.zeros(E, dtype=torch.int64)
+        dist.all_to_all_single(recv_counts, torch.from_numpy(counts))
+        rc = recv_counts.numpy().reshape(world, El)
+        x_recv = torch.zeros((world * cap, H), dtype=torch.float64)
+        dist.all_to_all_single(x_recv, torch.from_numpy(x_send))
+        x_recv = x_recv.numpy()
+        # ep_sort_rows with source stride cap: block (source r, local expert e).
+        n_recv = int(rc.sum())
+        x_sorted = np.zeros((n_recv, H))
+        row_src = np.full(n_recv, -1, np.int64)
+        for r in range(world):
+            for e in range(El):
+                src = r * cap + int(rc[r, :e].sum())
+                dst = int(rc[:, :e].sum()) + int(rc[:r, e].sum())
+                n = int(rc[r, e])
+                x_sorted[dst:dst + n] = x_recv[src:src + n]
+                row_src[dst:dst + n] = np.arange(src, src + n)
+        assert (row_src >= 0).all() and len(set(row_src.tolist())) == n_recv
+        # ep_schedule: one segment per local expert, expert-major, then the shared experts.
+        seg_off = np.concatenate([[0], np.cumsum(rc.sum(axis=0))])[:-1]
+        seg_cnt = rc.sum(axis=0)
+        assert seg_off[-1] + seg_cnt[-1] == n_recv if El else True
+        # Local experts; outputs stored at their receive positions.
+        y_ret = np.zeros((world * cap, H))
+        for e in range(El):
+            rows = slice(int(seg_off[e]), int(seg_off[e] + seg_cnt[e]))
+            ge = rank * El + e
+            y_ret[row_src[rows]] = _ffn(Wf["gate"][ge], Wf["up"][ge], Wf["down"][ge], x_sorted[rows])
+        y_back = torch.zeros((world * cap, H), dtype=torch.float64)
+        dist.all_to_all_single(y_back, torch.from_numpy(y_ret))
+        y_back = y_back.numpy()
+        # ep_combine: shared experts first, then the slots in selection order.
+        y = _ffn(Wf["shared_gate"], Wf["shared_up"], Wf["shared_down"], x.astype(np.float64))
+        for t in range(T):
+            for s in range(K):
+                y[t] += float(w[t, s]) * y_back[slot_row[t * K + s]]
+        if T > 0:
+            np.testing.assert_allclose(y, ref_y, rtol=1e-4, atol=1e-5)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,token_counts,max_tokens", [(2, (13, 7), 16), (2, (0, 5), 8), (4, (3, 0, 8, 8), 8)])
+def test_ep_fixed_block_protocol_gloo_ranks(world, token_counts, max_tokens):
+    mp.spawn(_worker_fixed, args=(world, _free_port(), token_counts, max_tokens), nprocs=world, join=True)
 
 
 # chunks > 1: the chunked exchange of lm_moe_ep_chunk_plan (4 local experts per rank
