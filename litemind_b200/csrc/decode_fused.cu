@@ -322,6 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // fetches of code run for the first time -- waits microseconds in the
             // memory queues, which costs more than streaming early gains.
             ok = mbar_wait(sched_ready, 0, abort_flag, args.status, kDevTimeoutProducer);
+            const uint64_t weight_policy = policy_evict_first();
             for (int list = 0; list <= 1 && ok; ++list) {
                 const int nkb = list == 1 ? nkb2 : nkb1;
                 const CUtensorMap* amap = list == 1 ? &map_w2 : &map_w13;
@@ -340,7 +341,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                             break;
                         }
                         mbar_arrive_expect_tx(&full[stage], kATile + C::kBTile);
-                        tma_load_2d(smem_a + stage * kATile, amap, &full[stage], 0, u.a_row + kb * kBlockM);
+                        if (args.weight_evict_first)
+                            tma_load_2d_hint(smem_a + stage * kATile, amap, &full[stage], 0, u.a_row + kb * kBlockM,
+                                             weight_policy);
+                        else
+                            tma_load_2d(smem_a + stage * kATile, amap, &full[stage], 0, u.a_row + kb * kBlockM);
                         if (u.bmap == kBx) {
                             tma_load_2d(smem_b + stage * C::kBTile, &map_x, &full[stage], kb * kBlockK, u.b_row);
                         } else {

@@ -97,6 +97,7 @@ struct lm_moe_ctx {
     int fused_max_tokens = lm::kDecodeMaxTokens;    // largest batch for it (LITEMIND_B200_FUSED_MAX_TOKENS)
     int fused_gather_from = lm::kDecodeDirectTokens + 1;  // smallest batch it gathers rows for
                                                           // (LITEMIND_B200_FUSED_GATHER_FROM)
+    bool fused_evict_first = false;  // weight tiles with an L2 evict-first hint (LITEMIND_B200_FUSED_EVICT_FIRST)
     unsigned long long* grid_bar = nullptr;  // the fused decode kernel's arrival counters (self-resetting)
     // Testing only (lm_moe_debug_set): arrivals the fused kernel's grid waits expect
     // beyond the grid (so the waits run out), and the bound of those waits (0: 2 s).
@@ -553,6 +554,7 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
     if (const char* f = std::getenv("LITEMIND_B200_FUSED_MAX_TOKENS")) ctx->fused_max_tokens = std::atoi(f);
     if (const char* f = std::getenv("LITEMIND_B200_FUSED_GATHER_FROM"))
         ctx->fused_gather_from = std::max(1, std::atoi(f));
+    if (const char* f = std::getenv("LITEMIND_B200_FUSED_EVICT_FIRST")) ctx->fused_evict_first = std::atoi(f) != 0;
     ctx->local_experts = c.n_routed_experts;
     ctx->n_seg = ctx->local_experts + c.n_shared_experts;
     ctx->routed_cap = c.max_tokens * c.num_experts_per_tok;
@@ -1092,6 +1094,7 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
         a.n_shared = c.n_shared_experts;
         a.rp = rp;
         a.gather = gather ? 1 : 0;
+        a.weight_evict_first = ctx->fused_evict_first ? 1 : 0;
         a.logits = ctx->logits;
         a.topk_idx = ctx->topk_idx;
         a.topk_w = ctx->topk_w;

@@ -165,6 +165,7 @@ struct DecodeArgs {
     int32_t n_shared;
     RouterParams rp;
     int32_t gather;            // 1: routed token rows are gathered into x_perm and tiled 32 at a time
+    int32_t weight_evict_first;  // 1: weight tiles load with an L2 evict-first hint (read once)
     float* logits;             // [T, E] (output, also the exchange between CTAs)
     int32_t* topk_idx;         // [T, k] outputs (gather mode: also the exchange between CTAs)
     float* topk_w;

@@ -1,0 +1,106 @@
+"""Batched prefill (include/litemind_b200/Prefill.hpp) against the reference's
+per-token prefill loop (src/DeepSeekRunner.cpp:472-482, :242-290).
+
+A three-layer checkpoint in SafeTensors shards -- layer 0 a dense feed-forward, layers
+1 and 2 MoE -- is loaded by the C++ harness, which runs all T prompt positions through
+every layer's feed-forward sub-layer in one call per layer.  The oracle then runs the
+reference's loop: position by position, layer by layer, rms_norm -> dense FFN or MoE
+block -> residual add.  The attention sub-layer is left out on both sides (it is not
+on this path); what is checked is that batching the positions changes nothing but
+rounding: per token, the final hidden state's increment agrees within the north
+star's tolerance.  Tokens whose routing sits within 1e-3 of a tie at some MoE layer
+are left out of the comparison (the GPU's experts read bf16 activations, so a
+near-tie may resolve the other way after drift); at least 90% of tokens must remain.
+"""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+from litemind_b200 import synthetic as syn  # noqa: E402
+from litemind_b200.checkpoint import layer_tensors, write_safetensors  # noqa: E402
+from oracle.oracle import RouterConfig  # noqa: E402
+from tests.parity import MAX_REL, MIN_COS, output_errors, softmax64  # noqa: E402
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+SHAPE = syn.MoeShape(hidden=256, inter=128, n_routed_experts=16, n_shared_experts=2, top_k=4)
+DENSE_INTER = 512
+TIE = 1e-3
+
+
+def _checkpoint(tmp_path):
+    rng = np.random.default_rng(61)
+    H = SHAPE.hidden
+    norms = [(1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32) for _ in range(3)]
+    dense = {k: syn.normal_bf16(61, (9, i), shp, 0.06) for i, (k, shp) in
+             enumerate((("gate", (DENSE_INTER, H)), ("up", (DENSE_INTER, H)), ("down", (H, DENSE_INTER))))}
+    moe = {l: syn.layer_weights(SHAPE, seed=62, layer=l, std=0.1) for l in (1, 2)}
+    tensors = {"model.layers.0.mlp.gate_proj.weight": ("BF16", dense["gate"]),
+               "model.layers.0.mlp.up_proj.weight": ("BF16", dense["up"]),
+               "model.layers.0.mlp.down_proj.weight": ("BF16", dense["down"]),
+               "model.layers.0.post_attention_layernorm.weight": ("F32", norms[0])}
+    for l in (1, 2):
+        tensors.update(layer_tensors(moe[l], l, SHAPE.n_shared_experts, norms[l]))
+    names = sorted(tensors)
+    paths = []
+    for k in range(2):
+        p = tmp_path / f"model-{k + 1:05d}-of-00002.safetensors"
+        write_safetensors(p, {n: tensors[n] for n in names[k::2]})
+        paths.append(str(p))
+    return paths, norms, dense, moe
+
+
+def _reference_loop(orc, hidden0, norms, dense, moe):
+    """The reference's prefill: one position at a time through every layer."""
+    T, H = hidden0.shape
+    cfg = RouterConfig(SHAPE.n_routed_experts, SHAPE.top_k)
+    out = hidden0.copy()
+    tied = np.zeros(T, bool)
+    for t in range(T):
+        h = hidden0[t].copy()
+        for l in range(3):
+            xn = orc.rms_norm(h, norms[l], 1e-6)
+            if l == 0:
+                g = orc.matvec_bf16(dense["gate"], xn)
+                u = orc.matvec_bf16(dense["up"], xn)
+                y = orc.matvec_bf16_accumulate(dense["down"], orc.silu_multiply(g, u), np.zeros(H, np.float32), 1.0)
+            else:
+                y, _, _, logits = orc.moe_layer(xn[None], moe[l], cfg, SHAPE.n_shared_experts, threads=0)
+                y = y[0]
+                p = np.sort(softmax64(logits[0][None])[0])[::-1]
+                tied[t] |= (p[SHAPE.top_k - 1] - p[SHAPE.top_k]) < TIE
+            h = orc.axpy(1.0, y, h)
+        out[t] = h
+    return out, tied
+
+
+@pytest.mark.parametrize("T", [40, 150])  # one cooperative launch per MoE layer; the grouped GEMMs
+def test_batched_prefill_matches_per_token_loop(tmp_path, oracle_lib, T):
+    from litemind_b200 import build
+
+    paths, norms, dense, moe = _checkpoint(tmp_path)
+    hidden0 = np.random.default_rng(63).standard_normal((T, SHAPE.hidden)).astype(np.float32)
+    (tmp_path / "in.f32").write_bytes(hidden0.tobytes())
+    build.build()
+    exe = tmp_path / "PrefillTest"
+    cuda = build._cuda_home()
+    cmd = ["g++", "-std=c++20", "-O1", "-Wall", "-Wextra", f"-I{ROOT}/include", f"-I{ROOT}/tests/cpp",
+           f"-I{cuda}/include", os.path.join(ROOT, "tests", "cpp", "PrefillTest.cpp"),
+           f"-L{ROOT}/litemind_b200", "-llitemind_b200", f"-Wl,-rpath,{ROOT}/litemind_b200",
+           f"-L{cuda}/lib64", "-lcudart", f"-Wl,-rpath,{cuda}/lib64", "-o", str(exe)]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    res = subprocess.run([str(exe), str(T), str(tmp_path / "in.f32"), str(tmp_path / "out.f32"), *paths],
+                         capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stdout + res.stderr
+    got = np.frombuffer((tmp_path / "out.f32").read_bytes(), np.float32).reshape(T, SHAPE.hidden)
+    ref, tied = _reference_loop(oracle_lib, hidden0, norms, dense, moe)
+    keep = ~tied
+    assert keep.mean() >= 0.9, f"{tied.sum()} of {T} tokens sit near a routing tie"
+    rel, cos = output_errors(got[keep] - hidden0[keep], ref[keep] - hidden0[keep])
+    assert rel.max() <= MAX_REL, f"max relative error {rel.max():.3e}"
+    assert cos.min() >= MIN_COS, f"min cosine {cos.min():.7f}"
