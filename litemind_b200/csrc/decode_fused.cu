@@ -11,13 +11,13 @@
 // first, before any weight is streamed: under a saturated weight stream every
 // global access of the routing waits microseconds in the memory queues.  Two modes:
 //
-//   direct  (T <= 32)  router dot products spread over every warp of the grid;
+//   direct  (small T)  router dot products spread over every warp of the grid;
 //           after counter 0 every CTA reads all T x E logits into shared memory and
 //           recomputes the whole routing identically (top-k, histogram, row order).
 //           Every expert's token operand is x itself (all T tokens as the MMA's N):
 //           the tensor cores are idle at these sizes anyway, and it spares a gather
 //           and a grid-wide wait; the epilogue keeps the expert's own tokens.
-//   gather  (T > 32)   router logits as (expert, 8 tokens) warp tasks; after counter
+//   gather  (larger T) router logits as (expert, 8 tokens) warp tasks; after counter
 //           0 each token's top-k is computed once in the grid (one warp per token)
 //           and published; after counter 3 every CTA reads all T x k selections and
 //           builds the histogram and row order; each CTA then copies its share of

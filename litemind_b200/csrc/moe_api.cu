@@ -95,9 +95,12 @@ struct lm_moe_ctx {
     int split_max_waves = 4;          // split-K below this many waves of tiles (LITEMIND_B200_SPLIT_WAVES)
     bool fused_decode = true;         // decode sizes on one GPU: one cooperative launch (LITEMIND_B200_FUSED_DECODE=0: off)
     int fused_max_tokens = lm::kDecodeMaxTokens;    // largest batch for it (LITEMIND_B200_FUSED_MAX_TOKENS)
-    int fused_gather_from = lm::kDecodeDirectTokens + 1;  // smallest batch it gathers rows for
-                                                          // (LITEMIND_B200_FUSED_GATHER_FROM)
-    bool fused_evict_first = false;  // weight tiles with an L2 evict-first hint (LITEMIND_B200_FUSED_EVICT_FIRST)
+    // Smallest batch the fused kernel gathers token rows for (LITEMIND_B200_FUSED_GATHER_FROM);
+    // measured on B200: gather mode is faster from 16 tokens up (T=32: 187 vs 194 us).
+    int fused_gather_from = 16;
+    // Weight tiles read with an L2 evict-first hint (LITEMIND_B200_FUSED_EVICT_FIRST=0: off):
+    // they are read once, and the hint keeps L2 for the rows the kernel re-reads.
+    bool fused_evict_first = true;
     unsigned long long* grid_bar = nullptr;  // the fused decode kernel's arrival counters (self-resetting)
     // Testing only (lm_moe_debug_set): arrivals the fused kernel's grid waits expect
     // beyond the grid (so the waits run out), and the bound of those waits (0: 2 s).
@@ -1064,9 +1067,9 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
     int n_slots = 0;
     const RouterParams rp = router_params(c);
     float* y_zero = accumulate ? nullptr : y;  // the down GEMM adds into y
-    // Decode sizes: the whole layer in one cooperative launch.  Up to
-    // kDecodeDirectTokens tokens every expert reads x itself; above, routed token rows
-    // are gathered in the kernel and tiled 32 at a time.
+    // Decode sizes: the whole layer in one cooperative launch.  Below fused_gather_from
+    // tokens every expert reads x itself (direct mode); from there on, routed token rows
+    // are gathered in the kernel and tiled 32 at a time (gather mode).
     const bool gather = T >= ctx->fused_gather_from;
     const int fused_bn = gather ? kDecodeColTile : T <= 16 ? 16 : 32;
     const int max_active = std::min(E, T * K);

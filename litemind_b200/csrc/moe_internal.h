@@ -150,7 +150,8 @@ struct GemmArgs {
 // one cooperative launch -- routing, dispatch, gate/up, down and the combine.
 constexpr int kDecodeMaxTokens = 128;
 constexpr int kDecodeMaxRows = 1024;        // tokens x top-k
-constexpr int kDecodeDirectTokens = 32;     // up to this many tokens: x itself is every expert's token operand
+constexpr int kDecodeDirectTokens = 32;     // direct mode takes at most this many tokens (x itself is every
+                                            // expert's token operand); gather mode takes any batch
 constexpr int kDecodeColTile = 32;          // token rows per column tile above that (gather mode)
 struct DecodeArgs {
     const uint16_t* x;         // [T, hidden] bf16 tokens (GEMM operand; logits too unless x_f32)

@@ -1,8 +1,9 @@
 """The fused decode kernel (one cooperative launch per layer for T <= 128 on one GPU).
 
 Parity against the oracle across the token counts that change its work split: in
-direct mode (T <= 32: one token, a token-tile boundary, 32) and in gather mode
-(33-128 tokens: column-tile boundaries at 32, 64 and 96, the largest batch), with a
+direct mode (by default below 16 tokens; up to 32 when forced: one token, a token-tile
+boundary, 32) and in gather mode (16-128 tokens: column-tile boundaries at 32, 64 and
+96, the largest batch), with a
 logit bias, with group-limited and renormalised routing, with accumulation into y,
 with f32 router activations (the block path), with gather mode forced down to a
 single token, and against the grouped multi-launch path it replaces.  Its phase
@@ -100,6 +101,19 @@ def test_fused_gather_forced_at_small_batches(oracle_lib, v2lite_weights):
         assert "decode_fused" in prof
         ry, ridx, rw, rlog = _oracle(oracle_lib, V2, v2lite_weights, x)
         assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what=f"forced gather T={T}")
+    layer.close()
+
+
+def test_fused_direct_forced_up_to_its_limit(oracle_lib, v2lite_weights):
+    """Direct mode (every expert reads x itself) kept up to its 32-token limit."""
+    layer = _layer_with_env(MoeConfig(max_tokens=128), LITEMIND_B200_FUSED_GATHER_FROM=33)
+    layer.upload_layer(0, v2lite_weights)
+    for T in (16, 17, 31, 32):
+        x = syn.tokens(V2, T, seed=180 + T)
+        y, idx, w, _, prof = _gpu(layer, x)
+        assert "decode_fused" in prof
+        ry, ridx, rw, rlog = _oracle(oracle_lib, V2, v2lite_weights, x)
+        assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what=f"forced direct T={T}")
     layer.close()
 
 

@@ -8,9 +8,10 @@ reference's loop: position by position, layer by layer, rms_norm -> dense FFN or
 block -> residual add.  The attention sub-layer is left out on both sides (it is not
 on this path); what is checked is that batching the positions changes nothing but
 rounding: per token, the final hidden state's increment agrees within the north
-star's tolerance.  Tokens whose routing sits within 1e-3 of a tie at some MoE layer
-are left out of the comparison (the GPU's experts read bf16 activations, so a
-near-tie may resolve the other way after drift); at least 90% of tokens must remain.
+star's tolerance.  A token may miss it only if its routing sits within 1e-3 of a tie
+(in probability) at some MoE layer -- the GPU's experts read bf16 activations, so
+after a layer of drift such a tie may resolve the other way -- and no more than 10%
+of the tokens may miss it.
 """
 import os
 import subprocess
@@ -99,8 +100,9 @@ def test_batched_prefill_matches_per_token_loop(tmp_path, oracle_lib, T):
     assert res.returncode == 0, res.stdout + res.stderr
     got = np.frombuffer((tmp_path / "out.f32").read_bytes(), np.float32).reshape(T, SHAPE.hidden)
     ref, tied = _reference_loop(oracle_lib, hidden0, norms, dense, moe)
-    keep = ~tied
-    assert keep.mean() >= 0.9, f"{tied.sum()} of {T} tokens sit near a routing tie"
-    rel, cos = output_errors(got[keep] - hidden0[keep], ref[keep] - hidden0[keep])
-    assert rel.max() <= MAX_REL, f"max relative error {rel.max():.3e}"
-    assert cos.min() >= MIN_COS, f"min cosine {cos.min():.7f}"
+    rel, cos = output_errors(got - hidden0, ref - hidden0)
+    miss = (rel > MAX_REL) | (cos < MIN_COS)
+    assert not (miss & ~tied).any(), (f"tokens {np.flatnonzero(miss & ~tied)[:10]} miss the tolerance away from "
+                                      f"any routing tie: max_rel {rel[~tied].max():.3e}, min_cos {cos[~tied].min():.7f}")
+    assert miss.sum() <= 0.1 * T, f"{miss.sum()} of {T} tokens miss the tolerance"
+    assert rel[~miss].max() <= MAX_REL and cos[~miss].min() >= MIN_COS
