@@ -148,8 +148,9 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device: int):
+    def __init__(self, device: int, interval_ms: int = 200):
         self.device = device
+        self.interval_ms = interval_ms
         self.proc = None
         self.path = None
 
@@ -159,7 +160,7 @@ class ClockSampler:
             os.close(fd)
             self.out = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.device), "-lms", "200"], stdout=self.out,
+                                          "-i", str(self.device), "-lms", str(self.interval_ms)], stdout=self.out,
                                          stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -191,7 +192,8 @@ class ClockSampler:
         os.unlink(self.path)
         return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxes) if maxes else None,
                 "reasons": sorted(reasons), "samples": len(sms),
-                "window": "nvidia-smi every 200 ms over the load window that ends with the timed steps"}
+                "window": f"nvidia-smi every {self.interval_ms} ms over the load window that ends with the timed "
+                          "steps"}
 
 
 # ── algorithmic work ──────────────────────────────────────────────────────
@@ -697,6 +699,38 @@ def kernel_roofline(prof: dict, ms_per_step: float, layer_b: int, gate_up_b: int
             "bytes_per_launch": k_bytes, "mean_launch_ms": mean, "timing": how, "share_of_step": share}
 
 
+# The fused kernel's per-CTA phase stamps (lm_moe_profile_trace), in kernel order.
+TRACE_PHASES = ((0, "start"), (1, "logits_written"), (2, "logits_seen"), (10, "logits_in_smem"),
+                (9, "topk_written"), (13, "topk_seen"), (11, "routed"), (12, "experts_scanned"),
+                (3, "schedule_built"), (14, "rows_gathered"), (15, "producer_saw_rows"), (4, "gate_up_done"),
+                (5, "producer_saw_h"), (6, "producer_done"), (8, "mma_done"), (7, "down_done"))
+
+
+def phase_trace(layer, x, y, flush, torch, bias=None) -> dict | None:
+    """One profiled forward of the fused kernel: per phase, the [min, median, max] over
+    CTAs of its stamp in microseconds from the earliest CTA start (L2 flushed first)."""
+    import numpy as np
+
+    layer.profile(True)
+    layer.profile_read(reset=True)
+    flush()
+    layer.forward(0, x, y=y, bias=bias)
+    prof = layer.profile_read(reset=True)
+    tr = layer.profile_trace().astype(np.int64) if "decode_fused" in prof else None
+    layer.profile(False)
+    layer.sync()
+    if tr is None or tr.size == 0:
+        return None
+    t0 = tr[:, 0].min()
+    out = {}
+    for slot, name in TRACE_PHASES:
+        col = tr[:, slot]
+        if (col > 0).any():
+            v = (col[col > 0] - t0) / 1000.0
+            out[name] = [round(float(v.min()), 1), round(float(np.median(v)), 1), round(float(v.max()), 1)]
+    return out
+
+
 def time_steps(layer, x, y, flush, steps, torch, bias=None, slot=0):
     """Per-step CUDA-event time (ms) of layer.forward on layer slot `slot`, L2 flushed before each."""
     total = 0.0
@@ -728,7 +762,24 @@ def measure_prefill(layer, W, flush, args, torch, peaks) -> dict:
     for _ in range(max(args.warmup, 3)):
         layer.forward(0, x, y=y, bias=bias)
     layer.sync()
-    clocks = ClockSampler(torch.cuda.current_device())
+    dev = torch.cuda.current_device()
+    # Burst: the steps right after the warm-up, as the dense bf16 peak's burst figure is
+    # measured (a few milliseconds-long GEMMs); clocks sampled every 50 ms meanwhile.
+    burst_clocks = ClockSampler(dev, interval_ms=50)
+    burst_clocks.start()
+    time.sleep(0.1)
+    ms = time_steps(layer, x, y, flush, max(args.steps, 20), torch, bias=bias)
+    burst_clock_info = burst_clocks.stop()
+    # Per-kernel device times in the same regime (a few steps, profiling events).
+    layer.profile(True)
+    layer.profile_read(reset=True)
+    for _ in range(5):
+        flush()
+        layer.forward(0, x, y=y, bias=bias)
+    prof = layer.profile_read(reset=True)
+    layer.profile(False)
+    # Sustained: the same steps after seconds of back-to-back load (power-capped clocks).
+    clocks = ClockSampler(dev)
     clocks.start()
     t0 = time.perf_counter()
     while time.perf_counter() - t0 < args.clock_window:
@@ -736,15 +787,8 @@ def measure_prefill(layer, W, flush, args, torch, peaks) -> dict:
             flush()
             layer.forward(0, x, y=y, bias=bias)
         torch.cuda.synchronize()
-    ms = time_steps(layer, x, y, flush, args.steps, torch, bias=bias)
+    ms_sustained = time_steps(layer, x, y, flush, args.steps, torch, bias=bias)
     clock_info = clocks.stop()
-    layer.profile(True)
-    layer.profile_read(reset=True)
-    for _ in range(args.steps):
-        flush()
-        layer.forward(0, x, y=y, bias=bias)
-    prof = layer.profile_read(reset=True)
-    layer.profile(False)
     counts = [int(v) for v in layer.expert_counts()]
     lf = layer_flops(shape, T)
     gu_f = gate_up_flops(shape, T)
@@ -756,13 +800,21 @@ def measure_prefill(layer, W, flush, args, torch, peaks) -> dict:
     total = sum(v[0] for v in prof.values())
     burst, sus = peaks["bf16_tflops"], peaks["bf16_tflops_sustained"]
     layer_tf = lf / (ms / 1e3) / 1e12
+    sus_tf = lf / (ms_sustained / 1e3) / 1e12
     out = {
         "tokens": T, "seed_tokens": SEED_PREFILL, "seed_weights": SEED_WEIGHTS,
         "expert_load": "Zipf(1.2) from a per-expert logit bias b_e = -1.2 ln(rank_e) over a seeded permutation",
         "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
+        "timing": "burst: the steps right after a 3-step warm-up (L2 flushed before each), as the burst bf16 "
+                  "peak is measured; clocks sampled every 50 ms",
         "roofline": {"bound": "tensor", "achieved": layer_tf, "peak": burst, "unit": "TFLOP/s",
                      "frac": layer_tf / burst, "peak_source": f"{peaks['source']} (bf16_tflops, burst)",
-                     "frac_of_sustained": layer_tf / sus, "flops_per_step": lf},
+                     "flops_per_step": lf},
+        "burst_clocks": burst_clock_info,
+        "sustained": {"ms_per_step": ms_sustained, "tokens_per_s": T / (ms_sustained / 1e3), "achieved": sus_tf,
+                      "peak": sus, "frac": sus_tf / sus,
+                      "peak_source": f"{peaks['source']} (bf16_tflops_sustained)",
+                      "timing": f"after {args.clock_window} s of back-to-back steps (1 kW power cap)"},
         "kernels": {
             "gemm_gate_up": {"mean_ms": gu_avg, "tflops": gu_f / (gu_avg / 1e3) / 1e12 if gu_avg else 0.0,
                              "frac": gu_f / (gu_avg / 1e3) / 1e12 / burst if gu_avg else 0.0},
@@ -770,6 +822,7 @@ def measure_prefill(layer, W, flush, args, torch, peaks) -> dict:
                           "frac": dn_f / (dn_avg / 1e3) / 1e12 / burst if dn_avg else 0.0},
             "share_of_step": {k: round(v[0] / total, 4) for k, v in prof.items()} if total else {}},
         "expert_rows": counts, "clocks": clock_info,
+        "kernel_timing": "profiling events around each launch in 5 steps right after the burst steps",
         "gpu_launches_per_step": kernels_per_forward(T, 1),
     }
     if not args.no_parity:
@@ -917,6 +970,8 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> int:
                             "GEMMs, overlapped with the NCCL dispatch and return of other chunks")
     layer_roofline = {"bytes": lb, "achieved": lb / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                       "frac": lb / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "touched_experts": touched}
+    if "decode_fused" in prof and world == 1:
+        roofline["phase_trace_us"] = phase_trace(layer, x, y, flush, torch, bias=bias)
     if prefill or world > 1:
         # Tensor-bound batches: FLOPs against the dense bf16 burst peak (the launches
         # are milliseconds long), the sustained figure beside it.
@@ -997,7 +1052,8 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> int:
             b = layer_bytes(shape, tt, t)
             sweep.append({"tokens": t, "seed_tokens": SEED_SWEEP, "tokens_per_s": t / (m / 1e3), "ms": m,
                           "touched_experts": tt, "layer_gbs": b / (m / 1e3) / 1e9,
-                          "frac_hbm": b / (m / 1e3) / 1e9 / peaks["hbm_gbs"]})
+                          "frac_hbm": b / (m / 1e3) / 1e9 / peaks["hbm_gbs"],
+                          "phase_trace_us": phase_trace(layer, xs, ys, flush, torch)})
     if extras and not args.no_prefill:
         prefill_obj = measure_prefill(layer, W, flush, args, torch, peaks)
     if extras and not args.no_ep_base:
