@@ -8,10 +8,10 @@ reference's loop: position by position, layer by layer, rms_norm -> dense FFN or
 block -> residual add.  The attention sub-layer is left out on both sides (it is not
 on this path); what is checked is that batching the positions changes nothing but
 rounding: per token, the final hidden state's increment agrees within the north
-star's tolerance.  A token may miss it only if its routing sits within 1e-3 of a tie
-(in probability) at some MoE layer -- the GPU's experts read bf16 activations, so
-after a layer of drift such a tie may resolve the other way -- and no more than 10%
-of the tokens may miss it.
+star's tolerance.  A token may miss it only if its k-th and (k+1)-th router logits lie
+within 0.05 of each other at some MoE layer -- the GPU's experts read bf16
+activations, so after a layer of drift such a near-tie may resolve the other way --
+and no more than 10% of the tokens may miss it.
 """
 import os
 import subprocess
@@ -26,12 +26,12 @@ torch = pytest.importorskip("torch")
 from litemind_b200 import synthetic as syn  # noqa: E402
 from litemind_b200.checkpoint import layer_tensors, write_safetensors  # noqa: E402
 from oracle.oracle import RouterConfig  # noqa: E402
-from tests.parity import MAX_REL, MIN_COS, output_errors, softmax64  # noqa: E402
+from tests.parity import MAX_REL, MIN_COS, output_errors  # noqa: E402
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 SHAPE = syn.MoeShape(hidden=256, inter=128, n_routed_experts=16, n_shared_experts=2, top_k=4)
 DENSE_INTER = 512
-TIE = 1e-3
+TIE = 0.05  # logit units
 
 
 def _checkpoint(tmp_path):
@@ -41,6 +41,11 @@ def _checkpoint(tmp_path):
     dense = {k: syn.normal_bf16(61, (9, i), shp, 0.06) for i, (k, shp) in
              enumerate((("gate", (DENSE_INTER, H)), ("up", (DENSE_INTER, H)), ("down", (H, DENSE_INTER))))}
     moe = {l: syn.layer_weights(SHAPE, seed=62, layer=l, std=0.1) for l in (1, 2)}
+    # A decisive router (logits with a standard deviation near 8): the chain of three
+    # layers compounds the bf16 drift of the GPU's expert activations, and a token whose
+    # routing is nearly tied would test that drift rather than the batching.
+    for l in (1, 2):
+        moe[l]["router"] = (moe[l]["router"] * np.float32(5.0)).astype(np.float32)
     tensors = {"model.layers.0.mlp.gate_proj.weight": ("BF16", dense["gate"]),
                "model.layers.0.mlp.up_proj.weight": ("BF16", dense["up"]),
                "model.layers.0.mlp.down_proj.weight": ("BF16", dense["down"]),
@@ -73,8 +78,8 @@ def _reference_loop(orc, hidden0, norms, dense, moe):
             else:
                 y, _, _, logits = orc.moe_layer(xn[None], moe[l], cfg, SHAPE.n_shared_experts, threads=0)
                 y = y[0]
-                p = np.sort(softmax64(logits[0][None])[0])[::-1]
-                tied[t] |= (p[SHAPE.top_k - 1] - p[SHAPE.top_k]) < TIE
+                z = np.sort(logits[0].astype(np.float64))[::-1]
+                tied[t] |= (z[SHAPE.top_k - 1] - z[SHAPE.top_k]) < TIE
             h = orc.axpy(1.0, y, h)
         out[t] = h
     return out, tied
