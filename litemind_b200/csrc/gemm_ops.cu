@@ -216,6 +216,20 @@ cudaError_t launch_pack_swiglu(const uint16_t* gate, const uint16_t* up, const u
     return cudaGetLastError();
 }
 
+// Loads every kernel of this file (see preload_kernels in moe_internal.h).
+cudaError_t preload_ops_kernels() {
+    cudaFuncAttributes a{};
+    const void* kernels[] = {
+        reinterpret_cast<const void*>(matvec_kernel<uint16_t>), reinterpret_cast<const void*>(matvec_kernel<float>),
+        reinterpret_cast<const void*>(softmax_rows_kernel),     reinterpret_cast<const void*>(silu_multiply_kernel),
+        reinterpret_cast<const void*>(axpy_kernel),             reinterpret_cast<const void*>(rms_norm_rows_kernel),
+        reinterpret_cast<const void*>(add_kernel),              reinterpret_cast<const void*>(pack_swiglu_kernel),
+    };
+    for (const void* k : kernels)
+        if (const cudaError_t e = cudaFuncGetAttributes(&a, k); e != cudaSuccess) return e;
+    return cudaSuccess;
+}
+
 }  // namespace lm
 
 using lm::blocks_for;

@@ -561,6 +561,30 @@ cudaError_t launch_one(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
 
 }  // namespace
 
+// Loads every instantiation launch_gemm_* can launch (see preload_kernels in moe_internal.h).
+cudaError_t preload_grouped_gemm_kernels() {
+    cudaFuncAttributes a{};
+    const void* kernels[] = {
+        reinterpret_cast<const void*>(moe_gemm_kernel<16, Kind::GateUp>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<32, Kind::GateUp>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<64, Kind::GateUp>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<128, Kind::GateUp>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<256, Kind::GateUp>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<16, Kind::Down>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<32, Kind::Down>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<64, Kind::Down>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<128, Kind::Down>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<256, Kind::Down>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<16, Kind::Router>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<32, Kind::Router>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<64, Kind::Router>),
+        reinterpret_cast<const void*>(moe_gemm_kernel<128, Kind::Router>),
+    };
+    for (const void* k : kernels)
+        if (const cudaError_t e = cudaFuncGetAttributes(&a, k); e != cudaSuccess) return e;
+    return cudaSuccess;
+}
+
 cudaError_t launch_gemm_gate_up(int bn, const CUtensorMap& w13, const CUtensorMap& xperm, const CUtensorMap& x,
                                 const GemmArgs& args, int sms, cudaStream_t stream, bool pdl) {
     switch (bn) {

@@ -396,6 +396,20 @@ cudaError_t launch_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtens
 
 }  // namespace
 
+// Loads every instantiation launch_gemm_*_pair can launch (see preload_kernels in moe_internal.h).
+cudaError_t preload_pair_gemm_kernels() {
+    cudaFuncAttributes a{};
+    const void* kernels[] = {
+        reinterpret_cast<const void*>(moe_gemm_pair_kernel<128, PKind::GateUp>),
+        reinterpret_cast<const void*>(moe_gemm_pair_kernel<256, PKind::GateUp>),
+        reinterpret_cast<const void*>(moe_gemm_pair_kernel<128, PKind::Down>),
+        reinterpret_cast<const void*>(moe_gemm_pair_kernel<256, PKind::Down>),
+    };
+    for (const void* k : kernels)
+        if (const cudaError_t e = cudaFuncGetAttributes(&a, k); e != cudaSuccess) return e;
+    return cudaSuccess;
+}
+
 cudaError_t launch_gemm_gate_up_pair(int bn, const CUtensorMap& w13, const CUtensorMap& xperm_half,
                                      const CUtensorMap& x_half, const GemmArgs& args, int sms, cudaStream_t stream,
                                      bool pdl) {

@@ -164,6 +164,20 @@ struct lm_moe_ctx {
     int ep_timeline_chunks = 0;
     int32_t* host_totals = nullptr;      // pinned [E]
     int32_t* host_recv = nullptr;        // pinned [nranks * local experts]
+    // Copy-engine exchange (LITEMIND_B200_EP_COPY, host-planned mode, nranks <= 8): every
+    // rank's x_perm, y_ret and flag buffer mapped here by IPC; one copy stream per peer.
+    bool ep_copy = false;
+    uint32_t ep_epoch = 0;
+    uint32_t* ep_flags = nullptr;        // this rank's flag slots: [N] rows ready, [kEpMaxChunks][N] outputs ready
+    lm::EpPeerFlags ep_peer_flags{};
+    uint16_t* ep_peer_xperm[lm::kEpCopyMaxRanks]{};
+    uint16_t* ep_peer_yret[lm::kEpCopyMaxRanks]{};
+    bool ep_peer_opened[lm::kEpCopyMaxRanks]{};  // IPC mappings to close at destroy
+    cudaStream_t ep_copy_stream[lm::kEpCopyMaxRanks]{};
+    cudaEvent_t ep_ev_pulled[lm::kEpMaxChunks][lm::kEpCopyMaxRanks]{};
+    cudaEvent_t ep_ev_returned[lm::kEpCopyMaxRanks]{};
+    int32_t* counts_all = nullptr;       // device [N, E]: every rank's rows per expert
+    int32_t* host_counts_all = nullptr;  // pinned copy
     CUtensorMap map_xrecv[5]{};
     CUtensorMap map_xsorted[5]{};
 
@@ -461,10 +475,20 @@ lm_status upload_shared_and_router(lm_moe_ctx* ctx, LayerWeights& L, const float
     return LM_OK;
 }
 
+// The expired exchange wait's record in this rank's flag buffer (copy-engine exchange).
+uint32_t* ep_diag(lm_moe_ctx* ctx) { return ctx->ep_flags + ep_flag_slots(ctx->nranks) - kEpDiagSlots; }
+
 // A status word the device recorded (already read back): on an error, clear it and
 // re-arm every counter an aborted launch may have left short, then report it.
 lm_status settle_status(lm_moe_ctx* ctx, int32_t status) {
     if (status != 0) {
+        std::string detail;
+        if (status == kDevTimeoutExchange && ctx->ep_flags != nullptr) {
+            uint32_t d[3] = {0, 0, 0};
+            if (cudaMemcpy(d, ep_diag(ctx), sizeof(d), cudaMemcpyDeviceToHost) == cudaSuccess)
+                detail = ": flag slot " + std::to_string(d[0]) + " held " + std::to_string(d[1]) + ", epoch " +
+                         std::to_string(d[2]) + " was awaited";
+        }
         LM_CUDA(ctx, cudaMemset(ctx->status, 0, sizeof(int32_t)));
         // An aborted fused decode launch leaves its grid counters short: restart them.
         LM_CUDA(ctx, cudaMemset(ctx->grid_bar, 0, kDecodeCounters * sizeof(unsigned long long)));
@@ -474,7 +498,7 @@ lm_status settle_status(lm_moe_ctx* ctx, int32_t status) {
                            : status == kDevBadRow ? "an output row outside its buffer"
                                                   : "a bounded wait expired";
         return fail(ctx, LM_ERR_DEVICE_TIMEOUT,
-                    std::string("a kernel stopped on ") + what + " (code " + std::to_string(status) +
+                    std::string("a kernel stopped on ") + what + " (code " + std::to_string(status) + detail +
                         "); results are invalid");
     }
     return LM_OK;
@@ -636,6 +660,18 @@ lm_status lm_moe_destroy(lm_moe_ctx* ctx) {
         if (e) cudaEventDestroy(e);
     if (ctx->host_totals) cudaFreeHost(ctx->host_totals);
     if (ctx->host_recv) cudaFreeHost(ctx->host_recv);
+    if (ctx->host_counts_all) cudaFreeHost(ctx->host_counts_all);
+    for (int r = 0; r < kEpCopyMaxRanks; ++r) {
+        if (ctx->ep_peer_opened[r]) {
+            cudaIpcCloseMemHandle(ctx->ep_peer_xperm[r]);
+            cudaIpcCloseMemHandle(ctx->ep_peer_yret[r]);
+            cudaIpcCloseMemHandle(ctx->ep_peer_flags.flags[r]);
+        }
+        if (ctx->ep_copy_stream[r]) cudaStreamDestroy(ctx->ep_copy_stream[r]);
+        if (ctx->ep_ev_returned[r]) cudaEventDestroy(ctx->ep_ev_returned[r]);
+        for (int k = 0; k < kEpMaxChunks; ++k)
+            if (ctx->ep_ev_pulled[k][r]) cudaEventDestroy(ctx->ep_ev_pulled[k][r]);
+    }
     for (auto& e : ctx->prof_events)
         if (e) cudaEventDestroy(e);
     delete ctx;
@@ -1331,16 +1367,39 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
         LM_CUDA(ctx, launch_gather_rows(x, ctx->row_token, T * K, H, ctx->x_perm, s, true));
     prof_mark(ctx, 1, s);
     slots[n_slots++] = 1;
-    // 2. Rows per (destination, expert) to every rank; one host sync to plan.
-    LM_NCCL(ctx, nc.GroupStart());
-    for (int d = 0; d < N; ++d) {
-        LM_NCCL(ctx, nc.Send(ctx->expert_totals + d * El, El, ncclInt32, d, ctx->comm, s));
-        LM_NCCL(ctx, nc.Recv(ctx->recv_counts + d * El, El, ncclInt32, d, ctx->comm, s));
+    // 2. Rows per (destination, expert) to every rank; one host sync to plan.  The
+    //    copy-engine exchange needs every rank's counts (where its rows sit in every
+    //    peer's buffers): all-gather them, and derive this rank's own slices.
+    const int32_t* counts_all = nullptr;  // copy mode: [N, E] rows each rank sends to each expert
+    if (ctx->ep_copy) {
+        LM_NCCL(ctx, nc.GroupStart());
+        for (int d = 0; d < N; ++d) {
+            LM_NCCL(ctx, nc.Send(ctx->expert_totals, E, ncclInt32, d, ctx->comm, s));
+            LM_NCCL(ctx, nc.Recv(ctx->counts_all + d * E, E, ncclInt32, d, ctx->comm, s));
+        }
+        LM_NCCL(ctx, nc.GroupEnd());
+        LM_CUDA(ctx, cudaMemcpyAsync(ctx->host_counts_all, ctx->counts_all, static_cast<size_t>(N) * E * sizeof(int32_t),
+                                     cudaMemcpyDeviceToHost, s));
+        LM_CUDA(ctx, cudaStreamSynchronize(s));
+        counts_all = ctx->host_counts_all;
+        for (int e = 0; e < E; ++e) ctx->host_totals[e] = counts_all[ctx->rank * E + e];
+        for (int r = 0; r < N; ++r)
+            for (int e = 0; e < El; ++e) ctx->host_recv[r * El + e] = counts_all[r * E + ctx->rank * El + e];
+        LM_CUDA(ctx, cudaMemcpyAsync(ctx->recv_counts, ctx->host_recv, static_cast<size_t>(N) * El * sizeof(int32_t),
+                                     cudaMemcpyHostToDevice, s));
+    } else {
+        LM_NCCL(ctx, nc.GroupStart());
+        for (int d = 0; d < N; ++d) {
+            LM_NCCL(ctx, nc.Send(ctx->expert_totals + d * El, El, ncclInt32, d, ctx->comm, s));
+            LM_NCCL(ctx, nc.Recv(ctx->recv_counts + d * El, El, ncclInt32, d, ctx->comm, s));
+        }
+        LM_NCCL(ctx, nc.GroupEnd());
+        LM_CUDA(ctx, cudaMemcpyAsync(ctx->host_totals, ctx->expert_totals, E * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                     s));
+        LM_CUDA(ctx, cudaMemcpyAsync(ctx->host_recv, ctx->recv_counts, N * El * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                     s));
+        LM_CUDA(ctx, cudaStreamSynchronize(s));
     }
-    LM_NCCL(ctx, nc.GroupEnd());
-    LM_CUDA(ctx, cudaMemcpyAsync(ctx->host_totals, ctx->expert_totals, E * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-    LM_CUDA(ctx, cudaMemcpyAsync(ctx->host_recv, ctx->recv_counts, N * El * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-    LM_CUDA(ctx, cudaStreamSynchronize(s));
     lm_ep_plan total;
     if (lm_moe_ep_plan(N, E, ctx->host_totals, ctx->host_recv, &total) != LM_OK)
         return fail(ctx, LM_ERR_INVALID_ARGUMENT, "invalid expert-parallel plan");
@@ -1352,7 +1411,9 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     // leave ep_nccl_ctas SMs to NCCL's kernels (capped to that many CTAs at init).
     const int C = ctx->ep_chunks;
     const bool piped = C > 1;
-    const int gemm_sms = piped ? std::max(2, (ctx->sms - ctx->ep_nccl_ctas) & ~1) : ctx->sms;
+    // NCCL's kernels run beside the chunked GEMMs and need SMs of their own; copy
+    // engines do not.
+    const int gemm_sms = piped && !ctx->ep_copy ? std::max(2, (ctx->sms - ctx->ep_nccl_ctas) & ~1) : ctx->sms;
     lm_ep_plan plans[kEpMaxChunks];
     for (int k = 0; k < C; ++k)
         if (lm_moe_ep_chunk_plan(N, E, C, k, ctx->host_totals, ctx->host_recv, &plans[k]) != LM_OK)
@@ -1481,6 +1542,116 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
         return LM_OK;
     };
     lm_status st;
+    if (ctx->ep_copy) {
+        // Copy-engine exchange.  Owner d's receive buffer holds chunk after chunk, source
+        // after source within a chunk; rank r's send buffer is sorted by global expert.
+        const int me = ctx->rank;
+        auto chunk_lo = [&](int k) { return k * El / C; };
+        auto rows_to = [&](int r, int d, int k) {  // rows rank r sends to owner d's chunk-k experts
+            int n = 0;
+            for (int e = chunk_lo(k); e < chunk_lo(k + 1); ++e) n += counts_all[r * E + d * El + e];
+            return n;
+        };
+        auto send_off = [&](int r, int d, int k) {  // where they start in r's send buffer
+            int n = 0;
+            for (int e = 0; e < d * El + chunk_lo(k); ++e) n += counts_all[r * E + e];
+            return n;
+        };
+        auto recv_off = [&](int d, int r, int k) {  // where they land in d's receive buffer
+            int n = 0;
+            for (int kk = 0; kk < k; ++kk)
+                for (int rr = 0; rr < N; ++rr) n += rows_to(rr, d, kk);
+            for (int rr = 0; rr < r; ++rr) n += rows_to(rr, d, k);
+            return n;
+        };
+        const uint32_t epoch = ++ctx->ep_epoch;
+        const uint64_t limit = ctx->debug_wait_limit_ns != 0 ? ctx->debug_wait_limit_ns : kWaitLimitNs;
+        const size_t row_bytes = static_cast<size_t>(H) * sizeof(uint16_t);
+        // Flag slots: [r] rank r's rows are in its send buffer; [N + k N + r] rank r's
+        // outputs for chunk k are in its y_ret.
+        auto slot_rows = [&](int r) { return r; };
+        auto slot_out = [&](int k, int r) { return N + k * N + r; };
+        const bool tl = ctx->profiling;
+        if (tl && ctx->ep_tl_events[0] == nullptr)
+            for (auto& e : ctx->ep_tl_events) LM_CUDA(ctx, cudaEventCreate(&e));
+        auto stamp = [&](int i) -> lm_status {
+            if (tl) LM_CUDA(ctx, cudaEventRecord(ctx->ep_tl_events[i], s));
+            return LM_OK;
+        };
+        if ((st = stamp(LM_EP_TIMELINE_MAX)) != LM_OK) return st;
+        // This rank's rows are in x_perm: every peer may pull its share.
+        LM_CUDA(ctx, launch_ep_signal(ctx->ep_peer_flags, me, slot_rows(me), epoch, s));
+        for (int k = 0; k < C; ++k) {
+            const int n = rows_to(me, me, k);
+            if (n > 0)
+                LM_CUDA(ctx, cudaMemcpyAsync(ctx->x_recv + static_cast<size_t>(recv_off(me, me, k)) * H,
+                                             ctx->x_perm + static_cast<size_t>(send_off(me, me, k)) * H, n * row_bytes,
+                                             cudaMemcpyDeviceToDevice, s));
+        }
+        // Per peer, on its copy stream: wait for its rows, pull them chunk by chunk; then,
+        // chunk by chunk, wait for its outputs of this rank's rows and pull those back.
+        for (int r = 0; r < N; ++r) {
+            if (r == me) continue;
+            cudaStream_t cs = ctx->ep_copy_stream[r];
+            LM_CUDA(ctx, launch_ep_wait(ctx->ep_flags, slot_rows(r), epoch, ctx->status, ep_diag(ctx), limit, cs));
+            for (int k = 0; k < C; ++k) {
+                const int n = rows_to(r, me, k);
+                if (n > 0)
+                    LM_CUDA(ctx, cudaMemcpyAsync(ctx->x_recv + static_cast<size_t>(recv_off(me, r, k)) * H,
+                                                 ctx->ep_peer_xperm[r] + static_cast<size_t>(send_off(r, me, k)) * H,
+                                                 n * row_bytes, cudaMemcpyDeviceToDevice, cs));
+                LM_CUDA(ctx, cudaEventRecord(ctx->ep_ev_pulled[k][r], cs));
+            }
+            for (int k = 0; k < C; ++k) {
+                LM_CUDA(ctx, launch_ep_wait(ctx->ep_flags, slot_out(k, r), epoch, ctx->status, ep_diag(ctx), limit, cs));
+                const int n = rows_to(me, r, k);
+                if (n > 0)
+                    LM_CUDA(ctx, cudaMemcpyAsync(ctx->y_back + static_cast<size_t>(send_off(me, r, k)) * H,
+                                                 ctx->ep_peer_yret[r] + static_cast<size_t>(recv_off(r, me, k)) * H,
+                                                 n * row_bytes, cudaMemcpyDeviceToDevice, cs));
+            }
+            LM_CUDA(ctx, cudaEventRecord(ctx->ep_ev_returned[r], cs));
+        }
+        prof_mark(ctx, 7, s);
+        slots[n_slots++] = 7;
+        // The shared experts need no peer rows: they run while the first chunk arrives.
+        if (piped && (st = gemms(C, false)) != LM_OK) return st;
+        if ((st = stamp(C)) != LM_OK) return st;
+        for (int k = 0; k < C; ++k) {
+            for (int r = 0; r < N; ++r)
+                if (r != me) LM_CUDA(ctx, cudaStreamWaitEvent(s, ctx->ep_ev_pulled[k][r], 0));
+            if ((st = stamp(k)) != LM_OK) return st;
+            if ((st = stamp(C + 1 + k)) != LM_OK) return st;
+            if ((st = sort(k, s, false)) != LM_OK) return st;
+            if ((st = gemms(k, false)) != LM_OK) return st;
+            if ((st = stamp(2 * C + 1 + k)) != LM_OK) return st;
+            // This rank's outputs of chunk k are in y_ret: the peers may pull theirs back.
+            LM_CUDA(ctx, launch_ep_signal(ctx->ep_peer_flags, me, slot_out(k, me), epoch, s));
+            const int n = rows_to(me, me, k);
+            if (n > 0)
+                LM_CUDA(ctx, cudaMemcpyAsync(ctx->y_back + static_cast<size_t>(send_off(me, me, k)) * H,
+                                             ctx->y_ret + static_cast<size_t>(recv_off(me, me, k)) * H, n * row_bytes,
+                                             cudaMemcpyDeviceToDevice, s));
+        }
+        prof_mark(ctx, 5, s);
+        slots[n_slots++] = 5;
+        for (int r = 0; r < N; ++r)
+            if (r != me) LM_CUDA(ctx, cudaStreamWaitEvent(s, ctx->ep_ev_returned[r], 0));
+        for (int k = 0; k < C; ++k)
+            if ((st = stamp(3 * C + 1 + k)) != LM_OK) return st;
+        LM_CUDA(ctx, launch_ep_combine(y, ctx->y_back, ctx->slot_row, ctx->topk_w, T, K, H, s, false));
+        if ((st = stamp(4 * C + 1)) != LM_OK) return st;
+        prof_mark(ctx, 4, s);
+        slots[n_slots++] = 4;
+        if ((st = prof_end(ctx, slots, n_slots)) != LM_OK) return st;
+        if (tl) {
+            for (int i = 0; i <= 4 * C + 1; ++i)
+                LM_CUDA(ctx, cudaEventElapsedTime(&ctx->ep_timeline[i], ctx->ep_tl_events[LM_EP_TIMELINE_MAX],
+                                                  ctx->ep_tl_events[i]));
+            ctx->ep_timeline_chunks = C;
+        }
+        return LM_OK;
+    }
     if (!piped) {
         // 3. Dispatch token rows.
         if ((st = exchange(0, false, s)) != LM_OK) return st;
@@ -1775,6 +1946,106 @@ lm_status lm_moe_ep_unique_id(void* out) {
     return LM_OK;
 }
 
+// Maps every peer's send rows (x_perm), returned outputs (y_ret) and flag slots into
+// this process (IPC handles exchanged with one small NCCL all-gather) and creates one
+// copy stream per peer.  Every rank calls it at lm_moe_ep_init; a peer is pulled from
+// only after it has signalled, in a forward, so no rank maps a buffer before its owner
+// finished this set-up.
+static lm_status ep_copy_setup(lm_moe_ctx* ctx) {
+    const int N = ctx->nranks, me = ctx->rank, E = ctx->cfg.n_routed_experts;
+    const NcclApi& nc = *ctx->nccl;
+    lm_status st;
+    const size_t n_flags = ep_flag_slots(N);
+    if ((st = alloc(ctx, &ctx->ep_flags, n_flags)) || (st = alloc(ctx, &ctx->counts_all, static_cast<size_t>(N) * E)))
+        return st;
+    LM_CUDA(ctx, cudaMemset(ctx->ep_flags, 0, n_flags * sizeof(uint32_t)));
+    LM_CUDA(ctx, cudaMallocHost(&ctx->host_counts_all, static_cast<size_t>(N) * E * sizeof(int32_t)));
+    cudaIpcMemHandle_t mine[3];
+    LM_CUDA(ctx, cudaIpcGetMemHandle(&mine[0], ctx->x_perm));
+    LM_CUDA(ctx, cudaIpcGetMemHandle(&mine[1], ctx->y_ret));
+    LM_CUDA(ctx, cudaIpcGetMemHandle(&mine[2], ctx->ep_flags));
+    constexpr size_t hb = sizeof(mine);
+    uint8_t* dev = nullptr;
+    if ((st = alloc(ctx, &dev, hb * static_cast<size_t>(N + 1))) != LM_OK) return st;
+    std::vector<cudaIpcMemHandle_t> all(static_cast<size_t>(3) * N);
+    cudaStream_t xs = nullptr;
+    LM_CUDA(ctx, cudaStreamCreateWithFlags(&xs, cudaStreamNonBlocking));
+    cudaError_t ce = cudaMemcpyAsync(dev, mine, hb, cudaMemcpyHostToDevice, xs);
+    ncclResult_t nr = ncclSuccess;
+    if (ce == cudaSuccess) {
+        nr = nc.GroupStart();
+        for (int d = 0; d < N && nr == ncclSuccess; ++d) {
+            nr = nc.Send(dev, hb, ncclInt8, d, ctx->comm, xs);
+            if (nr == ncclSuccess) nr = nc.Recv(dev + hb * (d + 1), hb, ncclInt8, d, ctx->comm, xs);
+        }
+        const ncclResult_t ne = nc.GroupEnd();
+        if (nr == ncclSuccess) nr = ne;
+    }
+    if (ce == cudaSuccess && nr == ncclSuccess)
+        ce = cudaMemcpyAsync(all.data(), dev + hb, hb * N, cudaMemcpyDeviceToHost, xs);
+    const cudaError_t cs = cudaStreamSynchronize(xs);
+    cudaStreamDestroy(xs);
+    if (nr != ncclSuccess) return fail(ctx, LM_ERR_COMM, std::string("IPC handle exchange: ") + nc.GetErrorString(nr));
+    if (ce != cudaSuccess) return cuda_fail(ctx, ce, "IPC handle exchange");
+    if (cs != cudaSuccess) return cuda_fail(ctx, cs, "IPC handle exchange");
+    ctx->ep_peer_flags.n = N;
+    for (int r = 0; r < N; ++r) {
+        if (r == me) {
+            ctx->ep_peer_xperm[r] = ctx->x_perm;
+            ctx->ep_peer_yret[r] = ctx->y_ret;
+            ctx->ep_peer_flags.flags[r] = ctx->ep_flags;
+            continue;
+        }
+        void* px = nullptr;
+        void* py = nullptr;
+        void* pf = nullptr;
+        LM_CUDA(ctx, cudaIpcOpenMemHandle(&px, all[3 * r + 0], cudaIpcMemLazyEnablePeerAccess));
+        LM_CUDA(ctx, cudaIpcOpenMemHandle(&py, all[3 * r + 1], cudaIpcMemLazyEnablePeerAccess));
+        LM_CUDA(ctx, cudaIpcOpenMemHandle(&pf, all[3 * r + 2], cudaIpcMemLazyEnablePeerAccess));
+        ctx->ep_peer_xperm[r] = static_cast<uint16_t*>(px);
+        ctx->ep_peer_yret[r] = static_cast<uint16_t*>(py);
+        ctx->ep_peer_flags.flags[r] = static_cast<uint32_t*>(pf);
+        ctx->ep_peer_opened[r] = true;
+        LM_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->ep_copy_stream[r], cudaStreamNonBlocking));
+        LM_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ep_ev_returned[r], cudaEventDisableTiming));
+        for (int k = 0; k < kEpMaxChunks; ++k)
+            LM_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ep_ev_pulled[k][r], cudaEventDisableTiming));
+    }
+    // Every kernel the expert-parallel forward can launch is loaded now, before any
+    // flag wait spins (a lazily loaded kernel's first launch could otherwise wait for
+    // a spinning wait that waits for the peer's GEMMs, which wait likewise).
+    for (cudaError_t (*preload)() : {preload_router_kernels, preload_grouped_gemm_kernels, preload_pair_gemm_kernels,
+                                     preload_ops_kernels, preload_ep_peer_kernels})
+        LM_CUDA(ctx, preload());
+    // Handshake (epoch 1): every rank stores into its slot of every peer's flags, waits
+    // (bounded) for every peer's store into its own, then reads back through a copy
+    // engine what it stored in each peer's buffer -- the three paths every forward uses.
+    LM_CUDA(ctx, launch_ep_signal(ctx->ep_peer_flags, me, me, 1u, nullptr));
+    for (int r = 0; r < N; ++r)
+        if (r != me) LM_CUDA(ctx, launch_ep_wait(ctx->ep_flags, r, 1u, ctx->status, ctx->ep_flags + n_flags - kEpDiagSlots,
+                                                 kWaitLimitNs, nullptr));
+    LM_CUDA(ctx, cudaDeviceSynchronize());
+    int32_t status = 0;
+    LM_CUDA(ctx, cudaMemcpy(&status, ctx->status, sizeof(status), cudaMemcpyDeviceToHost));
+    if (status != 0) {
+        cudaMemset(ctx->status, 0, sizeof(int32_t));
+        return fail(ctx, LM_ERR_COMM, "copy-engine exchange set-up: a peer's flag store never arrived (code " +
+                                          std::to_string(status) + "); set LITEMIND_B200_EP_COPY=0 to use NCCL");
+    }
+    for (int r = 0; r < N; ++r) {
+        if (r == me) continue;
+        uint32_t v = 0;
+        LM_CUDA(ctx, cudaMemcpy(&v, ctx->ep_peer_flags.flags[r] + me, sizeof(v), cudaMemcpyDeviceToHost));
+        if (v != 1u)
+            return fail(ctx, LM_ERR_COMM, "copy-engine exchange set-up: rank " + std::to_string(r) +
+                                              "'s flag slot reads " + std::to_string(v) +
+                                              " through a copy engine, 1 was stored");
+    }
+    ctx->ep_copy = true;
+    ctx->ep_epoch = 1;
+    return LM_OK;
+}
+
 lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t rank, int32_t nranks) {
     if (ctx == nullptr || nccl_unique_id == nullptr) return LM_ERR_INVALID_ARGUMENT;
     const lm_moe_config& c = ctx->cfg;
@@ -1864,13 +2135,18 @@ lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t ra
             LM_CUDA(ctx, cudaEventCreateWithFlags(&ctx->ep_ev_done[i], cudaEventDisableTiming));
         }
     }
+    // The host-planned exchange can move rows with copy engines out of IPC-mapped peer
+    // buffers (LITEMIND_B200_EP_COPY=1) on up to kEpCopyMaxRanks ranks, else NCCL send/recv.
+    bool want_copy = false;
+    if (const char* v = std::getenv("LITEMIND_B200_EP_COPY"))
+        want_copy = ctx->ep_cap == 0 && nranks <= kEpCopyMaxRanks && std::atoi(v) != 0;
     // Every rank must take the same steps in every exchange, and a peer's rows must
     // fit this rank's buffers: compare the settings that decide both, once.
     {
-        constexpr int kFields = 8;
+        constexpr int kFields = 9;
         const int32_t mine[kFields] = {c.hidden_size, c.moe_intermediate_size, c.n_routed_experts,
                                        c.n_shared_experts, c.num_experts_per_tok, c.max_tokens,
-                                       ctx->ep_cap, ctx->ep_chunks};
+                                       ctx->ep_cap, ctx->ep_chunks, want_copy ? 1 : 0};
         int32_t* dev = nullptr;
         if ((st = alloc(ctx, &dev, static_cast<size_t>(kFields) * (nranks + 1))) != LM_OK) return st;
         std::vector<int32_t> all(static_cast<size_t>(kFields) * nranks);
@@ -1897,9 +2173,10 @@ lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t ra
         for (int d = 0; d < nranks; ++d)
             if (std::memcmp(all.data() + static_cast<size_t>(kFields) * d, mine, sizeof(mine)) != 0)
                 return fail(ctx, LM_ERR_INVALID_ARGUMENT,
-                            "expert-parallel settings differ between ranks (shape, max_tokens or "
-                            "LITEMIND_B200_EP_CHUNKS): rank " + std::to_string(d));
+                            "expert-parallel settings differ between ranks (shape, max_tokens, "
+                            "LITEMIND_B200_EP_CHUNKS or LITEMIND_B200_EP_COPY): rank " + std::to_string(d));
     }
+    if (want_copy && (st = ep_copy_setup(ctx)) != LM_OK) return st;
     for (int i = 0; i < 5; ++i) {
         if (!encode_tensor_map_bf16(&ctx->map_xrecv[i], ctx->x_recv, cap, H, kBnChoices[i], 64, err) ||
             !encode_tensor_map_bf16(&ctx->map_xsorted[i], ctx->x_sorted, cap, H, kBnChoices[i], 64, err) ||

@@ -207,6 +207,31 @@ constexpr size_t kEpFixedMaxRows = 8192;
 // that one chunk's rows travel while another chunk's GEMMs run.
 constexpr int kEpMaxChunks = 8;
 
+// The copy-engine exchange (ep_peer.cu): ranks of one node pull rows out of IPC-mapped
+// peer buffers; readiness is an epoch stored into flag slots of each rank's flag buffer.
+constexpr int kEpCopyMaxRanks = 8;
+struct EpPeerFlags {
+    uint32_t* flags[kEpCopyMaxRanks];  // every rank's flag buffer (this rank's own at [self])
+    int32_t n;
+};
+cudaError_t launch_ep_signal(const EpPeerFlags& peers, int self, int slot, uint32_t epoch, cudaStream_t stream);
+cudaError_t launch_ep_wait(const uint32_t* flags, int slot, uint32_t epoch, int32_t* status, uint32_t* diag,
+                           uint64_t limit_ns, cudaStream_t stream);
+// Kernels load lazily by default (CUDA_MODULE_LOADING=LAZY): a kernel's first launch may
+// wait for the kernels already running on the device.  A flag wait that spins until a
+// peer's GEMMs finish must therefore never run while a kernel is still to be loaded on
+// either side: the copy-engine exchange loads every kernel the expert-parallel forward
+// can launch before its first wait (one function per source file).
+cudaError_t preload_router_kernels();
+cudaError_t preload_grouped_gemm_kernels();
+cudaError_t preload_pair_gemm_kernels();
+cudaError_t preload_ops_kernels();
+cudaError_t preload_ep_peer_kernels();
+// A flag buffer: N (rows ready) + kEpMaxChunks * N (outputs ready) slots, then the
+// expired wait's record (slot, value seen, epoch wanted).
+constexpr int kEpDiagSlots = 4;
+inline size_t ep_flag_slots(int nranks) { return static_cast<size_t>(nranks) * (1 + kEpMaxChunks) + kEpDiagSlots; }
+
 // Split-K workspace for gate/up partial tiles (bytes) and its ticket count.
 constexpr size_t kSplitWsBytes = size_t(32) << 20;
 constexpr int kSplitTickets = 4096;

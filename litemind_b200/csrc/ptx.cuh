@@ -22,6 +22,7 @@ constexpr int kDevTimeoutEpilogue = 3;
 constexpr int kDevBadTile = 4;
 constexpr int kDevTimeoutGrid = 5;  // a grid-wide arrival counter never reached its target
 constexpr int kDevBadRow = 6;       // an output row index outside its buffer (the store was skipped)
+constexpr int kDevTimeoutExchange = 7;  // a peer's readiness flag never reached this forward's epoch
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

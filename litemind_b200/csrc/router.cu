@@ -1095,4 +1095,47 @@ cudaError_t launch_route_small(const uint16_t* x, const float* x_f32, const floa
                                           first_expert, local_experts, shared_base, bn, mb1, mb2, stream, pdl);
 }
 
+// Loads every kernel and instantiation of this file (see preload_kernels in moe_internal.h).
+cudaError_t preload_router_kernels() {
+    cudaFuncAttributes a{};
+    const void* kernels[] = {
+        reinterpret_cast<const void*>(router_logits_warp_kernel<uint16_t>),
+        reinterpret_cast<const void*>(router_logits_warp_kernel<float>),
+        reinterpret_cast<const void*>(router_logits_tiled_kernel<uint16_t>),
+        reinterpret_cast<const void*>(router_logits_tiled_kernel<float>),
+        reinterpret_cast<const void*>(router_logits_reduce_kernel),
+        reinterpret_cast<const void*>(router_topk_kernel<1>),
+        reinterpret_cast<const void*>(router_topk_kernel<2>),
+        reinterpret_cast<const void*>(router_topk_kernel<4>),
+        reinterpret_cast<const void*>(router_topk_kernel<8>),
+        reinterpret_cast<const void*>(dispatch_scan_kernel),
+        reinterpret_cast<const void*>(place_kernel),
+        reinterpret_cast<const void*>(gather_rows_kernel),
+        reinterpret_cast<const void*>(ep_combine_kernel),
+        reinterpret_cast<const void*>(ep_sort_rows_kernel),
+        reinterpret_cast<const void*>(ep_pack_kernel),
+        reinterpret_cast<const void*>(ep_schedule_kernel),
+        reinterpret_cast<const void*>(dense_schedule_kernel),
+        reinterpret_cast<const void*>(route_small_kernel<uint16_t, 1>),
+        reinterpret_cast<const void*>(route_small_kernel<uint16_t, 2>),
+        reinterpret_cast<const void*>(route_small_kernel<uint16_t, 4>),
+        reinterpret_cast<const void*>(route_small_kernel<uint16_t, 8>),
+        reinterpret_cast<const void*>(route_small_kernel<float, 1>),
+        reinterpret_cast<const void*>(route_small_kernel<float, 2>),
+        reinterpret_cast<const void*>(route_small_kernel<float, 4>),
+        reinterpret_cast<const void*>(route_small_kernel<float, 8>),
+        reinterpret_cast<const void*>(route_mid_kernel<uint16_t, 1>),
+        reinterpret_cast<const void*>(route_mid_kernel<uint16_t, 2>),
+        reinterpret_cast<const void*>(route_mid_kernel<uint16_t, 4>),
+        reinterpret_cast<const void*>(route_mid_kernel<uint16_t, 8>),
+        reinterpret_cast<const void*>(route_mid_kernel<float, 1>),
+        reinterpret_cast<const void*>(route_mid_kernel<float, 2>),
+        reinterpret_cast<const void*>(route_mid_kernel<float, 4>),
+        reinterpret_cast<const void*>(route_mid_kernel<float, 8>),
+    };
+    for (const void* k : kernels)
+        if (const cudaError_t e = cudaFuncGetAttributes(&a, k); e != cudaSuccess) return e;
+    return cudaSuccess;
+}
+
 }  // namespace lm

@@ -27,8 +27,9 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, shape_name, token_counts, chunks):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LITEMIND_B200_EP_CHUNKS=str(chunks))
+def _worker(rank, world, port, shape_name, token_counts, chunks, copy=True):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LITEMIND_B200_EP_CHUNKS=str(chunks),
+                      LITEMIND_B200_EP_COPY="1" if copy else "0")
     from datetime import timedelta
 
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
@@ -48,7 +49,7 @@ def _worker(rank, world, port, shape_name, token_counts, chunks):
         T = token_counts[rank]
         xb = syn.tokens(shape, max(T, 1), seed=100 + rank)[:T]
         x = bf16_tensor(xb) if T > 0 else torch.zeros((0, shape.hidden), dtype=torch.bfloat16, device="cuda")
-        for _ in range(2):  # two calls in a row reuse every exchange buffer
+        for _ in range(3):  # calls in a row reuse every exchange buffer (and advance the flags' epoch)
             y = layer.forward(0, x)
             layer.sync()
         if T > 0:
@@ -68,8 +69,9 @@ def _worker(rank, world, port, shape_name, token_counts, chunks):
 # Up to max_tokens x min(k, local experts) rows per rank pair, ranks exchange fixed
 # blocks with the plan made on the device; (5000, 4100) and V2-Lite (700, 450) exceed
 # that and take the host-planned exchange: in one piece (chunks 1) or pipelined in
-# chunks of local experts on a second stream (4 chunks of 1 expert, 3 uneven chunks,
-# V2-Lite's 4 chunks of 8 experts).
+# chunks of local experts (4 chunks of 1 expert, 3 uneven chunks, V2-Lite's 4 chunks of
+# 8 experts).  The host-planned rows move by copy engines out of IPC-mapped peer
+# buffers (the default) or by NCCL (copy=False).
 @pytest.mark.parametrize("shape_name,token_counts,chunks", [("small", (37, 11), 4), ("small", (0, 20), 4),
                                                             ("small", (300, 300), 4), ("v2lite", (32, 64), 4),
                                                             ("small", (5000, 4100), 1), ("small", (5000, 4100), 4),
@@ -78,3 +80,11 @@ def test_expert_parallel_two_gpus(shape_name, token_counts, chunks):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     mp.spawn(_worker, args=(2, _free_port(), shape_name, token_counts, chunks), nprocs=2, join=True)
+
+
+@pytest.mark.parametrize("shape_name,token_counts,chunks", [("small", (5000, 4100), 1), ("small", (3000, 0), 3),
+                                                            ("v2lite", (700, 450), 4)])
+def test_expert_parallel_two_gpus_nccl_exchange(shape_name, token_counts, chunks):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.spawn(_worker, args=(2, _free_port(), shape_name, token_counts, chunks, False), nprocs=2, join=True)
