@@ -614,15 +614,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (epi_tid == 0) stamp(13);
             }
             if (ok) {
-                // (4g) Every CTA reads all selections and builds the same histogram.
-                for (int q = epi_tid; q < T * K; q += kEpiThreads) {
-                    const int e = __ldcg(args.topk_idx + q);
+                // (4g) Every CTA reads all selections (16 bytes per load, every load of a
+                // thread issued before any is used) and builds the same histogram.
+                const int n_pairs = T * K;
+                const int n_vec = n_pairs / 4;
+                constexpr int kVecPerThread = (kDecodeMaxRows / 4 + kEpiThreads - 1) / kEpiThreads;
+                int4 vi[kVecPerThread];
+                float4 vw[kVecPerThread];
+#pragma unroll
+                for (int j = 0; j < kVecPerThread; ++j) {
+                    const int v = epi_tid + j * kEpiThreads;
+                    if (v < n_vec) {
+                        vi[j] = __ldcg(reinterpret_cast<const int4*>(args.topk_idx) + v);
+                        vw[j] = __ldcg(reinterpret_cast<const float4*>(args.topk_w) + v);
+                    }
+                }
+                auto take = [&](int q, int e, float w) {
                     const int t = q / K;
                     rs.idx[q] = e;
-                    rs.w[q] = __ldcg(args.topk_w + q);
+                    rs.w[q] = w;
                     atomicAdd(&s_cnt[e], 1);
                     atomicOr(&rs.emask[e][t >> 5], 1u << (t & 31));
+                };
+#pragma unroll
+                for (int j = 0; j < kVecPerThread; ++j) {
+                    const int v = epi_tid + j * kEpiThreads;
+                    if (v < n_vec) {
+                        take(4 * v, vi[j].x, vw[j].x);
+                        take(4 * v + 1, vi[j].y, vw[j].y);
+                        take(4 * v + 2, vi[j].z, vw[j].z);
+                        take(4 * v + 3, vi[j].w, vw[j].w);
+                    }
                 }
+                for (int q = 4 * n_vec + epi_tid; q < n_pairs; q += kEpiThreads)
+                    take(q, __ldcg(args.topk_idx + q), __ldcg(args.topk_w + q));
                 named_bar_sync(1, kEpiThreads);
                 if (epi_tid == 0) stamp(11);
             }
@@ -708,10 +733,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int q0 = static_cast<int>(static_cast<int64_t>(n_pairs) * blockIdx.x / G);
                 const int q1 = static_cast<int>(static_cast<int64_t>(n_pairs) * (blockIdx.x + 1) / G);
                 const int vec = H / 8;
-                for (int q = q0; q < q1; ++q) {
-                    const uint4* src = reinterpret_cast<const uint4*>(args.x + static_cast<size_t>(s_row_token[q]) * H);
-                    uint4* dst = reinterpret_cast<uint4*>(args.x_perm + static_cast<size_t>(q) * H);
-                    for (int i = epi_tid; i < vec; i += kEpiThreads) dst[i] = src[i];
+                constexpr int kGatherBatch = 8;  // rows whose loads are in flight together
+                for (int qb = q0; qb < q1; qb += kGatherBatch) {
+                    for (int i = epi_tid; i < vec; i += kEpiThreads) {
+                        uint4 v[kGatherBatch];
+#pragma unroll
+                        for (int j = 0; j < kGatherBatch; ++j)
+                            if (qb + j < q1)
+                                v[j] = reinterpret_cast<const uint4*>(
+                                    args.x + static_cast<size_t>(s_row_token[qb + j]) * H)[i];
+#pragma unroll
+                        for (int j = 0; j < kGatherBatch; ++j)
+                            if (qb + j < q1)
+                                reinterpret_cast<uint4*>(args.x_perm + static_cast<size_t>(qb + j) * H)[i] = v[j];
+                    }
                 }
                 fence_proxy_async_global();
                 arrive_grid(kCtrXperm);

@@ -140,12 +140,6 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
-// Hint: bring `bytes` (a multiple of 16) of global memory at `src` (16-byte
-// aligned) into L2.  No completion to wait for.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // 2-D tile load global -> shared, completing `bytes` on `bar`.  x is the
 // innermost coordinate in elements and must be a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
