@@ -356,7 +356,7 @@ def stack_kernels_per_layer(tokens: int, world: int, sms: int = 148) -> int:
 
 
 def run_stack(args, rank: int, world: int, local_rank: int) -> int:
-    """`layers` x (RMSNorm -> MoE -> residual) over T tokens per rank."""
+    """The layer stack: `layers` x (RMSNorm -> MoE -> residual) over T tokens per rank."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -395,7 +395,7 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> int:
     clocks = ClockSampler(local_rank)
     clocks.start()
     t_load = time.perf_counter()
-    while time.perf_counter() - t_load < args.clock_window:
+    while load_window_open(t_load, args.clock_window, world, torch):
         step()
         torch.cuda.synchronize()
     if world > 1:
@@ -731,6 +731,21 @@ def phase_trace(layer, x, y, flush, torch, bias=None) -> dict | None:
     return out
 
 
+def load_window_open(t0: float, window: float, world: int, torch) -> bool:
+    """True while the clock-sampling load window is open.  Under torchrun every forward is
+    collective, so all ranks must run the same number of them: the ranks agree on the
+    minimum of their votes instead of each reading its own clock."""
+    go = time.perf_counter() - t0 < window
+    if world > 1:
+        import torch.distributed as dist
+
+        device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+        vote = torch.tensor([1 if go else 0], dtype=torch.int32, device=device)
+        dist.all_reduce(vote, op=dist.ReduceOp.MIN)
+        go = bool(vote.item())
+    return go
+
+
 def time_steps(layer, x, y, flush, steps, torch, bias=None, slot=0):
     """Per-step CUDA-event time (ms) of layer.forward on layer slot `slot`, L2 flushed before each."""
     total = 0.0
@@ -930,7 +945,7 @@ def run_layer(args, rank: int, world: int, local_rank: int) -> int:
     clocks = ClockSampler(local_rank)
     clocks.start()
     t_load = time.perf_counter()
-    while time.perf_counter() - t_load < args.clock_window:
+    while load_window_open(t_load, args.clock_window, world, torch):
         for _ in range(20 if T <= 1024 else 2):
             flush()
             layer.forward(0, x, y=y, bias=bias)

@@ -44,6 +44,38 @@ def test_loader_reference_arm_is_unavailable():
     assert d["impl"] == "reference" and "unavailable" in d
 
 
+def _window_worker(rank, world, port, result_dir):
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        # Rank 0's window closed long ago; rank 1's is still open.  Both must stop
+        # together, or rank 1 would enter a collective forward that rank 0 never joins.
+        t0 = time.perf_counter() - (100.0 if rank == 0 else 0.0)
+        answers = [bench.load_window_open(t0, 10.0, world, torch) for _ in range(3)]
+        with open(os.path.join(result_dir, f"rank{rank}.json"), "w") as f:
+            json.dump(answers, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_load_window_is_agreed_across_ranks(tmp_path):
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.spawn(_window_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    answers = [json.load(open(tmp_path / f"rank{r}.json")) for r in range(2)]
+    assert answers[0] == answers[1] == [False, False, False]
+
+
 def test_launch_counts_follow_dispatch_rules():
     k = bench.kernels_per_forward
     assert k(32, 1) == k(128, 1) == 1  # the fused decode kernel (direct and gather modes)
