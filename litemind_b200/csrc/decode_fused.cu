@@ -62,8 +62,6 @@ constexpr int kMaskWords = kDecodeMaxTokens / 32;  // token bit set per expert
 constexpr int kMaxGroups = kMaxExperts + kMaxShared;
 constexpr int kDynBudget = 210 * 1024;  // leaves room for the static shared arrays below
 constexpr int kMaxPending = 16;
-constexpr int kReduceItems = 4;  // float4 items of a partial-tile reduction per thread (32 rows x 32 / 256)
-constexpr int kReduceParts = 4;  // CTAs' partial sums loaded together
 constexpr int kLogitTokens = 8;  // gather mode: tokens per router-logit warp task
 
 // Grid counters (DecodeArgs::grid_bar).
@@ -164,7 +162,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    // the constant cache and wait behind the weight stream
     __shared__ int s_n_act;
     __shared__ int s_go[2];
-    __shared__ int s_split_last;
 
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smem_a = smem;
@@ -769,9 +766,48 @@ __global__ void __launch_bounds__(kThreads, 1)
             ListWalk walk;
             walk.init(tiles, nkb);
             int tile, kb0, kb1;
-            bool first_unit = true;
             while (walk.next(tile, kb0, kb1)) {
                 const UnitInfo u = unit_info(list, tile);
+                // TMEM columns holding results: direct-mode routed gate/up has every token
+                // as a column; otherwise the unit's own rows.
+                const int ncols = u.by_token ? T : u.nout;
+                const bool whole = kb0 == 0 && kb1 == nkb;
+                // A gate/up tile split over CTAs is completed by the CTA holding its first
+                // k-blocks: they end that CTA's range, so the other CTAs' shares (the
+                // starts of theirs) are written long before.  It fetches those partial
+                // sums while its own accumulator fills; its own sums never leave TMEM.
+                const bool completes = list == 0 && kb0 == 0 && !whole;
+                const int row = quad * 32 + lane;  // this thread's TMEM lane (weight row)
+                const int c0 = 16 * half;          // and its 16 columns (BN <= 32)
+                float pre[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) pre[j] = 0.0f;
+                if (completes) {
+                    const int64_t iters = static_cast<int64_t>(tiles) * nkb;
+                    const int64_t j0 = static_cast<int64_t>(tile) * nkb;
+                    // CTA owning iteration j: the largest c with iters * c / G <= j.
+                    const int c_hi = static_cast<int>(((j0 + nkb) * G + iters - 1) / iters) - 1;
+                    ok = broadcast(epi_tid == 0 ? count_wait_s32(args.split_ticket + tile, nkb - kb1, abort_flag,
+                                                                 args.status, kDevTimeoutEpilogue,
+                                                                 args.wait_limit_ns)
+                                                : true);
+                    if (!ok) break;
+                    __threadfence();
+                    if (c0 < ncols) {
+                        // The tile's other k-blocks start the ranges of CTAs blockIdx.x + 1 ..
+                        // c_hi, each the first unit there: slot 2 * cta.  Summed in CTA order.
+                        for (int cta = static_cast<int>(blockIdx.x) + 1; cta <= c_hi; ++cta) {
+                            if (iters * (cta + 1) / G == iters * cta / G) continue;  // empty range
+                            const float* part = args.split_ws + static_cast<size_t>(2 * cta) * (kBlockM * BN);
+                            float v[16];
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                v[j] = c0 + j < ncols ? __ldcg(part + (c0 + j) * kBlockM + row) : 0.0f;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) pre[j] += v[j];
+                        }
+                    }
+                }
                 ok = broadcast(epi_tid == 0 ? mbar_wait(&tmem_full[acc], acc_phase, abort_flag, args.status,
                                                         kDevTimeoutEpilogue)
                                             : true);
@@ -779,20 +815,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t t_row =
                     tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-                // TMEM columns holding results: direct-mode routed gate/up has every token
-                // as a column; otherwise the unit's own rows.
-                const int ncols = u.by_token ? T : u.nout;
-                const bool whole = kb0 == 0 && kb1 == nkb;
-                if (list == 0 && !whole) {
-                    // Partial gate/up tile: store the partial sums in this CTA's slot,
-                    // count k-blocks; the CTA completing the tile sums the slots in CTA
-                    // order and applies SiLU.
-                    const int slot = 2 * static_cast<int>(blockIdx.x) + (first_unit ? 0 : 1);
-                    float* wt = args.split_ws + static_cast<size_t>(slot) * (kBlockM * BN);
-                    const int row = quad * 32 + lane;
-#pragma unroll 1
-                    for (int c0 = 16 * half; c0 < BN; c0 += 32) {
-                        if (c0 >= ncols) break;
+                if (list == 0 && !whole && !completes) {
+                    // This CTA's share of a tile another CTA completes (the first unit of
+                    // its range): the partial sums to its slot, then the k-block count.
+                    float* wt = args.split_ws + static_cast<size_t>(2 * blockIdx.x) * (kBlockM * BN);
+                    if (c0 < ncols) {
                         uint32_t r[16];
                         tmem_ld16(t_row + c0, r);
                         tmem_ld_wait();
@@ -805,86 +832,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (lane == 0) mbar_arrive(&tmem_empty[acc]);
                     __threadfence();
                     named_bar_sync(1, kEpiThreads);
-                    const int ticket = tile;
-                    if (epi_tid == 0)
-                        s_split_last = atomicAdd(args.split_ticket + ticket, kb1 - kb0) + (kb1 - kb0) == nkb;
-                    named_bar_sync(1, kEpiThreads);
-                    if (s_split_last) {
-                        __threadfence();
-                        const int64_t iters = static_cast<int64_t>(tiles) * nkb;
-                        const int64_t j0 = static_cast<int64_t>(tile) * nkb;
-                        // CTA owning iteration j: the largest c with iters * c / G <= j.
-                        const int c_lo = static_cast<int>(((j0 + 1) * G + iters - 1) / iters) - 1;
-                        const int c_hi = static_cast<int>(((j0 + nkb) * G + iters - 1) / iters) - 1;
-                        // Items: (output row j, pair of intermediate columns) -> one float4 of
-                        // (gate, up, gate, up); all of a part's loads are in flight together.
-                        const int items = u.nout * 32;
-                        float4 sum[kReduceItems];
-#pragma unroll
-                        for (int k = 0; k < kReduceItems; ++k) sum[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        int col[kReduceItems];
-#pragma unroll
-                        for (int k = 0; k < kReduceItems; ++k) {
-                            const int q = epi_tid + k * kEpiThreads;
-                            const int j = q >> 5;
-                            col[k] = q < items ? (u.by_token ? s_row_token[u.hrow0 + j] : j) : 0;
-                        }
-                        // Parts in batches of kReduceParts, every load of a batch in flight
-                        // at once (under a saturated HBM stream each L2 round trip is long).
-                        for (int cb = c_lo; cb <= c_hi; cb += kReduceParts) {
-                            float4 v[kReduceItems][kReduceParts];
-#pragma unroll
-                            for (int pp = 0; pp < kReduceParts; ++pp) {
-                                const int cta = cb + pp;
-                                const int64_t b = iters * cta / G;
-                                const bool use = cta <= c_hi && iters * (cta + 1) / G != b;  // skip empty ranges
-                                const float* part =
-                                    args.split_ws + static_cast<size_t>(2 * cta + (b >= j0 ? 0 : 1)) * (kBlockM * BN);
-#pragma unroll
-                                for (int k = 0; k < kReduceItems; ++k) {
-                                    const int q = epi_tid + k * kEpiThreads;
-                                    v[k][pp] = (use && q < items) ? __ldcg(reinterpret_cast<const float4*>(
-                                                                        part + col[k] * kBlockM + 4 * (q & 31)))
-                                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-                                }
-                            }
-#pragma unroll
-                            for (int k = 0; k < kReduceItems; ++k) {
-#pragma unroll
-                                for (int pp = 0; pp < kReduceParts; ++pp) {
-                                    sum[k].x += v[k][pp].x;
-                                    sum[k].y += v[k][pp].y;
-                                    sum[k].z += v[k][pp].z;
-                                    sum[k].w += v[k][pp].w;
-                                }
-                            }
-                        }
-#pragma unroll
-                        for (int k = 0; k < kReduceItems; ++k) {
-                            const int q = epi_tid + k * kEpiThreads;
-                            if (q < items) {
-                                const int j = q >> 5;
-                                const __nv_bfloat162 hv = __floats2bfloat162_rn(silu_times(sum[k].x, sum[k].y),
-                                                                                silu_times(sum[k].z, sum[k].w));
-                                *reinterpret_cast<__nv_bfloat162*>(args.h + static_cast<size_t>(u.hrow0 + j) * I +
-                                                                   u.mb * 64 + 2 * (q & 31)) = hv;
-                            }
-                        }
-                        if (epi_tid == 0) args.split_ticket[ticket] = 0;
-                    }
+                    if (epi_tid == 0) red_release_add_s32(args.split_ticket + tile, kb1 - kb0);
                 } else if (list == 0) {
-                    // Whole gate/up tile: h = silu(gate) * up through a staging tile.
+                    // A whole gate/up tile, or a split one this CTA completes:
+                    // h = silu(gate) * up through a staging tile.
                     __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(staging);
-                    const int i_local = (quad * 32 + lane) >> 1;
-#pragma unroll 1
-                    for (int c0 = 16 * half; c0 < BN; c0 += 32) {
-                        if (c0 >= ncols) break;
+                    const int i_local = row >> 1;
+                    if (c0 < ncols) {
                         uint32_t r[16];
                         tmem_ld16(t_row + c0, r);
                         tmem_ld_wait();
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
-                            const float mine = __uint_as_float(r[j]);
+                            const float mine = __uint_as_float(r[j]) + pre[j];
                             const float other = __shfl_xor_sync(kFull, mine, 1);
                             if ((lane & 1) == 0)
                                 st[(c0 + j) * 64 + i_local] = __float2bfloat16_rn(silu_times(mine, other));
@@ -903,13 +863,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             reinterpret_cast<uint4*>(args.h + static_cast<size_t>(u.hrow0 + j) * I + u.mb * 64) + part;
                         *dst = src[col * 8 + part];
                     }
+                    if (completes && epi_tid == 0) args.split_ticket[tile] = 0;  // every share is consumed
                     named_bar_sync(1, kEpiThreads);
                 } else {
                     // Down: routing weight x output, added into y[token] (128-byte runs).
-                    const int d = u.mb * kBlockM + quad * 32 + lane;
-#pragma unroll 1
-                    for (int c0 = 16 * half; c0 < BN; c0 += 32) {
-                        if (c0 >= ncols) break;
+                    const int d = u.mb * kBlockM + row;
+                    if (c0 < ncols) {
                         uint32_t r[16];
                         tmem_ld16(t_row + c0, r);
                         tmem_ld_wait();
@@ -927,7 +886,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tmem_empty[acc]);
                 }
-                first_unit = false;
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1u;

@@ -135,6 +135,34 @@ __device__ __forceinline__ bool grid_wait(const unsigned long long* ctr, unsigne
     }
 }
 
+__device__ __forceinline__ int ld_acquire_s32(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_add_s32(int* p, int v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until *ctr >= target (a 32-bit count), with grid_wait's exits.
+__device__ __forceinline__ bool count_wait_s32(const int* ctr, int target, volatile int* abort_flag, int* status,
+                                               int code, uint64_t limit_ns = kWaitLimitNs) {
+    if (ld_acquire_s32(ctr) >= target) return true;
+    const uint64_t start = global_timer_ns();
+    while (true) {
+        if (ld_acquire_s32(ctr) >= target) return true;
+        if (*abort_flag || *reinterpret_cast<volatile int*>(status) != 0) {
+            *abort_flag = 1;
+            return false;
+        }
+        if (global_timer_ns() - start > limit_ns) {
+            *abort_flag = 1;
+            atomicCAS(status, 0, code);
+            return false;
+        }
+        __nanosleep(32);
+    }
+}
+
 // ── TMA ───────────────────────────────────────────────────────────────────
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
