@@ -133,6 +133,7 @@ struct lm_moe_ctx {
     float* y_stage = nullptr;
     float* bias_stage = nullptr;
     int32_t* status_host = nullptr;  // pinned: the status word read back with y, one sync per host call
+    int32_t* status_host_dev = nullptr;  // its device address (the push kernel writes it)
     float* norm_f32 = nullptr;
     uint16_t* norm_bf16 = nullptr;
     cudaStream_t own_stream = nullptr;
@@ -239,6 +240,18 @@ int choose_bn(int tokens, int top_k, int experts) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// The device address of a host buffer when it is page-locked (cudaHostAlloc,
+// cudaMallocHost, cudaHostRegister: under unified addressing every page-locked range is
+// mapped), else nullptr (pageable memory).
+const void* mapped_device_address(const void* host) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, host) != cudaSuccess) {
+        cudaGetLastError();  // not a CUDA-known pointer: clear the error, copy instead
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
 
 // Whether the placement kernel (one CTA per routing tile) also copies the token rows:
 // only past the routed-small path and with at least one tile per two SMs.  Below that
@@ -1750,24 +1763,40 @@ lm_status lm_moe_forward_host(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x_
         LM_CUDA(ctx, cudaMalloc(&ctx->y_stage, T * H * sizeof(float)));
         LM_CUDA(ctx, cudaMalloc(&ctx->bias_stage, static_cast<size_t>(c.n_routed_experts) * sizeof(float)));
         LM_CUDA(ctx, cudaMallocHost(&ctx->status_host, sizeof(int32_t)));
+        LM_CUDA(ctx, cudaHostGetDevicePointer(reinterpret_cast<void**>(&ctx->status_host_dev), ctx->status_host, 0));
         LM_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking));
     }
     cudaStream_t s = ctx->own_stream;
     const size_t n = static_cast<size_t>(tokens) * H;
-    LM_CUDA(ctx, cudaMemcpyAsync(ctx->x_stage, x_host, n * sizeof(uint16_t), cudaMemcpyHostToDevice, s));
-    const float* bias = nullptr;
-    if (logit_bias_host != nullptr) {
-        LM_CUDA(ctx, cudaMemcpyAsync(ctx->bias_stage, logit_bias_host, c.n_routed_experts * sizeof(float),
-                                     cudaMemcpyHostToDevice, s));
-        bias = ctx->bias_stage;
-    }
+    const size_t x_bytes = n * sizeof(uint16_t), y_bytes = n * sizeof(float);
+    const size_t bias_bytes = static_cast<size_t>(c.n_routed_experts) * sizeof(float);
+    // Pinned buffers are mapped into the device's address space: SMs move them (no
+    // copy-engine transfer and its fixed cost).  Pageable or unaligned ones are copied.
+    const void* x_map = host_io_eligible(x_host, x_bytes) ? mapped_device_address(x_host) : nullptr;
+    const void* bias_map = logit_bias_host != nullptr && host_io_eligible(logit_bias_host, bias_bytes)
+                               ? mapped_device_address(logit_bias_host)
+                               : nullptr;
+    void* y_map = host_io_eligible(y_host, y_bytes) ? const_cast<void*>(mapped_device_address(y_host)) : nullptr;
+    const bool bias_pulled = x_map != nullptr && bias_map != nullptr;
+    if (x_map != nullptr)
+        LM_CUDA(ctx, launch_host_pull(ctx->x_stage, x_map, x_bytes, ctx->bias_stage, bias_pulled ? bias_map : nullptr,
+                                      bias_bytes, ctx->sms, s));
+    else
+        LM_CUDA(ctx, cudaMemcpyAsync(ctx->x_stage, x_host, x_bytes, cudaMemcpyHostToDevice, s));
+    if (logit_bias_host != nullptr && !bias_pulled)
+        LM_CUDA(ctx, cudaMemcpyAsync(ctx->bias_stage, logit_bias_host, bias_bytes, cudaMemcpyHostToDevice, s));
+    const float* bias = logit_bias_host != nullptr ? ctx->bias_stage : nullptr;
     st = ctx->nranks > 1 ? forward_ep(ctx, layer, ctx->x_stage, nullptr, tokens, bias, ctx->y_stage, 0, s)
                          : forward_impl(ctx, layer, ctx->x_stage, nullptr, tokens, bias, ctx->y_stage, 0, s);
     if (st != LM_OK) return st;
     // y and the status word come back in the same stream order: one synchronisation
     // covers both.
-    LM_CUDA(ctx, cudaMemcpyAsync(y_host, ctx->y_stage, n * sizeof(float), cudaMemcpyDeviceToHost, s));
-    LM_CUDA(ctx, cudaMemcpyAsync(ctx->status_host, ctx->status, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    if (y_map != nullptr) {
+        LM_CUDA(ctx, launch_host_push(y_map, ctx->y_stage, y_bytes, ctx->status, ctx->status_host_dev, ctx->sms, s));
+    } else {
+        LM_CUDA(ctx, cudaMemcpyAsync(y_host, ctx->y_stage, y_bytes, cudaMemcpyDeviceToHost, s));
+        LM_CUDA(ctx, cudaMemcpyAsync(ctx->status_host, ctx->status, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    }
     LM_CUDA(ctx, cudaStreamSynchronize(s));
     return settle_status(ctx, *ctx->status_host);
 }
@@ -2015,7 +2044,7 @@ static lm_status ep_copy_setup(lm_moe_ctx* ctx) {
     // flag wait spins (a lazily loaded kernel's first launch could otherwise wait for
     // a spinning wait that waits for the peer's GEMMs, which wait likewise).
     for (cudaError_t (*preload)() : {preload_router_kernels, preload_grouped_gemm_kernels, preload_pair_gemm_kernels,
-                                     preload_ops_kernels, preload_ep_peer_kernels})
+                                     preload_ops_kernels, preload_ep_peer_kernels, preload_host_io_kernels})
         LM_CUDA(ctx, preload());
     // Handshake (epoch 1): every rank stores into its slot of every peer's flags, waits
     // (bounded) for every peer's store into its own, then reads back through a copy

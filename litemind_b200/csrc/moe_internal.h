@@ -227,6 +227,19 @@ cudaError_t preload_grouped_gemm_kernels();
 cudaError_t preload_pair_gemm_kernels();
 cudaError_t preload_ops_kernels();
 cudaError_t preload_ep_peer_kernels();
+cudaError_t preload_host_io_kernels();
+
+// lm_moe_forward_host's transfers by SMs over mapped pinned host memory (host_io.cu).
+// A buffer qualifies when it is 16-byte aligned and its size a multiple of 16 bytes.
+bool host_io_eligible(const void* p, size_t bytes);
+// dst0 <- src0 (bytes0) and, when src1 is not null, dst1 <- src1 (bytes1); sources are
+// device addresses of mapped host memory.  The next kernel may launch meanwhile.
+cudaError_t launch_host_pull(void* dst0, const void* src0_mapped, size_t bytes0, void* dst1,
+                             const void* src1_mapped, size_t bytes1, int sms, cudaStream_t stream);
+// dst (mapped host memory) <- src (bytes) and *status_host <- *status, after the previous
+// kernel in the stream has finished (programmatic dependent launch).
+cudaError_t launch_host_push(void* dst_mapped, const void* src, size_t bytes, const int32_t* status,
+                             int32_t* status_host_mapped, int sms, cudaStream_t stream);
 // A flag buffer: N (rows ready) + kEpMaxChunks * N (outputs ready) slots, then the
 // expired wait's record (slot, value seen, epoch wanted).
 constexpr int kEpDiagSlots = 4;

@@ -77,21 +77,32 @@ def test_expired_grid_wait_reports_timeout_and_context_recovers(setup, T):
     _check_ok(layer, W, xb, y.cpu().numpy())
 
 
-def test_host_entry_reports_timeout_with_one_sync(setup):
-    """lm_moe_forward_host reads the status word back with y: the same error, no hang."""
+@pytest.mark.parametrize("page_locked", [False, True])
+def test_host_entry_reports_timeout_with_one_sync(setup, page_locked):
+    """lm_moe_forward_host reads the status word back with y: the same error, no hang.
+    Pageable buffers come back by copy-engine transfers; page-locked ones by the push
+    kernel, which copies the status word too."""
     layer, W = setup
     xb = syn.tokens(SHAPE, 16, seed=13)
+
+    def call():
+        if not page_locked:
+            return layer.forward_host(0, xb)
+        x_host = torch.from_numpy(np.ascontiguousarray(xb).view(np.int16)).pin_memory()
+        y_host = torch.empty((16, SHAPE.hidden), dtype=torch.float32).pin_memory()
+        layer.forward_host_ptr(0, x_host.data_ptr(), 16, y_host.data_ptr())
+        return y_host.numpy().copy()
+
     layer.debug_set(_lib.LM_DEBUG_WAIT_LIMIT_NS, LIMIT_NS)
     layer.debug_set(_lib.LM_DEBUG_GRID_EXTRA, 3)
     try:
         with pytest.raises(_lib.LiteMindError) as err:
-            layer.forward_host(0, xb)
+            call()
     finally:
         layer.debug_set(_lib.LM_DEBUG_GRID_EXTRA, 0)
         layer.debug_set(_lib.LM_DEBUG_WAIT_LIMIT_NS, 0)
     assert err.value.status == _lib.LM_ERR_DEVICE_TIMEOUT
-    y = layer.forward_host(0, xb)
-    _check_ok(layer, W, xb, y)
+    _check_ok(layer, W, xb, call())
 
 
 def test_debug_knobs_are_checked(setup):

@@ -109,6 +109,40 @@ def test_forward_host_matches_device(small_layer):
     np.testing.assert_allclose(y_host, y_dev.cpu().numpy(), rtol=1e-5, atol=1e-6)
 
 
+def _page_locked(nbytes: int):
+    """A zeroed page-locked host buffer with 64 spare bytes (room for a misaligned start)."""
+    return torch.zeros(nbytes + 64, dtype=torch.uint8).pin_memory()
+
+
+def _read_f32(buf, offset: int, shape):
+    return np.frombuffer(buf.numpy().tobytes()[offset:offset + 4 * int(np.prod(shape))], np.float32).reshape(shape)
+
+
+@pytest.mark.parametrize("T,offset,with_bias", [(77, 0, False), (77, 2, False), (1, 0, True), (16, 0, True),
+                                                (16, 4, True)])
+def test_forward_host_page_locked_buffers(small_layer, T, offset, with_bias):
+    """Page-locked buffers: 16-byte aligned ones move by SM loads and stores over mapped
+    memory, misaligned ones (offset 2 or 4) by copy-engine transfers; both must give the
+    device-buffer forward's result, on two calls in a row."""
+    layer, _ = small_layer
+    xb = syn.tokens(SMALL, T, seed=T + 3)
+    bias = np.linspace(-1.0, 1.0, SMALL.n_routed_experts).astype(np.float32) if with_bias else None
+    y_dev = layer.forward(0, bf16_tensor(xb), bias=None if bias is None else torch.from_numpy(bias).cuda())
+    layer.sync()
+    x_buf = _page_locked(xb.nbytes)
+    x_buf.numpy()[offset:offset + xb.nbytes] = np.ascontiguousarray(xb).view(np.uint8).reshape(-1)
+    b_ptr = None
+    if bias is not None:
+        b_buf = _page_locked(bias.nbytes)
+        b_buf.numpy()[offset:offset + bias.nbytes] = bias.view(np.uint8)
+        b_ptr = b_buf.data_ptr() + offset
+    y_buf = _page_locked(T * SMALL.hidden * 4)
+    for call in range(2):
+        layer.forward_host_ptr(0, x_buf.data_ptr() + offset, T, y_buf.data_ptr() + offset, b_ptr)
+        y = _read_f32(y_buf, offset, (T, SMALL.hidden))
+        np.testing.assert_allclose(y, y_dev.cpu().numpy(), rtol=1e-5, atol=1e-6, err_msg=f"call {call}")
+
+
 # ── DeepSeek-V2-Lite shapes ────────────────────────────────────────────────
 
 @pytest.fixture(scope="module")
@@ -127,6 +161,20 @@ def test_v2lite_decode_parity(oracle_lib, v2lite_weights, v2_layer, T, seed):
     ry, ridx, rw, rlog = run_oracle(oracle_lib, syn.V2_LITE, v2lite_weights, x)
     stats = assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what=f"V2-Lite T={T}")
     print(f"T={T}: {stats}")
+
+
+@pytest.mark.parametrize("T", [1, 32, 128])
+def test_v2lite_forward_host_page_locked(v2lite_weights, v2_layer, T):
+    """The host entry with page-locked buffers (the e2e measurement's form) at decode sizes,
+    where the fused kernel runs between the pull and push kernels."""
+    xb = syn.tokens(syn.V2_LITE, T, seed=T)
+    y_dev = v2_layer.forward(0, bf16_tensor(xb))
+    v2_layer.sync()
+    x_host = torch.from_numpy(np.ascontiguousarray(xb).view(np.int16)).pin_memory()
+    y_host = torch.empty((T, syn.V2_LITE.hidden), dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        v2_layer.forward_host_ptr(0, x_host.data_ptr(), T, y_host.data_ptr())
+        np.testing.assert_allclose(y_host.numpy(), y_dev.cpu().numpy(), rtol=1e-5, atol=1e-6)
 
 
 @pytest.mark.parametrize("T,zipf", [(2048, False), (16384, True)])
