@@ -81,7 +81,9 @@ def kernels_per_forward(tokens: int, world: int, experts: int = 64, top_k: int =
     fixed-capacity exchange (small batches) pack, sort, device schedule, two GEMMs
     and the combine, or with the host-planned exchange the row gather (when the
     placement does not copy), a sort and two GEMMs per chunk of local experts (plus
-    the shared experts' two GEMMs when chunked) and the combine."""
+    the shared experts' two GEMMs when chunked) and the combine; when copy engines move
+    the rows (the default on 2 ranks, LITEMIND_B200_EP_COPY), also one readiness signal
+    for the rows and one per chunk, and per peer one wait for its rows and one per chunk."""
     gather = 0 if tokens > 32 and 2 * tokens >= 32 * sms else 1
     if world == 1:
         return 1 if tokens <= 128 else 4 if tokens <= 256 else 6 + gather
@@ -93,7 +95,10 @@ def kernels_per_forward(tokens: int, world: int, experts: int = 64, top_k: int =
     # Host-planned: per chunk of local experts a sort and two GEMMs; with more than one
     # chunk the shared experts get GEMMs of their own.
     chunks = max(1, min(int(os.environ.get("LITEMIND_B200_EP_CHUNKS", "2")), 8, local))
-    return route + gather + 3 * chunks + (2 if chunks > 1 else 0) + 1
+    copy_env = os.environ.get("LITEMIND_B200_EP_COPY")
+    copy = world == 2 if copy_env is None else (int(copy_env) != 0 and world <= 8)
+    signals = (1 + chunks + (world - 1) * (1 + chunks)) if copy else 0
+    return route + gather + 3 * chunks + (2 if chunks > 1 else 0) + 1 + signals
 
 
 def parse_args(argv=None):

@@ -86,9 +86,18 @@ def test_launch_counts_follow_dispatch_rules():
     # Host-planned, 2 chunks (the default): four routing kernels, per chunk a sort and two
     # GEMMs, the shared experts' two GEMMs, the combine.
     os.environ.pop("LITEMIND_B200_EP_CHUNKS", None)
+    os.environ.pop("LITEMIND_B200_EP_COPY", None)
     assert k(8192, 8) == 4 + 2 * 3 + 2 + 1
+    # Two ranks move the rows by copy engines by default: a signal for the rows and one
+    # per chunk, and the peer's wait for its rows and one per chunk.
+    assert k(8192, 2) == 4 + 2 * 3 + 2 + 1 + (1 + 2) + (1 + 2)
     os.environ["LITEMIND_B200_EP_CHUNKS"] = "1"
     try:
         assert k(8192, 8) == 4 + 3 + 1
+        os.environ["LITEMIND_B200_EP_COPY"] = "0"
+        assert k(8192, 2) == 4 + 3 + 1
+        os.environ["LITEMIND_B200_EP_COPY"] = "1"
+        assert k(8192, 4) == 4 + 3 + 1 + (1 + 1) + 3 * (1 + 1)
     finally:
         os.environ.pop("LITEMIND_B200_EP_CHUNKS", None)
+        os.environ.pop("LITEMIND_B200_EP_COPY", None)
