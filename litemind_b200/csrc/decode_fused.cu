@@ -318,7 +318,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             // every global access of the routing -- the logits, and the instruction
             // fetches of code run for the first time -- waits microseconds in the
             // memory queues, which costs more than streaming early gains.
-            ok = mbar_wait(sched_ready, 0, abort_flag, args.status, kDevTimeoutProducer);
+            const uint64_t pf_total = args.prefetch_len[0] + args.prefetch_len[1];
+            if (pf_total > 0) {
+                // The router logits are read once every CTA has written its share: from then
+                // on the routing touches only L2 and shared memory, and HBM would idle until
+                // the schedule exists.  Bring this CTA's share of the weights into L2 meanwhile.
+                ok = grid_wait(args.grid_bar + kCtrLogits, target, abort_flag, args.status, kDevTimeoutGrid,
+                               args.wait_limit_ns);
+                const uint64_t per = ((pf_total + G - 1) / G + 4095) & ~uint64_t(4095);
+                uint64_t off = per * blockIdx.x;
+                const uint64_t hi = off + per < pf_total ? off + per : pf_total;
+                while (ok && off < hi) {
+                    const int r = off < args.prefetch_len[0] ? 0 : 1;
+                    const uint64_t r0 = r == 0 ? 0 : args.prefetch_len[0];
+                    const uint64_t r_end = r == 0 && hi > args.prefetch_len[0] ? args.prefetch_len[0] : hi;
+                    const uint64_t n = r_end - off < 32768 ? r_end - off : 32768;
+                    bulk_prefetch_l2(args.prefetch_base[r] + (off - r0), static_cast<uint32_t>(n));
+                    off += n;
+                }
+            }
+            if (ok) ok = mbar_wait(sched_ready, 0, abort_flag, args.status, kDevTimeoutProducer);
             const uint64_t weight_policy = policy_evict_first();
             for (int list = 0; list <= 1 && ok; ++list) {
                 const int nkb = list == 1 ? nkb2 : nkb1;

@@ -184,6 +184,11 @@ struct DecodeArgs {
     uint64_t wait_limit_ns;        // bound of the grid waits
     int32_t* status;
     unsigned long long* trace;     // optional: kDecodeTraceSlots global-timer stamps per CTA
+    // Weights to bring into L2 while the routing runs with HBM otherwise idle: once the
+    // router logits are written, each CTA prefetches its share of these two byte ranges
+    // (lengths multiples of 4096, 0 = none).
+    const uint8_t* prefetch_base[2];
+    uint64_t prefetch_len[2];
 };
 constexpr int kDecodeCounters = 5;
 // Phase stamps of the fused decode kernel (profiling only), per CTA:

@@ -163,6 +163,12 @@ __device__ __forceinline__ bool count_wait_s32(const int* ctr, int target, volat
     }
 }
 
+// Hint: bring `bytes` (a multiple of 16) of global memory at `src` (16-byte aligned)
+// into L2.  Nothing to wait for.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // ── TMA ───────────────────────────────────────────────────────────────────
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
