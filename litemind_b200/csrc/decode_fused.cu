@@ -8,8 +8,10 @@
 // gridDim.x equal ranges), with grid-wide arrival counters between them.
 //
 // Routing (src/Gemm.cpp:132-137, MoeRouter::select src/MoeRouter.cpp:54-107) comes
-// first, before any weight is streamed: under a saturated weight stream every
-// global access of the routing waits microseconds in the memory queues.  Two modes:
+// first, before any weight is streamed through the MMA: under a saturated weight
+// stream every global access of the routing waits microseconds in the memory queues.
+// (In direct mode the producer only brings the shared experts' gate/up weights into
+// L2 once the router logits are read.)  Two modes:
 //
 //   direct  (small T)  router dot products spread over every warp of the grid;
 //           after counter 0 every CTA reads all T x E logits into shared memory and
@@ -34,8 +36,9 @@
 // Epilogues are the grouped GEMMs' (grouped_gemm.cu): h = silu(gate) * up in bf16
 // for gate/up (src/DeepSeekRunner.cpp:228-240), and the routing-weighted atomic add
 // into y for down (the weighted combine and un-permute of :273-288).  A gate/up tile
-// whose k-blocks two CTAs share is summed deterministically through the split
-// workspace (fixed CTA order); a shared down tile simply adds both parts into y.
+// whose k-blocks several CTAs share is completed by the one holding its first
+// k-blocks, which adds the others' partial sums (split workspace, fixed CTA order) to
+// its own; a shared down tile simply adds every part into y.
 //
 // Warp roles as in the grouped GEMMs: warp 0 TMA producer, warp 1 tcgen05.mma
 // issuer, warps 2-9 routing and then the epilogue.  The routing's scratch lives in
