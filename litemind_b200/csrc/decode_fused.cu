@@ -177,6 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tmem_empty = bars + 2 * S + 2;
     uint64_t* sched_ready = bars + 2 * S + 4;
     uint64_t* drain_bar = bars + 2 * S + 5;
+    uint64_t* logit_bar = bars + 2 * S + 6;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     RouteScratch& rs = *reinterpret_cast<RouteScratch*>(smem_a);
@@ -196,6 +197,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int mb2 = H / kBlockM;
     const int nkb2 = I / kBlockK;
     const int nsh = args.n_shared;
+    // Gather mode with bf16 activations: a CTA's router-logit tasks are one group of
+    // kLogitTokens tokens against kEpiWarps consecutive experts (when every task fits
+    // in one round), so their inputs are two contiguous ranges -- kEpiWarps router rows
+    // and the group's token rows.  The producer brings both into ring stages 4.. (free
+    // until the schedule exists; the routing scratch holds stages 0-3) with bulk copies:
+    // one round trip, where loads from global memory would take one per step of the
+    // dot products.
+    const int ntg = (T + kLogitTokens - 1) / kLogitTokens;
+    const bool staged = gather && args.x_f32 == nullptr && E % kEpiWarps == 0 && E * ntg <= G * kEpiWarps &&
+                        static_cast<int64_t>(kEpiWarps) * H * 4 + static_cast<int64_t>(kLogitTokens) * H * 2 <=
+                            static_cast<int64_t>(S - 4) * kATile;
+    const int task0 = static_cast<int>(blockIdx.x) * kEpiWarps;  // this CTA's first logit task
+    const bool has_tasks = task0 < E * ntg;
+    float* st_router = reinterpret_cast<float*>(smem_a + 4 * kATile);
+    uint16_t* st_x = reinterpret_cast<uint16_t*>(smem_a + 4 * kATile + static_cast<size_t>(kEpiWarps) * H * 4);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
@@ -208,6 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(sched_ready, 1);
         mbar_init(drain_bar, 1);
+        mbar_init(logit_bar, 1);
         s_rp = args.rp;
         *abort_flag = 0;
         fence_mbar_init();
@@ -287,6 +304,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t issued_mask = 0;
             uint32_t issued_phase = 0;
             bool ok = true;
+            if (staged && has_tasks) {
+                // The CTA's router rows and token rows for the logits (see `staged`).
+                const int tg = task0 / E;
+                const int e0 = task0 - tg * E;
+                const int t0 = tg * kLogitTokens;
+                const int nt = min(kLogitTokens, T - t0);
+                const uint32_t rbytes = static_cast<uint32_t>(kEpiWarps) * H * 4;
+                const uint32_t xbytes = static_cast<uint32_t>(nt) * H * 2;
+                mbar_arrive_expect_tx(logit_bar, rbytes + xbytes);
+                const uint8_t* rsrc = reinterpret_cast<const uint8_t*>(args.router + static_cast<size_t>(e0) * H);
+                const uint8_t* xsrc = reinterpret_cast<const uint8_t*>(args.x + static_cast<size_t>(t0) * H);
+                for (uint32_t off = 0; off < rbytes; off += 16384)
+                    bulk_load(reinterpret_cast<uint8_t*>(st_router) + off, rsrc + off,
+                              rbytes - off < 16384 ? rbytes - off : 16384, logit_bar);
+                for (uint32_t off = 0; off < xbytes; off += 16384)
+                    bulk_load(reinterpret_cast<uint8_t*>(st_x) + off, xsrc + off,
+                              xbytes - off < 16384 ? xbytes - off : 16384, logit_bar);
+            }
             // Token tiles whose rows are not written yet (x_perm before counter 2, h
             // before counter 1), oldest first: every x_perm entry precedes every h one.
             int pend_stage[kMaxPending], pend_map[kMaxPending], pend_y[kMaxPending], pend_x[kMaxPending];
@@ -399,6 +434,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int st = 0; st < S; ++st)
                     if (issued_mask & (1u << st)) mbar_wait_drain(&full[st], (issued_phase >> st) & 1u, 100000000ull);
             }
+            // The logit inputs' copies (long landed on every path that got this far).
+            if (staged && has_tasks) mbar_wait_drain(logit_bar, 0, 100000000ull);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -558,8 +595,48 @@ __global__ void __launch_bounds__(kThreads, 1)
             // (2g) Router logits as warp tasks of (expert e, 8 tokens): the warp streams
             // the router row once for its 8 tokens.  Consecutive warps take consecutive
             // experts of the same tokens, so a CTA's token rows stay in L1.
-            const int ntg = (T + kLogitTokens - 1) / kLogitTokens;
-            for (int p = blockIdx.x * kEpiWarps + ew; p < E * ntg; p += G * kEpiWarps) {
+            if (staged) {
+                // Inputs in shared memory: warp ew takes expert e0 + ew of the CTA's token
+                // group (every thread waits for the copies itself; an expired wait has
+                // recorded its status, which the grid wait below sees).
+                if (has_tasks && mbar_wait(logit_bar, 0, abort_flag, args.status, kDevTimeoutEpilogue)) {
+                    const int p = task0 + ew;
+                    const int tg = p / E;
+                    const int e = p - tg * E;
+                    const int t0 = tg * kLogitTokens;
+                    const int nt = min(kLogitTokens, T - t0);
+                    const float* wr = st_router + static_cast<size_t>(ew) * H;
+                    float acc[kLogitTokens];
+#pragma unroll
+                    for (int j = 0; j < kLogitTokens; ++j) acc[j] = 0.0f;
+                    for (int hh = lane * 8; hh < H; hh += 256) {
+                        const float4 w0 = *reinterpret_cast<const float4*>(wr + hh);
+                        const float4 w1 = *reinterpret_cast<const float4*>(wr + hh + 4);
+                        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                        for (int j = 0; j < kLogitTokens; ++j) {
+                            const uint4 raw = *reinterpret_cast<const uint4*>(st_x + static_cast<size_t>(min(j, nt - 1)) * H + hh);
+                            const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                acc[j] = fmaf(__uint_as_float(words[i] << 16), wv[2 * i], acc[j]);
+                                acc[j] = fmaf(__uint_as_float(words[i] & 0xFFFF0000u), wv[2 * i + 1], acc[j]);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < kLogitTokens; ++j) {
+#pragma unroll
+                        for (int off = 16; off > 0; off >>= 1) acc[j] += __shfl_xor_sync(kFull, acc[j], off);
+                    }
+                    float v = acc[0];
+#pragma unroll
+                    for (int j = 1; j < kLogitTokens; ++j)
+                        if (lane == j) v = acc[j];
+                    if (lane < nt) args.logits[(t0 + lane) * E + e] = args.bias != nullptr ? v + args.bias[e] : v;
+                }
+            }
+            for (int p = blockIdx.x * kEpiWarps + ew; !staged && p < E * ntg; p += G * kEpiWarps) {
                 const int tg = p / E;
                 const int e = p - tg * E;
                 const int t0 = tg * kLogitTokens;
@@ -735,6 +812,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     run += __shfl_sync(kFull, incl, 31);
                 }
             }
+            // The ring's stages held the routing's scratch and the logit inputs: order
+            // those shared-memory accesses before the pipeline's TMA writes.
+            fence_proxy_async_shared();
             named_bar_sync(1, kEpiThreads);
             if (epi_tid == 0) {
                 mbar_arrive(sched_ready);  // producer and MMA may decode the lists

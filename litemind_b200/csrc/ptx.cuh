@@ -163,6 +163,22 @@ __device__ __forceinline__ bool count_wait_s32(const int* ctr, int target, volat
     }
 }
 
+// Orders this thread's generic-proxy shared-memory accesses before later async-proxy
+// (TMA, bulk copy) writes to the same memory.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Copy `bytes` (a multiple of 16) of global memory at `src` (16-byte aligned) into this
+// CTA's shared memory at `smem_dst` (16-byte aligned), completing the bytes on `bar`.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // Hint: bring `bytes` (a multiple of 16) of global memory at `src` (16-byte aligned)
 // into L2.  Nothing to wait for.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
