@@ -101,11 +101,12 @@ struct lm_moe_ctx {
     // Weight tiles read with an L2 evict-first hint (LITEMIND_B200_FUSED_EVICT_FIRST=0: off):
     // they are read once, and the hint keeps L2 for the rows the kernel re-reads.
     bool fused_evict_first = true;
-    // Weights the fused kernel brings into L2 while it routes in direct mode, the shared
-    // experts' (known before routing) (LITEMIND_B200_FUSED_PREFETCH): 0 none, 1 their
-    // gate/up, 2 their gate/up and down.  Measured on B200: T=1 51.2 -> 47.0 us and T=8
-    // 123.9 -> 118.9 us with their gate/up; in gather mode the prefetch traffic slows the
-    // routing's L2 round trips by more than it saves (T=128: +1 to +3 us), so it is off there.
+    // In direct mode the fused kernel brings the shared experts' gate/up weights (known
+    // before routing) into L2 while it routes (LITEMIND_B200_FUSED_PREFETCH=0: off).
+    // Measured on B200: T=1 51.2 -> 47.0 us, T=8 123.9 -> 118.9 us.  In gather mode the
+    // prefetch traffic slows the routing's L2 round trips by more than it saves (T=128:
+    // +1 to +3 us), so it is off there; so is prefetching each CTA's share of the routed
+    // experts' weights once the schedule exists (T=1: 50 -> 55 us).
     int fused_prefetch = 1;
     unsigned long long* grid_bar = nullptr;  // the fused decode kernel's arrival counters (self-resetting)
     // Testing only (lm_moe_debug_set): arrivals the fused kernel's grid waits expect
@@ -602,7 +603,7 @@ lm_status lm_moe_create(const lm_moe_config* config, int device, lm_moe_ctx** ou
         ctx->fused_gather_from = std::max(1, std::atoi(f));
     if (const char* f = std::getenv("LITEMIND_B200_FUSED_EVICT_FIRST")) ctx->fused_evict_first = std::atoi(f) != 0;
     if (const char* f = std::getenv("LITEMIND_B200_FUSED_PREFETCH"))
-        ctx->fused_prefetch = std::min(2, std::max(0, std::atoi(f)));
+        ctx->fused_prefetch = std::min(1, std::max(0, std::atoi(f)));
     ctx->local_experts = c.n_routed_experts;
     ctx->n_seg = ctx->local_experts + c.n_shared_experts;
     ctx->routed_cap = c.max_tokens * c.num_experts_per_tok;
@@ -1176,16 +1177,11 @@ static lm_status forward_impl(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x,
                                                                                    kDecodeTraceSlots * 8, s));
         a.trace = ctx->profiling ? ctx->decode_trace : nullptr;
         if (!gather && ctx->fused_prefetch > 0) {
-            // w13 and w2 hold the routed experts' segments, then the shared experts'
-            // (2*I*H and H*I bf16 each): the shared ones are needed whatever the routing.
+            // w13 holds the routed experts' segments, then the shared experts' (2*I*H bf16
+            // each): the shared ones are needed whatever the routing.
             const uint64_t seg13 = static_cast<uint64_t>(2) * I * H * sizeof(uint16_t);
-            const uint64_t seg2 = static_cast<uint64_t>(H) * I * sizeof(uint16_t);
             a.prefetch_base[0] = reinterpret_cast<const uint8_t*>(L.w13) + ctx->local_experts * seg13;
             a.prefetch_len[0] = (c.n_shared_experts * seg13) & ~uint64_t(4095);
-            if (ctx->fused_prefetch > 1) {
-                a.prefetch_base[1] = reinterpret_cast<const uint8_t*>(L.w2) + ctx->local_experts * seg2;
-                a.prefetch_len[1] = (c.n_shared_experts * seg2) & ~uint64_t(4095);
-            }
         }
         const int fbi = bn_index(fused_bn);
         LM_CUDA(ctx, launch_moe_decode(fused_bn, L.map_w13, L.map_w2, map_x, ctx->map_xperm[bn_index(kDecodeColTile)],
