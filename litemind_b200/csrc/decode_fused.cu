@@ -497,8 +497,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quad = warp & 3;
         const int half = (warp - 2) >> 2;
         bool ok = true;
-        // One thread waits; the named barrier hands the verdict to all eight warps
-        // (the slot alternates so a slow warp never reads the next verdict).
+        // One thread waits; the named barrier hands the outcome to all eight warps
+        // (the slot alternates so a slow warp never reads the next outcome).
         int go_slot = 0;
         auto broadcast = [&](bool v) {
             if (epi_tid == 0) s_go[go_slot] = v ? 1 : 0;

@@ -340,9 +340,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            // One thread waits; the named barrier hands its verdict to all eight
+            // One thread waits; the named barrier hands its outcome to all eight
             // warps, so they leave together and never strand each other at a barrier.
-            // The verdict slot alternates per tile so a slow warp never reads the next one.
+            // The outcome slot alternates per tile so a slow warp never reads the next one.
             if (epi_tid == 0)
                 s_epi_go[iter & 1] =
                     mbar_wait(&tmem_full[acc], acc_phase, abort_flag, args.status, kDevTimeoutEpilogue) ? 1 : 0;
