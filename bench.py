@@ -864,9 +864,25 @@ def measure_ep_base(layer, flush, args, torch) -> dict:
         layer.forward(1, x, y=y)
     layer.sync()
     ms = time_steps(layer, x, y, flush, max(5, args.steps // 2), torch, slot=1)
+    # Sustained: after the same load window the N-GPU runs take before their timed steps
+    # (power-capped clocks), the like-for-like base for them.
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < args.clock_window:
+        for _ in range(2):
+            flush()
+            layer.forward(1, x, y=y)
+        torch.cuda.synchronize()
+    ms_sus = time_steps(layer, x, y, flush, max(5, args.steps // 2), torch, slot=1)
+    clock_info = clocks.stop()
     return {"tokens": T, "seed": SEED_EP, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
+            "timing": "burst: the steps right after a 3-step warm-up",
+            "sustained": {"ms_per_step": ms_sus, "tokens_per_s": T / (ms_sus / 1e3), "clocks": clock_info,
+                          "timing": f"after {args.clock_window} s of back-to-back steps, as the N-GPU lines are "
+                                    "timed"},
             "note": "the expert-parallel runs' per-rank workload on one GPU (weights and rank-0 tokens of seed 3): "
-                    "the base of the weak-scaling series"}
+                    "the base of the weak-scaling series (compare the N-GPU lines with `sustained`)"}
 
 
 def main(argv=None) -> int:
