@@ -284,7 +284,12 @@ lm_status lm_moe_profile_ep_timeline(lm_moe_ctx* ctx, float* ms, int32_t capacit
  * exchange) and all fail with LM_ERR_INVALID_ARGUMENT when any differs.  NCCL is
  * loaded at run time (libnccl.so.2).  NCCL's copy-engine peer transfers
  * (NCCL_P2P_USE_CUDA_MEMCPY set to non-zero) are refused with LM_ERR_UNSUPPORTED
- * before NCCL is touched.
+ * before NCCL is touched.  A peer that stops taking part (a rank that failed between
+ * forwards) never leaves the others waiting for ever: lm_moe_forward's wait for the row
+ * counts, lm_moe_sync and lm_moe_forward_host give up after 30 s (the
+ * LM_DEBUG_WAIT_LIMIT_NS knob shortens it), abort the communicator and return
+ * LM_ERR_COMM; every later forward on that context returns LM_ERR_COMM at once, and
+ * the context can only be destroyed.
  */
 lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t rank,
                          int32_t nranks);

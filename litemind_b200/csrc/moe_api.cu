@@ -23,6 +23,7 @@
 #include "host/SafeTensors.hpp"
 
 #include <algorithm>
+#include <chrono>
 #include <cstdlib>
 #include <cstdio>
 #include <cstring>
@@ -147,6 +148,7 @@ struct lm_moe_ctx {
 
     // Expert parallelism (lm_moe_ep_init).
     ncclComm_t comm = nullptr;
+    bool ep_aborted = false;  // a peer missed an exchange: the communicator was aborted
     const lm::NcclApi* nccl = nullptr;
     uint16_t* x_recv = nullptr;    // received token rows, (source rank, local expert) segments
     uint16_t* x_sorted = nullptr;  // received rows, expert-major (each expert's rows contiguous)
@@ -522,6 +524,42 @@ lm_status settle_status(lm_moe_ctx* ctx, int32_t status) {
                         "); results are invalid");
     }
     return LM_OK;
+}
+
+// How long a host wait on expert-parallel work may take before the peers are given up
+// on (LM_DEBUG_WAIT_LIMIT_NS shortens it, with the device waits, for tests).
+constexpr uint64_t kEpHostLimitNs = 30ull * 1000 * 1000 * 1000;
+
+// Waits for stream `s`, which may hold this rank's side of NCCL exchanges.  A peer that
+// never takes its side leaves NCCL's kernels waiting for it, and a plain stream
+// synchronisation would wait with them for ever.  So the stream is polled against a
+// deadline; on expiry the communicator is aborted (which ends its waiting kernels and
+// lets the stream drain) and the call fails with LM_ERR_COMM.  Expert parallelism on
+// this context is then unusable; the caller destroys it.
+lm_status ep_wait_stream(lm_moe_ctx* ctx, cudaStream_t s, const char* what) {
+    if (ctx->comm == nullptr) {
+        LM_CUDA(ctx, cudaStreamSynchronize(s));
+        return LM_OK;
+    }
+    const uint64_t limit = ctx->debug_wait_limit_ns != 0 ? ctx->debug_wait_limit_ns : kEpHostLimitNs;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (int polls = 0;; ++polls) {
+        const cudaError_t q = cudaStreamQuery(s);
+        if (q == cudaSuccess) return LM_OK;
+        if (q != cudaErrorNotReady) return cuda_fail(ctx, q, what);
+        const auto waited = std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0);
+        if (static_cast<uint64_t>(waited.count()) > limit) break;
+        // Spin at first (an exchange normally completes within milliseconds), then back off.
+        if (polls > 2000) std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    ctx->nccl->CommAbort(ctx->comm);
+    ctx->comm = nullptr;
+    ctx->ep_aborted = true;
+    cudaStreamSynchronize(s);  // the aborted kernels return; what follows them completes
+    cudaGetLastError();
+    return fail(ctx, LM_ERR_COMM,
+                std::string(what) + ": a peer did not take its part in the exchange within " +
+                    std::to_string(limit / 1000000) + " ms; the communicator was aborted");
 }
 }  // namespace
 }  // namespace lm
@@ -1364,6 +1402,8 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
     const LayerWeights& L = ctx->layers[layer];
     const int K = c.num_experts_per_tok, E = c.n_routed_experts, H = c.hidden_size, I = c.moe_intermediate_size;
     const int N = ctx->nranks, El = ctx->local_experts;
+    if (ctx->ep_aborted)
+        return fail(ctx, LM_ERR_COMM, "expert parallelism on this context ended when a peer missed an exchange");
     const NcclApi& nc = *ctx->nccl;
     const RouterParams rp = router_params(c);
     float* y_zero = accumulate ? nullptr : y;
@@ -1409,7 +1449,7 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
         LM_NCCL(ctx, nc.GroupEnd());
         LM_CUDA(ctx, cudaMemcpyAsync(ctx->host_counts_all, ctx->counts_all, static_cast<size_t>(N) * E * sizeof(int32_t),
                                      cudaMemcpyDeviceToHost, s));
-        LM_CUDA(ctx, cudaStreamSynchronize(s));
+        if (const lm_status ws = ep_wait_stream(ctx, s, "expert-parallel row counts"); ws != LM_OK) return ws;
         counts_all = ctx->host_counts_all;
         for (int e = 0; e < E; ++e) ctx->host_totals[e] = counts_all[ctx->rank * E + e];
         for (int r = 0; r < N; ++r)
@@ -1427,7 +1467,7 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
                                      s));
         LM_CUDA(ctx, cudaMemcpyAsync(ctx->host_recv, ctx->recv_counts, N * El * sizeof(int32_t), cudaMemcpyDeviceToHost,
                                      s));
-        LM_CUDA(ctx, cudaStreamSynchronize(s));
+        if (const lm_status ws = ep_wait_stream(ctx, s, "expert-parallel row counts"); ws != LM_OK) return ws;
     }
     lm_ep_plan total;
     if (lm_moe_ep_plan(N, E, ctx->host_totals, ctx->host_recv, &total) != LM_OK)
@@ -1813,7 +1853,7 @@ lm_status lm_moe_forward_host(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x_
         LM_CUDA(ctx, cudaMemcpyAsync(y_host, ctx->y_stage, y_bytes, cudaMemcpyDeviceToHost, s));
         LM_CUDA(ctx, cudaMemcpyAsync(ctx->status_host, ctx->status, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     }
-    LM_CUDA(ctx, cudaStreamSynchronize(s));
+    if ((st = ep_wait_stream(ctx, s, "lm_moe_forward_host")) != LM_OK) return st;
     return settle_status(ctx, *ctx->status_host);
 }
 
@@ -1847,7 +1887,7 @@ lm_status lm_moe_sync(lm_moe_ctx* ctx, void* stream) {
     if (ctx == nullptr) return LM_ERR_INVALID_ARGUMENT;
     lm_status st;
     if ((st = set_device(ctx)) != LM_OK) return st;
-    LM_CUDA(ctx, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    if ((st = ep_wait_stream(ctx, static_cast<cudaStream_t>(stream), "lm_moe_sync")) != LM_OK) return st;
     int32_t status = 0;
     LM_CUDA(ctx, cudaMemcpy(&status, ctx->status, sizeof(status), cudaMemcpyDeviceToHost));
     return settle_status(ctx, status);

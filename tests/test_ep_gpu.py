@@ -88,3 +88,73 @@ def test_expert_parallel_two_gpus_nccl_exchange(shape_name, token_counts, chunks
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     mp.spawn(_worker, args=(2, _free_port(), shape_name, token_counts, chunks, False), nprocs=2, join=True)
+
+
+def _silent_peer_worker(rank, world, port, tokens, copy, status_dir):
+    """Both ranks forward once; then each in turn stops taking part while staying alive
+    (no kernel or exchange of its own in flight), and the other's next forward must end
+    with LM_ERR_COMM within the shortened wait limit instead of waiting for ever."""
+    import json
+    import time
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LITEMIND_B200_EP_CHUNKS="2",
+                      LITEMIND_B200_EP_COPY="1" if copy else "0", NCCL_NVLS_ENABLE="0")
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        from litemind_b200 import _lib
+        from litemind_b200.moe import MoeConfig, MoeLayer, bf16_tensor
+
+        torch.cuda.set_device(rank)
+        W = syn.layer_weights(SMALL, seed=5, std=0.1)
+        uid = [MoeLayer.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        layer = MoeLayer(MoeConfig.from_shape(SMALL, max_tokens=tokens), device=rank)
+        layer.ep_init(uid[0], rank, world)
+        layer.upload_layer(0, W)
+        x = bf16_tensor(syn.tokens(SMALL, tokens, seed=100 + rank))
+        layer.forward(0, x)
+        layer.sync()
+        dist.barrier()
+        record = {}
+        for turn in range(world):  # rank `turn` forwards alone; its peer stays silent
+            if rank == turn:
+                layer.debug_set(_lib.LM_DEBUG_WAIT_LIMIT_NS, 300_000_000)
+                t0 = time.monotonic()
+                try:
+                    layer.forward(0, x)
+                    layer.sync()
+                    record["first"] = "no error"
+                except _lib.LiteMindError as e:
+                    record["first"] = e.status
+                record["seconds"] = time.monotonic() - t0
+                try:  # the context's expert parallelism is over: the next call fails at once
+                    layer.forward(0, x)
+                    layer.sync()
+                    record["second"] = "no error"
+                except _lib.LiteMindError as e:
+                    record["second"] = e.status
+            dist.barrier()
+        with open(os.path.join(status_dir, f"rank{rank}.json"), "w") as f:
+            json.dump(record, f)
+        layer.close()
+    finally:
+        dist.destroy_process_group()
+
+
+# 300 tokens: fixed blocks, the exchange enqueued without a host wait (the sync reports
+# it); 5000: the host-planned exchange, whose row counts the host waits for.
+@pytest.mark.parametrize("tokens,copy", [(300, False), (5000, True), (5000, False)])
+def test_silent_peer_ends_the_forward_with_an_error(tmp_path, tokens, copy):
+    import json
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.spawn(_silent_peer_worker, args=(2, _free_port(), tokens, copy, str(tmp_path)), nprocs=2, join=True)
+    from litemind_b200._lib import LM_ERR_COMM
+
+    for r in range(2):
+        rec = json.load(open(tmp_path / f"rank{r}.json"))
+        assert rec["first"] == LM_ERR_COMM, rec
+        assert rec["second"] == LM_ERR_COMM, rec
+        assert rec["seconds"] < 20.0, rec
