@@ -530,6 +530,17 @@ lm_status settle_status(lm_moe_ctx* ctx, int32_t status) {
 // on (LM_DEBUG_WAIT_LIMIT_NS shortens it, with the device waits, for tests).
 constexpr uint64_t kEpHostLimitNs = 30ull * 1000 * 1000 * 1000;
 
+// Ends expert parallelism on this context: aborts the communicator (which ends any of
+// its kernels still waiting for a peer, so `s` drains) and reports LM_ERR_COMM.
+lm_status ep_give_up(lm_moe_ctx* ctx, cudaStream_t s, const std::string& why) {
+    if (ctx->comm != nullptr) ctx->nccl->CommAbort(ctx->comm);
+    ctx->comm = nullptr;
+    ctx->ep_aborted = true;
+    cudaStreamSynchronize(s);
+    cudaGetLastError();
+    return fail(ctx, LM_ERR_COMM, why + "; the communicator was aborted");
+}
+
 // Waits for stream `s`, which may hold this rank's side of NCCL exchanges.  A peer that
 // never takes its side leaves NCCL's kernels waiting for it, and a plain stream
 // synchronisation would wait with them for ever.  So the stream is polled against a
@@ -543,23 +554,31 @@ lm_status ep_wait_stream(lm_moe_ctx* ctx, cudaStream_t s, const char* what) {
     }
     const uint64_t limit = ctx->debug_wait_limit_ns != 0 ? ctx->debug_wait_limit_ns : kEpHostLimitNs;
     const auto t0 = std::chrono::steady_clock::now();
+    std::string why;
     for (int polls = 0;; ++polls) {
         const cudaError_t q = cudaStreamQuery(s);
-        if (q == cudaSuccess) return LM_OK;
+        if (q == cudaSuccess) {
+            // An exchange whose peer went away can also end early with an error (the data
+            // it delivered is not to be used).
+            ncclResult_t async = ncclSuccess;
+            if (ctx->nccl->CommGetAsyncError(ctx->comm, &async) == ncclSuccess && async != ncclSuccess &&
+                async != ncclInProgress) {
+                why = std::string(what) + ": the exchange failed (" + ctx->nccl->GetErrorString(async) + ")";
+                break;
+            }
+            return LM_OK;
+        }
         if (q != cudaErrorNotReady) return cuda_fail(ctx, q, what);
         const auto waited = std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0);
-        if (static_cast<uint64_t>(waited.count()) > limit) break;
+        if (static_cast<uint64_t>(waited.count()) > limit) {
+            why = std::string(what) + ": a peer did not take its part in the exchange within " +
+                  std::to_string(limit / 1000000) + " ms";
+            break;
+        }
         // Spin at first (an exchange normally completes within milliseconds), then back off.
         if (polls > 2000) std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
-    ctx->nccl->CommAbort(ctx->comm);
-    ctx->comm = nullptr;
-    ctx->ep_aborted = true;
-    cudaStreamSynchronize(s);  // the aborted kernels return; what follows them completes
-    cudaGetLastError();
-    return fail(ctx, LM_ERR_COMM,
-                std::string(what) + ": a peer did not take its part in the exchange within " +
-                    std::to_string(limit / 1000000) + " ms; the communicator was aborted");
+    return ep_give_up(ctx, s, why);
 }
 }  // namespace
 }  // namespace lm
@@ -1451,6 +1470,15 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
                                      cudaMemcpyDeviceToHost, s));
         if (const lm_status ws = ep_wait_stream(ctx, s, "expert-parallel row counts"); ws != LM_OK) return ws;
         counts_all = ctx->host_counts_all;
+        // Every rank's counts locate rows in its own and its peers' buffers: they are
+        // checked before any copy uses them (each rank sends at most routed_cap rows).
+        for (int r = 0; r < N; ++r) {
+            int64_t sum = 0;
+            for (int e = 0; e < E; ++e) sum += counts_all[r * E + e] < 0 ? INT32_MAX : counts_all[r * E + e];
+            if (sum > ctx->routed_cap)
+                return ep_give_up(ctx, s, "expert-parallel row counts: rank " + std::to_string(r) +
+                                              "'s do not fit its send buffer");
+        }
         for (int e = 0; e < E; ++e) ctx->host_totals[e] = counts_all[ctx->rank * E + e];
         for (int r = 0; r < N; ++r)
             for (int e = 0; e < El; ++e) ctx->host_recv[r * El + e] = counts_all[r * E + ctx->rank * El + e];
@@ -1468,6 +1496,14 @@ static lm_status forward_ep(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, c
         LM_CUDA(ctx, cudaMemcpyAsync(ctx->host_recv, ctx->recv_counts, N * El * sizeof(int32_t), cudaMemcpyDeviceToHost,
                                      s));
         if (const lm_status ws = ep_wait_stream(ctx, s, "expert-parallel row counts"); ws != LM_OK) return ws;
+        for (int r = 0; r < N; ++r) {  // the receive buffer holds routed_cap rows per source
+            int64_t sum = 0;
+            for (int e = 0; e < El; ++e)
+                sum += ctx->host_recv[r * El + e] < 0 ? INT32_MAX : ctx->host_recv[r * El + e];
+            if (sum > ctx->routed_cap)
+                return ep_give_up(ctx, s, "expert-parallel row counts: rank " + std::to_string(r) +
+                                              "'s do not fit the receive buffer");
+        }
     }
     lm_ep_plan total;
     if (lm_moe_ep_plan(N, E, ctx->host_totals, ctx->host_recv, &total) != LM_OK)

@@ -151,10 +151,13 @@ def test_silent_peer_ends_the_forward_with_an_error(tmp_path, tokens, copy):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     mp.spawn(_silent_peer_worker, args=(2, _free_port(), tokens, copy, str(tmp_path)), nprocs=2, join=True)
-    from litemind_b200._lib import LM_ERR_COMM
+    from litemind_b200._lib import LM_ERR_COMM, LM_ERR_DEVICE_TIMEOUT
 
     for r in range(2):
         rec = json.load(open(tmp_path / f"rank{r}.json"))
-        assert rec["first"] == LM_ERR_COMM, rec
-        assert rec["second"] == LM_ERR_COMM, rec
-        assert rec["seconds"] < 20.0, rec
+        # The host's wait for the exchange gives up (LM_ERR_COMM), or -- when the exchange
+        # ends early because the peer's communicator is gone -- a device-side wait for the
+        # peer's readiness flag does (LM_ERR_DEVICE_TIMEOUT); either way within the limit.
+        assert rec["first"] in (LM_ERR_COMM, LM_ERR_DEVICE_TIMEOUT), (r, rec)
+        assert rec["second"] in (LM_ERR_COMM, LM_ERR_DEVICE_TIMEOUT), (r, rec)
+        assert rec["seconds"] < 20.0, (r, rec)
