@@ -222,6 +222,24 @@ def test_fused_group_limited_routing(oracle_lib, T, normalize):
     layer.close()
 
 
+@pytest.mark.parametrize("experts,T", [(12, 40), (12, 128), (16, 40), (16, 97)])
+def test_fused_gather_logit_inputs(oracle_lib, experts, T):
+    """Gather mode computes the router logits from inputs each CTA pulls into shared
+    memory with bulk copies when its tasks are one token group against 8 consecutive
+    experts (expert counts a multiple of 8), and from global memory otherwise: both,
+    with partial last token groups, against the oracle."""
+    shape = syn.MoeShape(hidden=512, inter=256, n_routed_experts=experts, n_shared_experts=2, top_k=3)
+    W = syn.layer_weights(shape, seed=51 + experts, std=0.05)
+    layer = MoeLayer(MoeConfig.from_shape(shape, max_tokens=128))
+    layer.upload_layer(0, W)
+    x = syn.tokens(shape, T, seed=52 + T)
+    y, idx, w, _, prof = _gpu(layer, x)
+    assert "decode_fused" in prof
+    ry, ridx, rw, rlog = _oracle(oracle_lib, shape, W, x, cfg=RouterConfig(experts, 3))
+    assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what=f"fused gather E={experts} T={T}")
+    layer.close()
+
+
 @pytest.mark.parametrize("T,normalize", [(33, False), (100, True), (128, False), (256, True)])
 def test_mid_batch_single_launch_routing(oracle_lib, T, normalize):
     """32 < T <= 256 routes in one launch (logits and routing per 32-token block,
