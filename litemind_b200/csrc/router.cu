@@ -233,20 +233,39 @@ __global__ void __launch_bounds__(kTopkThreads) router_topk_kernel(float* __rest
             rank_rp.scale = 1.0f;
             const Selection ranked = route_one_token<EPL>(lg, rank_rp, probs[warp], lane, 0.0f);
             const uint16_t* xt = fix.x + static_cast<size_t>(t) * fix.hidden;
-            for (int r = 0; r < rank_rp.top_k; ++r) {
-                const int e = __shfl_sync(kFull, ranked.idx, r);
-                const float* wr = fix.w + static_cast<size_t>(e) * fix.hidden;
-                float acc = 0.0f;
-                for (int h = lane * 8; h < fix.hidden; h += 256) {
-                    float xv[8], wv[8];
-                    load8(xt + h, xv);
-                    load8(wr + h, wv);
+            // kBatch experts share each pass over the hidden axis (each x chunk loaded
+            // once for all of them): a pass is a chain of dependent load rounds, and one
+            // ambiguous token decides when the whole launch ends.  Each dot product is
+            // summed in the same order as one at a time.
+            constexpr int kBatch = 2;
+            const int nr = rank_rp.top_k;
+            for (int r0 = 0; r0 < nr; r0 += kBatch) {
+                int e[kBatch];
+                const float* wr[kBatch];
+                float acc[kBatch];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) acc = fmaf(xv[i], wv[i], acc);
+                for (int j = 0; j < kBatch; ++j) {
+                    e[j] = __shfl_sync(kFull, ranked.idx, min(r0 + j, nr - 1));  // past nr: recomputed, unused
+                    wr[j] = fix.w + static_cast<size_t>(e[j]) * fix.hidden;
+                    acc[j] = 0.0f;
+                }
+                for (int h = lane * 8; h < fix.hidden; h += 256) {
+                    float xv[8];
+                    load8(xt + h, xv);
+#pragma unroll
+                    for (int j = 0; j < kBatch; ++j) {
+                        float wv[8];
+                        load8(wr[j] + h, wv);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) acc[j] = fmaf(xv[i], wv[i], acc[j]);
+                    }
                 }
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(kFull, acc, off);
-                if (lane == 0) lg[e] = fix.bias != nullptr ? acc + fix.bias[e] : acc;
+                for (int j = 0; j < kBatch; ++j) {
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) acc[j] += __shfl_xor_sync(kFull, acc[j], off);
+                    if (lane == 0 && r0 + j < nr) lg[e[j]] = fix.bias != nullptr ? acc[j] + fix.bias[e[j]] : acc[j];
+                }
             }
             __syncwarp();
             sel = route_one_token<EPL>(lg, rp, probs[warp], lane, 0.0f);
