@@ -73,8 +73,7 @@ FLUSH_BYTES = 256 << 20
 
 def kernels_per_forward(tokens: int, world: int, experts: int = 64, top_k: int = 6, sms: int = 148) -> int:
     """Our kernel launches in one forward (NCCL's own kernels not counted).
-    One GPU: T <= 128 is the fused decode kernel alone; 128 < T <= 256 the single-launch
-    routing kernel, the row gather and the two grouped GEMMs; above that router
+    One GPU: T <= 256 is the fused decode kernel alone; above that router
     logits, top-k, scan, placement and the two grouped GEMMs, plus a separate row
     gather unless the placement copies the rows itself (2 T >= 32 x SMs).  Expert parallel:
     the routing (fused route kernel for T <= 32, else four kernels), then with the
@@ -86,7 +85,7 @@ def kernels_per_forward(tokens: int, world: int, experts: int = 64, top_k: int =
     for the rows and one per chunk, and per peer one wait for its rows and one per chunk."""
     gather = 0 if tokens > 32 and 2 * tokens >= 32 * sms else 1
     if world == 1:
-        return 1 if tokens <= 128 else 4 if tokens <= 256 else 6 + gather
+        return 1 if tokens <= 256 else 6 + gather
     route = 1 if tokens <= 32 else 4
     local = experts // world
     fixed = world * tokens * min(top_k, local) <= 8192

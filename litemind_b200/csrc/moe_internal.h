@@ -146,10 +146,10 @@ struct GemmArgs {
     int32_t split_ws_floats;   // capacity of split_ws in floats
     int32_t split_max_waves;   // split when the tiles fill fewer waves of the grid than this (0: never)
 };
-// The fused decode kernel (decode_fused.cu): the whole layer for T <= 128 tokens in
+// The fused decode kernel (decode_fused.cu): the whole layer for T <= 256 tokens in
 // one cooperative launch -- routing, dispatch, gate/up, down and the combine.
-constexpr int kDecodeMaxTokens = 128;
-constexpr int kDecodeMaxRows = 1024;        // tokens x top-k
+constexpr int kDecodeMaxTokens = 256;
+constexpr int kDecodeMaxRows = 1536;        // tokens x top-k
 constexpr int kDecodeDirectTokens = 32;     // direct mode takes at most this many tokens (x itself is every
                                             // expert's token operand); gather mode takes any batch
 constexpr int kDecodeColTile = 32;          // token rows per column tile above that (gather mode)

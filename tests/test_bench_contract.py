@@ -78,8 +78,7 @@ def test_load_window_is_agreed_across_ranks(tmp_path):
 
 def test_launch_counts_follow_dispatch_rules():
     k = bench.kernels_per_forward
-    assert k(32, 1) == k(128, 1) == 1  # the fused decode kernel (direct and gather modes)
-    assert k(129, 1) == k(256, 1) == 4  # single-launch route, row gather, two GEMMs
+    assert k(32, 1) == k(128, 1) == k(256, 1) == 1  # the fused decode kernel (direct and gather modes)
     assert k(257, 1) == 7  # logits, top-k, scan, placement, gather, two GEMMs
     assert k(16384, 1) == 6  # the placement copies the rows itself
     assert k(32, 8) == 7  # fixed-block exchange: route, pack, sort, schedule, two GEMMs, combine

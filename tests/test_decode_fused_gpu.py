@@ -1,9 +1,9 @@
-"""The fused decode kernel (one cooperative launch per layer for T <= 128 on one GPU).
+"""The fused decode kernel (one cooperative launch per layer for T <= 256 on one GPU).
 
 Parity against the oracle across the token counts that change its work split: in
 direct mode (by default below 16 tokens; up to 32 when forced: one token, a token-tile
-boundary, 32) and in gather mode (16-128 tokens: column-tile boundaries at 32, 64 and
-96, the largest batch), with a
+boundary, 32) and in gather mode (16-256 tokens: column-tile boundaries at 32, 64, 96,
+128 and above, more tokens than CTAs, the largest batch), with a
 logit bias, with group-limited and renormalised routing, with accumulation into y,
 with f32 router activations (the block path), with gather mode forced down to a
 single token, and against the grouped multi-launch path it replaces.  Its phase
@@ -31,7 +31,7 @@ GROUPED = syn.MoeShape(hidden=512, inter=256, n_routed_experts=64, n_shared_expe
 
 @pytest.fixture(scope="module")
 def v2(v2lite_weights):
-    layer = MoeLayer(MoeConfig(max_tokens=128))
+    layer = MoeLayer(MoeConfig(max_tokens=256))
     layer.upload_layer(0, v2lite_weights)
     yield layer
     layer.close()
@@ -79,7 +79,7 @@ def test_fused_parity_across_token_counts(oracle_lib, v2lite_weights, v2, T):
     assert_layer_parity(y, idx, w, ry, ridx, rw, rlog, what=f"fused T={T}")
 
 
-@pytest.mark.parametrize("T", [33, 48, 63, 64, 65, 96, 127, 128])
+@pytest.mark.parametrize("T", [33, 48, 63, 64, 65, 96, 127, 128, 129, 160, 200, 255, 256])
 def test_fused_gather_parity_across_token_counts(oracle_lib, v2lite_weights, v2, T):
     x = syn.tokens(V2, T, seed=150 + T)
     y, idx, w, _, prof = _gpu(v2, x)
