@@ -69,6 +69,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     using C = PCfg<BN, KIND>;
     constexpr int S = C::kStages;
     constexpr uint32_t kIdesc = umma_idesc_bf16(2 * kRows, BN);
+    // A segment's last token block with at most BN/2 rows left runs at N = BN/2: the
+    // tensor cores skip the padding (384 rows per expert are 256 + 128, not 2 x 256).
+    constexpr uint32_t kIdescNarrow = umma_idesc_bf16(2 * kRows, BN / 2);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ int s_tiles[kMaxSegments + 1];
@@ -169,7 +172,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int mb = local - nb * mb_per;
                 const int a_tile0 = (s_wslot[s] * tiles128_per + 2 * mb + static_cast<int>(rank)) * num_kb;
                 const bool from_x = (KIND == PKind::GateUp) && s >= args.n_routed_local;
-                const int b_row = (from_x ? nb * BN : s_off[s] + nb * BN) + static_cast<int>(rank) * C::kBHalf;
+                // Each CTA holds its half of the block's N token rows: BN/2 of them, or
+                // BN/4 for a narrow last block (the box still loads BN/2; the MMA reads
+                // the first BN/4 of them).
+                const bool narrow = s_cnt[s] - nb * BN <= BN / 2;
+                const int b_row = (from_x ? nb * BN : s_off[s] + nb * BN) +
+                                  static_cast<int>(rank) * (narrow ? C::kBHalf / 2 : C::kBHalf);
                 const CUtensorMap* bmap = from_x ? &map_x : &map_b;
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status, kDevTimeoutProducer)) {
@@ -206,6 +214,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, args.status, kDevTimeoutMma)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                const int seg = find_segment(s_tiles, n_seg, tile);
+                const int nb = (tile - s_tiles[seg]) / mb_per;
+                const uint32_t idesc = s_cnt[seg] - nb * BN <= BN / 2 ? kIdescNarrow : kIdesc;
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag, args.status, kDevTimeoutMma)) {
                         ok = false;
@@ -216,7 +227,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const uint64_t b_desc = umma_desc_sw128(smem_u32(smem_b + stage * C::kBTile));
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk)
-                        umma_bf16_pair(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, kIdesc, (kb | kk) != 0);
+                        umma_bf16_pair(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb | kk) != 0);
                     issued_any = true;
                     umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 0));
                     umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));

@@ -177,9 +177,10 @@ def test_v2lite_forward_host_page_locked(v2lite_weights, v2_layer, T):
         np.testing.assert_allclose(y_host.numpy(), y_dev.cpu().numpy(), rtol=1e-5, atol=1e-6)
 
 
-@pytest.mark.parametrize("T,zipf", [(2048, False), (16384, True)])
+@pytest.mark.parametrize("T,zipf", [(2048, False), (4096, False), (16384, True)])
 def test_v2lite_prefill_sampled_parity(oracle_lib, v2lite_weights, v2_layer, T, zipf):
-    """Prefill: T=16384 with a Zipf(1.2) expert load, and a 2048-token batch."""
+    """Prefill: T=16384 with a Zipf(1.2) expert load, and 2048- and 4096-token batches
+    (about 384 rows per expert at 4096: each expert's last token block runs narrow)."""
     x = syn.tokens(syn.V2_LITE, T, seed=2)
     bias = syn.zipf_bias(syn.V2_LITE, seed=2) if zipf else None
     y, idx, w, _ = run_gpu(v2_layer, x, bias)
