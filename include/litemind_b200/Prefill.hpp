@@ -7,7 +7,7 @@
 // (src/DeepSeekRunner.cpp:242-290).  The feed-forward sub-layer treats each position
 // on its own, so once a layer's attention has run for all T prompt positions (a causal
 // attention over the prompt does), its feed-forward sub-layer runs for all T positions
-// in one call: one cooperative launch up to 128 tokens, the grouped tensor-core GEMMs
+// in one call: one cooperative launch up to 256 tokens, the grouped tensor-core GEMMs
 // above.  BatchedPrefill drives that loop; the hidden states stay on the device as f32
 // [T, hidden], and the caller's attention sub-layer is a callback.
 #pragma once
