@@ -197,20 +197,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int mb2 = H / kBlockM;
     const int nkb2 = I / kBlockK;
     const int nsh = args.n_shared;
-    // Gather mode with bf16 activations: a CTA's router-logit tasks are one group of
-    // kLogitTokens tokens against kEpiWarps consecutive experts (when every task fits
-    // in one round), so their inputs are two contiguous ranges -- kEpiWarps router rows
-    // and the group's token rows.  The producer brings both into ring stages 4.. (free
-    // until the schedule exists; the routing scratch holds stages 0-3) with bulk copies:
-    // one round trip, where loads from global memory would take one per step of the
-    // dot products.
+    // Gather mode with bf16 activations: a CTA's router-logit tasks are kEpiWarps
+    // consecutive experts (its expert block, one per warp) against one group of
+    // kLogitTokens tokens per round -- groups q, q + cta_per_eb, ... -- so their inputs
+    // are contiguous ranges: the block's router rows once and each round's token rows.
+    // The producer brings them all into the ring from stage 4 on (free until the schedule
+    // exists; the routing scratch holds stages 0-3; the token stages follow the weight
+    // stages) with bulk copies: one round trip, where loads from global memory would
+    // take one per step of the dot products.
     const int ntg = (T + kLogitTokens - 1) / kLogitTokens;
-    const bool staged = gather && args.x_f32 == nullptr && E % kEpiWarps == 0 && E * ntg <= G * kEpiWarps &&
-                        static_cast<int64_t>(kEpiWarps) * H * 4 + static_cast<int64_t>(kLogitTokens) * H * 2 <=
-                            static_cast<int64_t>(S - 4) * kATile;
-    const int task0 = static_cast<int>(blockIdx.x) * kEpiWarps;  // this CTA's first logit task
-    const bool has_tasks = task0 < E * ntg;
+    const int n_eb = E / kEpiWarps;                        // expert blocks
+    const int cta_per_eb = n_eb > 0 ? G / n_eb : 0;        // CTAs sharing an expert block
+    const int rounds = cta_per_eb > 0 ? (ntg + cta_per_eb - 1) / cta_per_eb : 0;
+    const bool staged = gather && args.x_f32 == nullptr && E % kEpiWarps == 0 && cta_per_eb > 0 && rounds <= 2 &&
+                        static_cast<int64_t>(kEpiWarps) * H * 4 + static_cast<int64_t>(rounds) * kLogitTokens * H * 2 <=
+                            static_cast<int64_t>(S - 4) * kATile + static_cast<int64_t>(S) * C::kBTile;
+    const int my_eb = n_eb > 0 ? static_cast<int>(blockIdx.x) % n_eb : 0;  // this CTA's expert block
+    const int my_q = n_eb > 0 ? static_cast<int>(blockIdx.x) / n_eb : 0;   // and its first token group
+    const bool has_tasks = staged && my_q < cta_per_eb && my_q < ntg;
     float* st_router = reinterpret_cast<float*>(smem_a + 4 * kATile);
+    // Round r's token rows: st_x + r * kLogitTokens * H.
     uint16_t* st_x = reinterpret_cast<uint16_t*>(smem_a + 4 * kATile + static_cast<size_t>(kEpiWarps) * H * 4);
 
     if (threadIdx.x == 0) {
@@ -304,23 +310,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t issued_mask = 0;
             uint32_t issued_phase = 0;
             bool ok = true;
-            if (staged && has_tasks) {
-                // The CTA's router rows and token rows for the logits (see `staged`).
-                const int tg = task0 / E;
-                const int e0 = task0 - tg * E;
-                const int t0 = tg * kLogitTokens;
-                const int nt = min(kLogitTokens, T - t0);
+            if (has_tasks) {
+                // The CTA's router rows and each round's token rows (see `staged`).
                 const uint32_t rbytes = static_cast<uint32_t>(kEpiWarps) * H * 4;
-                const uint32_t xbytes = static_cast<uint32_t>(nt) * H * 2;
-                mbar_arrive_expect_tx(logit_bar, rbytes + xbytes);
-                const uint8_t* rsrc = reinterpret_cast<const uint8_t*>(args.router + static_cast<size_t>(e0) * H);
-                const uint8_t* xsrc = reinterpret_cast<const uint8_t*>(args.x + static_cast<size_t>(t0) * H);
+                uint32_t xbytes[2] = {0, 0};
+                for (int r = 0; r < rounds; ++r) {
+                    const int tg = my_q + r * cta_per_eb;
+                    if (tg < ntg) xbytes[r] = static_cast<uint32_t>(min(kLogitTokens, T - tg * kLogitTokens)) * H * 2;
+                }
+                mbar_arrive_expect_tx(logit_bar, rbytes + xbytes[0] + xbytes[1]);
+                const uint8_t* rsrc =
+                    reinterpret_cast<const uint8_t*>(args.router + static_cast<size_t>(my_eb) * kEpiWarps * H);
                 for (uint32_t off = 0; off < rbytes; off += 16384)
                     bulk_load(reinterpret_cast<uint8_t*>(st_router) + off, rsrc + off,
                               rbytes - off < 16384 ? rbytes - off : 16384, logit_bar);
-                for (uint32_t off = 0; off < xbytes; off += 16384)
-                    bulk_load(reinterpret_cast<uint8_t*>(st_x) + off, xsrc + off,
-                              xbytes - off < 16384 ? xbytes - off : 16384, logit_bar);
+                for (int r = 0; r < rounds; ++r) {
+                    const int t0 = (my_q + r * cta_per_eb) * kLogitTokens;
+                    const uint8_t* xsrc = reinterpret_cast<const uint8_t*>(args.x + static_cast<size_t>(t0) * H);
+                    uint8_t* dst = reinterpret_cast<uint8_t*>(st_x + static_cast<size_t>(r) * kLogitTokens * H);
+                    for (uint32_t off = 0; off < xbytes[r]; off += 16384)
+                        bulk_load(dst + off, xsrc + off, xbytes[r] - off < 16384 ? xbytes[r] - off : 16384, logit_bar);
+                }
             }
             // Token tiles whose rows are not written yet (x_perm before counter 2, h
             // before counter 1), oldest first: every x_perm entry precedes every h one.
@@ -435,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (issued_mask & (1u << st)) mbar_wait_drain(&full[st], (issued_phase >> st) & 1u, 100000000ull);
             }
             // The logit inputs' copies (long landed on every path that got this far).
-            if (staged && has_tasks) mbar_wait_drain(logit_bar, 0, 100000000ull);
+            if (has_tasks) mbar_wait_drain(logit_bar, 0, 100000000ull);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -596,16 +606,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             // the router row once for its 8 tokens.  Consecutive warps take consecutive
             // experts of the same tokens, so a CTA's token rows stay in L1.
             if (staged) {
-                // Inputs in shared memory: warp ew takes expert e0 + ew of the CTA's token
-                // group (every thread waits for the copies itself; an expired wait has
-                // recorded its status, which the grid wait below sees).
-                if (has_tasks && mbar_wait(logit_bar, 0, abort_flag, args.status, kDevTimeoutEpilogue)) {
-                    const int p = task0 + ew;
-                    const int tg = p / E;
-                    const int e = p - tg * E;
+                // Inputs in shared memory: warp ew takes expert my_eb * kEpiWarps + ew of
+                // each round's token group (every thread waits for the copies itself; an
+                // expired wait has recorded its status, which the grid wait below sees).
+                const bool got = has_tasks && mbar_wait(logit_bar, 0, abort_flag, args.status, kDevTimeoutEpilogue);
+                for (int r = 0; got && r < rounds; ++r) {
+                    const int tg = my_q + r * cta_per_eb;
+                    if (tg >= ntg) break;
+                    const int e = my_eb * kEpiWarps + ew;
                     const int t0 = tg * kLogitTokens;
                     const int nt = min(kLogitTokens, T - t0);
                     const float* wr = st_router + static_cast<size_t>(ew) * H;
+                    const uint16_t* xr = st_x + static_cast<size_t>(r) * kLogitTokens * H;
                     float acc[kLogitTokens];
 #pragma unroll
                     for (int j = 0; j < kLogitTokens; ++j) acc[j] = 0.0f;
@@ -615,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
                         for (int j = 0; j < kLogitTokens; ++j) {
-                            const uint4 raw = *reinterpret_cast<const uint4*>(st_x + static_cast<size_t>(min(j, nt - 1)) * H + hh);
+                            const uint4 raw = *reinterpret_cast<const uint4*>(xr + static_cast<size_t>(min(j, nt - 1)) * H + hh);
                             const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
                             for (int i = 0; i < 4; ++i) {
