@@ -241,7 +241,7 @@ const char* lm_kernel_description(void) {
     // The device code of this library is compiled for sm_100a only (no PTX for JIT),
     // so the description is fixed at build time, as the reference's is.
     return "sm_100a kernels: tcgen05/TMEM tensor cores fed by TMA -- the whole MoE layer in one cooperative "
-           "launch up to 128 tokens, grouped SwiGLU GEMMs (1-CTA and CTA-pair) above, warp-per-token router; "
+           "launch up to 256 tokens, grouped SwiGLU GEMMs (1-CTA and CTA-pair) above, warp-per-token router; "
            "bf16 weights, f32 accumulate";
 }
 
