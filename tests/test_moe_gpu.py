@@ -119,11 +119,13 @@ def _read_f32(buf, offset: int, shape):
 
 
 @pytest.mark.parametrize("T,offset,with_bias", [(77, 0, False), (77, 2, False), (1, 0, True), (16, 0, True),
-                                                (16, 4, True)])
+                                                (16, 4, True), (300, 0, False), (1000, 0, True)])
 def test_forward_host_page_locked_buffers(small_layer, T, offset, with_bias):
     """Page-locked buffers: 16-byte aligned ones move by SM loads and stores over mapped
     memory, misaligned ones (offset 2 or 4) by copy-engine transfers; both must give the
-    device-buffer forward's result, on two calls in a row."""
+    device-buffer forward's result, on two calls in a row.  Up to 256 tokens the fused
+    kernel runs between the pull and push kernels; 300 and 1000 tokens take the grouped
+    launches (1000: tensor-core router logits), whose first kernel must wait for the pull."""
     layer, _ = small_layer
     xb = syn.tokens(SMALL, T, seed=T + 3)
     bias = np.linspace(-1.0, 1.0, SMALL.n_routed_experts).astype(np.float32) if with_bias else None
