@@ -74,6 +74,10 @@ struct lm_moe_ctx {
     int sms = 148;
     int rank = 0;
     int nranks = 1;
+    // Testing and profiling only (LITEMIND_B200_EP_SINGLE=1 at lm_moe_ep_init): a one-rank
+    // expert-parallel context runs the exchange path, NCCL sending to itself, instead of
+    // the local path, so that the exchange's kernels run on one GPU.
+    bool ep_single = false;
     int first_expert = 0;
     int local_experts = 0;
     int n_seg = 0;
@@ -1833,7 +1837,7 @@ lm_status lm_moe_forward(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x, int3
     if (tokens > 0 && (x == nullptr || y == nullptr || !aligned16(x) || !aligned16(y)))
         return fail(ctx, LM_ERR_INVALID_ARGUMENT, "x and y must be 16-byte aligned device pointers");
     if ((st = set_device(ctx)) != LM_OK) return st;
-    if (ctx->nranks > 1)
+    if (ctx->nranks > 1 || ctx->ep_single)
         return forward_ep(ctx, layer, x, nullptr, tokens, logit_bias, y, accumulate, static_cast<cudaStream_t>(stream));
     return forward_impl(ctx, layer, x, nullptr, tokens, logit_bias, y, accumulate, static_cast<cudaStream_t>(stream));
 }
@@ -1878,7 +1882,7 @@ lm_status lm_moe_forward_host(lm_moe_ctx* ctx, int32_t layer, const uint16_t* x_
     if (logit_bias_host != nullptr && !bias_pulled)
         LM_CUDA(ctx, cudaMemcpyAsync(ctx->bias_stage, logit_bias_host, bias_bytes, cudaMemcpyHostToDevice, s));
     const float* bias = logit_bias_host != nullptr ? ctx->bias_stage : nullptr;
-    st = ctx->nranks > 1 ? forward_ep(ctx, layer, ctx->x_stage, nullptr, tokens, bias, ctx->y_stage, 0, s)
+    st = ctx->nranks > 1 || ctx->ep_single ? forward_ep(ctx, layer, ctx->x_stage, nullptr, tokens, bias, ctx->y_stage, 0, s)
                          : forward_impl(ctx, layer, ctx->x_stage, nullptr, tokens, bias, ctx->y_stage, 0, s);
     if (st != LM_OK) return st;
     // y and the status word come back in the same stream order: one synchronisation
@@ -1915,7 +1919,8 @@ lm_status lm_moe_block_forward(lm_moe_ctx* ctx, int32_t layer, float* hidden, in
                                       c.hidden_size, c.rms_norm_eps, s));
     // The residual add (:290) is folded into the down-projection epilogue: it
     // accumulates straight into `hidden`.
-    if (ctx->nranks > 1) return forward_ep(ctx, layer, ctx->norm_bf16, ctx->norm_f32, tokens, nullptr, hidden, 1, s);
+    if (ctx->nranks > 1 || ctx->ep_single)
+        return forward_ep(ctx, layer, ctx->norm_bf16, ctx->norm_f32, tokens, nullptr, hidden, 1, s);
     return forward_impl(ctx, layer, ctx->norm_bf16, ctx->norm_f32, tokens, nullptr, hidden, 1, s);
 }
 
@@ -2218,6 +2223,7 @@ lm_status lm_moe_ep_init(lm_moe_ctx* ctx, const void* nccl_unique_id, int32_t ra
     }
     ctx->rank = rank;
     ctx->nranks = nranks;
+    if (const char* v = std::getenv("LITEMIND_B200_EP_SINGLE")) ctx->ep_single = nranks == 1 && std::atoi(v) != 0;
     ctx->first_expert = rank * El;
     ctx->local_experts = El;
     ctx->n_seg = El + c.n_shared_experts;

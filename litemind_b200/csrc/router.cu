@@ -470,15 +470,19 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(float* __restrict__ y, 
 // Expert parallelism: received rows arrive grouped by source rank, each source's
 // rows grouped by this rank's experts.  The grouped GEMMs want each expert's rows
 // contiguous, so each expert's weights stream once instead of once per source.
-// Block (b, y) with b = (source r, local expert e) copies rows [64 y, 64 y + 64) of
+// Block (b, y) with b = (source r, local expert e) copies rows [16 y, 16 y + 16) of
 // its group to their expert-major place and records where each came from, so the
-// down projection can store its output rows back in receive order.
+// down projection can store its output rows back in receive order.  The copy is
+// bound by the bytes in flight: each thread issues kSortUnroll 16-byte loads before
+// their stores, and the small blocks give several CTAs per SM (64-row blocks with one
+// load in flight per thread reached 17% of the DRAM bandwidth).
 //
 // A pipelined exchange moves the local experts in chunks [e_lo, e_hi): the receive
 // buffer is chunk-major (all rows of earlier chunks first), source-major within a
 // chunk.  One launch sorts one chunk; the whole range [0, El) is the unchunked
 // source-major layout.  The expert-major destination does not depend on chunking.
-constexpr int kSortRows = 64;
+constexpr int kSortRows = 16;
+constexpr int kSortUnroll = 4;
 // src_stride > 0: each source's rows sit in a fixed block of src_stride rows
 // (the fixed-capacity exchange, one chunk) instead of back to back.
 __global__ void __launch_bounds__(256) ep_sort_rows_kernel(const uint16_t* __restrict__ x_recv,
@@ -492,31 +496,50 @@ __global__ void __launch_bounds__(256) ep_sort_rows_kernel(const uint16_t* __res
     const int r = blockIdx.x / ne;
     const int e = e_lo + (blockIdx.x - r * ne);
     __shared__ int s_src, s_dst, s_cnt;
-    if (threadIdx.x == 0) {
-        int src = src_stride > 0 ? r * src_stride : 0, dst = 0;
-        for (int rr = 0; rr < N; ++rr) {
-            for (int ee = 0; ee < El; ++ee) {
-                const int c = recv_counts[rr * El + ee];
-                const bool before = src_stride > 0
-                                        ? (rr == r && ee < e)
-                                        : (ee < e_lo || (ee < e_hi && (rr < r || (rr == r && ee < e))));
-                if (before) src += c;  // chunk-major, then source-major position
-                if (ee < e || (ee == e && rr < r)) dst += c;  // expert-major position
-            }
+    if (threadIdx.x < 32) {
+        // The group's place in the receive buffer and in expert-major order: sums of
+        // the (source, expert) counts before it, over the first warp.
+        int src = 0, dst = 0;
+        for (int i = threadIdx.x; i < N * El; i += 32) {
+            const int rr = i / El, ee = i - rr * El;
+            const int c = recv_counts[i];
+            const bool before = src_stride > 0
+                                    ? (rr == r && ee < e)
+                                    : (ee < e_lo || (ee < e_hi && (rr < r || (rr == r && ee < e))));
+            if (before) src += c;  // chunk-major, then source-major position
+            if (ee < e || (ee == e && rr < r)) dst += c;  // expert-major position
         }
-        s_src = src;
-        s_dst = dst;
-        s_cnt = recv_counts[r * El + e];
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+            src += __shfl_xor_sync(0xffffffffu, src, d);
+            dst += __shfl_xor_sync(0xffffffffu, dst, d);
+        }
+        if (threadIdx.x == 0) {
+            s_src = (src_stride > 0 ? r * src_stride : 0) + src;
+            s_dst = dst;
+            s_cnt = recv_counts[r * El + e];
+        }
     }
     __syncthreads();
-    const int j0 = blockIdx.y * kSortRows;
-    const int rows = min(kSortRows, s_cnt - j0);
-    if (rows <= 0) return;
     const int vec = H / 8;
-    const uint4* src = reinterpret_cast<const uint4*>(x_recv) + static_cast<size_t>(s_src + j0) * vec;
-    uint4* dst = reinterpret_cast<uint4*>(x_sorted) + static_cast<size_t>(s_dst + j0) * vec;
-    for (int q = threadIdx.x; q < rows * vec; q += blockDim.x) dst[q] = src[q];
-    for (int j = threadIdx.x; j < rows; j += blockDim.x) row_src[s_dst + j0 + j] = s_src + j0 + j;
+    const int nt = static_cast<int>(blockDim.x);
+    // Row blocks y, y + gridDim.y, ... (the grid's y extent is capped).
+    for (int j0 = blockIdx.y * kSortRows; j0 < s_cnt; j0 += gridDim.y * kSortRows) {
+        const int rows = min(kSortRows, s_cnt - j0);
+        const uint4* src = reinterpret_cast<const uint4*>(x_recv) + static_cast<size_t>(s_src + j0) * vec;
+        uint4* dst = reinterpret_cast<uint4*>(x_sorted) + static_cast<size_t>(s_dst + j0) * vec;
+        const int n = rows * vec;
+        for (int base = threadIdx.x; base < n; base += nt * kSortUnroll) {
+            uint4 v[kSortUnroll];
+#pragma unroll
+            for (int u = 0; u < kSortUnroll; ++u)
+                if (base + u * nt < n) v[u] = __ldcs(src + base + u * nt);  // read once
+#pragma unroll
+            for (int u = 0; u < kSortUnroll; ++u)
+                if (base + u * nt < n) dst[base + u * nt] = v[u];
+        }
+        for (int j = threadIdx.x; j < rows; j += nt) row_src[s_dst + j0 + j] = s_src + j0 + j;
+    }
 }
 
 // Small T (<= kRouteTile): the whole routing stage in one launch.  CTA b computes
@@ -910,7 +933,8 @@ cudaError_t launch_ep_sort_rows(const uint16_t* x_recv, uint16_t* x_sorted, int3
     if (max_group_rows <= 0 || e_hi <= e_lo) return cudaSuccess;
     if (e_lo < 0 || e_hi > local_experts || (src_stride > 0 && (e_lo != 0 || e_hi != local_experts)))
         return cudaErrorInvalidValue;
-    const dim3 grid(nranks * (e_hi - e_lo), (max_group_rows + kSortRows - 1) / kSortRows);
+    const int blocks = (max_group_rows + kSortRows - 1) / kSortRows;
+    const dim3 grid(nranks * (e_hi - e_lo), std::min(blocks, 65535));
     return launch_k(ep_sort_rows_kernel, grid, dim3(256), stream, pdl, x_recv, x_sorted, row_src, recv_counts,
                     nranks, local_experts, hidden, src_stride, e_lo, e_hi);
 }
