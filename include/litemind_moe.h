@@ -329,7 +329,9 @@ lm_status lm_moe_ep_plan(int32_t nranks, int32_t experts, const int32_t* send_ex
  * lm_moe_forward uses LITEMIND_B200_EP_CHUNKS chunks (default 2, at most 8 and at
  * most El) when the context exchanges by host plan, with NCCL capped to
  * LITEMIND_B200_EP_NCCL_CTAS CTAs (default 32) and the GEMMs leaving it that many
- * SMs; every rank must use the same (lm_moe_ep_init checks).
+ * SMs; every rank must use the same (lm_moe_ep_init checks).  Testing and profiling
+ * only: with LITEMIND_B200_EP_SINGLE=1 at lm_moe_ep_init, a one-rank context runs this
+ * exchange path (NCCL sending to itself) instead of the local path.
  */
 lm_status lm_moe_ep_chunk_plan(int32_t nranks, int32_t experts, int32_t chunks, int32_t chunk,
                                const int32_t* send_expert_counts, const int32_t* recv_expert_counts,
