@@ -952,13 +952,26 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
     pdl_wait();
     pdl_launch_dependents();
     __shared__ int off[kMaxExperts + 1];
-    if (threadIdx.x == 0) {
-        int o = 0;
-        for (int e = 0; e < E; ++e) {
-            off[e] = o;
-            o += expert_totals[e];
+    if (threadIdx.x < 32) {
+        // Each expert's first expert-sorted row: an exclusive scan of the totals by the
+        // first warp, every total loaded in one round trip.
+        const int ln = threadIdx.x;
+        int cv[kMaxExperts / 32];
+#pragma unroll
+        for (int i = 0; i < kMaxExperts / 32; ++i) cv[i] = i * 32 + ln < E ? expert_totals[i * 32 + ln] : 0;
+        int run = 0;
+#pragma unroll
+        for (int i = 0; i < kMaxExperts / 32; ++i) {
+            int incl = cv[i];
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, d);
+                if (ln >= d) incl += v;
+            }
+            if (i * 32 + ln < E) off[i * 32 + ln] = run + incl - cv[i];
+            run += __shfl_sync(0xffffffffu, incl, 31);
         }
-        off[E] = o;
+        if (ln == 0) off[E] = run;
     }
     __syncthreads();
     const int n_rows = T * K;
@@ -976,10 +989,19 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
         return d * cap + (r - off[d * El]);
     };
     const int vec = H / 8;
+    constexpr int kPackUnroll = 8;  // a lane's 16-byte loads in flight together (a 4 KB row per warp)
     for (int r = warp; r < n_rows; r += n_warps) {
         const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row_token[r]) * H);
         uint4* dst = reinterpret_cast<uint4*>(x_send + static_cast<size_t>(padded(r)) * H);
-        for (int v = lane; v < vec; v += 32) dst[v] = src[v];
+        for (int v0 = 0; v0 < vec; v0 += 32 * kPackUnroll) {
+            uint4 t[kPackUnroll];
+#pragma unroll
+            for (int u = 0; u < kPackUnroll; ++u)
+                if (v0 + u * 32 + lane < vec) t[u] = src[v0 + u * 32 + lane];
+#pragma unroll
+            for (int u = 0; u < kPackUnroll; ++u)
+                if (v0 + u * 32 + lane < vec) dst[v0 + u * 32 + lane] = t[u];
+        }
     }
     for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < n_rows; q += gridDim.x * blockDim.x)
         if (slot_row[q] >= 0) slot_row[q] = padded(slot_row[q]);
